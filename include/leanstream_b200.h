@@ -1,0 +1,273 @@
+/*
+ * leanstream_b200.h -- C ABI of the B200 sparse streaming-MLP compute backend.
+ *
+ * This header is the whole drop-in boundary. It replaces two reference
+ * surfaces:
+ *   - backends/triton/enqueue.cpp + include/leanstream/triton_cuda.h
+ *     (the ls_triton_* ABI and TritonBackend::view);
+ *   - kernels/streaming_mlp.cu/.cuh and streaming_mlp_candidates.cu
+ *     (the CUDA reference backend: core_kernel -> consumer -> reduction).
+ * Only plain integers, pointers and POD structs cross it. No torch types.
+ *
+ * The structs marked "binary-compatible" have exactly the layout of the
+ * reference's C++ types. A C++ caller that owns a leanstream::runtime::Runtime
+ * can therefore reinterpret an ls_compute_backend as a ComputeBackend.
+ * The static asserts in leanstream_b200/csrc/ls_backend.cu check the layout.
+ *
+ * Memory model (discrete B200, PCIe host):
+ *   - Packed weights (cache, staging), scales, input/output vectors and the
+ *     optional activation / counter buffers are DEVICE memory.
+ *   - Descriptors, ready indices and ls_queue_control may be either device
+ *     memory or mapped pinned host memory (cudaHostAllocMapped). The kernel
+ *     reads them with system-scope acquire loads and never writes them.
+ *   - Claim counters live in a backend-owned device workspace. Discrete GPUs
+ *     do not provide host-native atomics, so QueueControl.claim_count and
+ *     consumer_path are left untouched.
+ * Every device-side wait is bounded by a %globaltimer deadline. On expiry
+ * the kernel records an LS_B200_DEV_* code in the status words and exits.
+ */
+#ifndef LEANSTREAM_B200_H
+#define LEANSTREAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Binary-compatible mirrors of the reference descriptor/queue types.  */
+/* ------------------------------------------------------------------ */
+
+/* ExecDesc (include/leanstream/types.h:16-20): five uint32, 20 bytes. */
+typedef struct ls_exec_desc {
+    uint32_t logical_group;  /* predictor / application ID */
+    uint32_t physical_group; /* selects the fp16 scale rows */
+    uint32_t source_slot;    /* slot in cache (kind 0) or staging (kind 1) */
+    uint32_t dest_slot;      /* deterministic partial / activation destination */
+    uint32_t source_kind;    /* LS_SOURCE_CACHE or LS_SOURCE_STAGING */
+} ls_exec_desc;
+
+enum { LS_SOURCE_CACHE = 0, LS_SOURCE_STAGING = 1 };
+
+/* ConsumerMode (types.h:13), an enum class : uint8_t. */
+enum { LS_MODE_BATCH_COMPAT = 0, LS_MODE_PROGRESSIVE = 1, LS_MODE_AUTO = 2 };
+
+/* QueueControl (include/leanstream/execution_queue.h:5-12): 128 bytes,
+ * epoch at byte 12, claim_count on its own cache line at byte 64. */
+typedef struct ls_queue_control {
+    uint32_t ready_count, reserved, total_count, epoch;
+    uint32_t batch_epoch, error, consumer_path, init_arrived, init_epoch;
+    uint32_t pad0[7];
+    uint32_t claim_count;
+    uint32_t pad1[15];
+} ls_queue_control;
+
+/* DeviceExecQueue (execution_queue.h:13-18). */
+typedef struct ls_device_exec_queue {
+    ls_exec_desc* descriptors;
+    uint32_t* ready_indices;
+    ls_queue_control* control;
+    uint32_t capacity;
+} ls_device_exec_queue;
+
+/* Span<ExecDesc> and Span<GroupId> (types.h:7-10). */
+typedef struct ls_exec_span { const ls_exec_desc* data; size_t size; } ls_exec_span;
+typedef struct ls_group_span { const int32_t* data; size_t size; } ls_group_span;
+
+/* ComputeBackend (include/leanstream/runtime.h:10-22). ConsumerMode is
+ * passed as its underlying uint8_t. */
+typedef struct ls_compute_backend {
+    void* context;
+    int (*enqueue)(void* context, uint32_t layer, const void* input, void* output, void* stream,
+                   ls_exec_span core, ls_device_exec_queue queue, uint32_t epoch, uint8_t mode);
+    bool (*complete)(void* context, uint32_t layer);
+    int (*commit)(void* context, uint32_t layer, ls_group_span ids);
+    int (*defer_commit)(void* context, uint32_t layer, ls_group_span ids, uint32_t epoch,
+                        void (*retired)(void*, uint32_t epoch), void* retirement_context);
+    void (*cancel)(void* context, uint32_t layer, uint32_t epoch);
+} ls_compute_backend;
+
+/* KernelCandidate (include/leanstream/kernel_selector.h:6-12). */
+typedef struct ls_kernel_candidate {
+    uint32_t id;
+    uint32_t workers;     /* persistent CTAs, as in the Triton catalog */
+    const char* name;
+    uint32_t cta_count, tile_size, unroll, group_batch, entry_point;
+    bool available;
+} ls_kernel_candidate;
+
+/* ------------------------------------------------------------------ */
+/* Backend geometry and borrowed buffers.                              */
+/* ------------------------------------------------------------------ */
+
+typedef struct ls_b200_geometry {
+    uint32_t hidden;        /* H: multiple of 256, at most 8192 */
+    uint32_t group_size;    /* G: neurons per logical group, 1..256 */
+    uint32_t group_count;   /* N: logical groups = dest slots = partial rows */
+    uint32_t max_layers;    /* number of per-layer completion words (0 -> 256) */
+    uint32_t cache_slots;   /* optional bound on cache source_slot (0 = unchecked) */
+    uint32_t staging_slots; /* optional bound on staging source_slot (0 = unchecked) */
+    uint32_t physical_groups; /* optional bound on physical_group (0 = unchecked) */
+    uint32_t timeout_us;    /* bound of every device wait (0 -> 5,000,000) */
+    float rms_eps;          /* epsilon of the optional RMSNorm prologue */
+} ls_b200_geometry;
+
+/* Flags of ls_b200_layer_args.flags. */
+enum {
+    LS_B200_NORM_INPUT = 1u << 0, /* apply HF RMSNorm to the input before the MLP */
+    LS_B200_NO_OUTPUT = 1u << 1   /* skip the fp16 output store (fp32 partial only) */
+};
+
+/* Every buffer of one MLP layer invocation. Borrowed until GPU completion. */
+typedef struct ls_b200_layer_args {
+    const void* input;        /* fp16 [H] */
+    void* output;             /* fp16 [H]: y = fp16(sum of partial rows) */
+    const uint8_t* cache;     /* packed INT4 groups (device memory) */
+    const uint8_t* staging;   /* packed INT4 groups (device memory; may equal cache) */
+    const void* scales;       /* fp16 [physical_group][G][3][H/128] */
+    const ls_exec_desc* core; /* core descriptors (GPU-addressable), dest slots first */
+    uint32_t core_count;
+    uint32_t epoch;           /* QueueControl.epoch this launch consumes (nonzero) */
+    ls_device_exec_queue queue;
+    uint8_t mode;             /* LS_MODE_* */
+    uint8_t pad[3];
+    uint32_t flags;           /* LS_B200_* flags */
+    int32_t candidate;        /* kernel candidate id, or -1 for the selector's choice */
+    uint32_t layer;           /* completion word index */
+    void* activations;        /* optional fp16 [N*G]: h at dest_slot*G + neuron */
+    uint32_t* executions;     /* optional [N]: +1 per executed descriptor, dest-indexed */
+    uint64_t* first_compute;  /* optional [N]: %globaltimer when a descriptor is claimed */
+    const void* residual;     /* optional fp16 [H]: hidden_out = fp16(residual + y) */
+    void* hidden_out;         /* optional fp16 [H] */
+    float* output_f32;        /* optional fp32 [H]: unrounded sum (tensor-parallel partial) */
+    const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
+} ls_b200_layer_args;
+
+/* Device status words (ls_b200_status). */
+enum {
+    LS_B200_STATUS_ERROR = 0,       /* first LS_B200_DEV_* code since the last clear */
+    LS_B200_STATUS_ERROR_EPOCH = 1, /* epoch of the launch that recorded it */
+    LS_B200_STATUS_ERROR_DETAIL = 2,/* position / slot involved */
+    LS_B200_STATUS_LAUNCHES = 3,    /* completed launches */
+    LS_B200_STATUS_WORDS = 4
+};
+enum {
+    LS_B200_DEV_OK = 0,
+    LS_B200_DEV_QUEUE_ERROR = 1,    /* QueueControl.error observed nonzero */
+    LS_B200_DEV_TIMEOUT_EPOCH = 2,  /* epoch / batch_epoch never published */
+    LS_B200_DEV_TIMEOUT_READY = 3,  /* a claimed position never became ready */
+    LS_B200_DEV_TIMEOUT_SYNC = 4,   /* an intra-kernel wait exceeded the deadline */
+    LS_B200_DEV_BAD_DESCRIPTOR = 5, /* slot / group / index out of range */
+    LS_B200_DEV_BAD_PLAN = 6        /* total_count exceeds capacity or slots */
+};
+
+/* ------------------------------------------------------------------ */
+/* Backend lifecycle (mirrors ls_triton_*, triton_cuda.h:49-57).        */
+/* ------------------------------------------------------------------ */
+
+/* ls_triton_create (triton_cuda.h:50): backend with the built-in fallback only. */
+void* ls_b200_create(void);
+/* ls_triton_create_table (triton_cuda.h:51): borrowed row-major LUT
+ * [layers * buckets] of candidate ids, immutable for the backend lifetime. */
+void* ls_b200_create_table(const uint8_t* lut, uint32_t layers, uint32_t buckets);
+/* ls_triton_destroy (triton_cuda.h:52). Caller must have proved GPU completion. */
+void ls_b200_destroy(void* backend);
+/* Cold setup, replaces ls_triton_bind (triton_cuda.h:54-55): validates the
+ * geometry, checks the device is sm_100, allocates the device workspace and
+ * the mapped status / completion words. Call once on the device that runs
+ * the launches; returns 0 or an errno-style code. */
+int ls_b200_configure(void* backend, const ls_b200_geometry* geometry);
+/* Borrowed buffers used by ls_b200_enqueue and the ComputeBackend view
+ * (MLPBuffers, kernels/streaming_mlp.cuh:6-14). input/output fields are
+ * overridden by ComputeBackend.enqueue's arguments. */
+int ls_b200_set_buffers(void* backend, const ls_b200_layer_args* buffers);
+/* KernelRuntimeState (kernel_selector.h:4) used by the next enqueue;
+ * TritonBackend::state (triton_cuda.h:38). */
+void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket);
+
+/* ------------------------------------------------------------------ */
+/* Submission.                                                          */
+/* ------------------------------------------------------------------ */
+
+/* One fused launch (A core + persistent B consumer + compact reduction)
+ * on `stream`: every buffer comes from `args`. No allocation,
+ * compilation or synchronisation. Replaces enqueue_streaming_mlp
+ * (kernels/streaming_mlp.cu:85-93). */
+int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream);
+/* ls_triton_enqueue (triton_cuda.h:56; enqueue.cpp:26-37): LUT-selected
+ * candidate, bound buffers and queue from ls_b200_set_buffers. */
+int ls_b200_enqueue(void* backend, uint32_t layer, uint32_t bucket, uint32_t epoch, void* stream);
+/* TritonBackend::view (enqueue.cpp:46): fills a ComputeBackend whose
+ * enqueue accepts BatchCompat, Progressive and Auto (Auto waits for the
+ * batch epoch, as streaming_mlp.cu:90 does). complete() polls the
+ * per-layer completion word; commit() accepts the next resident set
+ * (cache installation belongs to the application; returns 0). */
+int ls_b200_view(void* backend, ls_compute_backend* out);
+/* Last epoch whose launch for `layer` has fully finished on the GPU
+ * (reduction included), read from mapped memory without synchronising.
+ * This is the Done epoch of backends/triton/primitives.py:10-14. */
+int ls_b200_completed_epoch(void* backend, uint32_t layer, uint32_t* epoch);
+
+/* Tensor-parallel layer epilogue (one rank): after the fp32 partial outputs
+ * of all ranks are summed (NCCL allreduce of output_f32), round once to fp16
+ * and add the residual -- the single-GPU epilogue of
+ * backends/triton/reduction.py:14-20 split across the collective.
+ * output (optional): fp16 y; hidden_out (optional): fp16(residual + y). */
+int ls_b200_tp_epilogue(const float* y32, const void* residual, void* output, void* hidden_out, uint32_t hidden,
+                        void* stream);
+/* Bounded device-side delay (<= 100 ms) on `stream`. Benchmarks queue it
+ * ahead of event-bracketed launches so the brackets measure kernels only. */
+int ls_b200_spin(uint64_t nanoseconds, void* stream);
+
+/* Device status words (LS_B200_STATUS_*), read without synchronising. */
+int ls_b200_status(void* backend, uint32_t* words, uint32_t count);
+int ls_b200_clear_status(void* backend);
+/* Scratch sizes the backend allocated (partials, workspace), in bytes. */
+uint64_t ls_b200_scratch_bytes(void* backend);
+
+/* ------------------------------------------------------------------ */
+/* Kernel selection (src/runtime/kernel_selector.cpp, triton_backend.h). */
+/* ------------------------------------------------------------------ */
+
+/* quantize_io_load (kernel_selector.cpp:4-8). */
+uint32_t ls_b200_quantize_io_load(uint32_t remaining, uint32_t total, uint32_t buckets);
+/* KernelSelector::select (kernel_selector.cpp:17-22) over the B200 catalog. */
+uint32_t ls_b200_select(void* backend, uint32_t layer, uint32_t io_bucket);
+/* KernelSelector::candidate (kernel_selector.cpp:9-16). */
+int ls_b200_candidate(void* backend, uint32_t id, ls_kernel_candidate* out);
+/* Number of catalog entries and the fallback id. */
+uint32_t ls_b200_catalog_size(void);
+uint32_t ls_b200_default_candidate(void);
+
+/* ------------------------------------------------------------------ */
+/* Host producer: ExecutionQueue (src/runtime/execution_queue.cpp:4-46) */
+/* restated for callers that do not link the reference runtime.        */
+/* ------------------------------------------------------------------ */
+
+typedef struct ls_b200_queue {
+    ls_device_exec_queue view;
+    uint32_t tail, epoch, total;
+} ls_b200_queue;
+
+void ls_b200_queue_bind(ls_b200_queue* queue, ls_device_exec_queue view);
+int ls_b200_queue_reset(ls_b200_queue* queue, uint32_t epoch);
+int ls_b200_queue_prepare(ls_b200_queue* queue, uint32_t total);
+int ls_b200_queue_append_unpublished(ls_b200_queue* queue, uint32_t index);
+int ls_b200_queue_activate(ls_b200_queue* queue);
+int ls_b200_queue_seal(ls_b200_queue* queue, uint32_t total);
+int ls_b200_queue_publish_all(ls_b200_queue* queue);
+int ls_b200_queue_publish(ls_b200_queue* queue, uint32_t index);
+int ls_b200_queue_fail(ls_b200_queue* queue, uint32_t error);
+
+/* Library build identity: "sm_100a" plus the kernel revision. */
+const char* ls_b200_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LEANSTREAM_B200_H */

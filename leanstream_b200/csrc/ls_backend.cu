@@ -1,0 +1,465 @@
+// Host side of the B200 compute backend: backend object, kernel selector,
+// ExecutionQueue producer and the extern "C" ABI of include/leanstream_b200.h.
+//
+// Replaces backends/triton/enqueue.cpp (TritonBackend, ls_triton_*) and the
+// launch wrapper of kernels/streaming_mlp.cu:85-93 /
+// streaming_mlp_candidates.cu:3-11. The runtime above the boundary
+// (Runtime / LayerStep / WeightManager) is not touched: it reaches this
+// backend through ls_b200_view, which fills a ComputeBackend
+// (include/leanstream/runtime.h:10-22).
+#include <cerrno>
+#include <cstddef>
+#include <cstring>
+#include <new>
+#include <limits>
+#include <cuda_runtime.h>
+#include "ls_internal.h"
+
+// ---------------------------------------------------------------- layout checks
+static_assert(sizeof(ls_exec_desc) == 20, "ExecDesc is five uint32 (types.h:16-20)");
+static_assert(sizeof(ls_queue_control) == 128, "QueueControl is 128 bytes (execution_queue.h:12)");
+static_assert(offsetof(ls_queue_control, epoch) == 12, "execution_queue.h:10");
+static_assert(offsetof(ls_queue_control, error) == 20, "QueueControl.error at word 5");
+static_assert(offsetof(ls_queue_control, claim_count) == 64, "execution_queue.h:11");
+static_assert(sizeof(ls_device_exec_queue) == 32, "DeviceExecQueue: three pointers + capacity");
+static_assert(sizeof(ls_exec_span) == 16, "Span<T>: pointer + size_t");
+static_assert(offsetof(ls_compute_backend, cancel) == 5 * sizeof(void*), "ComputeBackend layout");
+
+namespace lsb {
+namespace {
+
+// ---------------------------------------------------------------- catalog
+// Candidate ids 0..3 keep the production Triton geometry of
+// include/leanstream/triton_backend.h:5-8 (4/8/16/32 persistent CTAs), so an
+// offline LUT written for it keeps its meaning. Id 4 is the B200 entry: one
+// persistent CTA per SM (resolved at configure), the fallback.
+constexpr ls_kernel_candidate kCatalog[] = {
+    {0, 4, "b200_ctas_4", 4, 0, 0, 0, 0, true},
+    {1, 8, "b200_ctas_8", 8, 0, 0, 0, 0, true},
+    {2, 16, "b200_ctas_16", 16, 0, 0, 0, 0, true},
+    {3, 32, "b200_ctas_32", 32, 0, 0, 0, 0, true},
+    {4, 0, "b200_ctas_per_sm", 0, 0, 0, 0, 0, true},
+};
+constexpr uint32_t kCatalogSize = sizeof(kCatalog) / sizeof(kCatalog[0]);
+constexpr uint32_t kDefaultCandidate = 4;
+
+uint32_t quantize_io_load(uint32_t remaining, uint32_t total, uint32_t buckets) {
+    // kernel_selector.cpp:4-8: floor(min(remaining,total)*buckets/total), clamped.
+    if (!total || !buckets) return 0;
+    if (remaining >= total) return buckets - 1;
+    return uint32_t(uint64_t(remaining) * buckets / total);
+}
+
+struct Backend {
+    // selector state (kernel_selector.h:27-41)
+    const uint8_t* lut = nullptr;
+    uint32_t lut_layers = 0, lut_buckets = 0;
+    uint32_t state_layer = 0, state_bucket = 0;
+    // configuration
+    bool configured = false;
+    int device = -1, sms = 0;
+    ls_b200_geometry geo{};
+    ls_b200_layer_args bound{};
+    bool bound_set = false;
+    // scratch (device) and mapped words (host)
+    float* partial = nullptr;
+    uint16_t* hbuf = nullptr;
+    Workspace* ws = nullptr;
+    uint32_t* status_host = nullptr;
+    uint32_t* status_dev = nullptr;
+    uint32_t* done_host = nullptr;
+    uint32_t* done_dev = nullptr;
+    uint32_t* last_epoch = nullptr;  // host: epoch of the last enqueue per layer
+    uint64_t scratch_bytes = 0;
+
+    ls_kernel_candidate candidate(uint32_t id) const {
+        // kernel_selector.cpp:9-16: invalid/unavailable ids fall back.
+        ls_kernel_candidate c = id < kCatalogSize ? kCatalog[id] : kCatalog[kDefaultCandidate];
+        if (c.id != id || !c.available) c = kCatalog[kDefaultCandidate];
+        if (c.cta_count == 0) {
+            c.cta_count = uint32_t(sms > 0 ? sms : 148);
+            c.workers = c.cta_count;
+        }
+        return c;
+    }
+    uint32_t select(uint32_t layer, uint32_t bucket) const {
+        // kernel_selector.cpp:17-22: direct row-major indexing, O(1), no allocation.
+        if (!lut || layer >= lut_layers || bucket >= lut_buckets ||
+            (lut_buckets && size_t(lut_layers) > std::numeric_limits<size_t>::max() / lut_buckets))
+            return kDefaultCandidate;
+        const uint32_t id = lut[size_t(layer) * lut_buckets + bucket];
+        return candidate(id).id;
+    }
+    void release() {
+        if (partial) cudaFree(partial);
+        if (hbuf) cudaFree(hbuf);
+        if (ws) cudaFree(ws);
+        if (status_host) cudaFreeHost(status_host);
+        if (done_host) cudaFreeHost(done_host);
+        delete[] last_epoch;
+        partial = nullptr;
+        hbuf = nullptr;
+        ws = nullptr;
+        status_host = status_dev = nullptr;
+        done_host = done_dev = nullptr;
+        last_epoch = nullptr;
+        configured = false;
+    }
+    ~Backend() { release(); }
+};
+
+int cuda_rc(cudaError_t e) { return e == cudaSuccess ? 0 : (int(e) > 0 ? int(e) : EIO); }
+
+int configure(Backend& b, const ls_b200_geometry& g) {
+    if (b.configured) return EBUSY;
+    const uint32_t H = g.hidden, G = g.group_size, N = g.group_count;
+    if (!H || H % 256 || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N) return EINVAL;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ENODEV;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return ENODEV;
+    if (prop.major != 10) return ENOTSUP;  // sm_100a image only
+    int rc = prepare_kernels();
+    if (rc) return cuda_rc(cudaError_t(rc));
+    b.device = dev;
+    b.sms = prop.multiProcessorCount;
+    b.geo = g;
+    if (!b.geo.max_layers) b.geo.max_layers = 256;
+    if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
+    const size_t partial_bytes = size_t(N) * H * sizeof(float);
+    const size_t h_bytes = size_t(N) * G * sizeof(uint16_t);
+    const size_t ws_bytes = sizeof(Workspace) + size_t(N) * sizeof(uint32_t);
+    cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&b.hbuf, h_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
+    if (e == cudaSuccess) e = cudaHostAlloc(&b.status_host, 64, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b.status_dev), b.status_host, 0);
+    if (e == cudaSuccess)
+        e = cudaHostAlloc(&b.done_host, size_t(b.geo.max_layers) * sizeof(uint32_t), cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b.done_dev), b.done_host, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        b.release();
+        return cuda_rc(e);
+    }
+    std::memset(b.status_host, 0, 64);
+    std::memset(b.done_host, 0, size_t(b.geo.max_layers) * sizeof(uint32_t));
+    b.last_epoch = new (std::nothrow) uint32_t[b.geo.max_layers]();
+    if (!b.last_epoch) {
+        b.release();
+        return ENOMEM;
+    }
+    b.scratch_bytes = partial_bytes + h_bytes + ws_bytes;
+    b.configured = true;
+    return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Hot path: parameter validation and one kernel launch. No allocation,
+// no synchronisation, no device queries (triton_cuda.h:19-20).
+int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
+    if (!b.configured) return EINVAL;
+    if (!a.epoch || !a.input || !a.scales || !a.queue.control || !a.queue.descriptors || !a.queue.ready_indices)
+        return EINVAL;
+    if (!a.cache && !a.staging) return EINVAL;
+    if (a.core_count && !a.core) return EINVAL;
+    if (!a.output && !a.output_f32 && !a.hidden_out) return EINVAL;
+    if (a.hidden_out && !a.residual) return EINVAL;
+    if (a.mode > LS_MODE_AUTO) return EINVAL;
+    if (a.layer >= b.geo.max_layers) return EINVAL;
+    if (a.core_count > b.geo.group_count) return ENOSPC;
+    if ((a.cache && !aligned16(a.cache)) || (a.staging && !aligned16(a.staging)) || !aligned16(a.scales) ||
+        (a.output_f32 && !aligned16(a.output_f32)))
+        return EINVAL;  // cp.async.bulk needs 16-byte aligned sources
+    const uint32_t id = a.candidate >= 0 ? uint32_t(a.candidate) : b.select(b.state_layer, b.state_bucket);
+    const ls_kernel_candidate c = b.candidate(id);
+    int grid = int(c.cta_count);
+    if (grid > b.sms) grid = b.sms;
+    KernelParams p{};
+    p.H = b.geo.hidden;
+    p.G = b.geo.group_size;
+    p.N = b.geo.group_count;
+    p.cache_slots = b.geo.cache_slots;
+    p.staging_slots = b.geo.staging_slots;
+    p.phys_groups = b.geo.physical_groups;
+    p.group_bytes = uint64_t(p.G) * 3 * p.H / 2;
+    p.timeout_ns = uint64_t(b.geo.timeout_us) * 1000ull;
+    p.eps = b.geo.rms_eps;
+    p.epoch = a.epoch;
+    p.mode = a.mode;
+    p.flags = a.flags;
+    p.layer = a.layer;
+    p.core_count = a.core_count;
+    p.x = static_cast<const uint16_t*>(a.input);
+    p.y = static_cast<uint16_t*>(a.output);
+    p.cache = a.cache ? a.cache : a.staging;
+    p.staging = a.staging ? a.staging : a.cache;
+    p.scales = static_cast<const uint16_t*>(a.scales);
+    p.core = a.core;
+    p.q = a.queue;
+    p.act = static_cast<uint16_t*>(a.activations);
+    p.execs = a.executions;
+    p.stamps = a.first_compute;
+    p.residual = static_cast<const uint16_t*>(a.residual);
+    p.hidden_out = static_cast<uint16_t*>(a.hidden_out);
+    p.y32 = a.output_f32;
+    p.norm_w = static_cast<const uint16_t*>(a.norm_weight);
+    p.partial = b.partial;
+    p.hbuf = b.hbuf;
+    p.ws = b.ws;
+    p.status = b.status_dev;
+    p.done = b.done_dev;
+    b.last_epoch[a.layer] = a.epoch;
+    const int rc = launch_fused_layer(p, grid, stream);
+    return rc ? cuda_rc(cudaError_t(rc)) : 0;
+}
+
+// ---------------------------------------------------------------- ComputeBackend
+int view_enqueue(void* ctx, uint32_t layer, const void* input, void* output, void* stream, ls_exec_span core,
+                 ls_device_exec_queue queue, uint32_t epoch, uint8_t mode) {
+    // TritonBackend::submit (enqueue.cpp:38-43), all three modes accepted.
+    auto* b = static_cast<Backend*>(ctx);
+    if (!b || !b->bound_set) return EINVAL;
+    if (core.size > std::numeric_limits<uint32_t>::max()) return EINVAL;
+    ls_b200_layer_args a = b->bound;
+    a.input = input;
+    a.output = output;
+    a.core = core.data;
+    a.core_count = uint32_t(core.size);
+    a.queue = queue;
+    a.epoch = epoch;
+    a.mode = mode;
+    a.layer = layer;
+    a.candidate = -1;
+    b->state_layer = layer;
+    return launch(*b, a, static_cast<cudaStream_t>(stream));
+}
+
+bool view_complete(void* ctx, uint32_t layer) {
+    auto* b = static_cast<Backend*>(ctx);
+    if (!b || !b->configured || layer >= b->geo.max_layers) return false;
+    const uint32_t want = b->last_epoch[layer];
+    if (!want) return true;
+    return __atomic_load_n(b->done_host + layer, __ATOMIC_ACQUIRE) == want;
+}
+
+int view_commit(void*, uint32_t, ls_group_span ids) {
+    // Cache installation is application policy (enqueue.cpp:45); this backend
+    // keeps no cache of its own, so committing a resident set is a no-op.
+    return (ids.size && !ids.data) ? EINVAL : 0;
+}
+
+void view_cancel(void*, uint32_t, uint32_t) {
+    // The Runtime publishes QueueControl.error before calling cancel
+    // (runtime.cpp:41,49,93); the kernel observes it and exits.
+}
+
+}  // namespace
+}  // namespace lsb
+
+using lsb::Backend;
+
+extern "C" {
+
+void* ls_b200_create(void) { return new (std::nothrow) Backend; }
+
+void* ls_b200_create_table(const uint8_t* lut, uint32_t layers, uint32_t buckets) {
+    auto* b = new (std::nothrow) Backend;
+    if (!b) return nullptr;
+    b->lut = lut;
+    b->lut_layers = layers;
+    b->lut_buckets = buckets;
+    return b;
+}
+
+void ls_b200_destroy(void* backend) { delete static_cast<Backend*>(backend); }
+
+int ls_b200_configure(void* backend, const ls_b200_geometry* geometry) {
+    if (!backend || !geometry) return EINVAL;
+    return lsb::configure(*static_cast<Backend*>(backend), *geometry);
+}
+
+int ls_b200_set_buffers(void* backend, const ls_b200_layer_args* buffers) {
+    if (!backend || !buffers) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    b->bound = *buffers;
+    b->bound_set = true;
+    return 0;
+}
+
+void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket) {
+    if (!backend) return;
+    auto* b = static_cast<Backend*>(backend);
+    b->state_layer = layer;
+    b->state_bucket = io_bucket;
+}
+
+int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream) {
+    if (!backend || !args) return EINVAL;
+    return lsb::launch(*static_cast<Backend*>(backend), *args, static_cast<cudaStream_t>(stream));
+}
+
+int ls_b200_enqueue(void* backend, uint32_t layer, uint32_t bucket, uint32_t epoch, void* stream) {
+    if (!backend) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    if (!b->bound_set) return EINVAL;
+    ls_b200_layer_args a = b->bound;
+    a.epoch = epoch;
+    a.layer = layer;
+    a.candidate = int32_t(b->select(layer, bucket));
+    return lsb::launch(*b, a, static_cast<cudaStream_t>(stream));
+}
+
+int ls_b200_view(void* backend, ls_compute_backend* out) {
+    if (!backend || !out) return EINVAL;
+    out->context = backend;
+    out->enqueue = lsb::view_enqueue;
+    out->complete = lsb::view_complete;
+    out->commit = lsb::view_commit;
+    out->defer_commit = nullptr;
+    out->cancel = lsb::view_cancel;
+    return 0;
+}
+
+int ls_b200_completed_epoch(void* backend, uint32_t layer, uint32_t* epoch) {
+    if (!backend || !epoch) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    if (!b->configured || layer >= b->geo.max_layers) return EINVAL;
+    *epoch = __atomic_load_n(b->done_host + layer, __ATOMIC_ACQUIRE);
+    return 0;
+}
+
+int ls_b200_status(void* backend, uint32_t* words, uint32_t count) {
+    if (!backend || !words) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    if (!b->configured) return EINVAL;
+    for (uint32_t i = 0; i < count && i < LS_B200_STATUS_WORDS; ++i)
+        words[i] = __atomic_load_n(b->status_host + i, __ATOMIC_ACQUIRE);
+    return 0;
+}
+
+int ls_b200_clear_status(void* backend) {
+    if (!backend) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    if (!b->configured) return EINVAL;
+    for (uint32_t i = 0; i < 3; ++i) __atomic_store_n(b->status_host + i, 0u, __ATOMIC_RELEASE);
+    return 0;
+}
+
+uint64_t ls_b200_scratch_bytes(void* backend) {
+    return backend ? static_cast<Backend*>(backend)->scratch_bytes : 0;
+}
+
+uint32_t ls_b200_quantize_io_load(uint32_t remaining, uint32_t total, uint32_t buckets) {
+    return lsb::quantize_io_load(remaining, total, buckets);
+}
+
+uint32_t ls_b200_select(void* backend, uint32_t layer, uint32_t io_bucket) {
+    if (!backend) return lsb::kDefaultCandidate;
+    return static_cast<Backend*>(backend)->select(layer, io_bucket);
+}
+
+int ls_b200_candidate(void* backend, uint32_t id, ls_kernel_candidate* out) {
+    if (!out) return EINVAL;
+    if (backend) {
+        *out = static_cast<Backend*>(backend)->candidate(id);
+    } else {
+        Backend tmp;
+        *out = tmp.candidate(id);
+    }
+    return 0;
+}
+
+uint32_t ls_b200_catalog_size(void) { return lsb::kCatalogSize; }
+uint32_t ls_b200_default_candidate(void) { return lsb::kDefaultCandidate; }
+
+// ---------------------------------------------------------------- ExecutionQueue
+// Restatement of src/runtime/execution_queue.cpp:4-46 over the C view: the
+// same release-store order (ready_count before epoch; batch_epoch when the
+// plan is complete) and the same single-shot error CAS. Errors are returned
+// instead of asserted.
+void ls_b200_queue_bind(ls_b200_queue* q, ls_device_exec_queue view) {
+    if (!q) return;
+    q->view = view;
+    q->tail = q->epoch = q->total = 0;
+}
+
+int ls_b200_queue_reset(ls_b200_queue* q, uint32_t epoch) {
+    if (!q || !q->view.control || !q->view.descriptors || !q->view.ready_indices || !epoch) return EINVAL;
+    ls_queue_control* c = q->view.control;
+    q->tail = q->total = 0;
+    q->epoch = epoch;
+    __atomic_store_n(&c->epoch, 0u, __ATOMIC_RELEASE);
+    c->ready_count = 0;
+    c->reserved = 0;
+    c->claim_count = 0;
+    c->total_count = 0;
+    c->batch_epoch = 0;
+    c->error = 0;
+    c->consumer_path = 0;
+    c->init_arrived = 0;
+    c->init_epoch = 0;
+    return 0;
+}
+
+int ls_b200_queue_prepare(ls_b200_queue* q, uint32_t total) {
+    if (!q || !q->view.control || total > q->view.capacity) return EINVAL;
+    q->total = total;
+    q->view.control->total_count = total;
+    return 0;
+}
+
+int ls_b200_queue_append_unpublished(ls_b200_queue* q, uint32_t index) {
+    if (!q || q->tail >= q->total || index >= q->total) return EINVAL;
+    for (uint32_t i = 0; i < q->tail; ++i)
+        if (q->view.ready_indices[i] == index) return EEXIST;
+    q->view.ready_indices[q->tail++] = index;
+    return 0;
+}
+
+int ls_b200_queue_activate(ls_b200_queue* q) {
+    if (!q || !q->view.control) return EINVAL;
+    ls_queue_control* c = q->view.control;
+    __atomic_store_n(&c->ready_count, q->tail, __ATOMIC_RELEASE);
+    __atomic_store_n(&c->epoch, q->epoch, __ATOMIC_RELEASE);
+    if (q->tail == q->total) __atomic_store_n(&c->batch_epoch, q->epoch, __ATOMIC_RELEASE);
+    return 0;
+}
+
+int ls_b200_queue_seal(ls_b200_queue* q, uint32_t total) {
+    const int rc = ls_b200_queue_prepare(q, total);
+    return rc ? rc : ls_b200_queue_activate(q);
+}
+
+int ls_b200_queue_publish_all(ls_b200_queue* q) {
+    if (!q || !q->view.control || q->tail != 0) return EINVAL;
+    for (uint32_t i = 0; i < q->total; ++i) q->view.ready_indices[i] = i;
+    q->tail = q->total;
+    __atomic_store_n(&q->view.control->ready_count, q->tail, __ATOMIC_RELEASE);
+    __atomic_store_n(&q->view.control->batch_epoch, q->epoch, __ATOMIC_RELEASE);
+    return 0;
+}
+
+int ls_b200_queue_publish(ls_b200_queue* q, uint32_t index) {
+    if (!q || !q->view.control || q->tail >= q->total || index >= q->total) return EINVAL;
+    for (uint32_t i = 0; i < q->tail; ++i)
+        if (q->view.ready_indices[i] == index) return EEXIST;
+    q->view.ready_indices[q->tail++] = index;
+    __atomic_store_n(&q->view.control->ready_count, q->tail, __ATOMIC_RELEASE);
+    if (q->tail == q->total) __atomic_store_n(&q->view.control->batch_epoch, q->epoch, __ATOMIC_RELEASE);
+    return 0;
+}
+
+int ls_b200_queue_fail(ls_b200_queue* q, uint32_t error) {
+    if (!q || !q->view.control) return EINVAL;
+    uint32_t clear = 0;
+    __atomic_compare_exchange_n(&q->view.control->error, &clear, error, false, __ATOMIC_RELEASE, __ATOMIC_RELAXED);
+    return 0;
+}
+
+const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-layer r1"; }
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+"""GPU parity of the fused sm_100a layer against the CPU oracle and the
+reference's closed forms, through the C ABI."""
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3  # max|y - y_ref| <= 2e-3 * ||y_ref||_inf
+
+
+def _half(z):
+    return float(np.float16(z))
+
+
+def closed_form(H, groups, G, q, scale=0.05, x=0.1):
+    """tests/persistent_mlp_test.cu:53-55 and tests/triton_smoke.py:74-76."""
+    gate = _half(H * _half(x) * _half(scale) * q)
+    act = _half(_half(gate / (1 + math.exp(-gate))) * gate)
+    return _half(groups * G * act * _half(scale) * q)
+
+
+def _closed_case(count, q, mode, candidate=-1, shuffled=False):
+    import torch
+    from gpu_harness import LayerBuffers, make_backend, run_layer, wait_stream
+    from leanstream_b200 import _native as N
+
+    H, G = 256, 2
+    all_groups = count + 1
+    byte = 0x11 if q == 1 else 0xFF
+    packed = np.full(all_groups * G * 3 * H // 2, byte, np.uint8)
+    scales = np.full(all_groups * G * 3 * H // 128, 0.05, np.float16)
+    x = np.full(H, 0.1, np.float16)
+    buf = LayerBuffers(H, G, all_groups, packed, scales, x, staging=packed.copy())
+    be = make_backend(H, G, all_groups)
+    core = [[0, 0, 0, 0, 0]]
+    rows = [[i + 1, i + 1, i + 1, i + 1, 0 if i % 2 else 1] for i in range(count)]
+    order = list(reversed(range(count))) if shuffled else None
+    run_layer(be, buf, core, rows, mode=mode, candidate=candidate, order=order)
+    wait_stream()
+    assert be.status()[N.STATUS_ERROR] == 0, be.status()
+    y = buf.y.cpu().numpy().astype(np.float32)
+    execs = buf.execs.cpu().numpy()
+    assert np.all(execs == 1), execs
+    expected = closed_form(H, all_groups, G, q)
+    assert np.all(np.abs(y - expected) < 0.002), (y[:4], expected)
+    be.close()
+    return buf.y.cpu().numpy().copy()
+
+
+@pytest.mark.parametrize("q", [1, -1])
+@pytest.mark.parametrize("count", [0, 1, 2, 16, 37])
+def test_closed_form_modes_bit_exact(native_lib, cuda_device, count, q):
+    from leanstream_b200 import _native as N
+
+    batch = _closed_case(count, q, N.MODE_BATCH_COMPAT)
+    progressive = _closed_case(count, q, N.MODE_PROGRESSIVE, shuffled=True)
+    auto = _closed_case(count, q, N.MODE_AUTO)
+    assert np.array_equal(batch.view(np.uint16), progressive.view(np.uint16))
+    assert np.array_equal(batch.view(np.uint16), auto.view(np.uint16))
+
+
+@pytest.mark.parametrize("candidate", [0, 1, 2, 3, 4])
+def test_closed_form_every_candidate(native_lib, cuda_device, candidate):
+    from leanstream_b200 import _native as N
+
+    y = _closed_case(16, 1, N.MODE_PROGRESSIVE, candidate=candidate, shuffled=True)
+    ref = _closed_case(16, 1, N.MODE_BATCH_COMPAT, candidate=4)
+    assert np.array_equal(y.view(np.uint16), ref.view(np.uint16))
+
+
+def _seeded_parity(H, n_groups, ids, seed, candidate=-1, core=0):
+    import torch
+    from gpu_harness import LayerBuffers, make_backend, run_layer, wait_stream
+    from leanstream_b200 import _native as N
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    G = 64
+    L = make_layer(seed, H, n_groups, G)
+    rows = descriptors(ids)
+    y_ref16, y_ref32, h_ref = O.mlp(H, G, L.x, L.packed, L.scales, rows, h_out_groups=n_groups)
+    buf = LayerBuffers(H, G, n_groups, L.packed, L.scales, L.x)
+    be = make_backend(H, G, n_groups, cache_slots=n_groups, physical_groups=n_groups)
+    core_rows, queue_rows = rows[:core], rows[core:]
+    # queue descriptors carry dest = core + index (weight_manager.cpp:177-178)
+    run_layer(be, buf, core_rows, queue_rows, mode=N.MODE_PROGRESSIVE, candidate=candidate)
+    wait_stream()
+    assert be.status()[N.STATUS_ERROR] == 0, be.status()
+    y = buf.y.cpu().numpy().astype(np.float32)
+    y32 = buf.y32.cpu().numpy()
+    ref = y_ref16.astype(np.float32)
+    err = np.abs(y - ref).max()
+    bound = TOL * np.abs(ref).max()
+    assert err <= bound, (err, bound)
+    assert np.abs(y32 - y_ref32).max() <= TOL * np.abs(y_ref32).max()
+    # h activations: identical fp16 except rare one-ulp flips from summation order
+    act = buf.act.cpu().numpy().reshape(n_groups, G)
+    href = h_ref.reshape(n_groups, G)
+    sel = np.asarray([r[3] for r in rows])
+    a, b = act[sel].astype(np.float32), href[sel].astype(np.float32)
+    mism = np.mean(a != b)
+    assert mism < 0.05, mism
+    assert np.abs(a - b).max() <= 2 * np.abs(b).max() * 2.0 ** -10
+    execs = buf.execs.cpu().numpy()
+    assert np.all(execs[sel] == 1) and execs.sum() == len(rows)
+    be.close()
+    return y, ref
+
+
+def test_config1_parity_predictor_ids(native_lib, cuda_device):
+    """Config 1: H 1024, 64 groups of 64; 16 groups selected by the reference
+    ls_predict on representative rows; seed 0."""
+    from leanstream_b200.synthetic import make_layer, representative_rows
+    from oracle import oracle as O
+
+    L = make_layer(0, 1024, 64, 64)
+    p = O.Predictor(64, 1024, 16, 1, 32)
+    ids = p.predict(representative_rows(L), L.x.astype(np.float32))
+    p.close()
+    assert len(set(ids.tolist())) == 16
+    _seeded_parity(1024, 64, ids, 0)
+
+
+@pytest.mark.parametrize("candidate", [0, 3, 4])
+def test_config1_parity_candidates_and_core(native_lib, cuda_device, candidate):
+    ids = np.random.default_rng(7).permutation(64)[:20]
+    _seeded_parity(1024, 64, ids, 3, candidate=candidate, core=4)
+
+
+def test_config2_parity(native_lib, cuda_device):
+    """Config 2: H 4096, 192 groups, 58 active (seeded ranking), all ready."""
+    from leanstream_b200.synthetic import seeded_selection
+
+    ids = seeded_selection(2, 192, 0.3)
+    assert len(ids) == 58
+    _seeded_parity(4096, 192, ids, 2)
