@@ -146,7 +146,23 @@ typedef struct ls_b200_layer_args {
     void* hidden_out;         /* optional fp16 [H] */
     float* output_f32;        /* optional fp32 [H]: unrounded sum (tensor-parallel partial) */
     const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
+    uint64_t* trace;          /* optional [grid][8] %globaltimer phase stamps per CTA
+                               * (LS_B200_TRACE_*); the Stamp buffers of
+                               * backends/triton/core.py:25 and persistent.py:37 */
 } ls_b200_layer_args;
+
+/* Phase stamps written per CTA when ls_b200_layer_args.trace is set. */
+enum {
+    LS_B200_TRACE_ENTRY = 0,     /* kernel entry */
+    LS_B200_TRACE_DECIDED = 1,   /* producer learned the consumer path */
+    LS_B200_TRACE_FIRST = 2,     /* first stage consumed */
+    LS_B200_TRACE_PIECES = 3,    /* consumers saw END */
+    LS_B200_TRACE_PRODUCED = 4,  /* producer issued END */
+    LS_B200_TRACE_BARRIER = 5,   /* grid barrier passed */
+    LS_B200_TRACE_REDUCED = 6,   /* reduction done */
+    LS_B200_TRACE_EXIT = 7,      /* CTA done (after the exit counter) */
+    LS_B200_TRACE_WORDS = 8
+};
 
 /* Device status words (ls_b200_status). */
 enum {

@@ -77,7 +77,8 @@ class LayerArgs(C.Structure):
                 ("queue", DeviceExecQueue), ("mode", C.c_uint8), ("pad", C.c_uint8 * 3), ("flags", C.c_uint32),
                 ("candidate", C.c_int32), ("layer", C.c_uint32), ("activations", C.c_void_p),
                 ("executions", C.c_void_p), ("first_compute", C.c_void_p), ("residual", C.c_void_p),
-                ("hidden_out", C.c_void_p), ("output_f32", C.c_void_p), ("norm_weight", C.c_void_p)]
+                ("hidden_out", C.c_void_p), ("output_f32", C.c_void_p), ("norm_weight", C.c_void_p),
+                ("trace", C.c_void_p)]
 
 
 class Queue(C.Structure):

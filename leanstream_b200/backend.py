@@ -162,7 +162,7 @@ class B200Backend:
     def layer_args(*, input=None, output=None, cache=None, staging=None, scales=None, core=None, core_count=0,
                    epoch=0, queue: Optional[N.DeviceExecQueue] = None, mode=N.MODE_PROGRESSIVE, flags=0,
                    candidate=-1, layer=0, activations=None, executions=None, first_compute=None, residual=None,
-                   hidden_out=None, output_f32=None, norm_weight=None) -> N.LayerArgs:
+                   hidden_out=None, output_f32=None, norm_weight=None, trace=None) -> N.LayerArgs:
         a = N.LayerArgs()
         a.input, a.output = _ptr(input), _ptr(output)
         a.cache, a.staging, a.scales = _ptr(cache), _ptr(staging), _ptr(scales)
@@ -173,6 +173,7 @@ class B200Backend:
         a.activations, a.executions, a.first_compute = _ptr(activations), _ptr(executions), _ptr(first_compute)
         a.residual, a.hidden_out, a.output_f32, a.norm_weight = (_ptr(residual), _ptr(hidden_out),
                                                                   _ptr(output_f32), _ptr(norm_weight))
+        a.trace = _ptr(trace)
         return a
 
     def set_buffers(self, **kw) -> None:

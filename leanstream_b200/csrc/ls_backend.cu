@@ -207,6 +207,7 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     p.hidden_out = static_cast<uint16_t*>(a.hidden_out);
     p.y32 = a.output_f32;
     p.norm_w = static_cast<const uint16_t*>(a.norm_weight);
+    p.trace = a.trace;
     p.partial = b.partial;
     p.hbuf = b.hbuf;
     p.ws = b.ws;

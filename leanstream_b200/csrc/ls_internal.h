@@ -58,6 +58,7 @@ struct KernelParams {
     uint16_t* hidden_out;
     float* y32;
     const uint16_t* norm_w;
+    uint64_t* trace;    // optional [grid][LS_B200_TRACE_WORDS]
     // backend scratch
     float* partial;     // [N][H] fp32, one row per descriptor position
     uint16_t* hbuf;     // [N][G] fp16 h, indexed like partial rows

@@ -201,6 +201,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_as_half(v)); }
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
+__device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
+    if (P.trace) P.trace[size_t(blockIdx.x) * LS_B200_TRACE_WORDS + word] = gtimer();
+}
+
 // Records the first error of this launch and asks the CTA to stop.
 __device__ __forceinline__ void raise_error(const KernelParams& P, SmemTail* t, uint32_t code, uint32_t detail) {
     if (atomicCAS(&P.ws->err, 0u, code) == 0u) P.ws->detail = detail;
@@ -467,6 +471,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
     }
     path = __shfl_sync(0xffffffffu, path, 0);
     total = __shfl_sync(0xffffffffu, total, 0);
+    if (pr.lane == 0) trace(P, LS_B200_TRACE_DECIDED);
     const uint32_t D = P.core_count + total;
 
     if (path == kPathFast) {
@@ -553,6 +558,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         }
     }
     producer_end(pr, P);
+    if (pr.lane == 0) trace(P, LS_B200_TRACE_PRODUCED);
 }
 
 // ------------------------------------------------------------ consumer side
@@ -765,7 +771,11 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             break;
         }
         const Piece pc = t->piece[s];
-        if (pc.kind == kPieceEnd) break;
+        if (idx == 0 && tid == 0) trace(P, LS_B200_TRACE_FIRST);
+        if (pc.kind == kPieceEnd) {
+            if (tid == 0) trace(P, LS_B200_TRACE_PIECES);
+            break;
+        }
         const uint8_t* st = stages + size_t(s) * kStageBytes;
         const bool aborted = __shfl_sync(0xffffffffu, t->abort, 0) != 0;  // warp-uniform snapshot
         if (pc.kind == kPieceGateUp) {
@@ -824,6 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(const KernelPa
     const int tid = threadIdx.x;
     const uint64_t deadline = gtimer() + P.timeout_ns;
     if (tid == 0) {
+        trace(P, LS_B200_TRACE_ENTRY);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&t->full_bar[s]), 33);                // producer lane 0 + 32 cp.async lanes
             mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps);  // one arrive per consumer warp
@@ -857,10 +868,12 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(const KernelPa
         // One CTA-uniform decision: reduce only a complete, error-free launch.
         const uint32_t path = ld_acquire_gpu(&ws->path);
         t->good = (path == kPathFast || path == kPathProgressive) && ld_acquire_gpu(&ws->err) == 0 && !t->abort;
+        trace(P, LS_B200_TRACE_BARRIER);
     }
     __syncthreads();
     if (t->good && tid < kConsumerThreads) run_reduction(P, t, P.core_count + ws->total);
     __syncthreads();
+    if (tid == 0) trace(P, LS_B200_TRACE_REDUCED);
 
     // Exit: the last CTA restores the workspace and publishes completion.
     if (tid == 0) {
@@ -888,6 +901,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(const KernelPa
             P.status[LS_B200_STATUS_LAUNCHES] += 1;
             st_release_sys(P.done + P.layer, P.epoch);
         }
+        trace(P, LS_B200_TRACE_EXIT);
     }
 }
 
