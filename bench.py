@@ -196,22 +196,69 @@ class Stack:
             flags=N.NORM_INPUT | (N.NO_OUTPUT if tp else 0), residual=None if tp else self.xs[layer],
             hidden_out=None if tp else self.xs[layer + 1], output_f32=self.y32 if tp else None)
 
-    def enqueue_token(self, plan_rows, stream):
-        """Enqueues one token (36 layers) on `stream`; returns launches of ours."""
+    def encode_token(self, plan_rows, base_dev):
+        """Encoded plans of one token for the multi-layer launch (one GPU)."""
+        import torch
+
+        blobs = [self.backend.encode_plan(self.layer_args(layer, plan_rows[layer])) for layer in range(LAYERS)]
+        host = torch.frombuffer(bytearray(b"".join(blobs)), dtype=torch.uint8).pin_memory()
+        dev = host.to(base_dev)
+        return host, dev
+
+    def enqueue_token(self, plan_rows, stream, encoded=None):
+        """Enqueues one token (all layers) on `stream`; returns launches of ours.
+        One GPU: one persistent multi-layer launch. N GPUs: per layer, the
+        fused layer kernel, an NCCL allreduce of the fp32 partial and the
+        epilogue kernel."""
         import torch.distributed as dist
 
         lib = self.N.load()
+        if self.world == 1:
+            host, dev = encoded
+            self.backend.launch_plans(dev, LAYERS, host, stream=stream)
+            return 1
         launches = 0
         for layer in range(LAYERS):
             self.backend.launch(self.layer_args(layer, plan_rows[layer]), stream)
             launches += 1
-            if self.world > 1:
-                dist.all_reduce(self.y32)
-                rc = lib.ls_b200_tp_epilogue(self.y32.data_ptr(), self.xs[layer].data_ptr(), self.y.data_ptr(),
-                                             self.xs[layer + 1].data_ptr(), H, stream.cuda_stream)
-                assert rc == 0
-                launches += 1
+            dist.all_reduce(self.y32)
+            rc = lib.ls_b200_tp_epilogue(self.y32.data_ptr(), self.xs[layer].data_ptr(), self.y.data_ptr(),
+                                         self.xs[layer + 1].data_ptr(), H, stream.cuda_stream)
+            assert rc == 0
+            launches += 1
         return launches
+
+
+def trace_report(st, encoded, stream):
+    """Phase stamps (LS_B200_TRACE_*, LS_B200_LTRACE_*) of one multi-layer
+    launch, summarised to stderr: per layer, the median over CTAs of each
+    stamp relative to the first CTA's entry."""
+    import torch
+
+    grid = torch.cuda.get_device_properties(0).multi_processor_count
+    trace = torch.zeros(grid * 8 + grid * LAYERS * 8, dtype=torch.int64, device=st.dev)
+    host, dev = encoded
+    with torch.cuda.stream(stream):
+        st.N.load().ls_b200_spin(1_000_000, stream.cuda_stream)
+        st.backend.launch_plans(dev, LAYERS, host, trace=trace, stream=stream)
+    torch.cuda.synchronize()
+    t = trace.cpu().numpy().astype(np.int64)
+    cta = t[: grid * 8].reshape(grid, 8)
+    lay = t[grid * 8:].reshape(grid, LAYERS, 8)
+    t0 = cta[:, 0].min()
+    rel = lambda a: np.where(a > 0, (a - t0) / 1000.0, np.nan)
+    names = {0: "entry", 1: "decided", 2: "first", 3: "pieces", 4: "produced", 6: "roles_done", 7: "exit"}
+    print("trace(us min/med/max): " + " ".join(
+        f"{n}={np.nanmin(rel(cta[:, i])):.1f}/{np.nanmedian(rel(cta[:, i])):.1f}/{np.nanmax(rel(cta[:, i])):.1f}"
+        for i, n in names.items()), file=sys.stderr)
+    lnames = ["decided", "issued", "pieces_done", "partials_ready", "reduced", "next_ready", "loaded"]
+    print("layer  " + " ".join(f"{n:>14s}" for n in lnames) + "   (median over CTAs / max)", file=sys.stderr)
+    for l in range(min(LAYERS, 6)):
+        cols = []
+        for w in range(7):
+            v = rel(lay[:, l, w])
+            cols.append(f"{np.nanmedian(v):6.1f}/{np.nanmax(v):6.1f}" if np.isfinite(v).any() else f"{'-':>13s}")
+        print(f"{l:5d}  " + " ".join(f"{c:>14s}" for c in cols), file=sys.stderr)
 
 
 def run_gpu(args, rank, world, local_rank):
@@ -243,10 +290,11 @@ def run_gpu(args, rank, world, local_rank):
         torch.cuda.synchronize()
     graphs = []
     launches_per_token = 0
+    encoded = [st.encode_token(st.plans_dev[s], st.dev) if world == 1 else None for s in range(steps_total)]
     for s in range(steps_total):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            launches_per_token = st.enqueue_token(st.plans_dev[s], torch.cuda.current_stream())
+            launches_per_token = st.enqueue_token(st.plans_dev[s], torch.cuda.current_stream(), encoded[s])
         graphs.append(g)
     torch.cuda.synchronize()
     barrier()
@@ -280,26 +328,46 @@ def run_gpu(args, rank, world, local_rank):
         raise RuntimeError(f"device status {status}")
     ms_per_step = ms / args.steps
 
-    # ---- kernel-only durations: pre-queued, event-bracketed fused launches
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * LAYERS)]
+    # ---- kernel-only durations: pre-queued, event-bracketed launches of the
+    # dominant kernel (one GPU: the multi-layer launch; N GPUs: the layer kernel)
     barrier()
-    with torch.cuda.stream(stream):
-        s = args.warmup
-        lib.ls_b200_spin(2_000_000, stream.cuda_stream)  # queue everything behind a 2 ms delay
-        for layer in range(LAYERS):
-            ev[2 * layer].record(stream)
-            st.backend.launch(st.layer_args(layer, st.plans_dev[s][layer]), stream)
-            ev[2 * layer + 1].record(stream)
-    torch.cuda.synchronize()
-    kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(LAYERS)]
-    kern_bytes = [n * ALG_BYTES_PER_GROUP for n in st.active_local[args.warmup]]
+    if world == 1:
+        reps = min(args.steps, 8)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * reps)]
+        with torch.cuda.stream(stream):
+            lib.ls_b200_spin(2_000_000, stream.cuda_stream)
+            for i in range(reps):
+                s = args.warmup + i
+                ev[2 * i].record(stream)
+                st.enqueue_token(st.plans_dev[s], stream, encoded[s])
+                ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps)]
+        kern_bytes = [sum(st.active_local[args.warmup + i]) * ALG_BYTES_PER_GROUP for i in range(reps)]
+        kernel_name = "fused_mlp_kernel (36-layer persistent launch)"
+    else:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * LAYERS)]
+        with torch.cuda.stream(stream):
+            s = args.warmup
+            lib.ls_b200_spin(2_000_000, stream.cuda_stream)  # queue everything behind a 2 ms delay
+            for layer in range(LAYERS):
+                ev[2 * layer].record(stream)
+                st.backend.launch(st.layer_args(layer, st.plans_dev[s][layer]), stream)
+                ev[2 * layer + 1].record(stream)
+        torch.cuda.synchronize()
+        kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(LAYERS)]
+        kern_bytes = [n * ALG_BYTES_PER_GROUP for n in st.active_local[args.warmup]]
+        kernel_name = "fused_mlp_kernel (one layer, per-rank shard)"
     achieved_gbs = sum(kern_bytes) / (sum(kern_ms) * 1e-3) / 1e9
+    if args.trace and world == 1:
+        trace_report(st, encoded[args.warmup], stream)
 
     # ---- e2e: host plans + host x in, host y out, through the C ABI each step
     barrier()
     e2e_graph = torch.cuda.CUDAGraph()
+    slot_encoded = st.encode_token(st.slot_dev, st.dev) if world == 1 else None
     with torch.cuda.graph(e2e_graph, stream=stream):
-        st.enqueue_token(st.slot_dev, torch.cuda.current_stream())
+        st.enqueue_token(st.slot_dev, torch.cuda.current_stream(), slot_encoded)
     x_host = st.x0.cpu().pin_memory()
     y_host = torch.zeros(H, dtype=torch.float16, pin_memory=True)
     h2d = st.plans_host[0].numel() * 4 + x_host.numel() * 2
@@ -371,7 +439,7 @@ def run_gpu(args, rank, world, local_rank):
                        "timing": "CUDA graph per token, CUDA events on the launching stream, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                          "frac": achieved_gbs / peak, "traffic": traffic,
-                         "kernel": "fused_layer_kernel", "kernel_us_mean": 1e3 * float(np.mean(kern_ms)),
+                         "kernel": kernel_name, "kernel_us_mean": 1e3 * float(np.mean(kern_ms)),
                          "algorithmic_bytes_per_group": ALG_BYTES_PER_GROUP,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback",
                          "frac_of_8TBs_nominal": achieved_gbs / 8000.0,
@@ -466,6 +534,7 @@ def main():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--trace", action="store_true", help="print per-CTA phase stamps of one launch to stderr")
     p.add_argument("--layers", type=int, default=36,
                    help="stack depth; smaller values only for profiling captures (the metric is quoted at 36)")
     args = p.parse_args()

@@ -146,9 +146,10 @@ typedef struct ls_b200_layer_args {
     void* hidden_out;         /* optional fp16 [H] */
     float* output_f32;        /* optional fp32 [H]: unrounded sum (tensor-parallel partial) */
     const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
-    uint64_t* trace;          /* optional [grid][8] %globaltimer phase stamps per CTA
-                               * (LS_B200_TRACE_*); the Stamp buffers of
-                               * backends/triton/core.py:25 and persistent.py:37 */
+    uint64_t* trace;          /* optional %globaltimer phase stamps: [grid][LS_B200_TRACE_WORDS]
+                               * per CTA, then [grid][layers][LS_B200_LAYER_TRACE_WORDS]
+                               * per CTA and layer (LS_B200_*TRACE_*); the Stamp
+                               * buffers of backends/triton/core.py:25, persistent.py:37 */
 } ls_b200_layer_args;
 
 /* Phase stamps written per CTA when ls_b200_layer_args.trace is set. */
@@ -163,13 +164,24 @@ enum {
     LS_B200_TRACE_EXIT = 7,      /* CTA done (after the exit counter) */
     LS_B200_TRACE_WORDS = 8
 };
+/* Per-layer phase stamps (after the per-CTA block). */
+enum {
+    LS_B200_LTRACE_DECIDED = 0,        /* producer decided the layer's path */
+    LS_B200_LTRACE_ISSUED = 1,         /* producer issued the layer's last piece */
+    LS_B200_LTRACE_PIECES_DONE = 2,    /* consumers reached the end-of-layer marker */
+    LS_B200_LTRACE_PARTIALS_READY = 3, /* all partial rows of the layer written (reducer warps) */
+    LS_B200_LTRACE_REDUCED = 4,        /* this CTA's reduction blocks done */
+    LS_B200_LTRACE_NEXT_READY = 5,     /* every reduction block of the layer done */
+    LS_B200_LTRACE_LOADED = 6,         /* next layer's activation loaded (stamped under that layer) */
+    LS_B200_LAYER_TRACE_WORDS = 8
+};
 
 /* Device status words (ls_b200_status). */
 enum {
-    LS_B200_STATUS_ERROR = 0,       /* first LS_B200_DEV_* code since the last clear */
-    LS_B200_STATUS_ERROR_EPOCH = 1, /* epoch of the launch that recorded it */
-    LS_B200_STATUS_ERROR_DETAIL = 2,/* position / slot involved */
-    LS_B200_STATUS_LAUNCHES = 3,    /* completed launches */
+    LS_B200_STATUS_ERROR = 0,       /* LS_B200_DEV_* code of the latest failed launch */
+    LS_B200_STATUS_ERROR_EPOCH = 1, /* epoch (first layer) of that launch */
+    LS_B200_STATUS_ERROR_DETAIL = 2,/* position / slot / wait site involved */
+    LS_B200_STATUS_LAUNCHES = 3,    /* sequence number of the latest completed launch */
     LS_B200_STATUS_WORDS = 4
 };
 enum {
@@ -215,6 +227,17 @@ void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket);
  * compilation or synchronisation. Replaces enqueue_streaming_mlp
  * (kernels/streaming_mlp.cu:85-93). */
 int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream);
+/* Multi-layer launch: `count` layers in ONE persistent launch, each layer
+ * reading the previous layer's hidden_out as input (a decode stack with the
+ * residual / RMSNorm epilogue fused). Plans are encoded on the host with
+ * ls_b200_encode_plan (ls_b200_plan_size bytes each); the caller copies
+ * them to 16-byte-aligned device memory (stream-ordered before the launch)
+ * and passes both copies: the device array is read by the kernel, the host
+ * array is validated and records per-layer completion epochs. */
+uint32_t ls_b200_plan_size(void);
+int ls_b200_encode_plan(void* backend, const ls_b200_layer_args* args, void* plan);
+int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count, const void* host_plans,
+                         int32_t candidate, uint64_t* trace, void* stream);
 /* ls_triton_enqueue (triton_cuda.h:56; enqueue.cpp:26-37): LUT-selected
  * candidate, bound buffers and queue from ls_b200_set_buffers. */
 int ls_b200_enqueue(void* backend, uint32_t layer, uint32_t bucket, uint32_t epoch, void* stream);

@@ -98,6 +98,10 @@ SIGNATURES = {
     "ls_b200_set_state": (None, [C.c_void_p, C.c_uint32, C.c_uint32]),
     "ls_b200_launch": (C.c_int, [C.c_void_p, C.POINTER(LayerArgs), C.c_void_p]),
     "ls_b200_enqueue": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "ls_b200_plan_size": (C.c_uint32, []),
+    "ls_b200_encode_plan": (C.c_int, [C.c_void_p, C.POINTER(LayerArgs), C.c_void_p]),
+    "ls_b200_launch_plans": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_int32, C.c_void_p,
+                                       C.c_void_p]),
     "ls_b200_view": (C.c_int, [C.c_void_p, C.POINTER(ComputeBackend)]),
     "ls_b200_completed_epoch": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_uint32)]),
     "ls_b200_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_uint32]),

@@ -190,6 +190,23 @@ class B200Backend:
     def launch_rc(self, args: N.LayerArgs, stream=None) -> int:
         return int(self.lib.ls_b200_launch(self.context, C.byref(args), _stream(stream)))
 
+    def plan_size(self) -> int:
+        return int(self.lib.ls_b200_plan_size())
+
+    def encode_plan(self, args: N.LayerArgs) -> bytes:
+        """Encodes one layer (validated on the host) for ls_b200_launch_plans."""
+        buf = (C.c_uint8 * self.plan_size())()
+        _check(self.lib.ls_b200_encode_plan(self.context, C.byref(args), buf), "ls_b200_encode_plan")
+        return bytes(buf)
+
+    def launch_plans(self, device_plans, count: int, host_plans, candidate: int = -1, trace=None,
+                     stream=None) -> None:
+        """One persistent launch over `count` layers. `device_plans` is a
+        16-byte-aligned device copy of `host_plans` (encoded plans)."""
+        hp = host_plans if isinstance(host_plans, int) else _ptr(host_plans)
+        _check(self.lib.ls_b200_launch_plans(self.context, _ptr(device_plans), count, hp, candidate, _ptr(trace),
+                                             _stream(stream)), "ls_b200_launch_plans")
+
     def enqueue(self, layer: int, io_bucket: int, epoch: int, stream=None) -> None:
         _check(self.lib.ls_b200_enqueue(self.context, layer, io_bucket, epoch, _stream(stream)), "ls_b200_enqueue")
 

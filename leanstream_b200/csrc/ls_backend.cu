@@ -64,7 +64,8 @@ struct Backend {
     // scratch (device) and mapped words (host)
     float* partial = nullptr;
     uint16_t* hbuf = nullptr;
-    Workspace* ws = nullptr;
+    uint32_t* ws = nullptr;
+    uint32_t seq = 0;
     uint32_t* status_host = nullptr;
     uint32_t* status_dev = nullptr;
     uint32_t* done_host = nullptr;
@@ -128,7 +129,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
     const size_t partial_bytes = size_t(N) * H * sizeof(float);
     const size_t h_bytes = size_t(N) * G * sizeof(uint16_t);
-    const size_t ws_bytes = sizeof(Workspace) + size_t(N) * sizeof(uint32_t);
+    const size_t ws_bytes = size_t(ws_words(b.geo.max_layers, N)) * sizeof(uint32_t);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.hbuf, h_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
@@ -158,9 +159,9 @@ int configure(Backend& b, const ls_b200_geometry& g) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Hot path: parameter validation and one kernel launch. No allocation,
-// no synchronisation, no device queries (triton_cuda.h:19-20).
-int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
+// Validates one layer's arguments and encodes its plan. Host only, no
+// CUDA calls.
+int encode(const Backend& b, const ls_b200_layer_args& a, LayerPlan* out) {
     if (!b.configured) return EINVAL;
     if (!a.epoch || !a.input || !a.scales || !a.queue.control || !a.queue.descriptors || !a.queue.ready_indices)
         return EINVAL;
@@ -171,28 +172,12 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     if (a.mode > LS_MODE_AUTO) return EINVAL;
     if (a.layer >= b.geo.max_layers) return EINVAL;
     if (a.core_count > b.geo.group_count) return ENOSPC;
+    // cp.async.bulk sources and the 16-byte activation loads need alignment
     if ((a.cache && !aligned16(a.cache)) || (a.staging && !aligned16(a.staging)) || !aligned16(a.scales) ||
+        !aligned16(a.input) || (a.norm_weight && !aligned16(a.norm_weight)) ||
         (a.output_f32 && !aligned16(a.output_f32)))
-        return EINVAL;  // cp.async.bulk needs 16-byte aligned sources
-    const uint32_t id = a.candidate >= 0 ? uint32_t(a.candidate) : b.select(b.state_layer, b.state_bucket);
-    const ls_kernel_candidate c = b.candidate(id);
-    int grid = int(c.cta_count);
-    if (grid > b.sms) grid = b.sms;
-    KernelParams p{};
-    p.H = b.geo.hidden;
-    p.G = b.geo.group_size;
-    p.N = b.geo.group_count;
-    p.cache_slots = b.geo.cache_slots;
-    p.staging_slots = b.geo.staging_slots;
-    p.phys_groups = b.geo.physical_groups;
-    p.group_bytes = uint64_t(p.G) * 3 * p.H / 2;
-    p.timeout_ns = uint64_t(b.geo.timeout_us) * 1000ull;
-    p.eps = b.geo.rms_eps;
-    p.epoch = a.epoch;
-    p.mode = a.mode;
-    p.flags = a.flags;
-    p.layer = a.layer;
-    p.core_count = a.core_count;
+        return EINVAL;
+    LayerPlan p{};
     p.x = static_cast<const uint16_t*>(a.input);
     p.y = static_cast<uint16_t*>(a.output);
     p.cache = a.cache ? a.cache : a.staging;
@@ -207,14 +192,55 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     p.hidden_out = static_cast<uint16_t*>(a.hidden_out);
     p.y32 = a.output_f32;
     p.norm_w = static_cast<const uint16_t*>(a.norm_weight);
-    p.trace = a.trace;
+    p.epoch = a.epoch;
+    p.mode = a.mode;
+    p.flags = a.flags;
+    p.layer = a.layer;
+    p.core_count = a.core_count;
+    *out = p;
+    return 0;
+}
+
+KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace) {
+    KernelParams p{};
+    p.H = b.geo.hidden;
+    p.G = b.geo.group_size;
+    p.N = b.geo.group_count;
+    p.cache_slots = b.geo.cache_slots;
+    p.staging_slots = b.geo.staging_slots;
+    p.phys_groups = b.geo.physical_groups;
+    p.group_bytes = uint64_t(p.G) * 3 * p.H / 2;
+    p.timeout_ns = uint64_t(b.geo.timeout_us) * 1000ull;
+    p.eps = b.geo.rms_eps;
+    p.nlayers = nlayers;
+    p.max_layers = b.geo.max_layers;
+    p.seq = ++b.seq;
     p.partial = b.partial;
     p.hbuf = b.hbuf;
     p.ws = b.ws;
     p.status = b.status_dev;
     p.done = b.done_dev;
+    p.trace = trace;
+    return p;
+}
+
+int grid_for(const Backend& b, int32_t candidate) {
+    const uint32_t id = candidate >= 0 ? uint32_t(candidate) : b.select(b.state_layer, b.state_bucket);
+    int grid = int(b.candidate(id).cta_count);
+    return grid > b.sms ? b.sms : grid;
+}
+
+// Hot path: parameter validation and one kernel launch. No allocation,
+// no synchronisation, no device queries (triton_cuda.h:19-20).
+int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
+    LayerPlan plan;
+    int rc = encode(b, a, &plan);
+    if (rc) return rc;
+    KernelParams p = base_params(b, 1, a.trace);
+    p.plans = nullptr;
+    p.first = plan;
     b.last_epoch[a.layer] = a.epoch;
-    const int rc = launch_fused_layer(p, grid, stream);
+    rc = launch_fused(p, grid_for(b, a.candidate), stream);
     return rc ? cuda_rc(cudaError_t(rc)) : 0;
 }
 
@@ -301,6 +327,36 @@ void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket) {
 int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream) {
     if (!backend || !args) return EINVAL;
     return lsb::launch(*static_cast<Backend*>(backend), *args, static_cast<cudaStream_t>(stream));
+}
+
+uint32_t ls_b200_plan_size(void) { return uint32_t(sizeof(lsb::LayerPlan)); }
+
+int ls_b200_encode_plan(void* backend, const ls_b200_layer_args* args, void* plan) {
+    if (!backend || !args || !plan) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    lsb::LayerPlan p;
+    const int rc = lsb::encode(*b, *args, &p);
+    if (rc) return rc;
+    std::memcpy(plan, &p, sizeof(p));
+    return 0;
+}
+
+int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count, const void* host_plans,
+                         int32_t candidate, uint64_t* trace, void* stream) {
+    if (!backend || !device_plans || !host_plans || !count) return EINVAL;
+    auto* b = static_cast<Backend*>(backend);
+    if (!b->configured || count > b->geo.max_layers) return EINVAL;
+    if ((reinterpret_cast<uintptr_t>(device_plans) & 15u) != 0) return EINVAL;
+    const auto* hp = static_cast<const lsb::LayerPlan*>(host_plans);
+    for (uint32_t i = 0; i < count; ++i) {
+        if (hp[i].layer >= b->geo.max_layers || !hp[i].epoch) return EINVAL;
+        b->last_epoch[hp[i].layer] = hp[i].epoch;
+    }
+    lsb::KernelParams p = lsb::base_params(*b, count, trace);
+    p.plans = static_cast<const lsb::LayerPlan*>(device_plans);
+    p.first = hp[0];
+    const int rc = lsb::launch_fused(p, lsb::grid_for(*b, candidate), static_cast<cudaStream_t>(stream));
+    return rc ? lsb::cuda_rc(cudaError_t(rc)) : 0;
 }
 
 int ls_b200_enqueue(void* backend, uint32_t layer, uint32_t bucket, uint32_t epoch, void* stream) {
@@ -461,6 +517,6 @@ int ls_b200_queue_fail(ls_b200_queue* q, uint32_t error) {
     return 0;
 }
 
-const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-layer r1"; }
+const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-mlp v2 (multi-layer)"; }
 
 }  // extern "C"

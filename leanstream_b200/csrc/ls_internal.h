@@ -13,39 +13,21 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 
 // Shared-memory ring: each stage holds up to 32 KB of packed INT4 rows and
-// up to 4 KB of fp16 scales. Six stages keep ~190 KB of HBM reads in flight
-// per SM, enough to cover DRAM latency at the per-SM share of HBM bandwidth.
+// 2 KB of fp16 scales. Six stages keep ~200 KB of HBM reads in flight per
+// SM -- more than one layer's per-SM share at config 2/3 -- so the producer
+// can run a full layer ahead of the consumers.
 constexpr int kStages = 6;
 constexpr int kStageData = 32 * 1024;
-constexpr int kStageScale = 4 * 1024;
+constexpr int kStageScale = 2 * 1024;
 constexpr int kStageBytes = kStageData + kStageScale;
 constexpr int kMaxGroupSize = 256;
-constexpr int kMaxHidden = 4096;  // register-resident activation limit (MAXC <= 4)
+constexpr int kMaxHidden = 4096;  // register-resident activation limit (4 chunks per lane)
 
-// Device workspace. Zero at rest: the last CTA of every launch restores it.
-struct Workspace {
-    uint32_t path;    // 0 undecided, 1 all-ready fast path, 2 progressive claims, 3 abort
-    uint32_t total;   // QueueControl.total_count of this launch
-    uint32_t claim;   // next claim position (core descriptors first)
-    uint32_t arrive;  // grid barrier before the reduction
-    uint32_t exit;    // CTAs that finished
-    uint32_t err;     // first LS_B200_DEV_* error of this launch
-    uint32_t detail;  // index involved in that error
-    uint32_t pad[25];
-    // followed by done_h[group_count]: neurons of each partial row whose h is published
-};
-constexpr uint32_t kPathFast = 1, kPathProgressive = 2, kPathAbort = 3;
-
-// Everything one launch needs, passed by value.
-struct KernelParams {
-    uint32_t H, G, N;
-    uint32_t cache_slots, staging_slots, phys_groups;  // 0 = unchecked
-    uint64_t group_bytes;
-    uint64_t timeout_ns;
-    float eps;
-    uint32_t epoch, mode, flags, layer, core_count;
-    const uint16_t* x;
-    uint16_t* y;
+// One MLP layer of a launch (POD, copied into kernel parameters or read from
+// a device array for multi-layer launches).
+struct alignas(16) LayerPlan {
+    const uint16_t* x;        // fp16 [H] input (normalised in-kernel when flagged)
+    uint16_t* y;              // fp16 [H] output (optional)
     const uint8_t* cache;
     const uint8_t* staging;
     const uint16_t* scales;
@@ -58,17 +40,40 @@ struct KernelParams {
     uint16_t* hidden_out;
     float* y32;
     const uint16_t* norm_w;
-    uint64_t* trace;    // optional [grid][LS_B200_TRACE_WORDS]
-    // backend scratch
-    float* partial;     // [N][H] fp32, one row per descriptor position
-    uint16_t* hbuf;     // [N][G] fp16 h, indexed like partial rows
-    Workspace* ws;      // device workspace (+ done_h)
-    uint32_t* status;   // mapped host words (LS_B200_STATUS_*)
-    uint32_t* done;     // mapped host per-layer completion epochs
+    uint32_t epoch, mode, flags, layer, core_count;
+    uint32_t pad[3];
 };
 
-// Host-side launcher implemented in ls_kernel.cu.
-int launch_fused_layer(const KernelParams& p, int grid, cudaStream_t stream);
+// Workspace words (device memory, zero at rest; the last CTA of every
+// launch restores the words it used).
+constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
+constexpr uint32_t kWsPerLayer = 4;  // path, claim, partials-done CTAs, reduced column blocks
+__host__ __device__ inline uint32_t ws_words(uint32_t max_layers, uint32_t N) {
+    return kWsHeader + kWsPerLayer * max_layers + max_layers * N;
+}
+
+// Everything one launch needs, passed by value.
+struct KernelParams {
+    uint32_t H, G, N;
+    uint32_t cache_slots, staging_slots, phys_groups;  // 0 = unchecked
+    uint64_t group_bytes;
+    uint64_t timeout_ns;
+    float eps;
+    uint32_t nlayers;     // layers executed by this launch
+    uint32_t max_layers;  // workspace capacity
+    uint32_t seq;         // launch sequence number (status word)
+    float* partial;       // [N][H] fp32, one row per descriptor position
+    uint16_t* hbuf;       // [N][G] fp16 h, indexed like partial rows
+    uint32_t* ws;         // workspace words
+    uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
+    uint32_t* done;       // mapped host per-layer completion epochs
+    uint64_t* trace;      // optional [grid][LS_B200_TRACE_WORDS]
+    const LayerPlan* plans;  // device array for nlayers > 1, else nullptr
+    LayerPlan first;         // layer 0 when plans == nullptr
+};
+
+// Host-side launchers implemented in ls_kernel.cu.
+int launch_fused(const KernelParams& p, int grid, cudaStream_t stream);
 int prepare_kernels();  // raise the dynamic shared-memory limit once
 size_t kernel_smem_bytes();
 

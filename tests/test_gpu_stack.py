@@ -82,3 +82,55 @@ def test_stack_chain(native_lib, cuda_device, H):
         ref = nxt.astype(np.float32)
         assert np.abs(got - ref).max() <= TOL * np.abs(ref).max() + 1e-3, (l, np.abs(got - ref).max())
     be.close()
+
+
+def test_multilayer_launch_matches_per_layer(native_lib, cuda_device):
+    """One persistent launch over L layers (ls_b200_launch_plans) must equal,
+    bit for bit, L chained single-layer launches (same canonical arithmetic)."""
+    import torch
+    from gpu_harness import to_dev, wait_stream
+    from leanstream_b200 import B200Backend, ExecutionQueue
+    from leanstream_b200 import _native as N
+    from leanstream_b200.synthetic import descriptors, make_layer
+
+    H, G, n, layers = 4096, 64, 40, 5
+    Ls = [make_layer(300 + l, H, n, G) for l in range(layers)]
+    sets = [np.sort(np.random.default_rng(50 + l).permutation(n)[: 8 + 4 * l]) for l in range(layers)]
+    be = B200Backend().configure(H, G, n, max_layers=layers, rms_eps=1e-5)
+    x0 = to_dev(Ls[0].x.view(np.int16), torch.float16)
+    keep, queues = [], []
+    for l in range(layers):
+        q = ExecutionQueue(n)
+        q.reset(l + 1)
+        q.write_descriptors(descriptors(sets[l]))
+        q.prepare(len(sets[l]))
+        q.publish_all()
+        q.activate()
+        queues.append(q)
+        keep += [to_dev(Ls[l].packed), to_dev(Ls[l].scales.reshape(-1).view(np.int16), torch.float16)]
+
+    def run(multi):
+        xs = [x0.clone()] + [torch.zeros(H, dtype=torch.float16, device="cuda") for _ in range(layers)]
+        y = torch.zeros(H, dtype=torch.float16, device="cuda")
+        args = [be.layer_args(input=xs[l], output=y, cache=keep[2 * l], scales=keep[2 * l + 1], epoch=l + 1,
+                              queue=queues[l].view, mode=N.MODE_BATCH_COMPAT, layer=l, flags=N.NORM_INPUT,
+                              residual=xs[l], hidden_out=xs[l + 1]) for l in range(layers)]
+        if multi:
+            host = torch.frombuffer(bytearray(b"".join(be.encode_plan(a) for a in args)), dtype=torch.uint8)
+            dev = host.cuda()
+            be.launch_plans(dev, layers, host.numpy().ctypes.data)
+        else:
+            for a in args:
+                be.launch(a)
+        wait_stream()
+        assert be.status()[N.STATUS_ERROR] == 0, be.status()
+        return [x.cpu().numpy().view(np.uint16).copy() for x in xs]
+
+    single = run(False)
+    multi = run(True)
+    for l in range(1, layers + 1):
+        assert np.array_equal(single[l], multi[l]), l
+        assert np.isfinite(single[l].view(np.float16).astype(np.float32)).all()
+    for l in range(layers):
+        assert be.completed_epoch(l) == l + 1
+    be.close()
