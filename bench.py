@@ -236,7 +236,8 @@ def trace_report(st, encoded, stream):
     import torch
 
     grid = torch.cuda.get_device_properties(0).multi_processor_count
-    trace = torch.zeros(grid * 8 + grid * LAYERS * 8, dtype=torch.int64, device=st.dev)
+    pieces = 128
+    trace = torch.zeros(grid * 8 + grid * LAYERS * 8 + 4 * pieces * 4, dtype=torch.int64, device=st.dev)
     host, dev = encoded
     with torch.cuda.stream(stream):
         st.N.load().ls_b200_spin(1_000_000, stream.cuda_stream)
@@ -244,7 +245,8 @@ def trace_report(st, encoded, stream):
     torch.cuda.synchronize()
     t = trace.cpu().numpy().astype(np.int64)
     cta = t[: grid * 8].reshape(grid, 8)
-    lay = t[grid * 8:].reshape(grid, LAYERS, 8)
+    lay = t[grid * 8: grid * 8 + grid * LAYERS * 8].reshape(grid, LAYERS, 8)
+    pcs = t[grid * 8 + grid * LAYERS * 8:].reshape(4, pieces, 4)
     t0 = cta[:, 0].min()
     rel = lambda a: np.where(a > 0, (a - t0) / 1000.0, np.nan)
     names = {0: "entry", 1: "decided", 2: "first", 3: "pieces", 4: "produced", 6: "roles_done", 7: "exit"}
@@ -259,6 +261,12 @@ def trace_report(st, encoded, stream):
             v = rel(lay[:, l, w])
             cols.append(f"{np.nanmedian(v):6.1f}/{np.nanmax(v):6.1f}" if np.isfinite(v).any() else f"{'-':>13s}")
         print(f"{l:5d}  " + " ".join(f"{c:>14s}" for c in cols), file=sys.stderr)
+    print("CTA0 pieces: idx issued closed ready done (us)", file=sys.stderr)
+    for i in range(min(pieces, 40)):
+        v = rel(pcs[0, i])
+        if not np.isfinite(v).any():
+            break
+        print(f"  {i:3d} " + " ".join(f"{x:7.1f}" for x in v), file=sys.stderr)
 
 
 def run_gpu(args, rank, world, local_rank):

@@ -95,7 +95,8 @@ typedef struct ls_compute_backend {
 /* KernelCandidate (include/leanstream/kernel_selector.h:6-12). */
 typedef struct ls_kernel_candidate {
     uint32_t id;
-    uint32_t workers;     /* persistent CTAs, as in the Triton catalog */
+    uint32_t workers;     /* persistent CTAs, as in the Triton catalog
+                           * entry_point: 1 = tensor-core gate/up, 0 = CUDA-core fma */
     const char* name;
     uint32_t cta_count, tile_size, unroll, group_batch, entry_point;
     bool available;
@@ -106,7 +107,7 @@ typedef struct ls_kernel_candidate {
 /* ------------------------------------------------------------------ */
 
 typedef struct ls_b200_geometry {
-    uint32_t hidden;        /* H: multiple of 256, at most 8192 */
+    uint32_t hidden;        /* H: 256, 512, 1024, 2048 or 4096 */
     uint32_t group_size;    /* G: neurons per logical group, 1..256 */
     uint32_t group_count;   /* N: logical groups = dest slots = partial rows */
     uint32_t max_layers;    /* number of per-layer completion words (0 -> 256) */
@@ -148,7 +149,8 @@ typedef struct ls_b200_layer_args {
     const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
     uint64_t* trace;          /* optional %globaltimer phase stamps: [grid][LS_B200_TRACE_WORDS]
                                * per CTA, then [grid][layers][LS_B200_LAYER_TRACE_WORDS]
-                               * per CTA and layer (LS_B200_*TRACE_*); the Stamp
+                               * per CTA and layer, then [4][LS_B200_PIECE_TRACE_PIECES][4]
+                               * per piece of CTAs 0..3 (LS_B200_*TRACE_*); the Stamp
                                * buffers of backends/triton/core.py:25, persistent.py:37 */
 } ls_b200_layer_args;
 
@@ -175,6 +177,10 @@ enum {
     LS_B200_LTRACE_LOADED = 6,         /* next layer's activation loaded (stamped under that layer) */
     LS_B200_LAYER_TRACE_WORDS = 8
 };
+/* Per-piece stamps of CTAs 0..3 (after the per-layer block):
+ * [4][LS_B200_PIECE_TRACE_PIECES][4] = producer issued, producer closed,
+ * consumer warp 0 saw the stage full, consumer warp 0 finished it. */
+enum { LS_B200_PIECE_TRACE_PIECES = 128 };
 
 /* Device status words (ls_b200_status). */
 enum {

@@ -32,13 +32,16 @@ namespace {
 // Candidate ids 0..3 keep the production Triton geometry of
 // include/leanstream/triton_backend.h:5-8 (4/8/16/32 persistent CTAs), so an
 // offline LUT written for it keeps its meaning. Id 4 is the B200 entry: one
-// persistent CTA per SM (resolved at configure), the fallback.
+// persistent CTA per SM (resolved at configure), the fallback. entry_point
+// selects the gate/up inner product: 1 = tensor-core mma.sync, 0 = CUDA-core
+// fp16xfp16->fp32 fma (id 5, same grid as id 4).
 constexpr ls_kernel_candidate kCatalog[] = {
-    {0, 4, "b200_ctas_4", 4, 0, 0, 0, 0, true},
-    {1, 8, "b200_ctas_8", 8, 0, 0, 0, 0, true},
-    {2, 16, "b200_ctas_16", 16, 0, 0, 0, 0, true},
-    {3, 32, "b200_ctas_32", 32, 0, 0, 0, 0, true},
-    {4, 0, "b200_ctas_per_sm", 0, 0, 0, 0, 0, true},
+    {0, 4, "b200_ctas_4", 4, 0, 0, 0, 1, true},
+    {1, 8, "b200_ctas_8", 8, 0, 0, 0, 1, true},
+    {2, 16, "b200_ctas_16", 16, 0, 0, 0, 1, true},
+    {3, 32, "b200_ctas_32", 32, 0, 0, 0, 1, true},
+    {4, 0, "b200_ctas_per_sm", 0, 0, 0, 0, 1, true},
+    {5, 0, "b200_ctas_per_sm_fma", 0, 0, 0, 0, 0, true},
 };
 constexpr uint32_t kCatalogSize = sizeof(kCatalog) / sizeof(kCatalog[0]);
 constexpr uint32_t kDefaultCandidate = 4;
@@ -63,7 +66,7 @@ struct Backend {
     bool bound_set = false;
     // scratch (device) and mapped words (host)
     float* partial = nullptr;
-    uint16_t* hbuf = nullptr;
+    unsigned long long* hbuf = nullptr;
     uint32_t* ws = nullptr;
     uint32_t seq = 0;
     uint32_t* status_host = nullptr;
@@ -114,7 +117,10 @@ int cuda_rc(cudaError_t e) { return e == cudaSuccess ? 0 : (int(e) > 0 ? int(e) 
 int configure(Backend& b, const ls_b200_geometry& g) {
     if (b.configured) return EBUSY;
     const uint32_t H = g.hidden, G = g.group_size, N = g.group_count;
-    if (!H || H % 256 || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N) return EINVAL;
+    // H = 256 * {1, 2, 4, 8, 16}: each consumer warp owns H/8 coordinates
+    const uint32_t sb = H / 256;
+    if (!H || H % 256 || (sb & (sb - 1)) || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N)
+        return EINVAL;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ENODEV;
     cudaDeviceProp prop{};
@@ -128,13 +134,14 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     if (!b.geo.max_layers) b.geo.max_layers = 256;
     if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
     const size_t partial_bytes = size_t(N) * H * sizeof(float);
-    const size_t h_bytes = size_t(N) * G * sizeof(uint16_t);
+    const size_t h_bytes = size_t(N) * G * sizeof(unsigned long long);
     const size_t ws_bytes = size_t(ws_words(b.geo.max_layers, N)) * sizeof(uint32_t);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.hbuf, h_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.hbuf, 0, h_bytes);  // tag 0 is never a valid tag
     if (e == cudaSuccess) e = cudaHostAlloc(&b.status_host, 64, cudaHostAllocMapped);
     if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b.status_dev), b.status_host, 0);
     if (e == cudaSuccess)
@@ -224,9 +231,11 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace) {
     return p;
 }
 
-int grid_for(const Backend& b, int32_t candidate) {
+int grid_for(const Backend& b, int32_t candidate, uint32_t* variant) {
     const uint32_t id = candidate >= 0 ? uint32_t(candidate) : b.select(b.state_layer, b.state_bucket);
-    int grid = int(b.candidate(id).cta_count);
+    const ls_kernel_candidate c = b.candidate(id);
+    *variant = c.entry_point;
+    int grid = int(c.cta_count);
     return grid > b.sms ? b.sms : grid;
 }
 
@@ -240,7 +249,8 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     p.plans = nullptr;
     p.first = plan;
     b.last_epoch[a.layer] = a.epoch;
-    rc = launch_fused(p, grid_for(b, a.candidate), stream);
+    const int grid = grid_for(b, a.candidate, &p.variant);
+    rc = launch_fused(p, grid, stream);
     return rc ? cuda_rc(cudaError_t(rc)) : 0;
 }
 
@@ -355,7 +365,8 @@ int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count
     lsb::KernelParams p = lsb::base_params(*b, count, trace);
     p.plans = static_cast<const lsb::LayerPlan*>(device_plans);
     p.first = hp[0];
-    const int rc = lsb::launch_fused(p, lsb::grid_for(*b, candidate), static_cast<cudaStream_t>(stream));
+    const int grid = lsb::grid_for(*b, candidate, &p.variant);
+    const int rc = lsb::launch_fused(p, grid, static_cast<cudaStream_t>(stream));
     return rc ? lsb::cuda_rc(cudaError_t(rc)) : 0;
 }
 
@@ -517,6 +528,6 @@ int ls_b200_queue_fail(ls_b200_queue* q, uint32_t error) {
     return 0;
 }
 
-const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-mlp v2 (multi-layer)"; }
+const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-mlp v3 (tagged h, split-K gate/up)"; }
 
 }  // extern "C"

@@ -12,14 +12,17 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 
-// Shared-memory ring: each stage holds up to 32 KB of packed INT4 rows and
-// 2 KB of fp16 scales. Six stages keep ~200 KB of HBM reads in flight per
-// SM -- more than one layer's per-SM share at config 2/3 -- so the producer
-// can run a full layer ahead of the consumers.
+// Shared-memory ring: each stage holds up to 33 KB of packed INT4 rows and a
+// 3 KB auxiliary area (fp16 scales, staged h values, cross-warp partials).
+// Six stages keep ~200 KB of HBM reads in flight per SM -- more than one
+// layer's per-SM share at config 2/3 -- so the producer can run a full
+// layer ahead of the consumers.
 constexpr int kStages = 6;
-constexpr int kStageData = 32 * 1024;
-constexpr int kStageScale = 2 * 1024;
-constexpr int kStageBytes = kStageData + kStageScale;
+constexpr int kStageData = 33 * 1024;
+constexpr int kStageAux = 3 * 1024;
+constexpr int kStageBytes = kStageData + kStageAux;
+constexpr int kAuxSecond = 2048;   // aux offset of DOWN h values / GATEUP partials
+constexpr int kGateupMax = 16;     // neurons per GATEUP piece
 constexpr int kMaxGroupSize = 256;
 constexpr int kMaxHidden = 4096;  // register-resident activation limit (4 chunks per lane)
 
@@ -48,8 +51,8 @@ struct alignas(16) LayerPlan {
 // launch restores the words it used).
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
 constexpr uint32_t kWsPerLayer = 4;  // path, claim, partials-done CTAs, reduced column blocks
-__host__ __device__ inline uint32_t ws_words(uint32_t max_layers, uint32_t N) {
-    return kWsHeader + kWsPerLayer * max_layers + max_layers * N;
+__host__ __device__ inline uint32_t ws_words(uint32_t max_layers, uint32_t) {
+    return kWsHeader + kWsPerLayer * max_layers;
 }
 
 // Everything one launch needs, passed by value.
@@ -61,9 +64,10 @@ struct KernelParams {
     float eps;
     uint32_t nlayers;     // layers executed by this launch
     uint32_t max_layers;  // workspace capacity
-    uint32_t seq;         // launch sequence number (status word)
+    uint32_t seq;         // launch sequence number (status word, h tags)
+    uint32_t variant;     // 0: CUDA-core FMA gate/up, 1: tensor-core (mma.sync) gate/up
     float* partial;       // [N][H] fp32, one row per descriptor position
-    uint16_t* hbuf;       // [N][G] fp16 h, indexed like partial rows
+    unsigned long long* hbuf;  // [N][G] tagged h words: (tag << 32) | fp16 h
     uint32_t* ws;         // workspace words
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
     uint32_t* done;       // mapped host per-layer completion epochs

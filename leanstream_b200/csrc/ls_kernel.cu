@@ -30,16 +30,24 @@
 //     each claimed descriptor.
 // Canonical arithmetic, shared by both schedules (so BatchCompat and
 // Progressive outputs are bit-identical, tests/persistent_mlp_test.cu:65):
-//   g, u : per lane, 16-byte chunks j = lane + 32 i, 4 pair accumulators,
-//          then a fixed xor-butterfly over the warp;
+//   g, u : the hidden dimension is split into 8 fixed slices, one per
+//          consumer warp; each warp reduces its slice for 8 neurons at a time
+//          (tensor-core mma.sync m16n8k16 with the 8 gate rows and 8 up rows
+//          as A and x as column 0 of B, or CUDA-core fp16xfp16->fp32 fmas with
+//          the same data mapping), and the 8 slice sums are added in warp
+//          order by the last warp to finish the piece;
 //   down : per column, one fp32 chain over the descriptor's neurons in order;
 //   y    : per column, partial rows summed in row order.
+// h travels between CTAs as 64-bit words (launch/layer tag << 32 | fp16 h):
+// the tag makes a single relaxed store self-validating, so publishing h
+// needs no fence or counter. The producer warp polls those words and copies
+// h into the DOWN piece's stage, off the consumers' critical path.
 // Rounding boundaries (core.py:17,49-52; reduction.py:15): w = fp16(q*s),
 // g,u -> fp16, SiLU -> fp16, h -> fp16, fp32 partials, y -> fp16 once.
 //
-// Synchronisation uses counters with bounded waits only -- no named
-// barriers inside loops -- so a warp that gives up can never strand the
-// others. Every wait ends at a %globaltimer deadline and records an error.
+// Synchronisation uses counters and tagged words with bounded waits only --
+// no named barriers inside loops -- so a warp that gives up can never strand
+// the others. Every wait ends at a %globaltimer deadline and records an error.
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include "ls_internal.h"
@@ -84,7 +92,7 @@ struct SmemTail {
     unsigned long long empty_bar[kStages];
     Piece piece[kStages];
     DescView dtab[32];  // producer's descriptor window
-    __half hs[kConsumerWarps * kMaxGroupSize];
+    uint32_t gcnt[kStages];  // warps done with a GATEUP piece (per stage)
     alignas(16) __half xs[kMaxHidden];  // activation of the current layer, staged once per CTA
     uint32_t warps_done;     // consumer warps that finished a layer (monotonic)
     volatile uint32_t abort;
@@ -125,7 +133,14 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -181,6 +196,17 @@ __device__ __forceinline__ float mfma(__half a, __half b, float c) {
     asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
     return d;
 }
+// Tensor-core step: D(16x8,f32) += A(16x16,f16) * B(16x8,f16).
+__device__ __forceinline__ void mma16816(float (&d)[4], __half2 a0, __half2 a1, __half2 a2, __half2 a3, __half2 b0,
+                                         __half2 b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(*reinterpret_cast<uint32_t*>(&a0)), "r"(*reinterpret_cast<uint32_t*>(&a1)),
+          "r"(*reinterpret_cast<uint32_t*>(&a2)), "r"(*reinterpret_cast<uint32_t*>(&a3)),
+          "r"(*reinterpret_cast<uint32_t*>(&b0)), "r"(*reinterpret_cast<uint32_t*>(&b1)));
+}
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
     __half2 h;
     *reinterpret_cast<uint32_t*>(&h) = v;
@@ -205,18 +231,6 @@ __device__ __forceinline__ void unpack8(uint32_t w, __half2 (&q)[4]) {
     q[3] = __hfma2(as_h2(hi2), k16, k72);
 }
 
-// gate/up accumulation of one 32-bit word (8 coordinates) against x.
-__device__ __forceinline__ void dot_word(uint32_t w, __half2 s, const __half2* x, float (&acc)[4]) {
-    __half2 q[4];
-    unpack8(w, q);
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        const __half2 v = __hmul2(q[p], s);  // == fp16(float(q) * float(s)), core.py:17
-        acc[p] = mfma(__low2half(v), __low2half(x[p]), acc[p]);
-        acc[p] = mfma(__high2half(v), __high2half(x[p]), acc[p]);
-    }
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -228,11 +242,19 @@ __device__ __forceinline__ float round16(float v) { return __half2float(__float2
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
     return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] claim [2] partials-done CTAs [3] reduced blocks
 }
-__device__ __forceinline__ uint32_t* done_h(const KernelParams& P, uint32_t l) {
-    return P.ws + kWsHeader + kWsPerLayer * P.max_layers + size_t(l) * P.N;
+// Tag of h words written by layer l of this launch (never 0: seq >= 1).
+__device__ __forceinline__ unsigned long long h_tag(const KernelParams& P, uint32_t l) {
+    return (static_cast<unsigned long long>((P.seq << 8) | (l & 0xffu))) << 32;
 }
 __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
     if (P.trace) P.trace[size_t(blockIdx.x) * LS_B200_TRACE_WORDS + word] = gtimer();
+}
+// Per-piece stamps of CTAs 0..3 after the per-layer block:
+// [4][LS_B200_PIECE_TRACE_PIECES][4] = issued, closed (producer), ready, done (consumer warp 0).
+__device__ __forceinline__ void trace_piece(const KernelParams& P, uint32_t piece, uint32_t word) {
+    if (P.trace && blockIdx.x < 4 && piece < LS_B200_PIECE_TRACE_PIECES)
+        P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(gridDim.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
+                (size_t(blockIdx.x) * LS_B200_PIECE_TRACE_PIECES + piece) * 4 + word] = gtimer();
 }
 // Per-layer stamps after the launch-level block: [grid][nlayers][LS_B200_LAYER_TRACE_WORDS].
 __device__ __forceinline__ void trace_layer(const KernelParams& P, uint32_t l, uint32_t word) {
@@ -281,6 +303,14 @@ __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_
 }
 
 // ------------------------------------------------------------ producer side
+// A DOWN stage whose rows are in flight but whose h values are not yet
+// staged: the producer keeps issuing later pieces and closes it once the
+// tagged h words of its rows appear.
+struct OpenStage {
+    uint32_t stage, hrow, rows, layer;  // hrow: first tagged word (partial row * G + r0)
+    uint32_t piece;                     // piece index (trace)
+};
+
 struct Producer {
     uint32_t idx;   // pieces issued so far (stage = idx % kStages)
     uint32_t lane;
@@ -289,25 +319,84 @@ struct Producer {
     uint64_t deadline;
     uint32_t wbase;  // first descriptor position held in t->dtab
     uint32_t wlayer;
+    OpenStage open[kStages];
+    uint32_t open_head, open_count;
 };
 
-// Waits until the next stage is free; lane 0 polls, the warp learns the result.
+__device__ bool producer_try_close(Producer& pr, const KernelParams& P, bool blocking);
+
+// Waits until the next stage is free, closing open DOWN stages meanwhile
+// (one of them may be the stage being waited for).
 __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
     const uint32_t s = pr.idx % kStages;
     const uint32_t parity = ((pr.idx / kStages) & 1u) ^ 1u;
-    uint32_t ok = 1;
-    if (pr.lane == 0) {
-        const uint32_t bar = smem_u32(&pr.t->empty_bar[s]);
-        uint32_t spins = 0;
-        while (!mbar_try_wait(bar, parity)) {
-            if ((++spins & 255u) == 0 && gtimer() > pr.deadline + kProducerGraceNs) {
-                raise_error(P, pr.t, LS_B200_DEV_TIMEOUT_SYNC, 1);
-                ok = 0;
-                break;
-            }
+    const uint32_t bar = smem_u32(&pr.t->empty_bar[s]);
+    uint32_t spins = 0;
+    for (;;) {
+        uint32_t ready = 0;
+        if (pr.lane == 0) ready = mbar_try_wait(bar, parity) ? 1u : 0u;
+        if (__shfl_sync(0xffffffffu, ready, 0)) return true;
+        if (pr.open_count) {
+            producer_try_close(pr, P, false);
+            continue;
+        }
+        uint32_t late = 0;
+        if (pr.lane == 0 && (++spins & 255u) == 0 && gtimer() > pr.deadline + kProducerGraceNs) late = 1;
+        if (__shfl_sync(0xffffffffu, late, 0)) {
+            if (pr.lane == 0) raise_error(P, pr.t, LS_B200_DEV_TIMEOUT_SYNC, 1);
+            return false;
         }
     }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Completes a stage: 32 cp.async arrivals (one per lane, when its scale /
+// h copies land) plus one release arrival by lane 0 after the warp's
+// shared-memory writes. The full barrier expects 34 arrivals in total.
+__device__ __forceinline__ void producer_close(Producer& pr, uint32_t s) {
+    const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
+    cp_async_arrive_noinc(bar);
+    __syncwarp();
+    if (pr.lane == 0) mbar_arrive(bar);
+}
+__device__ __forceinline__ void producer_stamp(const KernelParams& P, const Producer& pr, uint32_t piece,
+                                               uint32_t word) {
+    if (pr.lane == 0) trace_piece(P, piece, word);
+}
+
+// Tries to close the oldest open DOWN stage: polls the tagged h words of its
+// rows once (or until they appear / the deadline passes, when blocking).
+__device__ bool producer_try_close(Producer& pr, const KernelParams& P, bool blocking) {
+    if (!pr.open_count) return true;
+    const OpenStage o = pr.open[pr.open_head];
+    const unsigned long long tag = h_tag(P, o.layer);
+    uint32_t hv = 0, spins = 0;
+    bool ok_all = false;
+    for (;;) {
+        uint32_t ok = 1;
+        if (pr.lane < o.rows) {
+            const unsigned long long w = ld_relaxed_gpu_u64(P.hbuf + o.hrow + pr.lane);
+            ok = (w & 0xffffffff00000000ull) == tag;
+            hv = uint32_t(w) & 0xffffu;
+        }
+        if (__all_sync(0xffffffffu, ok)) { ok_all = true; break; }
+        if (!blocking) return false;
+        uint32_t late = 0;
+        if (pr.lane == 0 && (++spins & 63u) == 0 && (pr.t->abort || gtimer() > pr.deadline)) late = 1;
+        if (__shfl_sync(0xffffffffu, late, 0)) break;
+        __nanosleep(32);
+    }
+    if (!ok_all && pr.lane == 0 && !pr.t->abort) raise_error(P, pr.t, LS_B200_DEV_TIMEOUT_SYNC, 3);
+    uint8_t* st = pr.stages + size_t(o.stage) * kStageBytes;
+    if (pr.lane < o.rows) reinterpret_cast<uint16_t*>(st + kStageData + kAuxSecond)[pr.lane] = uint16_t(hv);
+    producer_close(pr, o.stage);
+    producer_stamp(P, pr, o.piece, 1);
+    pr.open_head = (pr.open_head + 1) % kStages;
+    --pr.open_count;
+    return ok_all;
+}
+
+__device__ void producer_flush(Producer& pr, const KernelParams& P) {
+    while (pr.open_count) producer_try_close(pr, P, true);
 }
 
 // A data-less piece (LAYER or FINAL marker).
@@ -323,7 +412,9 @@ __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t ki
         pc.flags = flags;
         mbar_arrive_expect_tx(smem_u32(&pr.t->full_bar[s]), 0);
     }
-    cp_async_arrive_noinc(smem_u32(&pr.t->full_bar[s]));
+    producer_stamp(P, pr, pr.idx, 0);
+    producer_close(pr, s);
+    producer_stamp(P, pr, pr.idx, 1);
     ++pr.idx;
     return true;
 }
@@ -346,19 +437,25 @@ __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const Layer
         pc.n0 = n0;
         pc.count = count;
         mbar_arrive_expect_tx(bar, count * H);
+        // rows at a pitch of H + 16 bytes: the consumers' 4-byte loads of 8
+        // rows then hit 32 distinct banks
         for (uint32_t k = 0; k < count; ++k)
-            bulk_g2s(smem_u32(st + size_t(k) * H), d.src + (n0 + k) * rec, H, bar);
+            bulk_g2s(smem_u32(st + size_t(k) * (H + 16)), d.src + (n0 + k) * rec, H, bar);
     }
-    // gate+up scales: H/128 words per neuron, at the start of its scale row.
+    // gate+up scales: H/128 words per neuron, at the start of its scale row;
+    // staged at a pitch of H/128 + 1 words so that 8 neurons' scales sit in
+    // 8 different banks.
     const uint32_t wpn = H / 128;
     const uint32_t words = count * wpn;
     const uint32_t sdst = smem_u32(st + kStageData);
     for (uint32_t i = pr.lane; i < words; i += 32) {
         const uint32_t k = i / wpn, w = i % wpn;
         const uint16_t* src = L.scales + (size_t(d.phys) * P.G + n0 + k) * (3 * H / 128) + 2 * w;
-        cp_async4(sdst + 4 * i, src);
+        cp_async4(sdst + 4 * (k * (wpn + 1) + w), src);
     }
-    cp_async_arrive_noinc(bar);
+    producer_stamp(P, pr, pr.idx, 0);
+    producer_close(pr, s);
+    producer_stamp(P, pr, pr.idx, 1);
     ++pr.idx;
     return true;
 }
@@ -402,7 +499,12 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
             L.scales + (size_t(d.phys) * P.G + r0 + r) * (3 * H / 128) + 2 * (H / 128) + sb0 + 2 * w;
         cp_async4(sdst + 4 * i, src);
     }
-    cp_async_arrive_noinc(bar);
+    // The stage stays open until the h of rows [r0, r0+rows) -- written by
+    // the GATEUP pieces of this layer, in any CTA -- is staged next to it.
+    const uint32_t slot = (pr.open_head + pr.open_count) % kStages;
+    producer_stamp(P, pr, pr.idx, 0);
+    pr.open[slot] = OpenStage{s, uint32_t(d.row * P.G + r0), rows, layer, pr.idx};
+    ++pr.open_count;
     ++pr.idx;
     return true;
 }
@@ -417,8 +519,8 @@ __device__ __forceinline__ uint32_t down_chunks(const KernelParams& P) {
     return m < hc ? m : hc;
 }
 __device__ __forceinline__ uint32_t gateup_neurons(const KernelParams& P) {
-    const uint32_t n = kStageData / P.H;
-    return n < 32u ? n : 32u;
+    const uint32_t n = kStageData / (P.H + 16);
+    return n < uint32_t(kGateupMax) ? n : uint32_t(kGateupMax);
 }
 
 // DOWN pieces of chunks [k0, k0+m) of one descriptor, all row groups.
@@ -528,7 +630,14 @@ __device__ void stamp(const LayerPlan& L, const DescView& d) {
 
 // Producer warp main loop over the layers of the launch.
 __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
-    Producer pr{0, threadIdx.x & 31u, stages, t, deadline, 0xffffffffu, 0xffffffffu};
+    Producer pr;
+    pr.idx = 0;
+    pr.lane = threadIdx.x & 31u;
+    pr.stages = stages;
+    pr.t = t;
+    pr.deadline = deadline;
+    pr.wbase = pr.wlayer = 0xffffffffu;
+    pr.open_head = pr.open_count = 0;
     bool ok = true;
     for (uint32_t l = 0; ok && l < P.nlayers; ++l) {
         const LayerPlan& L = plan_at(P, l);
@@ -610,128 +719,154 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         if (ok) ok = producer_marker(pr, P, kPieceLayer, l, D, t->abort ? 0u : kLayerGood);
     }
     producer_marker(pr, P, kPieceFinal, 0, 0, 0);
+    producer_flush(pr, P);
     if (pr.lane == 0) trace(P, LS_B200_TRACE_PRODUCED);
 }
 
 // ------------------------------------------------------------ consumer side
-template <int MAXC>
-struct Activation {
-    __half2 x[MAXC][16];  // chunk i of this lane: pairs (c, c+4) per 8-coordinate word
+// Register-resident activation fragments of one warp's hidden slice:
+// x[b][p] = (x[c + p], x[c + p + 4]), c = slice start + 32 b + 8 (lane & 3).
+// For the tensor-core path these are the B fragments (column 0) of
+// m16n8k16 for logical k = (2t, 2t+1) and (2t+8, 2t+9).
+template <int SB>
+struct Frag {
+    __half2 x[SB][4];
 };
 
-// Loads this lane's activation chunks with 16-byte loads and, when flagged,
-// applies the HF RMSNorm of predictor_shared_input.cu:16-33 per warp:
+// Builds this warp's fragments from the CTA's staged activation, applying
+// the HF RMSNorm of predictor_shared_input.cu:16-33 when flagged:
 // inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv)).
-// The sum is per lane in chunk order, then a fixed butterfly: every warp of
-// every CTA computes the same value.
-template <int MAXC>
-__device__ void load_activation(const KernelParams& P, const LayerPlan& L, const __half* xs, Activation<MAXC>& a,
+// The sum runs per lane over 8-coordinate groups lane*8 + 256 i, then a
+// fixed butterfly: every warp of every CTA computes the same value.
+template <int SB>
+__device__ void load_activation(const KernelParams& P, const LayerPlan& L, const __half* xs, Frag<SB>& f, int warp,
                                 int lane) {
-    const uint32_t hc = P.H / 32;
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-        const uint32_t j = lane + 32 * i;
-        uint4 w[4];
-        if (j < hc) {
-            const uint4* src = reinterpret_cast<const uint4*>(xs + 32 * j);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) w[v] = src[v];
-        } else {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) w[v] = make_uint4(0, 0, 0, 0);
-        }
-        // word v holds coordinates 8v..8v+7 as 4 half2 (2e, 2e+1)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-            const __half2* h = reinterpret_cast<const __half2*>(&w[v]);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const __half lo = (p & 1) ? __high2half(h[p >> 1]) : __low2half(h[p >> 1]);
-                const __half hi = (p & 1) ? __high2half(h[2 + (p >> 1)]) : __low2half(h[2 + (p >> 1)]);
-                a.x[i][4 * v + p] = __halves2half2(lo, hi);  // (coord 8v+p, 8v+p+4)
-            }
+    const uint32_t H = P.H;
+    const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
+    float inv = 1.f;
+    if (norm) {
+        float ss = 0.f;
+        for (uint32_t c = 8 * lane; c < H; c += 256) {
+            const uint4 w = *reinterpret_cast<const uint4*>(xs + c);
+            const __half2* h = reinterpret_cast<const __half2*>(&w);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(h[e]);
-                ss += f.x * f.x;
-                ss += f.y * f.y;
+                const float2 v = __half22float2(h[e]);
+                ss += v.x * v.x;
+                ss += v.y * v.y;
             }
         }
+        inv = rsqrtf(warp_sum(ss) / float(H) + P.eps);
     }
-    if (L.flags & LS_B200_NORM_INPUT) {
-        const float inv = rsqrtf(warp_sum(ss) / float(P.H) + P.eps);
+    const uint32_t base = warp * (H / 8) + 8 * (lane & 3);
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const uint32_t j = lane + 32 * i;
-            __half2 wv[16];
-            if (L.norm_w && j < hc) {
-                const uint4* src = reinterpret_cast<const uint4*>(L.norm_w + 32 * j);
+    for (int b = 0; b < SB; ++b) {
+        const uint32_t c = base + 32 * b;
+        const uint4 w = *reinterpret_cast<const uint4*>(xs + c);
+        const __half* h = reinterpret_cast<const __half*>(&w);
+        __half v[8];
 #pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    const uint4 w = __ldg(src + v);
-                    const __half2* h = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        const __half lo = (p & 1) ? __high2half(h[p >> 1]) : __low2half(h[p >> 1]);
-                        const __half hi = (p & 1) ? __high2half(h[2 + (p >> 1)]) : __low2half(h[2 + (p >> 1)]);
-                        wv[4 * v + p] = __halves2half2(lo, hi);
-                    }
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float2 f = __half22float2(a.x[i][k]);
-                __half2 n = __halves2half2(__float2half_rn(f.x * inv), __float2half_rn(f.y * inv));
-                if (L.norm_w && j < hc) n = __hmul2(wv[k], n);
-                a.x[i][k] = n;
-            }
+        for (int e = 0; e < 8; ++e) {
+            v[e] = h[e];
+            if (norm) v[e] = __float2half_rn(__half2float(v[e]) * inv);
         }
+        if (norm && L.norm_w) {
+            const uint4 nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w + c));
+            const __half* wh = reinterpret_cast<const __half*>(&nw);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) f.x[b][p] = __halves2half2(v[p], v[p + 4]);
     }
 }
 
-template <int MAXC>
-__device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, const uint8_t* st,
-                               const Activation<MAXC>& a, int warp, int lane) {
-    const uint32_t H = P.H, hc = H / 32;
+// GATEUP piece: this warp's hidden slice for every neuron of the piece, in
+// tiles of 8 neurons; the slice sums go to the stage's partial area and the
+// last warp to finish adds them in warp order, forms h and publishes it.
+template <int SB, bool MMA>
+__device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, uint8_t* st, SmemTail* t,
+                               uint32_t s, const Frag<SB>& f, int warp, int lane) {
+    const uint32_t H = P.H, pitch = H + 16;
+    const int g = lane >> 2, tq = lane & 3;
+    const uint32_t slice = warp * (H / 8);  // first coordinate of this warp's slice
     const __half* sc = reinterpret_cast<const __half*>(st + kStageData);
-    uint32_t* dh = done_h(P, pc.layer) + pc.row;
-    for (uint32_t k = warp; k < pc.count; k += kConsumerWarps) {
-        const uint8_t* row = st + size_t(k) * H;
-        const __half* scr = sc + size_t(k) * (H / 64);
-        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+    float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxSecond);  // [warp][kGateupMax]
+    for (uint32_t r0 = 0; r0 < pc.count; r0 += 8) {
+        const uint32_t k = r0 + g;  // neuron of the piece handled by this lane quad
+        const uint8_t* row = st + size_t(k) * pitch + slice / 2 + 4 * tq;
+        const __half* scr = sc + size_t(k) * 2 * (H / 128 + 1);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // second tensor-core chain (odd sub-blocks)
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const uint32_t j = lane + 32 * i;
-            if (j < hc) {
-                const uint4 wg = *reinterpret_cast<const uint4*>(row + 16 * j);
-                const uint4 wu = *reinterpret_cast<const uint4*>(row + H / 2 + 16 * j);
-                const __half2 sg = __half2half2(scr[j >> 2]);
-                const __half2 su = __half2half2(scr[(H >> 7) + (j >> 2)]);
-                dot_word(wg.x, sg, &a.x[i][0], ag);
-                dot_word(wu.x, su, &a.x[i][0], au);
-                dot_word(wg.y, sg, &a.x[i][4], ag);
-                dot_word(wu.y, su, &a.x[i][4], au);
-                dot_word(wg.z, sg, &a.x[i][8], ag);
-                dot_word(wu.z, su, &a.x[i][8], au);
-                dot_word(wg.w, sg, &a.x[i][12], ag);
-                dot_word(wu.w, su, &a.x[i][12], au);
+        for (int b = 0; b < SB; ++b) {
+            const uint32_t wg = *reinterpret_cast<const uint32_t*>(row + 16 * b);
+            const uint32_t wu = *reinterpret_cast<const uint32_t*>(row + H / 2 + 16 * b);
+            const uint32_t blk = (slice + 32 * b) >> 7;
+            const __half2 sg = __half2half2(scr[blk]);
+            const __half2 su = __half2half2(scr[(H >> 7) + blk]);  // gate: H/128 halves, then up
+            __half2 qg[4], qu[4];
+            unpack8(wg, qg);
+            unpack8(wu, qu);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                qg[p] = __hmul2(qg[p], sg);  // == fp16(float(q) * float(s)), core.py:17
+                qu[p] = __hmul2(qu[p], su);
+            }
+            if constexpr (MMA) {
+                // rows 0-7: gate rows of the 8 neurons, rows 8-15: their up rows
+                float(&d)[4] = (b & 1) ? acc2 : acc;
+                mma16816(d, qg[0], qu[0], qg[1], qu[1], f.x[b][0], f.x[b][1]);
+                mma16816(d, qg[2], qu[2], qg[3], qu[3], f.x[b][2], f.x[b][3]);
+            } else {
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    acc[p & 1] = mfma(__low2half(qg[p]), __low2half(f.x[b][p]), acc[p & 1]);
+                    acc[p & 1] = mfma(__high2half(qg[p]), __high2half(f.x[b][p]), acc[p & 1]);
+                    acc[2 + (p & 1)] = mfma(__low2half(qu[p]), __low2half(f.x[b][p]), acc[2 + (p & 1)]);
+                    acc[2 + (p & 1)] = mfma(__high2half(qu[p]), __high2half(f.x[b][p]), acc[2 + (p & 1)]);
+                }
             }
         }
-        float g = (ag[0] + ag[1]) + (ag[2] + ag[3]);
-        float u = (au[0] + au[1]) + (au[2] + au[3]);
-        g = warp_sum(g);
-        u = warp_sum(u);
-        if (lane == 0) {
-            const float g16 = round16(g), u16 = round16(u);
-            const float s = round16(g16 / (1.f + expf(-g16)));
-            const __half h = __float2half_rn(s * u16);
-            const uint32_t n = pc.n0 + k;
-            P.hbuf[size_t(pc.row) * P.G + n] = __half_as_ushort(h);
-            if (L.act) L.act[size_t(pc.dest) * P.G + n] = __half_as_ushort(h);
-            red_release_gpu(dh, 1u);
+        float gs, us;
+        if constexpr (MMA) {
+            gs = acc[0] + acc2[0];  // D[g][0]: lane (g, 0)
+            us = acc[2] + acc2[2];  // D[g+8][0]
+        } else {
+            gs = acc[0] + acc[1];
+            us = acc[2] + acc[3];
+            gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+            us += __shfl_xor_sync(0xffffffffu, us, 1);
+            gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+            us += __shfl_xor_sync(0xffffffffu, us, 2);
         }
+        if (tq == 0 && k < pc.count) part[warp * kGateupMax + k] = make_float2(gs, us);
     }
+    // Last warp to finish this piece combines the slice sums.
+    __syncwarp();
+    __threadfence_block();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(&t->gcnt[s], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != uint32_t(kConsumerWarps) - 1) return;
+    __threadfence_block();
+    if (uint32_t(lane) < pc.count) {
+        float gsum = 0.f, usum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const float2 v = part[w * kGateupMax + lane];
+            gsum += v.x;
+            usum += v.y;
+        }
+        const float g16 = round16(gsum), u16 = round16(usum);
+        const float sl = round16(g16 / (1.f + expf(-g16)));
+        const uint16_t h = __half_as_ushort(__float2half_rn(sl * u16));
+        const uint32_t n = pc.n0 + lane;
+        st_relaxed_gpu_u64(P.hbuf + size_t(pc.row) * P.G + n, h_tag(P, pc.layer) | h);
+        if (L.act) L.act[size_t(pc.dest) * P.G + n] = h;
+    }
+    __syncwarp();
+    if (lane == 0) t->gcnt[s] = 0;
 }
 
 // DOWN piece: thread owns 8 columns (4 packed bytes) of the range.
@@ -752,7 +887,7 @@ __device__ void consume_down(const Piece& pc, const uint8_t* st, const __half* h
         for (int e = 0; e < 4; ++e) {
             wv[e] = *reinterpret_cast<const uint32_t*>(base + size_t(r + e) * pitch);
             s2[e] = __half2half2(sc[(r + e) * pc.nsb + sbi]);
-            hh[e] = hs[pc.n0 + r + e];
+            hh[e] = hs[r + e];
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -769,7 +904,7 @@ __device__ void consume_down(const Piece& pc, const uint8_t* st, const __half* h
     for (; r < pc.count; ++r) {
         const uint32_t wv = *reinterpret_cast<const uint32_t*>(base + size_t(r) * pitch);
         const __half2 s2 = __half2half2(sc[r * pc.nsb + sbi]);
-        const __half hh = hs[pc.n0 + r];
+        const __half hh = hs[r];
         __half2 q[4];
         unpack8(wv, q);
 #pragma unroll
@@ -799,17 +934,6 @@ __device__ bool warp_wait_count(const KernelParams& P, SmemTail* t, const uint32
         }
     }
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-// Per-warp staging of the h values of `row` (layer l): lane 0 waits until
-// all G neurons of the row published h, then the warp copies them into its
-// private shared-memory slice.
-__device__ bool stage_h_warp(const KernelParams& P, SmemTail* t, uint32_t l, uint32_t row, int lane, __half* hs,
-                             uint64_t deadline) {
-    if (!warp_wait_count(P, t, done_h(P, l) + row, P.G, deadline, 3, true, lane)) return false;
-    for (uint32_t n = lane; n < P.G; n += 32) hs[n] = __ushort_as_half(__ldcg(P.hbuf + size_t(row) * P.G + n));
-    __syncwarp();
-    return true;
 }
 
 // Compact reduction of one 32-column block (reduction.py:6-28,
@@ -868,16 +992,15 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
     if (lane == 0) t->xready = l + 1;
 }
 
-template <int MAXC>
+template <int SB, bool MMA>
 __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __half* hs = t->hs + warp * kMaxGroupSize;
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    Activation<MAXC> a;
+    Frag<SB> a;
     if (warp == 0) stage_x(P, *L, t, 0, lane);
     smem_wait(P, t, &t->xready, 1, deadline + kSyncGraceNs, 7, lane);
-    load_activation<MAXC>(P, *L, t->xs, a, lane);
+    load_activation<SB>(P, *L, t->xs, a, warp, lane);
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -907,26 +1030,25 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             break;
         }
         const Piece pc = t->piece[s];
+        if (tid == 0) trace_piece(P, idx, 2);
         if (idx == 0 && tid == 0) trace(P, LS_B200_TRACE_FIRST);
         if (tid == 0 && pc.kind == kPieceLayer) trace_layer(P, l, LS_B200_LTRACE_PIECES_DONE);
         if (pc.kind == kPieceFinal) {
             if (tid == 0) trace(P, LS_B200_TRACE_PIECES);
             break;
         }
-        const uint8_t* st = stages + size_t(s) * kStageBytes;
+        uint8_t* st = stages + size_t(s) * kStageBytes;
         const bool aborted = __shfl_sync(0xffffffffu, t->abort, 0) != 0;  // warp-uniform snapshot
         if (pc.kind == kPieceGateUp) {
-            if (!aborted) consume_gateup<MAXC>(P, *L, pc, st, a, warp, lane);
+            // every warp takes part (the last one resets the piece counter)
+            consume_gateup<SB, MMA>(P, *L, pc, st, t, s, a, warp, lane);
         } else if (pc.kind == kPieceDown) {
-            bool have_h = true;
             if (pc.flags & kFirstRows) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-                if (uint32_t(warp * 32) < 4 * pc.chunks && !aborted)
-                    have_h = stage_h_warp(P, t, l, pc.row, lane, hs, deadline);
             }
-            if (!aborted && have_h) {
-                consume_down(pc, st, hs, acc, tid);
+            if (!aborted) {
+                consume_down(pc, st, reinterpret_cast<const __half*>(st + kStageData + kAuxSecond), acc, tid);
                 if ((pc.flags & kLastRows) && uint32_t(tid) < 4 * pc.chunks) {
                     float* dst = P.partial + size_t(pc.row) * P.H + 32 * pc.k0 + 8 * tid;
                     reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -936,6 +1058,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             }
         }
         __syncwarp();
+        if (tid == 0) trace_piece(P, idx, 3);
         if (lane == 0) mbar_arrive(smem_u32(&t->empty_bar[s]));
         if (pc.kind != kPieceLayer) continue;
 
@@ -977,12 +1100,12 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         if (!smem_wait(P, t, &t->xready, l + 2, limit, 6, lane)) continue;
         ++l;
         L = next;
-        load_activation<MAXC>(P, *L, t->xs, a, lane);
+        load_activation<SB>(P, *L, t->xs, a, warp, lane);
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
     }
 }
 
-template <int MAXC>
+template <int SB, bool MMA>
 __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_constant__ KernelParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
@@ -992,8 +1115,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     if (tid == 0) {
         trace(P, LS_B200_TRACE_ENTRY);
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(smem_u32(&t->full_bar[s]), 33);                // producer lane 0 + 32 cp.async lanes
+            mbar_init(smem_u32(&t->full_bar[s]), 34);                // lane 0 expect_tx + 32 cp.async + lane 0 close
             mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps);  // one arrive per consumer warp
+            t->gcnt[s] = 0;
         }
         t->warps_done = 0;
         t->abort = 0;
@@ -1007,7 +1131,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     if (tid >= kConsumerThreads) {
         run_producer(P, stages, t, deadline);
     } else {
-        run_consumers<MAXC>(P, stages, t, deadline);
+        run_consumers<SB, MMA>(P, stages, t, deadline);
     }
     __syncthreads();
     if (tid == 0) {
@@ -1022,8 +1146,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
         __threadfence();
         const uint32_t nl = P.nlayers;
         for (uint32_t i = tid; i < kWsPerLayer * nl; i += blockDim.x) P.ws[kWsHeader + i] = 0;
-        for (uint32_t l = 0; l < nl; ++l)
-            for (uint32_t i = tid; i < P.N; i += blockDim.x) done_h(P, l)[i] = 0;
         __syncthreads();
         if (tid == 0) {
             const uint32_t err = P.ws[kWsErr];
@@ -1046,27 +1168,39 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     if (tid == 0) trace(P, LS_B200_TRACE_EXIT);
 }
 
-template <int MAXC>
+template <int SB, bool MMA>
 static int launch_t(const KernelParams& p, int grid, cudaStream_t stream) {
-    fused_mlp_kernel<MAXC><<<grid, kThreads, kernel_smem_bytes(), stream>>>(p);
+    fused_mlp_kernel<SB, MMA><<<grid, kThreads, kernel_smem_bytes(), stream>>>(p);
     return int(cudaGetLastError());
+}
+
+template <int SB, bool MMA>
+static cudaError_t raise_smem(int bytes) {
+    return cudaFuncSetAttribute(fused_mlp_kernel<SB, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int prepare_kernels() {
     const int bytes = int(kernel_smem_bytes());
-    cudaError_t e = cudaFuncSetAttribute(fused_mlp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(fused_mlp_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(fused_mlp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    return int(e);
+    const cudaError_t errs[] = {raise_smem<1, false>(bytes),  raise_smem<2, false>(bytes), raise_smem<4, false>(bytes),
+                                raise_smem<8, false>(bytes),  raise_smem<16, false>(bytes), raise_smem<1, true>(bytes),
+                                raise_smem<2, true>(bytes),   raise_smem<4, true>(bytes),  raise_smem<8, true>(bytes),
+                                raise_smem<16, true>(bytes)};
+    for (cudaError_t e : errs)
+        if (e != cudaSuccess) return int(e);
+    return 0;
 }
 
+// H = 256 * SB with SB in {1, 2, 4, 8, 16} (each warp owns H/8 coordinates).
 int launch_fused(const KernelParams& p, int grid, cudaStream_t stream) {
-    const uint32_t hc = p.H / 32;
-    if (hc <= 32) return launch_t<1>(p, grid, stream);
-    if (hc <= 64) return launch_t<2>(p, grid, stream);
-    return launch_t<4>(p, grid, stream);
+    const bool mma = p.variant != 0;
+    switch (p.H / 256) {
+        case 1: return mma ? launch_t<1, true>(p, grid, stream) : launch_t<1, false>(p, grid, stream);
+        case 2: return mma ? launch_t<2, true>(p, grid, stream) : launch_t<2, false>(p, grid, stream);
+        case 4: return mma ? launch_t<4, true>(p, grid, stream) : launch_t<4, false>(p, grid, stream);
+        case 8: return mma ? launch_t<8, true>(p, grid, stream) : launch_t<8, false>(p, grid, stream);
+        case 16: return mma ? launch_t<16, true>(p, grid, stream) : launch_t<16, false>(p, grid, stream);
+        default: return int(cudaErrorInvalidValue);
+    }
 }
 
 }  // namespace lsb

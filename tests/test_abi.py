@@ -65,13 +65,14 @@ def test_catalog_and_fallback(native_lib):
     from leanstream_b200 import _native as N
 
     lib = native_lib
-    assert lib.ls_b200_catalog_size() == 5
+    assert lib.ls_b200_catalog_size() == 6
     default = lib.ls_b200_default_candidate()
     assert default == 4
     c = N.KernelCandidate()
     for cid, ctas in enumerate([4, 8, 16, 32]):  # triton_backend.h:5-8 geometry kept
         assert lib.ls_b200_candidate(None, cid, C.byref(c)) == 0
-        assert c.id == cid and c.cta_count == ctas and c.workers == ctas and c.available
+        assert c.id == cid and c.cta_count == ctas and c.workers == ctas and c.available and c.entry_point == 1
+    assert lib.ls_b200_candidate(None, 5, C.byref(c)) == 0 and c.id == 5 and c.entry_point == 0
     assert lib.ls_b200_candidate(None, 99, C.byref(c)) == 0 and c.id == default
     assert lib.ls_b200_candidate(None, 255, C.byref(c)) == 0 and c.id == default
 
@@ -177,7 +178,8 @@ def test_geometry_validation_before_device_use(native_lib):
 
     lib = native_lib
     ctx = lib.ls_b200_create()
-    for h, g, n in [(0, 64, 8), (1000, 64, 8), (8448, 64, 8), (1024, 0, 8), (1024, 512, 8), (1024, 64, 0)]:
+    for h, g, n in [(0, 64, 8), (1000, 64, 8), (768, 64, 8), (8448, 64, 8), (1024, 0, 8), (1024, 512, 8),
+                    (1024, 64, 0)]:
         geo = N.Geometry(h, g, n, 0, 0, 0, 0, 0, 1e-5)
         assert lib.ls_b200_configure(ctx, C.byref(geo)) != 0
     lib.ls_b200_destroy(ctx)

@@ -61,12 +61,12 @@ def test_closed_form_modes_bit_exact(native_lib, cuda_device, count, q):
     assert np.array_equal(batch.view(np.uint16), auto.view(np.uint16))
 
 
-@pytest.mark.parametrize("candidate", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("candidate", [0, 1, 2, 3, 4, 5])
 def test_closed_form_every_candidate(native_lib, cuda_device, candidate):
     from leanstream_b200 import _native as N
 
     y = _closed_case(16, 1, N.MODE_PROGRESSIVE, candidate=candidate, shuffled=True)
-    ref = _closed_case(16, 1, N.MODE_BATCH_COMPAT, candidate=4)
+    ref = _closed_case(16, 1, N.MODE_BATCH_COMPAT, candidate=candidate)
     assert np.array_equal(y.view(np.uint16), ref.view(np.uint16))
 
 
@@ -123,16 +123,17 @@ def test_config1_parity_predictor_ids(native_lib, cuda_device):
     _seeded_parity(1024, 64, ids, 0)
 
 
-@pytest.mark.parametrize("candidate", [0, 3, 4])
+@pytest.mark.parametrize("candidate", [0, 3, 4, 5])
 def test_config1_parity_candidates_and_core(native_lib, cuda_device, candidate):
     ids = np.random.default_rng(7).permutation(64)[:20]
     _seeded_parity(1024, 64, ids, 3, candidate=candidate, core=4)
 
 
-def test_config2_parity(native_lib, cuda_device):
+@pytest.mark.parametrize("candidate", [4, 5])
+def test_config2_parity(native_lib, cuda_device, candidate):
     """Config 2: H 4096, 192 groups, 58 active (seeded ranking), all ready."""
     from leanstream_b200.synthetic import seeded_selection
 
     ids = seeded_selection(2, 192, 0.3)
     assert len(ids) == 58
-    _seeded_parity(4096, 192, ids, 2)
+    _seeded_parity(4096, 192, ids, 2, candidate=candidate)
