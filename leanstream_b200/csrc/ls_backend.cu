@@ -133,7 +133,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     b.geo = g;
     if (!b.geo.max_layers) b.geo.max_layers = 256;
     if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
-    const size_t partial_bytes = size_t(N) * H * sizeof(float);
+    const size_t partial_bytes = size_t(2) * N * H * sizeof(float);  // two row halves per descriptor
     const size_t h_bytes = size_t(N) * G * sizeof(unsigned long long);
     const size_t ws_bytes = size_t(ws_words(b.geo.max_layers, N)) * sizeof(uint32_t);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);

@@ -7,8 +7,10 @@
 
 namespace lsb {
 
-// CTA shape: eight consumer warps plus one TMA producer warp.
-constexpr int kConsumerWarps = 8;
+// CTA shape: sixteen consumer warps plus one TMA producer warp. Warps w and
+// w + 8 share hidden slice w % 8 (gate/up) and split the rows of a DOWN piece.
+constexpr int kConsumerWarps = 16;
+constexpr int kSlices = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 
@@ -18,10 +20,10 @@ constexpr int kThreads = kConsumerThreads + 32;
 // layer's per-SM share at config 2/3 -- so the producer can run a full
 // layer ahead of the consumers.
 constexpr int kStages = 6;
-constexpr int kStageData = 33 * 1024;
-constexpr int kStageAux = 3 * 1024;
+constexpr int kStageData = 33024;  // 8 rows of H = 4096 at a pitch of H + 16, plus slack
+constexpr int kStageAux = 36864 - kStageData;
 constexpr int kStageBytes = kStageData + kStageAux;
-constexpr int kAuxSecond = 2048;   // aux offset of DOWN h values / GATEUP partials
+constexpr int kAuxSecond = 1280;   // aux offset of DOWN h values / GATEUP partials
 constexpr int kGateupMax = 16;     // neurons per GATEUP piece
 constexpr int kMaxGroupSize = 256;
 constexpr int kMaxHidden = 4096;  // register-resident activation limit (4 chunks per lane)
@@ -66,7 +68,7 @@ struct KernelParams {
     uint32_t max_layers;  // workspace capacity
     uint32_t seq;         // launch sequence number (status word, h tags)
     uint32_t variant;     // 0: CUDA-core FMA gate/up, 1: tensor-core (mma.sync) gate/up
-    float* partial;       // [N][H] fp32, one row per descriptor position
+    float* partial;       // [2N][H] fp32, two rows (row halves) per descriptor position
     unsigned long long* hbuf;  // [N][G] tagged h words: (tag << 32) | fp16 h
     uint32_t* ws;         // workspace words
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)

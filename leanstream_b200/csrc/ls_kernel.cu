@@ -336,10 +336,8 @@ __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
         uint32_t ready = 0;
         if (pr.lane == 0) ready = mbar_try_wait(bar, parity) ? 1u : 0u;
         if (__shfl_sync(0xffffffffu, ready, 0)) return true;
-        if (pr.open_count) {
-            producer_try_close(pr, P, false);
-            continue;
-        }
+        if (pr.open_count && producer_try_close(pr, P, false)) continue;
+        __nanosleep(spins < 64 ? 64 : 256);  // back off: keep L2 free for the consumers
         uint32_t late = 0;
         if (pr.lane == 0 && (++spins & 255u) == 0 && gtimer() > pr.deadline + kProducerGraceNs) late = 1;
         if (__shfl_sync(0xffffffffu, late, 0)) {
@@ -724,13 +722,22 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
 }
 
 // ------------------------------------------------------------ consumer side
-// Register-resident activation fragments of one warp's hidden slice:
-// x[b][p] = (x[c + p], x[c + p + 4]), c = slice start + 32 b + 8 (lane & 3).
-// For the tensor-core path these are the B fragments (column 0) of
+// Register-resident activation fragments of one warp's share of the hidden
+// dimension: slice w % 8 (H/8 coordinates = SB 32-coordinate sub-blocks),
+// sub-blocks [half*SBH, half*SBH + SBH) with half = w / 8.
+// x[b][p] = (x[c + p], x[c + p + 4]), c = sub-block start + 8 (lane & 3):
+// for the tensor-core path these are the B fragments (column 0) of
 // m16n8k16 for logical k = (2t, 2t+1) and (2t+8, 2t+9).
-template <int SB>
+template <int SBH>
 struct Frag {
-    __half2 x[SB][4];
+    __half2 x[SBH][4];
+};
+
+template <int SB>
+struct Split {
+    static constexpr int SBH = SB > 1 ? SB / 2 : 1;
+    __device__ static int first(int warp) { return SB > 1 ? (warp / kSlices) * SBH : 0; }
+    __device__ static int count(int warp) { return SB > 1 ? SBH : (warp < kSlices ? 1 : 0); }
 };
 
 // Builds this warp's fragments from the CTA's staged activation, applying
@@ -739,8 +746,9 @@ struct Frag {
 // The sum runs per lane over 8-coordinate groups lane*8 + 256 i, then a
 // fixed butterfly: every warp of every CTA computes the same value.
 template <int SB>
-__device__ void load_activation(const KernelParams& P, const LayerPlan& L, const __half* xs, Frag<SB>& f, int warp,
-                                int lane) {
+__device__ void load_activation(const KernelParams& P, const LayerPlan& L, const __half* xs,
+                                Frag<Split<SB>::SBH>& f, int warp, int lane) {
+    constexpr int SBH = Split<SB>::SBH;
     const uint32_t H = P.H;
     const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
     float inv = 1.f;
@@ -758,10 +766,10 @@ __device__ void load_activation(const KernelParams& P, const LayerPlan& L, const
         }
         inv = rsqrtf(warp_sum(ss) / float(H) + P.eps);
     }
-    const uint32_t base = warp * (H / 8) + 8 * (lane & 3);
+    const uint32_t base = (warp % kSlices) * (H / 8) + 32 * Split<SB>::first(warp) + 8 * (lane & 3);
 #pragma unroll
-    for (int b = 0; b < SB; ++b) {
-        const uint32_t c = base + 32 * b;
+    for (int b = 0; b < SBH; ++b) {
+        const uint32_t c = (base + 32 * b) % H;  // in range even for an idle half (SB == 1)
         const uint4 w = *reinterpret_cast<const uint4*>(xs + c);
         const __half* h = reinterpret_cast<const __half*>(&w);
         __half v[8];
@@ -781,17 +789,20 @@ __device__ void load_activation(const KernelParams& P, const LayerPlan& L, const
     }
 }
 
-// GATEUP piece: this warp's hidden slice for every neuron of the piece, in
-// tiles of 8 neurons; the slice sums go to the stage's partial area and the
-// last warp to finish adds them in warp order, forms h and publishes it.
+// GATEUP piece: this warp's share of its hidden slice for every neuron of the
+// piece, in tiles of 8 neurons; the partial sums go to the stage's partial
+// area and the last warp to finish adds the 16 of them in warp order, forms h
+// and publishes it.
 template <int SB, bool MMA>
 __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, uint8_t* st, SmemTail* t,
-                               uint32_t s, const Frag<SB>& f, int warp, int lane) {
+                               uint32_t s, const Frag<Split<SB>::SBH>& f, int warp, int lane) {
+    constexpr int SBH = Split<SB>::SBH;
     const uint32_t H = P.H, pitch = H + 16;
     const int g = lane >> 2, tq = lane & 3;
-    const uint32_t slice = warp * (H / 8);  // first coordinate of this warp's slice
+    const int nsub = Split<SB>::count(warp);
+    const uint32_t slice = (warp % kSlices) * (H / 8) + 32 * Split<SB>::first(warp);  // first coordinate
     const __half* sc = reinterpret_cast<const __half*>(st + kStageData);
-    float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxSecond);  // [warp][kGateupMax]
+    float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxSecond);  // [warp][count]
     for (uint32_t r0 = 0; r0 < pc.count; r0 += 8) {
         const uint32_t k = r0 + g;  // neuron of the piece handled by this lane quad
         const uint8_t* row = st + size_t(k) * pitch + slice / 2 + 4 * tq;
@@ -799,7 +810,8 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // second tensor-core chain (odd sub-blocks)
 #pragma unroll
-        for (int b = 0; b < SB; ++b) {
+        for (int b = 0; b < SBH; ++b) {
+            if (b >= nsub) break;
             const uint32_t wg = *reinterpret_cast<const uint32_t*>(row + 16 * b);
             const uint32_t wu = *reinterpret_cast<const uint32_t*>(row + H / 2 + 16 * b);
             const uint32_t blk = (slice + 32 * b) >> 7;
@@ -840,9 +852,9 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
             gs += __shfl_xor_sync(0xffffffffu, gs, 2);
             us += __shfl_xor_sync(0xffffffffu, us, 2);
         }
-        if (tq == 0 && k < pc.count) part[warp * kGateupMax + k] = make_float2(gs, us);
+        if (tq == 0 && k < pc.count) part[warp * pc.count + k] = make_float2(gs, us);
     }
-    // Last warp to finish this piece combines the slice sums.
+    // Last warp to finish this piece combines the partial sums.
     __syncwarp();
     __threadfence_block();
     uint32_t old = 0;
@@ -854,7 +866,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
         float gsum = 0.f, usum = 0.f;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) {
-            const float2 v = part[w * kGateupMax + lane];
+            const float2 v = part[w * pc.count + lane];
             gsum += v.x;
             usum += v.y;
         }
@@ -869,17 +881,22 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
     if (lane == 0) t->gcnt[s] = 0;
 }
 
-// DOWN piece: thread owns 8 columns (4 packed bytes) of the range.
+// DOWN piece: thread owns 8 columns (4 packed bytes) of the range and one
+// half of the piece's rows (threads [0,256): first half, [256,512): second).
+__device__ __forceinline__ uint32_t down_half_split(uint32_t rows) { return (rows + 1) / 2; }
+
 __device__ void consume_down(const Piece& pc, const uint8_t* st, const __half* hs, float (&acc)[8], int tid) {
     const uint32_t pitch = 16 * pc.chunks;
-    const uint32_t ntask = 4 * pc.chunks;
-    if (uint32_t(tid) >= ntask) return;
+    const uint32_t task = uint32_t(tid) & 255u, half = uint32_t(tid) >> 8;
+    if (task >= 4 * pc.chunks) return;
+    const uint32_t split = down_half_split(pc.count);
+    const uint32_t rb = half ? split : 0, re = half ? pc.count : split;
     const __half* sc = reinterpret_cast<const __half*>(st + kStageData);
-    const uint32_t col = 32 * pc.k0 + 8 * tid;
+    const uint32_t col = 32 * pc.k0 + 8 * task;
     const uint32_t sbi = (col >> 7) - pc.sb0;
-    const uint8_t* base = st + 4 * tid;
-    uint32_t r = 0;
-    for (; r + 4 <= pc.count; r += 4) {
+    const uint8_t* base = st + 4 * task;
+    uint32_t r = rb;
+    for (; r + 4 <= re; r += 4) {
         uint32_t wv[4];
         __half2 s2[4];
         __half hh[4];
@@ -901,7 +918,7 @@ __device__ void consume_down(const Piece& pc, const uint8_t* st, const __half* h
             }
         }
     }
-    for (; r < pc.count; ++r) {
+    for (; r < re; ++r) {
         const uint32_t wv = *reinterpret_cast<const uint32_t*>(base + size_t(r) * pitch);
         const __half2 s2 = __half2half2(sc[r * pc.nsb + sbi]);
         const __half hh = hs[r];
@@ -937,22 +954,31 @@ __device__ bool warp_wait_count(const KernelParams& P, SmemTail* t, const uint32
 }
 
 // Compact reduction of one 32-column block (reduction.py:6-28,
-// streaming_mlp.cu:80-84): lane = column, partial rows summed in order;
-// then the layer epilogue (fp16 output, residual add, fp32 output).
+// streaming_mlp.cu:80-84): lane = column, the 2 partial rows (row halves) of
+// every descriptor summed in row order, loads issued 32 at a time; then the
+// layer epilogue (fp16 output, residual add, fp32 output).
 __device__ void reduce_block(const KernelParams& P, const LayerPlan& L, uint32_t blk, uint32_t rows, bool write,
                              int lane) {
     const uint32_t H = P.H, c = 32 * blk + lane;
     const float* p = P.partial + c;
+    const uint32_t n = 2 * rows;
     float s = 0.f;
     uint32_t r = 0;
-    for (; r + 8 <= rows; r += 8) {
+    for (; r + 32 <= n; r += 32) {
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __ldcg(p + size_t(r + e) * H);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s += v[e];
+    }
+    for (; r + 8 <= n; r += 8) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = __ldcg(p + size_t(r + e) * H);
 #pragma unroll
         for (int e = 0; e < 8; ++e) s += v[e];
     }
-    for (; r < rows; ++r) s += __ldcg(p + size_t(r) * H);
+    for (; r < n; ++r) s += __ldcg(p + size_t(r) * H);
     if (!write) return;
     if (L.y32) L.y32[c] = s;
     const __half y16 = __float2half_rn(s);
@@ -997,7 +1023,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    Frag<SB> a;
+    Frag<Split<SB>::SBH> a;
     if (warp == 0) stage_x(P, *L, t, 0, lane);
     smem_wait(P, t, &t->xready, 1, deadline + kSyncGraceNs, 7, lane);
     load_activation<SB>(P, *L, t->xs, a, warp, lane);
@@ -1049,8 +1075,9 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             }
             if (!aborted) {
                 consume_down(pc, st, reinterpret_cast<const __half*>(st + kStageData + kAuxSecond), acc, tid);
-                if ((pc.flags & kLastRows) && uint32_t(tid) < 4 * pc.chunks) {
-                    float* dst = P.partial + size_t(pc.row) * P.H + 32 * pc.k0 + 8 * tid;
+                if ((pc.flags & kLastRows) && (uint32_t(tid) & 255u) < 4 * pc.chunks) {
+                    float* dst = P.partial + (size_t(pc.row) * 2 + (uint32_t(tid) >> 8)) * P.H + 32 * pc.k0 +
+                                 8 * (uint32_t(tid) & 255u);
                     reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
                     reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
                 }
