@@ -33,15 +33,16 @@ namespace {
 // include/leanstream/triton_backend.h:5-8 (4/8/16/32 persistent CTAs), so an
 // offline LUT written for it keeps its meaning. Id 4 is the B200 entry: one
 // persistent CTA per SM (resolved at configure), the fallback. entry_point
-// selects the gate/up inner product: 1 = tensor-core mma.sync, 0 = CUDA-core
-// fp16xfp16->fp32 fma (id 5, same grid as id 4).
+// selects the arithmetic variant: 1 = fp16 scales applied per 128-block
+// around the tensor-core sums, 0 = weights rounded to fp16(q * s) first as
+// backends/triton/core.py:17 does (id 5, same grid as id 4).
 constexpr ls_kernel_candidate kCatalog[] = {
     {0, 4, "b200_ctas_4", 4, 0, 0, 0, 1, true},
     {1, 8, "b200_ctas_8", 8, 0, 0, 0, 1, true},
     {2, 16, "b200_ctas_16", 16, 0, 0, 0, 1, true},
     {3, 32, "b200_ctas_32", 32, 0, 0, 0, 1, true},
     {4, 0, "b200_ctas_per_sm", 0, 0, 0, 0, 1, true},
-    {5, 0, "b200_ctas_per_sm_fma", 0, 0, 0, 0, 0, true},
+    {5, 0, "b200_ctas_per_sm_exact", 0, 0, 0, 0, 0, true},
 };
 constexpr uint32_t kCatalogSize = sizeof(kCatalog) / sizeof(kCatalog[0]);
 constexpr uint32_t kDefaultCandidate = 4;
@@ -66,7 +67,6 @@ struct Backend {
     bool bound_set = false;
     // scratch (device) and mapped words (host)
     float* partial = nullptr;
-    unsigned long long* hbuf = nullptr;
     uint32_t* ws = nullptr;
     uint32_t seq = 0;
     uint32_t* status_host = nullptr;
@@ -96,13 +96,11 @@ struct Backend {
     }
     void release() {
         if (partial) cudaFree(partial);
-        if (hbuf) cudaFree(hbuf);
         if (ws) cudaFree(ws);
         if (status_host) cudaFreeHost(status_host);
         if (done_host) cudaFreeHost(done_host);
         delete[] last_epoch;
         partial = nullptr;
-        hbuf = nullptr;
         ws = nullptr;
         status_host = status_dev = nullptr;
         done_host = done_dev = nullptr;
@@ -117,7 +115,7 @@ int cuda_rc(cudaError_t e) { return e == cudaSuccess ? 0 : (int(e) > 0 ? int(e) 
 int configure(Backend& b, const ls_b200_geometry& g) {
     if (b.configured) return EBUSY;
     const uint32_t H = g.hidden, G = g.group_size, N = g.group_count;
-    // H = 256 * {1, 2, 4, 8, 16}: each consumer warp owns H/8 coordinates
+    // H = 256 * {1, 2, 4, 8, 16}: the kernel is instantiated per hidden size
     const uint32_t sb = H / 256;
     if (!H || H % 256 || (sb & (sb - 1)) || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N)
         return EINVAL;
@@ -133,15 +131,13 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     b.geo = g;
     if (!b.geo.max_layers) b.geo.max_layers = 256;
     if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
-    const size_t partial_bytes = size_t(2) * N * H * sizeof(float);  // two row halves per descriptor
-    const size_t h_bytes = size_t(N) * G * sizeof(unsigned long long);
-    const size_t ws_bytes = size_t(ws_words(b.geo.max_layers, N)) * sizeof(uint32_t);
+    // one fp32 partial output row per slab of every descriptor row
+    const size_t partial_bytes = size_t(N) * slabs_per_group(G) * H * sizeof(float);
+    const size_t ws_bytes = size_t(ws_words(b.geo.max_layers)) * sizeof(uint32_t);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&b.hbuf, h_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
-    if (e == cudaSuccess) e = cudaMemset(b.hbuf, 0, h_bytes);  // tag 0 is never a valid tag
     if (e == cudaSuccess) e = cudaHostAlloc(&b.status_host, 64, cudaHostAllocMapped);
     if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b.status_dev), b.status_host, 0);
     if (e == cudaSuccess)
@@ -159,7 +155,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
         b.release();
         return ENOMEM;
     }
-    b.scratch_bytes = partial_bytes + h_bytes + ws_bytes;
+    b.scratch_bytes = partial_bytes + ws_bytes;
     b.configured = true;
     return 0;
 }
@@ -223,7 +219,6 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace) {
     p.max_layers = b.geo.max_layers;
     p.seq = ++b.seq;
     p.partial = b.partial;
-    p.hbuf = b.hbuf;
     p.ws = b.ws;
     p.status = b.status_dev;
     p.done = b.done_dev;
@@ -528,6 +523,6 @@ int ls_b200_queue_fail(ls_b200_queue* q, uint32_t error) {
     return 0;
 }
 
-const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-mlp v3 (tagged h, split-K gate/up)"; }
+const char* ls_b200_build_info(void) { return "leanstream_b200 sm_100a fused-mlp v4 (CTA-local slabs, tensor-core gate/up and down)"; }
 
 }  // extern "C"

@@ -7,26 +7,27 @@
 
 namespace lsb {
 
-// CTA shape: sixteen consumer warps plus one TMA producer warp. Warps w and
-// w + 8 share hidden slice w % 8 (gate/up) and split the rows of a DOWN piece.
+// CTA shape: sixteen consumer warps plus one TMA producer warp, one CTA per SM.
 constexpr int kConsumerWarps = 16;
-constexpr int kSlices = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 
-// Shared-memory ring: each stage holds up to 33 KB of packed INT4 rows and a
-// 3 KB auxiliary area (fp16 scales, staged h values, cross-warp partials).
-// Six stages keep ~200 KB of HBM reads in flight per SM -- more than one
-// layer's per-SM share at config 2/3 -- so the producer can run a full
-// layer ahead of the consumers.
+// Work unit: a slab of up to 16 consecutive neurons of one descriptor. One
+// CTA computes a slab's gate/up rows, its h values and its down rows, and
+// writes the slab's fp32 partial output row; h never leaves the CTA.
+constexpr uint32_t kSlab = 16;
+
+// Shared-memory ring: a stage holds either the gate+up records of 8 neurons
+// (pitch H + 16 bytes) or the down rows of one slab (pitch H/2 + 16 bytes),
+// plus an auxiliary area with the stage's fp16 scales (<= 1 KB) and the
+// GATEUP warp partials (1 KB). Six stages = two slabs of H = 4096 in flight.
 constexpr int kStages = 6;
-constexpr int kStageData = 33024;  // 8 rows of H = 4096 at a pitch of H + 16, plus slack
-constexpr int kStageAux = 36864 - kStageData;
+constexpr int kStageData = 33024;  // 16 x (2048 + 16) = 8 x (4096 + 16) + 128
+constexpr int kStageAux = 2048;
+constexpr int kAuxPartials = 1024;  // aux offset of the GATEUP warp partials
 constexpr int kStageBytes = kStageData + kStageAux;
-constexpr int kAuxSecond = 1280;   // aux offset of DOWN h values / GATEUP partials
-constexpr int kGateupMax = 16;     // neurons per GATEUP piece
 constexpr int kMaxGroupSize = 256;
-constexpr int kMaxHidden = 4096;  // register-resident activation limit (4 chunks per lane)
+constexpr int kMaxHidden = 4096;
 
 // One MLP layer of a launch (POD, copied into kernel parameters or read from
 // a device array for multi-layer launches).
@@ -52,10 +53,11 @@ struct alignas(16) LayerPlan {
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
-constexpr uint32_t kWsPerLayer = 4;  // path, claim, partials-done CTAs, reduced column blocks
-__host__ __device__ inline uint32_t ws_words(uint32_t max_layers, uint32_t) {
-    return kWsHeader + kWsPerLayer * max_layers;
-}
+constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, partial-rows-done CTAs, reduced column blocks
+__host__ __device__ inline uint32_t ws_words(uint32_t max_layers) { return kWsHeader + kWsPerLayer * max_layers; }
+
+// Slabs per group and partial rows of the scratch buffer.
+__host__ __device__ inline uint32_t slabs_per_group(uint32_t G) { return (G + kSlab - 1) / kSlab; }
 
 // Everything one launch needs, passed by value.
 struct KernelParams {
@@ -66,14 +68,13 @@ struct KernelParams {
     float eps;
     uint32_t nlayers;     // layers executed by this launch
     uint32_t max_layers;  // workspace capacity
-    uint32_t seq;         // launch sequence number (status word, h tags)
-    uint32_t variant;     // 0: CUDA-core FMA gate/up, 1: tensor-core (mma.sync) gate/up
-    float* partial;       // [2N][H] fp32, two rows (row halves) per descriptor position
-    unsigned long long* hbuf;  // [N][G] tagged h words: (tag << 32) | fp16 h
+    uint32_t seq;         // launch sequence number (status word)
+    uint32_t variant;     // 1: scales applied per 128-block after the tensor-core sums; 0: fp16(q*s) weights
+    float* partial;       // [N * slabs_per_group(G)][H] fp32 slab partial rows
     uint32_t* ws;         // workspace words
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
     uint32_t* done;       // mapped host per-layer completion epochs
-    uint64_t* trace;      // optional [grid][LS_B200_TRACE_WORDS]
+    uint64_t* trace;      // optional phase stamps
     const LayerPlan* plans;  // device array for nlayers > 1, else nullptr
     LayerPlan first;         // layer 0 when plans == nullptr
 };

@@ -7,47 +7,51 @@
 // residual + RMSNorm glue (reduction.py:17-20;
 // examples/ministral/native/predictor_shared_input.cu:16-33).
 //
-// CTA = 8 consumer warps + 1 producer warp, one CTA per SM. The producer
-// streams packed INT4 rows into a 6-stage shared-memory ring with
-// cp.async.bulk (TMA bulk copies, no multicast) and fp16 scales with
-// cp.async, completing one mbarrier per stage. It runs ahead across layer
-// boundaries: weights do not depend on activations, so the next layer's
-// rows are in flight while consumers synchronise on the current one.
+// CTA = 16 consumer warps + 1 producer warp, one CTA per SM.
 //
-// Work is described by "pieces" the producer writes next to each stage:
-//   GATEUP: gate+up rows of up to 32 neurons -> h = fp16(fp16(SiLU(g)) * u)
-//   DOWN:   rows x column range of one descriptor's down matrix -> fp32
-//           partial row segment (one partial row per descriptor position)
-//   LAYER:  end of a layer; carries the partial-row count
-//   FINAL:  end of the launch
-// Schedules:
-//   fast path (all queue descriptors ready at decision time; BatchCompat):
-//     static, balanced split of all neurons (GATEUP) and of all
-//     (descriptor, 32-column chunk) pairs (DOWN) over the grid; a DOWN piece
-//     waits on a per-descriptor counter of published h values.
-//   progressive path: CTAs claim descriptor positions in ready order from a
-//     device-memory counter (core descriptors first) and run all pieces of
-//     each claimed descriptor.
-// Canonical arithmetic, shared by both schedules (so BatchCompat and
-// Progressive outputs are bit-identical, tests/persistent_mlp_test.cu:65):
-//   g, u : the hidden dimension is split into 8 fixed slices, one per
-//          consumer warp; each warp reduces its slice for 8 neurons at a time
-//          (tensor-core mma.sync m16n8k16 with the 8 gate rows and 8 up rows
-//          as A and x as column 0 of B, or CUDA-core fp16xfp16->fp32 fmas with
-//          the same data mapping), and the 8 slice sums are added in warp
-//          order by the last warp to finish the piece;
-//   down : per column, one fp32 chain over the descriptor's neurons in order;
-//   y    : per column, partial rows summed in row order.
-// h travels between CTAs as 64-bit words (launch/layer tag << 32 | fp16 h):
-// the tag makes a single relaxed store self-validating, so publishing h
-// needs no fence or counter. The producer warp polls those words and copies
-// h into the DOWN piece's stage, off the consumers' critical path.
-// Rounding boundaries (core.py:17,49-52; reduction.py:15): w = fp16(q*s),
-// g,u -> fp16, SiLU -> fp16, h -> fp16, fp32 partials, y -> fp16 once.
+// Work unit: a slab = up to 16 consecutive neurons of one descriptor (group).
+// The CTA that owns a slab computes its gate/up rows, its h values and its
+// down rows, and writes one fp32 partial output row for it, so h never
+// crosses CTAs. Slabs are split statically over the grid when the whole
+// plan is ready at decision time (fast path, BatchCompat / Auto), or claimed
+// in ready order from a device counter (progressive path).
 //
-// Synchronisation uses counters and tagged words with bounded waits only --
-// no named barriers inside loops -- so a warp that gives up can never strand
-// the others. Every wait ends at a %globaltimer deadline and records an error.
+// Producer warp: streams each slab into a 6-stage shared-memory ring as
+// three pieces -- GATEUP (gate+up records of 8 neurons, one cp.async.bulk
+// per neuron, pitch H+16), GATEUP (the next 8) and DOWN (the slab's down
+// rows, pitch H/2+16) -- plus their fp16 scales (cp.async), completing one
+// mbarrier per stage. Weights do not depend on activations, so the producer
+// runs ahead across layer boundaries while the consumers synchronise.
+//
+// Consumers (tensor cores, mma.sync m16n8k16, fp32 accumulation):
+//   GATEUP: A = 8 gate rows + 8 up rows of the piece's neurons, B = x; the
+//           hidden dimension is split over the warps; the last warp to
+//           finish sums the warp partials in warp order and forms
+//           h = fp16(fp16(SiLU(fp16 g)) * fp16 u).
+//   DOWN:   A = down weights with neurons along K (nibbles of two neurons
+//           interleaved with PRMT), B = h; one 16-neuron MMA per 16 columns.
+//   Two arithmetic variants (identical data flow):
+//     variant 1 (default): nibbles become exact fp16 subnormals
+//       (q + 8) * 2^-24 with one LOP3 per pair; the per-128 fp16 scale is
+//       applied once per block after the tensor-core sum (gate/up) or folded
+//       into B as h * s, carried as an fp16 value plus its fp16 residual
+//       (down), and the +8 offset is removed with the block sum of B.
+//       Products and sums are fp32, so outputs stay within the fp32-reference
+//       tolerance, but w is never rounded to fp16.
+//     variant 0: w = fp16(q * s) exactly as backends/triton/core.py:17
+//       before the MMA; B = x or h.
+//   Canonical arithmetic (identical for both schedules, so BatchCompat and
+//   Progressive outputs are bit-identical, tests/persistent_mlp_test.cu:65):
+//   a slab's h and partial row depend only on the slab; y sums the partial
+//   rows (row = descriptor row * slabs-per-group + slab) in a fixed tree of
+//   16-row chunks.
+// End of layer: every CTA counts itself done; CTAs 0..H/32-1 reduce one
+// 32-column block each and apply the epilogue (fp16 output, fp32 output,
+// residual add); then every CTA loads the next layer's input (RMSNorm).
+//
+// Every wait is bounded by a %globaltimer deadline and records an error;
+// consumer warps synchronise through an mbarrier with bounded waits (never
+// bar.sync), so a warp that gives up cannot strand the others.
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include "ls_internal.h"
@@ -55,7 +59,7 @@
 namespace lsb {
 
 enum : uint32_t { kPieceFinal = 0, kPieceGateUp = 1, kPieceDown = 2, kPieceLayer = 3 };
-enum : uint32_t { kFirstRows = 1u, kLastRows = 2u, kCompletes = 4u, kLayerGood = 8u };
+enum : uint32_t { kCompletes = 4u, kLayerGood = 8u };
 constexpr uint32_t kPathFast = 1, kPathProgressive = 2, kPathAbort = 3;
 
 // Wait bounds, ordered so that a stalled launch always drains its ring:
@@ -68,17 +72,14 @@ constexpr uint64_t kSyncGraceNs = 3000000000ull;
 
 struct Piece {
     uint32_t kind;
-    uint32_t row;     // partial row = descriptor position (core first, then queue index)
-    uint32_t dest;    // descriptor dest_slot (activation / counter index)
-    uint32_t n0;      // GATEUP: first neuron; DOWN: first row of the down matrix
-    uint32_t count;   // GATEUP: neurons; DOWN: rows; LAYER: partial rows of the layer
-    uint32_t k0;      // DOWN: first 16-byte chunk (32 columns)
-    uint32_t chunks;  // DOWN: 16-byte chunks per row
-    uint32_t sb0;     // DOWN: first scale index (even) of the column range
-    uint32_t nsb;     // DOWN: scale halves per row (even)
+    uint32_t row;    // DOWN: partial row (descriptor row * slabs per group + slab)
+    uint32_t dest;   // descriptor dest_slot (activation / counter index)
+    uint32_t n0;     // first neuron of the piece within the group
+    uint32_t count;  // neurons; LAYER: partial rows of the layer
+    uint32_t need;   // DOWN: GATEUP pieces that must be finalised first
     uint32_t flags;
-    uint32_t layer;   // launch-local layer index
-    uint32_t pad[5];
+    uint32_t layer;  // launch-local layer index
+    uint32_t pad[8];
 };
 static_assert(sizeof(Piece) == 64, "piece record");
 
@@ -90,16 +91,19 @@ struct DescView {
 struct SmemTail {
     unsigned long long full_bar[kStages];
     unsigned long long empty_bar[kStages];
+    unsigned long long cbar;  // consumer-warp barrier (16 arrivals per phase)
     Piece piece[kStages];
-    DescView dtab[32];  // producer's descriptor window
-    uint32_t gcnt[kStages];  // warps done with a GATEUP piece (per stage)
-    alignas(16) __half xs[kMaxHidden];  // activation of the current layer, staged once per CTA
-    uint32_t warps_done;     // consumer warps that finished a layer (monotonic)
+    DescView dtab[32];        // producer's descriptor window
+    uint32_t gcnt[kStages];   // warps done with a GATEUP piece (per stage)
+    alignas(16) uint4 xf[kMaxHidden / 8];  // activation in B-fragment order, 8 coordinates per entry
+    float xs32[kMaxHidden / 32];           // fp32 sum of each 32-coordinate sub-block of x
+    float red[kConsumerWarps];             // RMSNorm warp sums
+    float red2[kConsumerWarps][32];        // reduction warp sums
+    __half hs[kSlab];                      // h of the slab being computed
+    volatile uint32_t octets_done;         // GATEUP pieces finalised (monotonic)
     volatile uint32_t abort;
-    volatile uint32_t xready;     // layers whose activation is staged in xs
-    volatile uint32_t partials;   // layers whose partial rows are complete grid-wide
+    volatile uint32_t flag;                // CTA-uniform decision broadcast by thread 0
     uint32_t last;
-    uint32_t pad[3];
 };
 
 size_t kernel_smem_bytes() { return size_t(kStages) * kStageBytes + sizeof(SmemTail); }
@@ -132,14 +136,6 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -180,8 +176,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+template <int BYTES>
+__device__ __forceinline__ void cp_async(uint32_t dst, const void* src) {
+    if constexpr (BYTES == 16) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    } else if constexpr (BYTES == 8) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+    } else {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+    }
 }
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
@@ -190,45 +193,36 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// Mixed-precision fma: d = a*b + c with fp16 a, b (exact product) and fp32 c.
-__device__ __forceinline__ float mfma(__half a, __half b, float c) {
-    float d;
-    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
-    return d;
-}
 // Tensor-core step: D(16x8,f32) += A(16x16,f16) * B(16x8,f16).
-__device__ __forceinline__ void mma16816(float (&d)[4], __half2 a0, __half2 a1, __half2 a2, __half2 a3, __half2 b0,
-                                         __half2 b1) {
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(*reinterpret_cast<uint32_t*>(&a0)), "r"(*reinterpret_cast<uint32_t*>(&a1)),
-          "r"(*reinterpret_cast<uint32_t*>(&a2)), "r"(*reinterpret_cast<uint32_t*>(&a3)),
-          "r"(*reinterpret_cast<uint32_t*>(&b0)), "r"(*reinterpret_cast<uint32_t*>(&b1)));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ __half2 as_h2(uint32_t v) {
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) {
     __half2 h;
     *reinterpret_cast<uint32_t*>(&h) = v;
     return h;
 }
 
-// Eight signed two's-complement nibbles (low nibble = even coordinate,
-// backends/triton/core.py:14-15) -> four half2 of exact integers:
-// q[p] = (coord p, coord p+4), p = 0..3.
-__device__ __forceinline__ void unpack8(uint32_t w, __half2 (&q)[4]) {
-    const uint32_t lo = (w & 0x000F000Fu) ^ 0x64086408u;  // 1024 + (q + 8)
-    const uint32_t hi = (w & 0x00F000F0u) ^ 0x64806480u;  // 1024 + 16 (q + 8)
-    const uint32_t w8 = w >> 8;
-    const uint32_t lo2 = (w8 & 0x000F000Fu) ^ 0x64086408u;
-    const uint32_t hi2 = (w8 & 0x00F000F0u) ^ 0x64806480u;
-    const __half2 k1032 = __float2half2_rn(1032.f);
-    const __half2 k16 = __float2half2_rn(0.0625f);
-    const __half2 k72 = __float2half2_rn(-72.f);
-    q[0] = __hsub2(as_h2(lo), k1032);
-    q[1] = __hfma2(as_h2(hi), k16, k72);
-    q[2] = __hsub2(as_h2(lo2), k1032);
-    q[3] = __hfma2(as_h2(hi2), k16, k72);
+// ---- nibble decoding. A 32-bit word holds two 16-bit halves; mask m selects
+// one signed two's-complement nibble per half (low nibble = even coordinate,
+// backends/triton/core.py:14-15).
+// Subnormal form: (q + 8) * 2^-24 (low nibble) or 16 (q + 8) * 2^-24 (high
+// nibble), exact fp16 values built by one LOP3.
+__device__ __forceinline__ uint32_t sub_lo(uint32_t w) { return (w & 0x000F000Fu) ^ 0x00080008u; }
+__device__ __forceinline__ uint32_t sub_hi(uint32_t w) { return (w & 0x00F000F0u) ^ 0x00800080u; }
+// Exact-integer form: q as fp16.
+__device__ __forceinline__ __half2 int_lo(uint32_t w) {
+    return __hsub2(bits_h2((w & 0x000F000Fu) ^ 0x64086408u), __float2half2_rn(1032.f));  // 1024 + (q + 8)
+}
+__device__ __forceinline__ __half2 int_hi(uint32_t w) {
+    return __hfma2(bits_h2((w & 0x00F000F0u) ^ 0x64806480u), __float2half2_rn(0.0625f),
+                   __float2half2_rn(-72.f));  // (1024 + 16 (q + 8)) / 16 - 72
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -240,11 +234,7 @@ __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
-    return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] claim [2] partials-done CTAs [3] reduced blocks
-}
-// Tag of h words written by layer l of this launch (never 0: seq >= 1).
-__device__ __forceinline__ unsigned long long h_tag(const KernelParams& P, uint32_t l) {
-    return (static_cast<unsigned long long>((P.seq << 8) | (l & 0xffu))) << 32;
+    return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] claim [2] partial-rows-done CTAs [3] reduced blocks
 }
 __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
     if (P.trace) P.trace[size_t(blockIdx.x) * LS_B200_TRACE_WORDS + word] = gtimer();
@@ -275,7 +265,7 @@ __device__ __forceinline__ const LayerPlan& plan_at(const KernelParams& P, uint3
 // ------------------------------------------------------------ descriptors
 // Descriptor at canonical position d: core[d] for d < core_count, else the
 // queue descriptor published at ready position d - core_count
-// (streaming_mlp.cu:60, persistent.py:80). Partial row: d for core, else
+// (streaming_mlp.cu:60, persistent.py:80). Descriptor row: d for core, else
 // core_count + descriptor index (custom_triton.md:54).
 __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_t d) {
     const uint32_t* c;
@@ -303,30 +293,18 @@ __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_
 }
 
 // ------------------------------------------------------------ producer side
-// A DOWN stage whose rows are in flight but whose h values are not yet
-// staged: the producer keeps issuing later pieces and closes it once the
-// tagged h words of its rows appear.
-struct OpenStage {
-    uint32_t stage, hrow, rows, layer;  // hrow: first tagged word (partial row * G + r0)
-    uint32_t piece;                     // piece index (trace)
-};
-
 struct Producer {
-    uint32_t idx;   // pieces issued so far (stage = idx % kStages)
+    uint32_t idx;     // pieces issued so far (stage = idx % kStages)
+    uint32_t octets;  // GATEUP pieces issued so far
     uint32_t lane;
     uint8_t* stages;
     SmemTail* t;
     uint64_t deadline;
     uint32_t wbase;  // first descriptor position held in t->dtab
     uint32_t wlayer;
-    OpenStage open[kStages];
-    uint32_t open_head, open_count;
 };
 
-__device__ bool producer_try_close(Producer& pr, const KernelParams& P, bool blocking);
-
-// Waits until the next stage is free, closing open DOWN stages meanwhile
-// (one of them may be the stage being waited for).
+// Waits until the next stage is free.
 __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
     const uint32_t s = pr.idx % kStages;
     const uint32_t parity = ((pr.idx / kStages) & 1u) ^ 1u;
@@ -336,8 +314,7 @@ __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
         uint32_t ready = 0;
         if (pr.lane == 0) ready = mbar_try_wait(bar, parity) ? 1u : 0u;
         if (__shfl_sync(0xffffffffu, ready, 0)) return true;
-        if (pr.open_count && producer_try_close(pr, P, false)) continue;
-        __nanosleep(spins < 64 ? 64 : 256);  // back off: keep L2 free for the consumers
+        __nanosleep(spins < 64 ? 32 : 256);  // back off: keep issue slots free for the consumers
         uint32_t late = 0;
         if (pr.lane == 0 && (++spins & 255u) == 0 && gtimer() > pr.deadline + kProducerGraceNs) late = 1;
         if (__shfl_sync(0xffffffffu, late, 0)) {
@@ -347,54 +324,17 @@ __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
     }
 }
 
-// Completes a stage: 32 cp.async arrivals (one per lane, when its scale /
-// h copies land) plus one release arrival by lane 0 after the warp's
-// shared-memory writes. The full barrier expects 34 arrivals in total.
-__device__ __forceinline__ void producer_close(Producer& pr, uint32_t s) {
+// Completes a stage: 32 cp.async arrivals (one per lane, when its scale
+// copies land) plus one arrival by lane 0 after the piece record is written.
+// With lane 0's expect_tx arrival the full barrier expects 34 in total.
+__device__ __forceinline__ void producer_close(Producer& pr, const KernelParams& P, uint32_t s) {
     const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
     cp_async_arrive_noinc(bar);
     __syncwarp();
-    if (pr.lane == 0) mbar_arrive(bar);
-}
-__device__ __forceinline__ void producer_stamp(const KernelParams& P, const Producer& pr, uint32_t piece,
-                                               uint32_t word) {
-    if (pr.lane == 0) trace_piece(P, piece, word);
-}
-
-// Tries to close the oldest open DOWN stage: polls the tagged h words of its
-// rows once (or until they appear / the deadline passes, when blocking).
-__device__ bool producer_try_close(Producer& pr, const KernelParams& P, bool blocking) {
-    if (!pr.open_count) return true;
-    const OpenStage o = pr.open[pr.open_head];
-    const unsigned long long tag = h_tag(P, o.layer);
-    uint32_t hv = 0, spins = 0;
-    bool ok_all = false;
-    for (;;) {
-        uint32_t ok = 1;
-        if (pr.lane < o.rows) {
-            const unsigned long long w = ld_relaxed_gpu_u64(P.hbuf + o.hrow + pr.lane);
-            ok = (w & 0xffffffff00000000ull) == tag;
-            hv = uint32_t(w) & 0xffffu;
-        }
-        if (__all_sync(0xffffffffu, ok)) { ok_all = true; break; }
-        if (!blocking) return false;
-        uint32_t late = 0;
-        if (pr.lane == 0 && (++spins & 63u) == 0 && (pr.t->abort || gtimer() > pr.deadline)) late = 1;
-        if (__shfl_sync(0xffffffffu, late, 0)) break;
-        __nanosleep(32);
+    if (pr.lane == 0) {
+        mbar_arrive(bar);
+        trace_piece(P, pr.idx, 1);
     }
-    if (!ok_all && pr.lane == 0 && !pr.t->abort) raise_error(P, pr.t, LS_B200_DEV_TIMEOUT_SYNC, 3);
-    uint8_t* st = pr.stages + size_t(o.stage) * kStageBytes;
-    if (pr.lane < o.rows) reinterpret_cast<uint16_t*>(st + kStageData + kAuxSecond)[pr.lane] = uint16_t(hv);
-    producer_close(pr, o.stage);
-    producer_stamp(P, pr, o.piece, 1);
-    pr.open_head = (pr.open_head + 1) % kStages;
-    --pr.open_count;
-    return ok_all;
-}
-
-__device__ void producer_flush(Producer& pr, const KernelParams& P) {
-    while (pr.open_count) producer_try_close(pr, P, true);
 }
 
 // A data-less piece (LAYER or FINAL marker).
@@ -408,153 +348,113 @@ __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t ki
         pc.layer = layer;
         pc.count = rows;
         pc.flags = flags;
+        trace_piece(P, pr.idx, 0);
         mbar_arrive_expect_tx(smem_u32(&pr.t->full_bar[s]), 0);
     }
-    producer_stamp(P, pr, pr.idx, 0);
-    producer_close(pr, s);
-    producer_stamp(P, pr, pr.idx, 1);
+    producer_close(pr, P, s);
     ++pr.idx;
     return true;
 }
 
-// GATEUP piece: neurons [n0, n0+count) of one descriptor.
+// Scale copy granule: 16 bytes when every scale row and segment is 16-byte
+// aligned (H >= 1024: row pitch 3H/64 bytes), else the segment size.
+template <int H>
+struct ScaleCopy {
+    static constexpr int kUnit = H >= 1024 ? 16 : H / 64;
+    static constexpr uint32_t kRow = 3 * H / 64;   // bytes of one neuron's scales
+    static constexpr uint32_t kGateUp = H / 32;    // gate + up scale bytes of one neuron
+    static constexpr uint32_t kDown = H / 64;      // down scale bytes of one neuron
+};
+
+// GATEUP piece: gate+up records of neurons [n0, n0+cnt) (cnt <= 8).
+template <int H>
 __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                                uint32_t layer, uint32_t n0, uint32_t count) {
+                                uint32_t layer, uint32_t n0, uint32_t cnt) {
     if (!producer_acquire_stage(pr, P)) return false;
     const uint32_t s = pr.idx % kStages;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
     const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
-    const uint32_t H = P.H;
-    const uint64_t rec = uint64_t(3) * H / 2;  // bytes per neuron record
+    constexpr uint64_t rec = uint64_t(3) * H / 2;  // bytes per neuron record
     if (pr.lane == 0) {
         Piece& pc = pr.t->piece[s];
         pc.kind = kPieceGateUp;
         pc.layer = layer;
-        pc.row = d.row;
         pc.dest = d.dest;
         pc.n0 = n0;
-        pc.count = count;
-        mbar_arrive_expect_tx(bar, count * H);
-        // rows at a pitch of H + 16 bytes: the consumers' 4-byte loads of 8
-        // rows then hit 32 distinct banks
-        for (uint32_t k = 0; k < count; ++k)
+        pc.count = cnt;
+        pc.flags = 0;
+        trace_piece(P, pr.idx, 0);
+        mbar_arrive_expect_tx(bar, cnt * H);
+        for (uint32_t k = 0; k < cnt; ++k)
             bulk_g2s(smem_u32(st + size_t(k) * (H + 16)), d.src + (n0 + k) * rec, H, bar);
     }
-    // gate+up scales: H/128 words per neuron, at the start of its scale row;
-    // staged at a pitch of H/128 + 1 words so that 8 neurons' scales sit in
-    // 8 different banks.
-    const uint32_t wpn = H / 128;
-    const uint32_t words = count * wpn;
+    using SC = ScaleCopy<H>;
+    constexpr uint32_t upn = SC::kGateUp / SC::kUnit;
+    const uint8_t* sbase = reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow;
     const uint32_t sdst = smem_u32(st + kStageData);
-    for (uint32_t i = pr.lane; i < words; i += 32) {
-        const uint32_t k = i / wpn, w = i % wpn;
-        const uint16_t* src = L.scales + (size_t(d.phys) * P.G + n0 + k) * (3 * H / 128) + 2 * w;
-        cp_async4(sdst + 4 * (k * (wpn + 1) + w), src);
+    for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
+        const uint32_t k = i / upn, o = i % upn;
+        cp_async<SC::kUnit>(sdst + k * SC::kGateUp + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
     }
-    producer_stamp(P, pr, pr.idx, 0);
-    producer_close(pr, s);
-    producer_stamp(P, pr, pr.idx, 1);
+    producer_close(pr, P, s);
     ++pr.idx;
+    ++pr.octets;
     return true;
 }
 
-// DOWN piece: rows [r0, r0+rows) x chunks [k0, k0+m) of one descriptor.
+// DOWN piece: down rows of neurons [n0, n0+cnt) (one slab, cnt <= 16).
+template <int H>
 __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                              uint32_t layer, uint32_t r0, uint32_t rows, uint32_t k0, uint32_t m, uint32_t flags) {
+                              uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t row, uint32_t flags) {
     if (!producer_acquire_stage(pr, P)) return false;
     const uint32_t s = pr.idx % kStages;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
     const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
-    const uint32_t H = P.H;
-    const uint64_t rec = uint64_t(3) * H / 2;
-    const uint32_t pitch = 16 * m;
-    const uint32_t sb0 = (k0 / 4) & ~1u;
-    const uint32_t sb1 = ((k0 + m - 1) / 4 + 2) & ~1u;
-    const uint32_t nsb = sb1 - sb0;
+    constexpr uint64_t rec = uint64_t(3) * H / 2;
     if (pr.lane == 0) {
         Piece& pc = pr.t->piece[s];
         pc.kind = kPieceDown;
         pc.layer = layer;
-        pc.row = d.row;
+        pc.row = row;
         pc.dest = d.dest;
-        pc.n0 = r0;
-        pc.count = rows;
-        pc.k0 = k0;
-        pc.chunks = m;
-        pc.sb0 = sb0;
-        pc.nsb = nsb;
+        pc.n0 = n0;
+        pc.count = cnt;
+        pc.need = pr.octets;
         pc.flags = flags;
-        mbar_arrive_expect_tx(bar, rows * pitch);
-        for (uint32_t r = 0; r < rows; ++r)
-            bulk_g2s(smem_u32(st + size_t(r) * pitch), d.src + (r0 + r) * rec + H + 16 * k0, pitch, bar);
+        trace_piece(P, pr.idx, 0);
+        mbar_arrive_expect_tx(bar, cnt * (H / 2));
+        for (uint32_t r = 0; r < cnt; ++r)
+            bulk_g2s(smem_u32(st + size_t(r) * (H / 2 + 16)), d.src + (n0 + r) * rec + H, H / 2, bar);
     }
-    const uint32_t wpr = nsb / 2;  // words per row
-    const uint32_t words = rows * wpr;
+    using SC = ScaleCopy<H>;
+    constexpr uint32_t upn = SC::kDown / SC::kUnit;
+    const uint8_t* sbase =
+        reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow + SC::kGateUp;
     const uint32_t sdst = smem_u32(st + kStageData);
-    for (uint32_t i = pr.lane; i < words; i += 32) {
-        const uint32_t r = i / wpr, w = i % wpr;
-        const uint16_t* src =
-            L.scales + (size_t(d.phys) * P.G + r0 + r) * (3 * H / 128) + 2 * (H / 128) + sb0 + 2 * w;
-        cp_async4(sdst + 4 * i, src);
+    for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
+        const uint32_t r = i / upn, o = i % upn;
+        cp_async<SC::kUnit>(sdst + r * SC::kDown + o * SC::kUnit, sbase + r * SC::kRow + o * SC::kUnit);
     }
-    // The stage stays open until the h of rows [r0, r0+rows) -- written by
-    // the GATEUP pieces of this layer, in any CTA -- is staged next to it.
-    const uint32_t slot = (pr.open_head + pr.open_count) % kStages;
-    producer_stamp(P, pr, pr.idx, 0);
-    pr.open[slot] = OpenStage{s, uint32_t(d.row * P.G + r0), rows, layer, pr.idx};
-    ++pr.open_count;
+    producer_close(pr, P, s);
     ++pr.idx;
     return true;
 }
 
-// Rows per DOWN piece and 16-byte chunks per DOWN piece (<= 64 so that one
-// consumer thread owns one 8-column task).
-__device__ __forceinline__ uint32_t down_rows(const KernelParams& P) { return P.G < 32u ? P.G : 32u; }
-__device__ __forceinline__ uint32_t down_chunks(const KernelParams& P) {
-    const uint32_t hc = P.H / 32;
-    uint32_t m = (kStageData / down_rows(P)) / 16;
-    if (m > 64u) m = 64u;
-    return m < hc ? m : hc;
-}
-__device__ __forceinline__ uint32_t gateup_neurons(const KernelParams& P) {
-    const uint32_t n = kStageData / (P.H + 16);
-    return n < uint32_t(kGateupMax) ? n : uint32_t(kGateupMax);
-}
-
-// DOWN pieces of chunks [k0, k0+m) of one descriptor, all row groups.
-__device__ bool producer_down_range(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                                    uint32_t layer, uint32_t k0, uint32_t m) {
-    const uint32_t G = P.G, hc = P.H / 32, rr = down_rows(P);
-    for (uint32_t r = 0; r < G; r += rr) {
-        const uint32_t rows = (G - r) < rr ? (G - r) : rr;
-        uint32_t f = 0;
-        if (r == 0) f |= kFirstRows;
-        if (r + rows == G) f |= kLastRows;
-        if (r + rows == G && k0 + m == hc) f |= kCompletes;
-        if (!producer_down(pr, P, L, d, layer, r, rows, k0, m, f) || pr.t->abort) return false;
-    }
-    return true;
-}
-
-// All pieces of one descriptor (progressive path).
-__device__ bool producer_descriptor(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                                    uint32_t layer) {
-    const uint32_t G = P.G, hc = P.H / 32;
-    const uint32_t np = gateup_neurons(P);
-    for (uint32_t n = 0; n < G; n += np) {
-        const uint32_t c = (G - n) < np ? (G - n) : np;
-        if (!producer_gateup(pr, P, L, d, layer, n, c) || pr.t->abort) return false;
-    }
-    const uint32_t mm = down_chunks(P);
-    for (uint32_t k = 0; k < hc; k += mm) {
-        const uint32_t m = (hc - k) < mm ? (hc - k) : mm;
-        if (!producer_down_range(pr, P, L, d, layer, k, m)) return false;
-    }
-    return true;
+// All pieces of slab `slab` of one descriptor.
+template <int H>
+__device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
+                              uint32_t layer, uint32_t slab) {
+    const uint32_t spg = slabs_per_group(P.G);
+    const uint32_t n0 = slab * kSlab;
+    const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
+    if (!producer_gateup<H>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u) || pr.t->abort) return false;
+    if (cnt > 8u && (!producer_gateup<H>(pr, P, L, d, layer, n0 + 8, cnt - 8) || pr.t->abort)) return false;
+    const uint32_t flags = slab + 1 == spg ? kCompletes : 0u;
+    return producer_down<H>(pr, P, L, d, layer, n0, cnt, d.row * spg + slab, flags) && !pr.t->abort;
 }
 
 // Loads the descriptor window [base, base+32) into shared memory, one
-// descriptor per lane (two dependent reads per lane).
+// descriptor per lane.
 __device__ bool producer_window(Producer& pr, const KernelParams& P, const LayerPlan& L, uint32_t layer,
                                 uint32_t base, uint32_t D) {
     const uint32_t d = base + pr.lane;
@@ -627,15 +527,17 @@ __device__ void stamp(const LayerPlan& L, const DescView& d) {
 }
 
 // Producer warp main loop over the layers of the launch.
+template <int H>
 __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     Producer pr;
     pr.idx = 0;
+    pr.octets = 0;
     pr.lane = threadIdx.x & 31u;
     pr.stages = stages;
     pr.t = t;
     pr.deadline = deadline;
     pr.wbase = pr.wlayer = 0xffffffffu;
-    pr.open_head = pr.open_count = 0;
+    const uint32_t spg = slabs_per_group(P.G);
     bool ok = true;
     for (uint32_t l = 0; ok && l < P.nlayers; ++l) {
         const LayerPlan& L = plan_at(P, l);
@@ -647,38 +549,19 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_DECIDED);
         if (path == kPathAbort) break;
         const uint32_t D = L.core_count + total;
+        const uint32_t NS = D * spg;
         pr.wbase = pr.wlayer = 0xffffffffu;
         if (path == kPathFast) {
-            const uint32_t G = P.G, hc = P.H / 32;
-            const uint64_t NT = uint64_t(D) * G, CT = uint64_t(D) * hc;
+            // Static balanced split of the layer's slab positions.
             const uint32_t b = blockIdx.x, grid = gridDim.x;
-            const uint64_t u1 = NT * (b + 1) / grid, v1 = CT * (b + 1) / grid;
-            uint64_t u = NT * b / grid, v = CT * b / grid;
-            const uint32_t np = gateup_neurons(P), mm = down_chunks(P);
-            // GATEUP pieces over this CTA's neuron range.
-            while (ok && u < u1) {
-                const uint32_t d = uint32_t(u / G), n = uint32_t(u % G);
+            const uint32_t u1 = uint32_t(uint64_t(NS) * (b + 1) / grid);
+            for (uint32_t u = uint32_t(uint64_t(NS) * b / grid); ok && u < u1; ++u) {
+                const uint32_t d = u / spg, slab = u % spg;
                 if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32) ok = producer_window(pr, P, L, l, d, D);
                 if (!ok) break;
                 const DescView dv = t->dtab[d - pr.wbase];
-                if (n == 0 && pr.lane == 0) stamp(L, dv);
-                uint32_t c = G - n;
-                if (c > np) c = np;
-                if (u + c > u1) c = uint32_t(u1 - u);
-                ok = producer_gateup(pr, P, L, dv, l, n, c) && !t->abort;
-                u += c;
-            }
-            // DOWN pieces over this CTA's (descriptor, chunk) range.
-            while (ok && v < v1) {
-                const uint32_t d = uint32_t(v / hc), k = uint32_t(v % hc);
-                if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32) ok = producer_window(pr, P, L, l, d, D);
-                if (!ok) break;
-                const DescView dv = t->dtab[d - pr.wbase];
-                uint32_t m = hc - k;
-                if (m > mm) m = mm;
-                if (v + m > v1) m = uint32_t(v1 - v);
-                ok = producer_down_range(pr, P, L, dv, l, k, m);
-                v += m;
+                if (slab == 0 && pr.lane == 0) stamp(L, dv);
+                ok = producer_slab<H>(pr, P, L, dv, l, slab);
             }
         } else {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(L.q.control);
@@ -687,12 +570,13 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 uint32_t pos = 0, code = 0;
                 if (pr.lane == 0) {
                     pos = atomicAdd(claim, 1u);
-                    if (pos >= D) {
+                    const uint32_t d = pos / spg;
+                    if (pos >= NS) {
                         code = 0xffffffffu;  // exhausted
-                    } else if (pos >= L.core_count) {
-                        // Wait until the claimed queue position is published
-                        // (persistent.py:71-90; streaming_mlp.cu:63-75).
-                        const uint32_t q = pos - L.core_count;
+                    } else if (d >= L.core_count) {
+                        // Wait until the descriptor of the claimed slab is
+                        // published (persistent.py:71-90; streaming_mlp.cu:63-75).
+                        const uint32_t q = d - L.core_count;
                         for (;;) {
                             if (ld_acquire_sys(words + 5)) { code = LS_B200_DEV_QUEUE_ERROR; break; }
                             if (ld_acquire_sys(words + 0) > q) break;
@@ -705,154 +589,179 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 code = __shfl_sync(0xffffffffu, code, 0);
                 pos = __shfl_sync(0xffffffffu, pos, 0);
                 if (code) break;
-                ok = producer_window(pr, P, L, l, pos, pos + 1);  // one descriptor, lane 0
+                const uint32_t d = pos / spg, slab = pos % spg;
+                ok = producer_window(pr, P, L, l, d, d + 1);  // one descriptor, lane 0
                 if (!ok) break;
                 const DescView dv = t->dtab[0];
-                if (pr.lane == 0) stamp(L, dv);
-                ok = producer_descriptor(pr, P, L, dv, l);
+                if (slab == 0 && pr.lane == 0) stamp(L, dv);
+                ok = producer_slab<H>(pr, P, L, dv, l, slab);
             }
             if (t->abort) ok = false;
         }
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_ISSUED);
-        if (ok) ok = producer_marker(pr, P, kPieceLayer, l, D, t->abort ? 0u : kLayerGood);
+        if (ok) ok = producer_marker(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
     }
     producer_marker(pr, P, kPieceFinal, 0, 0, 0);
-    producer_flush(pr, P);
     if (pr.lane == 0) trace(P, LS_B200_TRACE_PRODUCED);
 }
 
 // ------------------------------------------------------------ consumer side
-// Register-resident activation fragments of one warp's share of the hidden
-// dimension: slice w % 8 (H/8 coordinates = SB 32-coordinate sub-blocks),
-// sub-blocks [half*SBH, half*SBH + SBH) with half = w / 8.
-// x[b][p] = (x[c + p], x[c + p + 4]), c = sub-block start + 8 (lane & 3):
-// for the tensor-core path these are the B fragments (column 0) of
-// m16n8k16 for logical k = (2t, 2t+1) and (2t+8, 2t+9).
-template <int SBH>
-struct Frag {
-    __half2 x[SBH][4];
-};
+// Bounded barrier of the 16 consumer warps (an mbarrier, 16 arrivals per
+// phase). Every consumer warp passes the same sequence of these barriers;
+// `phase` counts them. Returns false when the wait gave up.
+__device__ bool csync(const KernelParams& P, SmemTail* t, uint32_t& phase, uint64_t limit, int lane) {
+    __syncwarp();
+    const uint32_t bar = smem_u32(&t->cbar);
+    if (lane == 0) mbar_arrive(bar);
+    const uint32_t parity = phase & 1u;
+    ++phase;
+    uint32_t spins = 0;
+    for (;;) {
+        const bool ready = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ready)) return true;
+        uint32_t late = 0;
+        if (lane == 0 && (++spins & 255u) == 0 && gtimer() > limit) late = 1;
+        if (__shfl_sync(0xffffffffu, late, 0)) {
+            if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 8);
+            return false;
+        }
+    }
+}
 
-template <int SB>
-struct Split {
-    static constexpr int SBH = SB > 1 ? SB / 2 : 1;
-    __device__ static int first(int warp) { return SB > 1 ? (warp / kSlices) * SBH : 0; }
-    __device__ static int count(int warp) { return SB > 1 ? SBH : (warp < kSlices ? 1 : 0); }
-};
+// Bounded wait of one thread until *counter >= target (acquire, gpu scope).
+__device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* counter, uint32_t target,
+                           uint64_t limit, uint32_t detail) {
+    uint32_t spins = 0;
+    while (ld_acquire_gpu(counter) < target) {
+        if ((++spins & 63u) == 0 && gtimer() > limit) {
+            raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, detail);
+            return false;
+        }
+        __nanosleep(20);
+    }
+    return true;
+}
 
-// Builds this warp's fragments from the CTA's staged activation, applying
-// the HF RMSNorm of predictor_shared_input.cu:16-33 when flagged:
-// inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv)).
-// The sum runs per lane over 8-coordinate groups lane*8 + 256 i, then a
-// fixed butterfly: every warp of every CTA computes the same value.
-template <int SB>
-__device__ void load_activation(const KernelParams& P, const LayerPlan& L, const __half* xs,
-                                Frag<Split<SB>::SBH>& f, int warp, int lane) {
-    constexpr int SBH = Split<SB>::SBH;
-    const uint32_t H = P.H;
+// Loads the layer's input, applies the HF RMSNorm of
+// predictor_shared_input.cu:16-33 when flagged
+// (inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv))), and
+// stores it in B-fragment order: entry u = coordinates 8u..8u+7 as half2
+// pairs (0,4) (1,5) (2,6) (3,7); xs32[b] = fp32 sum of sub-block b.
+// Every CTA computes the same sum in the same order.
+template <int H>
+__device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t& cph, uint64_t limit,
+                        int tid) {
+    constexpr int NU = H / 8;  // one 8-coordinate unit per thread (H <= 4096)
+    const int warp = tid >> 5, lane = tid & 31;
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    float ss = 0.f;
+    if (tid < NU) {
+        raw = __ldcg(reinterpret_cast<const uint4*>(L.x) + tid);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 v = __half22float2(h[e]);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+        }
+    }
     const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
     float inv = 1.f;
     if (norm) {
-        float ss = 0.f;
-        for (uint32_t c = 8 * lane; c < H; c += 256) {
-            const uint4 w = *reinterpret_cast<const uint4*>(xs + c);
-            const __half2* h = reinterpret_cast<const __half2*>(&w);
+        ss = warp_sum(ss);
+        if (lane == 0) t->red[warp] = ss;
+        csync(P, t, cph, limit, lane);
+        float tot = 0.f;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 v = __half22float2(h[e]);
-                ss += v.x * v.x;
-                ss += v.y * v.y;
-            }
-        }
-        inv = rsqrtf(warp_sum(ss) / float(H) + P.eps);
+        for (int w = 0; w < kConsumerWarps; ++w) tot += t->red[w];
+        inv = rsqrtf(tot / float(H) + P.eps);
     }
-    const uint32_t base = (warp % kSlices) * (H / 8) + 32 * Split<SB>::first(warp) + 8 * (lane & 3);
-#pragma unroll
-    for (int b = 0; b < SBH; ++b) {
-        const uint32_t c = (base + 32 * b) % H;  // in range even for an idle half (SB == 1)
-        const uint4 w = *reinterpret_cast<const uint4*>(xs + c);
-        const __half* h = reinterpret_cast<const __half*>(&w);
+    if (tid < NU) {
         __half v[8];
+        const __half* h = reinterpret_cast<const __half*>(&raw);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            v[e] = h[e];
-            if (norm) v[e] = __float2half_rn(__half2float(v[e]) * inv);
-        }
+        for (int e = 0; e < 8; ++e) v[e] = norm ? __float2half_rn(__half2float(h[e]) * inv) : h[e];
         if (norm && L.norm_w) {
-            const uint4 nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w + c));
+            const uint4 nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + tid);
             const __half* wh = reinterpret_cast<const __half*>(&nw);
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
         }
+        uint4 f;
+        f.x = h2_bits(__halves2half2(v[0], v[4]));
+        f.y = h2_bits(__halves2half2(v[1], v[5]));
+        f.z = h2_bits(__halves2half2(v[2], v[6]));
+        f.w = h2_bits(__halves2half2(v[3], v[7]));
+        t->xf[tid] = f;
+        float xsum = 0.f;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) f.x[b][p] = __halves2half2(v[p], v[p + 4]);
+        for (int e = 0; e < 8; ++e) xsum += __half2float(v[e]);
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+        if ((tid & 3) == 0) t->xs32[tid >> 2] = xsum;
     }
+    csync(P, t, cph, limit, lane);
 }
 
-// GATEUP piece: this warp's share of its hidden slice for every neuron of the
-// piece, in tiles of 8 neurons; the partial sums go to the stage's partial
-// area and the last warp to finish adds the 16 of them in warp order, forms h
-// and publishes it.
-template <int SB, bool MMA>
+// GATEUP piece: warp w reduces sub-blocks [w*SBW, (w+1)*SBW) (32 hidden
+// coordinates each) for the piece's 8 neurons; the last warp to finish sums
+// the warp partials in warp order and forms h.
+template <int H, bool F>
 __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, uint8_t* st, SmemTail* t,
-                               uint32_t s, const Frag<Split<SB>::SBH>& f, int warp, int lane) {
-    constexpr int SBH = Split<SB>::SBH;
-    const uint32_t H = P.H, pitch = H + 16;
+                               uint32_t s, int warp, int lane) {
+    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
+    constexpr int CH = SBW < 4 ? SBW : 4;  // sub-blocks per scale block handled at once
+    constexpr int PG = H + 16;
+    constexpr int SPN = 2 * (H / 128);  // scale halves per neuron (gate, then up)
     const int g = lane >> 2, tq = lane & 3;
-    const int nsub = Split<SB>::count(warp);
-    const uint32_t slice = (warp % kSlices) * (H / 8) + 32 * Split<SB>::first(warp);  // first coordinate
-    const __half* sc = reinterpret_cast<const __half*>(st + kStageData);
-    float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxSecond);  // [warp][count]
-    for (uint32_t r0 = 0; r0 < pc.count; r0 += 8) {
-        const uint32_t k = r0 + g;  // neuron of the piece handled by this lane quad
-        const uint8_t* row = st + size_t(k) * pitch + slice / 2 + 4 * tq;
-        const __half* scr = sc + size_t(k) * 2 * (H / 128 + 1);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // second tensor-core chain (odd sub-blocks)
+    float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxPartials);  // [warp][8]
+    __syncwarp();  // mma.sync is .aligned: enter converged whatever the caller's waits did
+    if (warp < AW) {
+        const uint8_t* rowg = st + g * PG + 4 * tq;
+        const __half* sc = reinterpret_cast<const __half*>(st + kStageData) + g * SPN;
+        float pg = 0.f, pu = 0.f;
 #pragma unroll
-        for (int b = 0; b < SBH; ++b) {
-            if (b >= nsub) break;
-            const uint32_t wg = *reinterpret_cast<const uint32_t*>(row + 16 * b);
-            const uint32_t wu = *reinterpret_cast<const uint32_t*>(row + H / 2 + 16 * b);
-            const uint32_t blk = (slice + 32 * b) >> 7;
-            const __half2 sg = __half2half2(scr[blk]);
-            const __half2 su = __half2half2(scr[(H >> 7) + blk]);  // gate: H/128 halves, then up
-            __half2 qg[4], qu[4];
-            unpack8(wg, qg);
-            unpack8(wu, qu);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                qg[p] = __hmul2(qg[p], sg);  // == fp16(float(q) * float(s)), core.py:17
-                qu[p] = __hmul2(qu[p], su);
+        for (int j0 = 0; j0 < SBW; j0 += CH) {
+            const int blk = (warp * SBW + j0) / 4;
+            float al[4] = {0.f, 0.f, 0.f, 0.f}, ah[4] = {0.f, 0.f, 0.f, 0.f};
+            float X = 0.f;
+            __half2 sg2, su2;
+            if constexpr (!F) {
+                sg2 = __half2half2(sc[blk]);
+                su2 = __half2half2(sc[H / 128 + blk]);
             }
-            if constexpr (MMA) {
-                // rows 0-7: gate rows of the 8 neurons, rows 8-15: their up rows
-                float(&d)[4] = (b & 1) ? acc2 : acc;
-                mma16816(d, qg[0], qu[0], qg[1], qu[1], f.x[b][0], f.x[b][1]);
-                mma16816(d, qg[2], qu[2], qg[3], qu[3], f.x[b][2], f.x[b][3]);
-            } else {
 #pragma unroll
-                for (int p = 0; p < 4; ++p) {
-                    acc[p & 1] = mfma(__low2half(qg[p]), __low2half(f.x[b][p]), acc[p & 1]);
-                    acc[p & 1] = mfma(__high2half(qg[p]), __high2half(f.x[b][p]), acc[p & 1]);
-                    acc[2 + (p & 1)] = mfma(__low2half(qu[p]), __low2half(f.x[b][p]), acc[2 + (p & 1)]);
-                    acc[2 + (p & 1)] = mfma(__high2half(qu[p]), __high2half(f.x[b][p]), acc[2 + (p & 1)]);
+            for (int j = 0; j < CH; ++j) {
+                const int sb = warp * SBW + j0 + j;
+                const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
+                const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
+                const uint4 xv = t->xf[sb * 4 + tq];
+                const uint32_t wg8 = wg >> 8, wu8 = wu >> 8;
+                if constexpr (F) {
+                    X += t->xs32[sb];
+                    // even coordinates (0,4),(2,6) and odd (1,5),(3,7) in separate sums
+                    mma16816(al, sub_lo(wg), sub_lo(wu), sub_lo(wg8), sub_lo(wu8), xv.x, xv.z);
+                    mma16816(ah, sub_hi(wg), sub_hi(wu), sub_hi(wg8), sub_hi(wu8), xv.y, xv.w);
+                } else {
+                    const uint32_t g0 = h2_bits(__hmul2(int_lo(wg), sg2)), g1 = h2_bits(__hmul2(int_hi(wg), sg2));
+                    const uint32_t g2 = h2_bits(__hmul2(int_lo(wg8), sg2)), g3 = h2_bits(__hmul2(int_hi(wg8), sg2));
+                    const uint32_t u0 = h2_bits(__hmul2(int_lo(wu), su2)), u1 = h2_bits(__hmul2(int_hi(wu), su2));
+                    const uint32_t u2 = h2_bits(__hmul2(int_lo(wu8), su2)), u3 = h2_bits(__hmul2(int_hi(wu8), su2));
+                    mma16816(al, g0, u0, g2, u2, xv.x, xv.z);
+                    mma16816(al, g1, u1, g3, u3, xv.y, xv.w);
                 }
             }
+            if constexpr (F) {
+                const float sg = __half2float(sc[blk]), su = __half2float(sc[H / 128 + blk]);
+                // D = sum (q + 8) x  (even: x 2^-24, odd: x 16 * 2^-24)
+                pg = fmaf(sg, fmaf(16777216.f, al[0], fmaf(1048576.f, ah[0], -8.f * X)), pg);
+                pu = fmaf(su, fmaf(16777216.f, al[2], fmaf(1048576.f, ah[2], -8.f * X)), pu);
+            } else {
+                pg += al[0];
+                pu += al[2];
+            }
         }
-        float gs, us;
-        if constexpr (MMA) {
-            gs = acc[0] + acc2[0];  // D[g][0]: lane (g, 0)
-            us = acc[2] + acc2[2];  // D[g+8][0]
-        } else {
-            gs = acc[0] + acc[1];
-            us = acc[2] + acc[3];
-            gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-            us += __shfl_xor_sync(0xffffffffu, us, 1);
-            gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-            us += __shfl_xor_sync(0xffffffffu, us, 2);
-        }
-        if (tq == 0 && k < pc.count) part[warp * pc.count + k] = make_float2(gs, us);
+        if (tq == 0) part[warp * 8 + g] = make_float2(pg, pu);
     }
     // Last warp to finish this piece combines the partial sums.
     __syncwarp();
@@ -865,172 +774,208 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
     if (uint32_t(lane) < pc.count) {
         float gsum = 0.f, usum = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            const float2 v = part[w * pc.count + lane];
+        for (int w = 0; w < AW; ++w) {
+            const float2 v = part[w * 8 + lane];
             gsum += v.x;
             usum += v.y;
         }
         const float g16 = round16(gsum), u16 = round16(usum);
         const float sl = round16(g16 / (1.f + expf(-g16)));
-        const uint16_t h = __half_as_ushort(__float2half_rn(sl * u16));
-        const uint32_t n = pc.n0 + lane;
-        st_relaxed_gpu_u64(P.hbuf + size_t(pc.row) * P.G + n, h_tag(P, pc.layer) | h);
-        if (L.act) L.act[size_t(pc.dest) * P.G + n] = h;
+        const __half h = __float2half_rn(sl * u16);
+        t->hs[(pc.n0 & (kSlab - 1)) + lane] = h;
+        if (L.act) L.act[size_t(pc.dest) * P.G + pc.n0 + lane] = __half_as_ushort(h);
     }
     __syncwarp();
-    if (lane == 0) t->gcnt[s] = 0;
-}
-
-// DOWN piece: thread owns 8 columns (4 packed bytes) of the range and one
-// half of the piece's rows (threads [0,256): first half, [256,512): second).
-__device__ __forceinline__ uint32_t down_half_split(uint32_t rows) { return (rows + 1) / 2; }
-
-__device__ void consume_down(const Piece& pc, const uint8_t* st, const __half* hs, float (&acc)[8], int tid) {
-    const uint32_t pitch = 16 * pc.chunks;
-    const uint32_t task = uint32_t(tid) & 255u, half = uint32_t(tid) >> 8;
-    if (task >= 4 * pc.chunks) return;
-    const uint32_t split = down_half_split(pc.count);
-    const uint32_t rb = half ? split : 0, re = half ? pc.count : split;
-    const __half* sc = reinterpret_cast<const __half*>(st + kStageData);
-    const uint32_t col = 32 * pc.k0 + 8 * task;
-    const uint32_t sbi = (col >> 7) - pc.sb0;
-    const uint8_t* base = st + 4 * task;
-    uint32_t r = rb;
-    for (; r + 4 <= re; r += 4) {
-        uint32_t wv[4];
-        __half2 s2[4];
-        __half hh[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            wv[e] = *reinterpret_cast<const uint32_t*>(base + size_t(r + e) * pitch);
-            s2[e] = __half2half2(sc[(r + e) * pc.nsb + sbi]);
-            hh[e] = hs[r + e];
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            __half2 q[4];
-            unpack8(wv[e], q);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const __half2 v = __hmul2(q[p], s2[e]);
-                acc[p] = mfma(__low2half(v), hh[e], acc[p]);
-                acc[p + 4] = mfma(__high2half(v), hh[e], acc[p + 4]);
-            }
-        }
-    }
-    for (; r < re; ++r) {
-        const uint32_t wv = *reinterpret_cast<const uint32_t*>(base + size_t(r) * pitch);
-        const __half2 s2 = __half2half2(sc[r * pc.nsb + sbi]);
-        const __half hh = hs[r];
-        __half2 q[4];
-        unpack8(wv, q);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const __half2 v = __hmul2(q[p], s2);
-            acc[p] = mfma(__low2half(v), hh, acc[p]);
-            acc[p + 4] = mfma(__high2half(v), hh, acc[p + 4]);
-        }
-    }
-}
-
-// Bounded warp-level wait until *counter >= target (acquire, gpu scope).
-// `stop_on_abort`: give up early when this CTA already failed.
-__device__ bool warp_wait_count(const KernelParams& P, SmemTail* t, const uint32_t* counter, uint32_t target,
-                                uint64_t limit, uint32_t detail, bool stop_on_abort, int lane) {
-    uint32_t ok = 1;
+    __threadfence_block();
     if (lane == 0) {
-        uint32_t spins = 0;
-        while (ld_acquire_gpu(counter) < target) {
-            if (stop_on_abort && t->abort) { ok = 0; break; }
-            if ((++spins & 63u) == 0 && gtimer() > limit) {
-                raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, detail);
-                ok = 0;
-                break;
-            }
-            __nanosleep(32);
-        }
+        t->gcnt[s] = 0;
+        t->octets_done = t->octets_done + 1;
     }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// Compact reduction of one 32-column block (reduction.py:6-28,
-// streaming_mlp.cu:80-84): lane = column, the 2 partial rows (row halves) of
-// every descriptor summed in row order, loads issued 32 at a time; then the
-// layer epilogue (fp16 output, residual add, fp32 output).
-__device__ void reduce_block(const KernelParams& P, const LayerPlan& L, uint32_t blk, uint32_t rows, bool write,
+// DOWN piece: warp w owns 64-column tiles [w*TPW, (w+1)*TPW); in each, lane
+// (g, t) reads the 8 columns 8g..8g+7 of neurons 2t, 2t+1, 2t+8, 2t+9, pairs
+// the two neurons of each column with PRMT and runs four 16-neuron MMAs
+// (MMA j: columns 8g+j and 8g+j+4). The slab's partial row goes to global
+// memory, 256 contiguous bytes per warp and tile.
+template <int H, bool F>
+__device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8_t* st, const SmemTail* t, int warp,
                              int lane) {
-    const uint32_t H = P.H, c = 32 * blk + lane;
-    const float* p = P.partial + c;
-    const uint32_t n = 2 * rows;
-    float s = 0.f;
-    uint32_t r = 0;
-    for (; r + 32 <= n; r += 32) {
-        float v[32];
+    constexpr int NT = H / 64, DW = NT < kConsumerWarps ? NT : kConsumerWarps, TPW = NT / DW;
+    constexpr int PD = H / 2 + 16;
+    constexpr int SPN = H / 128;  // down scale halves per neuron
+    if (warp >= DW) return;
+    __syncwarp();  // mma.sync is .aligned: enter converged
+    const int g = lane >> 2, tq = lane & 3;
+    const uint32_t cnt = pc.count;
+    const int n0 = 2 * tq, n1 = n0 + 1, n2 = n0 + 8, n3 = n0 + 9;
+    const __half zero = __float2half_rn(0.f);
+    const __half hv0 = uint32_t(n0) < cnt ? t->hs[n0] : zero, hv1 = uint32_t(n1) < cnt ? t->hs[n1] : zero;
+    const __half hv2 = uint32_t(n2) < cnt ? t->hs[n2] : zero, hv3 = uint32_t(n3) < cnt ? t->hs[n3] : zero;
+    const __half* sd = reinterpret_cast<const __half*>(st + kStageData);
+    float* out = P.partial + size_t(pc.row) * H;
+    uint32_t b0 = 0, b1 = 0, r0 = 0, r1 = 0, s01 = 0, s23 = 0;
+    float hsum = 0.f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __ldcg(p + size_t(r + e) * H);
+    for (int i = 0; i < TPW; ++i) {
+        const int tile = warp * TPW + i;
+        const int blk = tile >> 1;  // 128-column scale block
+        if (i == 0 || (tile & 1) == 0) {
+            const __half c0 = uint32_t(n0) < cnt ? sd[n0 * SPN + blk] : zero;
+            const __half c1 = uint32_t(n1) < cnt ? sd[n1 * SPN + blk] : zero;
+            const __half c2 = uint32_t(n2) < cnt ? sd[n2 * SPN + blk] : zero;
+            const __half c3 = uint32_t(n3) < cnt ? sd[n3 * SPN + blk] : zero;
+            if constexpr (F) {
+                // B carries h * s (exact in fp32) as an fp16 value plus its
+                // fp16 residual, fed to two MMAs into the same accumulator;
+                // the +8 offset of A is removed with their sum over the slab.
+                const float f[4] = {__half2float(hv0) * __half2float(c0), __half2float(hv1) * __half2float(c1),
+                                    __half2float(hv2) * __half2float(c2), __half2float(hv3) * __half2float(c3)};
+                __half hi[4], lo[4];
+                hsum = 0.f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s += v[e];
+                for (int e = 0; e < 4; ++e) {
+                    hi[e] = __float2half_rn(f[e]);
+                    lo[e] = __float2half_rn(f[e] - __half2float(hi[e]));
+                    hsum += __half2float(hi[e]) + __half2float(lo[e]);
+                }
+                b0 = h2_bits(__halves2half2(hi[0], hi[1]));
+                b1 = h2_bits(__halves2half2(hi[2], hi[3]));
+                r0 = h2_bits(__halves2half2(lo[0], lo[1]));
+                r1 = h2_bits(__halves2half2(lo[2], lo[3]));
+                hsum += __shfl_xor_sync(0xffffffffu, hsum, 1);
+                hsum += __shfl_xor_sync(0xffffffffu, hsum, 2);
+            } else {
+                b0 = h2_bits(__halves2half2(hv0, hv1));
+                b1 = h2_bits(__halves2half2(hv2, hv3));
+                s01 = h2_bits(__halves2half2(c0, c1));
+                s23 = h2_bits(__halves2half2(c2, c3));
+            }
+        }
+        const uint8_t* base = st + 32 * tile + 4 * g;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(base + n0 * PD);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(base + n1 * PD);
+        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(base + n2 * PD);
+        const uint32_t w3 = *reinterpret_cast<const uint32_t*>(base + n3 * PD);
+        // Interleave: [w0.b0 w0.b1 w1.b0 w1.b1] holds columns 0-3 of both neurons.
+        const uint32_t p01[2] = {__byte_perm(w0, w1, 0x5410), __byte_perm(w0, w1, 0x7632)};
+        const uint32_t p23[2] = {__byte_perm(w2, w3, 0x5410), __byte_perm(w2, w3, 0x7632)};
+        uint32_t a01[8], a23[8];  // column c: (neuron 2t, 2t+1) and (2t+8, 2t+9)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t x = p01[hh], x8 = x >> 8, y = p23[hh], y8 = y >> 8;
+            if constexpr (F) {
+                a01[4 * hh + 0] = sub_lo(x);
+                a01[4 * hh + 1] = sub_hi(x);
+                a01[4 * hh + 2] = sub_lo(x8);
+                a01[4 * hh + 3] = sub_hi(x8);
+                a23[4 * hh + 0] = sub_lo(y);
+                a23[4 * hh + 1] = sub_hi(y);
+                a23[4 * hh + 2] = sub_lo(y8);
+                a23[4 * hh + 3] = sub_hi(y8);
+            } else {
+                const __half2 t01 = bits_h2(s01), t23 = bits_h2(s23);
+                a01[4 * hh + 0] = h2_bits(__hmul2(int_lo(x), t01));
+                a01[4 * hh + 1] = h2_bits(__hmul2(int_hi(x), t01));
+                a01[4 * hh + 2] = h2_bits(__hmul2(int_lo(x8), t01));
+                a01[4 * hh + 3] = h2_bits(__hmul2(int_hi(x8), t01));
+                a23[4 * hh + 0] = h2_bits(__hmul2(int_lo(y), t23));
+                a23[4 * hh + 1] = h2_bits(__hmul2(int_hi(y), t23));
+                a23[4 * hh + 2] = h2_bits(__hmul2(int_lo(y8), t23));
+                a23[4 * hh + 3] = h2_bits(__hmul2(int_hi(y8), t23));
+            }
+        }
+        float acc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+            mma16816(acc[j], a01[j], a01[j + 4], a23[j], a23[j + 4], b0, b1);
+            if constexpr (F) mma16816(acc[j], a01[j], a01[j + 4], a23[j], a23[j + 4], r0, r1);
+        }
+        // lane (g, t) stores columns 8g + 2t, 8g + 2t + 1
+        const bool hi_half = (tq & 2) != 0, odd = (tq & 1) != 0;
+        const float m0 = hi_half ? acc[0][2] : acc[0][0], m1 = hi_half ? acc[1][2] : acc[1][0];
+        const float m2 = hi_half ? acc[2][2] : acc[2][0], m3 = hi_half ? acc[3][2] : acc[3][0];
+        float v0 = odd ? m2 : m0, v1 = odd ? m3 : m1;
+        if constexpr (F) {
+            v0 = fmaf(16777216.f, v0, -8.f * hsum);  // even column: (q + 8) 2^-24
+            v1 = fmaf(1048576.f, v1, -8.f * hsum);   // odd column: 16 (q + 8) 2^-24
+        }
+        *reinterpret_cast<float2*>(out + 64 * tile + 8 * g + 2 * tq) = make_float2(v0, v1);
     }
-    for (; r + 8 <= n; r += 8) {
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = __ldcg(p + size_t(r + e) * H);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) s += v[e];
-    }
-    for (; r < n; ++r) s += __ldcg(p + size_t(r) * H);
-    if (!write) return;
-    if (L.y32) L.y32[c] = s;
-    const __half y16 = __float2half_rn(s);
-    if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
-    if (L.hidden_out && L.residual)
-        L.hidden_out[c] = __half_as_ushort(__float2half_rn(h2f(L.residual[c]) + __half2float(y16)));
 }
 
-// Bounded wait until a volatile shared-memory word reaches `target`.
-__device__ bool smem_wait(const KernelParams& P, SmemTail* t, volatile uint32_t* word, uint32_t target,
-                          uint64_t limit, uint32_t detail, int lane) {
-    uint32_t ok = 1;
-    if (lane == 0) {
-        uint32_t spins = 0;
-        while (*word < target) {
-            if ((++spins & 255u) == 0 && gtimer() > limit) {
-                raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, detail);
-                ok = 0;
-                break;
+// End of layer l: partial rows -> reduction -> epilogue. Canonical sum per
+// column: rows in chunks of 16 (row order inside a chunk), chunk c added to
+// warp c % 16's running sum in chunk order, then the 16 warp sums in warp
+// order (reduction.py:6-28, streaming_mlp.cu:80-84 sum rows in row order).
+template <int H>
+__device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t rows, bool good,
+                          SmemTail* t, uint32_t& cph, uint64_t limit, int tid) {
+    constexpr uint32_t NBLK = H / 32;
+    const int warp = tid >> 5, lane = tid & 31;
+    uint32_t* wl = ws_layer(P, l);
+    __threadfence();  // this warp's partial rows are visible at gpu scope
+    csync(P, t, cph, limit, lane);
+    if (tid == 0) red_release_gpu(wl + 2, 1u);
+    if (blockIdx.x >= NBLK) return;
+    if (tid == 0) {
+        const bool ready = wait_count(P, t, wl + 2, gridDim.x, limit, 5);
+        t->flag = (ready ? 1u : 0u) | ((ready && good && ld_acquire_gpu(P.ws + kWsErr) == 0) ? 2u : 0u);
+        trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
+    }
+    csync(P, t, cph, limit, lane);
+    const uint32_t flag = t->flag;
+    const uint32_t nch = (rows + 15) / 16;
+    for (uint32_t blk = blockIdx.x; blk < NBLK; blk += gridDim.x) {
+        float acc = 0.f;
+        if (flag & 1u) {
+            for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
+                const float* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
+                const uint32_t nr = rows - 16 * c;
+                float v[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = uint32_t(e) < nr ? __ldcg(p + size_t(e) * H) : 0.f;
+                float cs = v[0];
+#pragma unroll
+                for (int e = 1; e < 16; ++e) cs += v[e];
+                acc += cs;
             }
-            __nanosleep(20);
+        }
+        t->red2[warp][lane] = acc;
+        csync(P, t, cph, limit, lane);
+        if (warp == 0 && (flag & 2u)) {
+            float y = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
+            const uint32_t c = 32 * blk + lane;
+            if (L.y32) L.y32[c] = y;
+            const __half y16 = __float2half_rn(y);
+            if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
+            if (L.hidden_out && L.residual)
+                L.hidden_out[c] = __half_as_ushort(__float2half_rn(h2f(__ldcg(L.residual + c)) + __half2float(y16)));
+        }
+        csync(P, t, cph, limit, lane);  // red2 is reused by the next block
+    }
+    if (warp == 0) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+            red_release_gpu(wl + 3, 1u);
+            trace_layer(P, l, LS_B200_LTRACE_REDUCED);
         }
     }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    __threadfence_block();
-    return ok != 0;
 }
 
-// Warp 0 stages layer l's activation into shared memory once per CTA
-// (16-byte loads, bypassing L1: the previous layer's reducers wrote it).
-__device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t l, int lane) {
-    const uint4* src = reinterpret_cast<const uint4*>(L.x);
-    uint4* dst = reinterpret_cast<uint4*>(t->xs);
-    for (uint32_t i = lane; i < P.H / 8; i += 32) dst[i] = __ldcg(src + i);
-    __syncwarp();
-    __threadfence_block();
-    if (lane == 0) t->xready = l + 1;
-}
-
-template <int SB, bool MMA>
+template <int H, bool F>
 __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
+    constexpr uint32_t NBLK = H / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint64_t limit = deadline + kSyncGraceNs;
+    uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    Frag<Split<SB>::SBH> a;
-    if (warp == 0) stage_x(P, *L, t, 0, lane);
-    smem_wait(P, t, &t->xready, 1, deadline + kSyncGraceNs, 7, lane);
-    load_activation<SB>(P, *L, t->xs, a, warp, lane);
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    const uint32_t nblk = P.H / 32;
+    stage_x<H>(P, *L, t, cph, limit, tid);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % kStages;
         const uint32_t parity = (idx / kStages) & 1u;
@@ -1051,7 +996,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         }
         if (timed_out) {
             // The producer stopped without a FINAL marker; nothing is in
-            // flight for this stage. No barrier follows, so leaving is safe.
+            // flight for this stage.
             if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 4);
             break;
         }
@@ -1064,23 +1009,29 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             break;
         }
         uint8_t* st = stages + size_t(s) * kStageBytes;
-        const bool aborted = __shfl_sync(0xffffffffu, t->abort, 0) != 0;  // warp-uniform snapshot
         if (pc.kind == kPieceGateUp) {
-            // every warp takes part (the last one resets the piece counter)
-            consume_gateup<SB, MMA>(P, *L, pc, st, t, s, a, warp, lane);
+            // every warp takes part (the last one finalises h)
+            consume_gateup<H, F>(P, *L, pc, st, t, s, warp, lane);
         } else if (pc.kind == kPieceDown) {
-            if (pc.flags & kFirstRows) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-            }
-            if (!aborted) {
-                consume_down(pc, st, reinterpret_cast<const __half*>(st + kStageData + kAuxSecond), acc, tid);
-                if ((pc.flags & kLastRows) && (uint32_t(tid) & 255u) < 4 * pc.chunks) {
-                    float* dst = P.partial + (size_t(pc.row) * 2 + (uint32_t(tid) >> 8)) * P.H + 32 * pc.k0 +
-                                 8 * (uint32_t(tid) & 255u);
-                    reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-                    reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+            // h of the slab: finalised by the last warp of its GATEUP pieces.
+            // Every lane polls, so the warp leaves the wait converged (the
+            // MMAs that follow are .aligned).
+            bool ok = true;
+            uint32_t sp = 0;
+            for (;;) {
+                if (__all_sync(0xffffffffu, t->octets_done >= pc.need)) break;
+                uint32_t late = 0;
+                if (lane == 0 && (t->abort || ((++sp & 255u) == 0 && gtimer() > limit))) late = 1;
+                if (__shfl_sync(0xffffffffu, late, 0)) {
+                    if (lane == 0 && !t->abort) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 9);
+                    ok = false;
+                    break;
                 }
+            }
+            __threadfence_block();
+            const bool aborted = __shfl_sync(0xffffffffu, t->abort, 0) != 0;
+            if (ok && !aborted) {
+                consume_down<H, F>(P, pc, st, t, warp, lane);
                 if ((pc.flags & kCompletes) && tid == 0 && L->execs) atomicAdd(L->execs + pc.dest, 1u);
             }
         }
@@ -1090,49 +1041,21 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         if (pc.kind != kPieceLayer) continue;
 
         // ---- end of layer l: partial rows -> reduction -> next activation.
-        // One poller per CTA for each grid-wide counter; the other warps
-        // wait on shared-memory words, so the L2 sees at most gridDim.x
-        // pollers per counter.
-        uint32_t* wl = ws_layer(P, l);
-        const uint64_t limit = deadline + kSyncGraceNs;
-        __threadfence();  // this warp's partial rows are visible at gpu scope
-        if (lane == 0) {
-            const uint32_t old = atomicAdd(&t->warps_done, 1u);
-            if (old == uint32_t(kConsumerWarps) * (l + 1) - 1) red_release_gpu(wl + 2, 1u);
-        }
-        const bool good = (pc.flags & kLayerGood) != 0;
-        const uint32_t first_blk = blockIdx.x * kConsumerWarps;
-        if (first_blk < nblk) {  // this CTA owns reduction blocks
-            if (warp == 0) {
-                if (warp_wait_count(P, t, wl + 2, gridDim.x, limit, 5, false, lane) && lane == 0) t->partials = l + 1;
-                if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
-            }
-            for (uint32_t blk = first_blk + warp; blk < nblk; blk += gridDim.x * kConsumerWarps) {
-                const bool ready = smem_wait(P, t, &t->partials, l + 1, limit, 5, lane);
-                const bool write = ready && good && ld_acquire_gpu(P.ws + kWsErr) == 0;
-                if (ready) reduce_block(P, *L, blk, pc.count, write, lane);
-                __threadfence();
-                if (lane == 0) red_release_gpu(wl + 3, 1u);
-            }
-        }
-        if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
+        end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid);
         if (l + 1 >= P.nlayers) continue;  // the FINAL marker follows
-        const LayerPlan* next = &plan_at(P, l + 1);
-        if (warp == 0) {
-            if (warp_wait_count(P, t, wl + 3, nblk, limit, 6, false, lane)) {
-                if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
-                stage_x(P, *next, t, l + 1, lane);
-            }
+        if (tid == 0) {
+            wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
+            trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
         }
-        if (!smem_wait(P, t, &t->xready, l + 2, limit, 6, lane)) continue;
+        csync(P, t, cph, limit, lane);
         ++l;
-        L = next;
-        load_activation<SB>(P, *L, t->xs, a, warp, lane);
+        L = &plan_at(P, l);
+        stage_x<H>(P, *L, t, cph, limit, tid);
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
     }
 }
 
-template <int SB, bool MMA>
+template <int H, bool F>
 __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_constant__ KernelParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
@@ -1146,19 +1069,19 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
             mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps);  // one arrive per consumer warp
             t->gcnt[s] = 0;
         }
-        t->warps_done = 0;
+        mbar_init(smem_u32(&t->cbar), kConsumerWarps);
+        t->octets_done = 0;
         t->abort = 0;
-        t->xready = 0;
-        t->partials = 0;
+        t->flag = 0;
         t->last = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     if (tid >= kConsumerThreads) {
-        run_producer(P, stages, t, deadline);
+        run_producer<H>(P, stages, t, deadline);
     } else {
-        run_consumers<SB, MMA>(P, stages, t, deadline);
+        run_consumers<H, F>(P, stages, t, deadline);
     }
     __syncthreads();
     if (tid == 0) {
@@ -1195,37 +1118,38 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     if (tid == 0) trace(P, LS_B200_TRACE_EXIT);
 }
 
-template <int SB, bool MMA>
+template <int H, bool F>
 static int launch_t(const KernelParams& p, int grid, cudaStream_t stream) {
-    fused_mlp_kernel<SB, MMA><<<grid, kThreads, kernel_smem_bytes(), stream>>>(p);
+    fused_mlp_kernel<H, F><<<grid, kThreads, kernel_smem_bytes(), stream>>>(p);
     return int(cudaGetLastError());
 }
 
-template <int SB, bool MMA>
+template <int H, bool F>
 static cudaError_t raise_smem(int bytes) {
-    return cudaFuncSetAttribute(fused_mlp_kernel<SB, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return cudaFuncSetAttribute(fused_mlp_kernel<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int prepare_kernels() {
     const int bytes = int(kernel_smem_bytes());
-    const cudaError_t errs[] = {raise_smem<1, false>(bytes),  raise_smem<2, false>(bytes), raise_smem<4, false>(bytes),
-                                raise_smem<8, false>(bytes),  raise_smem<16, false>(bytes), raise_smem<1, true>(bytes),
-                                raise_smem<2, true>(bytes),   raise_smem<4, true>(bytes),  raise_smem<8, true>(bytes),
-                                raise_smem<16, true>(bytes)};
+    const cudaError_t errs[] = {raise_smem<256, false>(bytes),  raise_smem<512, false>(bytes),
+                                raise_smem<1024, false>(bytes), raise_smem<2048, false>(bytes),
+                                raise_smem<4096, false>(bytes), raise_smem<256, true>(bytes),
+                                raise_smem<512, true>(bytes),   raise_smem<1024, true>(bytes),
+                                raise_smem<2048, true>(bytes),  raise_smem<4096, true>(bytes)};
     for (cudaError_t e : errs)
         if (e != cudaSuccess) return int(e);
     return 0;
 }
 
-// H = 256 * SB with SB in {1, 2, 4, 8, 16} (each warp owns H/8 coordinates).
+// H in {256, 512, 1024, 2048, 4096}.
 int launch_fused(const KernelParams& p, int grid, cudaStream_t stream) {
-    const bool mma = p.variant != 0;
-    switch (p.H / 256) {
-        case 1: return mma ? launch_t<1, true>(p, grid, stream) : launch_t<1, false>(p, grid, stream);
-        case 2: return mma ? launch_t<2, true>(p, grid, stream) : launch_t<2, false>(p, grid, stream);
-        case 4: return mma ? launch_t<4, true>(p, grid, stream) : launch_t<4, false>(p, grid, stream);
-        case 8: return mma ? launch_t<8, true>(p, grid, stream) : launch_t<8, false>(p, grid, stream);
-        case 16: return mma ? launch_t<16, true>(p, grid, stream) : launch_t<16, false>(p, grid, stream);
+    const bool f = p.variant != 0;
+    switch (p.H) {
+        case 256: return f ? launch_t<256, true>(p, grid, stream) : launch_t<256, false>(p, grid, stream);
+        case 512: return f ? launch_t<512, true>(p, grid, stream) : launch_t<512, false>(p, grid, stream);
+        case 1024: return f ? launch_t<1024, true>(p, grid, stream) : launch_t<1024, false>(p, grid, stream);
+        case 2048: return f ? launch_t<2048, true>(p, grid, stream) : launch_t<2048, false>(p, grid, stream);
+        case 4096: return f ? launch_t<4096, true>(p, grid, stream) : launch_t<4096, false>(p, grid, stream);
         default: return int(cudaErrorInvalidValue);
     }
 }

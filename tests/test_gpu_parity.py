@@ -61,12 +61,15 @@ def test_closed_form_modes_bit_exact(native_lib, cuda_device, count, q):
     assert np.array_equal(batch.view(np.uint16), auto.view(np.uint16))
 
 
+@pytest.mark.parametrize("count", [16, 37])
 @pytest.mark.parametrize("candidate", [0, 1, 2, 3, 4, 5])
-def test_closed_form_every_candidate(native_lib, cuda_device, candidate):
+def test_closed_form_every_candidate(native_lib, cuda_device, candidate, count):
+    """Small grids give a CTA several slabs, so its stage ring wraps while
+    some warps still wait for h (persistent_mlp_test.cu:62 sweeps workers)."""
     from leanstream_b200 import _native as N
 
-    y = _closed_case(16, 1, N.MODE_PROGRESSIVE, candidate=candidate, shuffled=True)
-    ref = _closed_case(16, 1, N.MODE_BATCH_COMPAT, candidate=candidate)
+    y = _closed_case(count, 1, N.MODE_PROGRESSIVE, candidate=candidate, shuffled=True)
+    ref = _closed_case(count, 1, N.MODE_BATCH_COMPAT, candidate=candidate)
     assert np.array_equal(y.view(np.uint16), ref.view(np.uint16))
 
 
@@ -95,13 +98,22 @@ def _seeded_parity(H, n_groups, ids, seed, candidate=-1, core=0):
     bound = TOL * np.abs(ref).max()
     assert err <= bound, (err, bound)
     assert np.abs(y32 - y_ref32).max() <= TOL * np.abs(y_ref32).max()
-    # h activations: identical fp16 except rare one-ulp flips from summation order
+    # h activations. Candidate 5 rounds every weight to fp16(q*s) before the
+    # product, as the reference does: identical fp16 h except rare one-ulp
+    # flips from summation order. The other candidates apply the fp16 scale
+    # once per 128-block after an exact integer-weight sum; g then differs from
+    # the reference's rounded-weight sum by ~1e-4 relative, which flips about
+    # half of the fp16 roundings of g/u/h by one step -- bounded here, and
+    # far inside the output tolerance checked above.
     act = buf.act.cpu().numpy().reshape(n_groups, G)
     href = h_ref.reshape(n_groups, G)
     sel = np.asarray([r[3] for r in rows])
     a, b = act[sel].astype(np.float32), href[sel].astype(np.float32)
     mism = np.mean(a != b)
-    assert mism < 0.05, mism
+    if candidate == 5:
+        assert mism < 0.05, mism
+    else:
+        assert mism < 0.75, mism
     assert np.abs(a - b).max() <= 2 * np.abs(b).max() * 2.0 ** -10
     execs = buf.execs.cpu().numpy()
     assert np.all(execs[sel] == 1) and execs.sum() == len(rows)
