@@ -66,7 +66,9 @@ struct Backend {
     ls_b200_layer_args bound{};
     bool bound_set = false;
     // scratch (device) and mapped words (host)
-    float* partial = nullptr;
+    unsigned long long* partial = nullptr;  // tagged slab partial rows
+    unsigned long long* xbuf = nullptr;     // tagged layer output handed to the next layer
+    size_t partial_bytes = 0, xbuf_bytes = 0;
     uint32_t* ws = nullptr;
     uint32_t seq = 0;
     uint32_t* status_host = nullptr;
@@ -96,11 +98,13 @@ struct Backend {
     }
     void release() {
         if (partial) cudaFree(partial);
+        if (xbuf) cudaFree(xbuf);
         if (ws) cudaFree(ws);
         if (status_host) cudaFreeHost(status_host);
         if (done_host) cudaFreeHost(done_host);
         delete[] last_epoch;
         partial = nullptr;
+        xbuf = nullptr;
         ws = nullptr;
         status_host = status_dev = nullptr;
         done_host = done_dev = nullptr;
@@ -131,13 +135,19 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     b.geo = g;
     if (!b.geo.max_layers) b.geo.max_layers = 256;
     if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
-    // one fp32 partial output row per slab of every descriptor row
-    const size_t partial_bytes = size_t(N) * slabs_per_group(G) * H * sizeof(float);
+    // one tagged fp32 partial output row per slab of every descriptor row,
+    // and one tagged fp16 pair per two hidden coordinates; tag 0 never occurs
+    const size_t partial_bytes = size_t(N) * slabs_per_group(G) * H * sizeof(unsigned long long);
+    const size_t xbuf_bytes = size_t(H / 2) * sizeof(unsigned long long);
     const size_t ws_bytes = size_t(ws_words(b.geo.max_layers)) * sizeof(uint32_t);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&b.xbuf, xbuf_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.xbuf, 0, xbuf_bytes);
+    b.partial_bytes = partial_bytes;
+    b.xbuf_bytes = xbuf_bytes;
     if (e == cudaSuccess) e = cudaHostAlloc(&b.status_host, 64, cudaHostAllocMapped);
     if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b.status_dev), b.status_host, 0);
     if (e == cudaSuccess)
@@ -155,7 +165,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
         b.release();
         return ENOMEM;
     }
-    b.scratch_bytes = partial_bytes + ws_bytes;
+    b.scratch_bytes = partial_bytes + xbuf_bytes + ws_bytes;
     b.configured = true;
     return 0;
 }
@@ -204,7 +214,7 @@ int encode(const Backend& b, const ls_b200_layer_args& a, LayerPlan* out) {
     return 0;
 }
 
-KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace) {
+KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace, cudaStream_t stream) {
     KernelParams p{};
     p.H = b.geo.hidden;
     p.G = b.geo.group_size;
@@ -217,8 +227,17 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace) {
     p.eps = b.geo.rms_eps;
     p.nlayers = nlayers;
     p.max_layers = b.geo.max_layers;
-    p.seq = ++b.seq;
+    // Scratch words carry tag (seq mod 2^24) << 8 | layer. When the sequence
+    // wraps, the scratch is cleared on the stream (no allocation) so that no
+    // word written 2^24 launches earlier can carry a current tag.
+    p.seq = ++b.seq & kSeqMask;
+    if (p.seq == 0) {
+        cudaMemsetAsync(b.partial, 0, b.partial_bytes, stream);
+        cudaMemsetAsync(b.xbuf, 0, b.xbuf_bytes, stream);
+        p.seq = ++b.seq & kSeqMask;
+    }
     p.partial = b.partial;
+    p.xbuf = b.xbuf;
     p.ws = b.ws;
     p.status = b.status_dev;
     p.done = b.done_dev;
@@ -240,7 +259,7 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     LayerPlan plan;
     int rc = encode(b, a, &plan);
     if (rc) return rc;
-    KernelParams p = base_params(b, 1, a.trace);
+    KernelParams p = base_params(b, 1, a.trace, stream);
     p.plans = nullptr;
     p.first = plan;
     b.last_epoch[a.layer] = a.epoch;
@@ -357,7 +376,7 @@ int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count
         if (hp[i].layer >= b->geo.max_layers || !hp[i].epoch) return EINVAL;
         b->last_epoch[hp[i].layer] = hp[i].epoch;
     }
-    lsb::KernelParams p = lsb::base_params(*b, count, trace);
+    lsb::KernelParams p = lsb::base_params(*b, count, trace, static_cast<cudaStream_t>(stream));
     p.plans = static_cast<const lsb::LayerPlan*>(device_plans);
     p.first = hp[0];
     const int grid = lsb::grid_for(*b, candidate, &p.variant);

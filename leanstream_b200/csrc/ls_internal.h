@@ -19,12 +19,13 @@ constexpr uint32_t kSlab = 16;
 
 // Shared-memory ring: a stage holds either the gate+up records of 8 neurons
 // (pitch H + 16 bytes) or the down rows of one slab (pitch H/2 + 16 bytes),
-// plus an auxiliary area with the stage's fp16 scales (<= 1 KB) and the
-// GATEUP warp partials (1 KB). Six stages = two slabs of H = 4096 in flight.
+// plus an auxiliary area with the stage's fp16 scales (one row per neuron,
+// padded by 16 bytes so that the rows start in different banks; <= 1280 B)
+// and the GATEUP warp partials (1 KB). Six stages = two slabs of H = 4096.
 constexpr int kStages = 6;
 constexpr int kStageData = 33024;  // 16 x (2048 + 16) = 8 x (4096 + 16) + 128
-constexpr int kStageAux = 2048;
-constexpr int kAuxPartials = 1024;  // aux offset of the GATEUP warp partials
+constexpr int kStageAux = 2304;
+constexpr int kAuxPartials = 1280;  // aux offset of the GATEUP warp partials
 constexpr int kStageBytes = kStageData + kStageAux;
 constexpr int kMaxGroupSize = 256;
 constexpr int kMaxHidden = 4096;
@@ -53,7 +54,8 @@ struct alignas(16) LayerPlan {
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
-constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, partial-rows-done CTAs, reduced column blocks
+constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, (unused), reduced column blocks
+constexpr uint32_t kSeqMask = 0xFFFFFFu;  // launch sequence bits inside scratch tags
 __host__ __device__ inline uint32_t ws_words(uint32_t max_layers) { return kWsHeader + kWsPerLayer * max_layers; }
 
 // Slabs per group and partial rows of the scratch buffer.
@@ -70,7 +72,8 @@ struct KernelParams {
     uint32_t max_layers;  // workspace capacity
     uint32_t seq;         // launch sequence number (status word)
     uint32_t variant;     // 1: scales applied per 128-block after the tensor-core sums; 0: fp16(q*s) weights
-    float* partial;       // [N * slabs_per_group(G)][H] fp32 slab partial rows
+    unsigned long long* partial;  // [N * slabs_per_group(G)][H] tagged fp32 slab partial rows
+    unsigned long long* xbuf;     // [H/2] tagged fp16 pairs: a layer's hidden_out for the next layer
     uint32_t* ws;         // workspace words
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
     uint32_t* done;       // mapped host per-layer completion epochs

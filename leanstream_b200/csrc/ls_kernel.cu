@@ -88,6 +88,8 @@ struct DescView {
     uint32_t phys, dest, row, ok;
 };
 
+constexpr int kXPlane = kMaxHidden + 32;  // bytes per digit plane of the fixed-point activation
+
 struct SmemTail {
     unsigned long long full_bar[kStages];
     unsigned long long empty_bar[kStages];
@@ -95,8 +97,14 @@ struct SmemTail {
     Piece piece[kStages];
     DescView dtab[32];        // producer's descriptor window
     uint32_t gcnt[kStages];   // warps done with a GATEUP piece (per stage)
-    alignas(16) uint4 xf[kMaxHidden / 8];  // activation in B-fragment order, 8 coordinates per entry
-    float xs32[kMaxHidden / 32];           // fp32 sum of each 32-coordinate sub-block of x
+    // Activation of the current layer in B-fragment order (see stage_x):
+    // variant 1: three planes of signed 8-bit digits, uint2 per 8 coordinates,
+    //            planes kXPlane bytes apart (8 banks apart);
+    // variant 0: uint4 of four fp16 pairs per 8 coordinates.
+    alignas(16) uint8_t xarea[3 * kXPlane];
+    int msum[kMaxHidden / 32];  // variant 1: sum of the fixed-point x over each 32-coordinate sub-block
+    int msum64[kMaxHidden / 64];  // variant 1: the same over each 64-coordinate group
+    float xscale;               // variant 1: x = fixed-point value * xscale
     float red[kConsumerWarps];             // RMSNorm warp sums
     float red2[kConsumerWarps][32];        // reduction warp sums
     __half hs[kSlab];                      // h of the slab being computed
@@ -142,6 +150,22 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ ulonglong2 ld_volatile_v2u64(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile_v2u64(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1,%2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long a) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
 }
 __device__ __forceinline__ void red_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -236,6 +260,13 @@ __device__ __forceinline__ float round16(float v) { return __half2float(__float2
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
     return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] claim [2] partial-rows-done CTAs [3] reduced blocks
 }
+// Tag of the scratch words written by launch-local layer l (never 0: seq >= 1).
+// A 64-bit word (tag << 32 | value) is written by one store, so a reader that
+// sees the current tag also sees the value: no fence or counter is needed.
+__device__ __forceinline__ uint32_t scratch_tag(const KernelParams& P, uint32_t l) {
+    return (P.seq << 8) | (l & 0xffu);
+}
+__device__ __forceinline__ bool grid_failed(const KernelParams& P) { return ld_acquire_gpu(P.ws + kWsErr) != 0; }
 __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
     if (P.trace) P.trace[size_t(blockIdx.x) * LS_B200_TRACE_WORDS + word] = gtimer();
 }
@@ -358,16 +389,25 @@ __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t ki
 
 // Scale copy granule: 16 bytes when every scale row and segment is 16-byte
 // aligned (H >= 1024: row pitch 3H/64 bytes), else the segment size.
+// Staged scale rows are padded by 16 bytes so that consecutive neurons' rows
+// start 4 banks apart (conflict-free reads by the MMA lane layout).
 template <int H>
 struct ScaleCopy {
     static constexpr int kUnit = H >= 1024 ? 16 : H / 64;
     static constexpr uint32_t kRow = 3 * H / 64;   // bytes of one neuron's scales
     static constexpr uint32_t kGateUp = H / 32;    // gate + up scale bytes of one neuron
     static constexpr uint32_t kDown = H / 64;      // down scale bytes of one neuron
+    static constexpr uint32_t kGateUpPitch = kGateUp + 16;
+    static constexpr uint32_t kDownPitch = kDown + 16;
 };
 
+// Row pitch of a staged GATEUP record: variant 1 reads 8 bytes per lane, so
+// rows start 8 banks apart (H + 32); variant 0 reads 4 bytes (H + 16).
+template <int H, bool F>
+__host__ __device__ constexpr int gateup_pitch() { return F ? H + 32 : H + 16; }
+
 // GATEUP piece: gate+up records of neurons [n0, n0+cnt) (cnt <= 8).
-template <int H>
+template <int H, bool F>
 __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
                                 uint32_t layer, uint32_t n0, uint32_t cnt) {
     if (!producer_acquire_stage(pr, P)) return false;
@@ -386,7 +426,7 @@ __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const Layer
         trace_piece(P, pr.idx, 0);
         mbar_arrive_expect_tx(bar, cnt * H);
         for (uint32_t k = 0; k < cnt; ++k)
-            bulk_g2s(smem_u32(st + size_t(k) * (H + 16)), d.src + (n0 + k) * rec, H, bar);
+            bulk_g2s(smem_u32(st + size_t(k) * gateup_pitch<H, F>()), d.src + (n0 + k) * rec, H, bar);
     }
     using SC = ScaleCopy<H>;
     constexpr uint32_t upn = SC::kGateUp / SC::kUnit;
@@ -394,7 +434,7 @@ __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const Layer
     const uint32_t sdst = smem_u32(st + kStageData);
     for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
         const uint32_t k = i / upn, o = i % upn;
-        cp_async<SC::kUnit>(sdst + k * SC::kGateUp + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
+        cp_async<SC::kUnit>(sdst + k * SC::kGateUpPitch + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
     }
     producer_close(pr, P, s);
     ++pr.idx;
@@ -433,7 +473,7 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
     const uint32_t sdst = smem_u32(st + kStageData);
     for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
         const uint32_t r = i / upn, o = i % upn;
-        cp_async<SC::kUnit>(sdst + r * SC::kDown + o * SC::kUnit, sbase + r * SC::kRow + o * SC::kUnit);
+        cp_async<SC::kUnit>(sdst + r * SC::kDownPitch + o * SC::kUnit, sbase + r * SC::kRow + o * SC::kUnit);
     }
     producer_close(pr, P, s);
     ++pr.idx;
@@ -441,14 +481,14 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
 }
 
 // All pieces of slab `slab` of one descriptor.
-template <int H>
+template <int H, bool F>
 __device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
                               uint32_t layer, uint32_t slab) {
     const uint32_t spg = slabs_per_group(P.G);
     const uint32_t n0 = slab * kSlab;
     const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
-    if (!producer_gateup<H>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u) || pr.t->abort) return false;
-    if (cnt > 8u && (!producer_gateup<H>(pr, P, L, d, layer, n0 + 8, cnt - 8) || pr.t->abort)) return false;
+    if (!producer_gateup<H, F>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u) || pr.t->abort) return false;
+    if (cnt > 8u && (!producer_gateup<H, F>(pr, P, L, d, layer, n0 + 8, cnt - 8) || pr.t->abort)) return false;
     const uint32_t flags = slab + 1 == spg ? kCompletes : 0u;
     return producer_down<H>(pr, P, L, d, layer, n0, cnt, d.row * spg + slab, flags) && !pr.t->abort;
 }
@@ -527,7 +567,7 @@ __device__ void stamp(const LayerPlan& L, const DescView& d) {
 }
 
 // Producer warp main loop over the layers of the launch.
-template <int H>
+template <int H, bool F>
 __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     Producer pr;
     pr.idx = 0;
@@ -561,7 +601,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 if (!ok) break;
                 const DescView dv = t->dtab[d - pr.wbase];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
-                ok = producer_slab<H>(pr, P, L, dv, l, slab);
+                ok = producer_slab<H, F>(pr, P, L, dv, l, slab);
             }
         } else {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(L.q.control);
@@ -594,7 +634,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 if (!ok) break;
                 const DescView dv = t->dtab[0];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
-                ok = producer_slab<H>(pr, P, L, dv, l, slab);
+                ok = producer_slab<H, F>(pr, P, L, dv, l, slab);
             }
             if (t->abort) ok = false;
         }
@@ -645,18 +685,50 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
 // Loads the layer's input, applies the HF RMSNorm of
 // predictor_shared_input.cu:16-33 when flagged
 // (inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv))), and
-// stores it in B-fragment order: entry u = coordinates 8u..8u+7 as half2
-// pairs (0,4) (1,5) (2,6) (3,7); xs32[b] = fp32 sum of sub-block b.
-// Every CTA computes the same sum in the same order.
-template <int H>
+// stores it in the B-fragment order of the gate/up MMAs, thread u handling
+// coordinates 8u..8u+7 (sub-block u/4, lane quad position u%4):
+//   variant 1: x' as 22-bit fixed point, M = rint(x' * 2^(21-E)) with E the
+//     exponent of max|x'| (so |M| < 2^22, exact for every x' within 2^12 of
+//     the maximum and within 2^-22 * max|x'| otherwise), split into three
+//     balanced signed 8-bit digits M = d0 + 256 d1 + 65536 d2; plane p holds,
+//     per unit, the digits of coordinates (0,2,4,6) and (1,3,5,7);
+//   variant 0: fp16 pairs (0,4) (1,5) (2,6) (3,7).
+// Every CTA computes the same values in the same order.
+// `tagged` (chained layers): the input is the previous layer's output, read
+// from the tagged scratch copy as soon as its words carry `tag` -- no
+// grid-wide barrier between layers.
+template <int H, bool F>
 __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t& cph, uint64_t limit,
-                        int tid) {
+                        int tid, bool tagged, uint32_t tag) {
     constexpr int NU = H / 8;  // one 8-coordinate unit per thread (H <= 4096)
     const int warp = tid >> 5, lane = tid & 31;
     uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     float ss = 0.f;
     if (tid < NU) {
-        raw = __ldcg(reinterpret_cast<const uint4*>(L.x) + tid);
+        if (tagged) {
+            const unsigned long long* src = P.xbuf + 4 * tid;
+            ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
+            uint32_t spins = 0;
+            for (;;) {
+                const bool ok = uint32_t(a.x >> 32) == tag && uint32_t(a.y >> 32) == tag &&
+                                uint32_t(b.x >> 32) == tag && uint32_t(b.y >> 32) == tag;
+                if (__all_sync(0xffffffffu, ok)) break;
+                uint32_t late = 0;
+                if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit)) late = 1;
+                if (__shfl_sync(0xffffffffu, late, 0)) {
+                    if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 6);
+                    break;
+                }
+                __nanosleep(32);
+                if (!ok) {
+                    a = ld_volatile_v2u64(src);
+                    b = ld_volatile_v2u64(src + 2);
+                }
+            }
+            raw = make_uint4(uint32_t(a.x), uint32_t(a.y), uint32_t(b.x), uint32_t(b.y));
+        } else {
+            raw = __ldcg(reinterpret_cast<const uint4*>(L.x) + tid);
+        }
         const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -676,43 +748,100 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         for (int w = 0; w < kConsumerWarps; ++w) tot += t->red[w];
         inv = rsqrtf(tot / float(H) + P.eps);
     }
-    if (tid < NU) {
-        __half v[8];
+    __half v[8];
+    {
         const __half* h = reinterpret_cast<const __half*>(&raw);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = norm ? __float2half_rn(__half2float(h[e]) * inv) : h[e];
-        if (norm && L.norm_w) {
+        if (norm && L.norm_w && tid < NU) {
             const uint4 nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + tid);
             const __half* wh = reinterpret_cast<const __half*>(&nw);
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
         }
-        uint4 f;
-        f.x = h2_bits(__halves2half2(v[0], v[4]));
-        f.y = h2_bits(__halves2half2(v[1], v[5]));
-        f.z = h2_bits(__halves2half2(v[2], v[6]));
-        f.w = h2_bits(__halves2half2(v[3], v[7]));
-        t->xf[tid] = f;
-        float xsum = 0.f;
+    }
+    if constexpr (F) {
+        // block maximum of |x'| -> exponent E (the same in every CTA)
+        float mx = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xsum += __half2float(v[e]);
-        xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
-        xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
-        if ((tid & 3) == 0) t->xs32[tid >> 2] = xsum;
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(__half2float(v[e])));
+#pragma unroll
+        for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (lane == 0) t->red2[0][warp] = mx;
+        csync(P, t, cph, limit, lane);
+        mx = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, t->red2[0][w]);
+        const int E = mx > 0.f ? int((__float_as_uint(mx) >> 23) & 0xffu) - 127 : 0;
+        const float up = __uint_as_float(uint32_t(127 + 21 - E) << 23);    // 2^(21-E)
+        if (tid == 0) t->xscale = __uint_as_float(uint32_t(127 - 21 + E) << 23);  // 2^(E-21)
+        if (tid < NU) {
+            uint32_t pe[3] = {0u, 0u, 0u}, po[3] = {0u, 0u, 0u};
+            int msum = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int m = __float2int_rn(__half2float(v[e]) * up);
+                msum += m;
+                const int d0 = int(int8_t(m & 0xff));
+                const int m1 = (m - d0) >> 8;
+                const int d1 = int(int8_t(m1 & 0xff));
+                const int d2 = (m1 - d1) >> 8;
+                const int sh = 8 * (e >> 1);
+                uint32_t* dst = (e & 1) ? po : pe;
+                dst[0] |= uint32_t(d0 & 0xff) << sh;
+                dst[1] |= uint32_t(d1 & 0xff) << sh;
+                dst[2] |= uint32_t(d2 & 0xff) << sh;
+            }
+#pragma unroll
+            for (int p = 0; p < 3; ++p)
+                reinterpret_cast<uint2*>(t->xarea + p * kXPlane)[tid] = make_uint2(pe[p], po[p]);
+            msum += __shfl_xor_sync(0xffffffffu, msum, 1);
+            msum += __shfl_xor_sync(0xffffffffu, msum, 2);
+            if ((tid & 3) == 0) t->msum[tid >> 2] = msum;
+            msum += __shfl_xor_sync(0xffffffffu, msum, 4);
+            if ((tid & 7) == 0) t->msum64[tid >> 3] = msum;
+        }
+    } else {
+        if (tid < NU) {
+            uint4 f;
+            f.x = h2_bits(__halves2half2(v[0], v[4]));
+            f.y = h2_bits(__halves2half2(v[1], v[5]));
+            f.z = h2_bits(__halves2half2(v[2], v[6]));
+            f.w = h2_bits(__halves2half2(v[3], v[7]));
+            reinterpret_cast<uint4*>(t->xarea)[tid] = f;
+        }
     }
     csync(P, t, cph, limit, lane);
 }
 
+// Tensor-core step on 8-bit integers: D(16x8,s32) += A(16x32,u8) * B(32x8,s8).
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // GATEUP piece: warp w reduces sub-blocks [w*SBW, (w+1)*SBW) (32 hidden
-// coordinates each) for the piece's 8 neurons; the last warp to finish sums
-// the warp partials in warp order and forms h.
+// coordinates each) for the piece's 8 neurons (MMA rows 0-7: gate rows,
+// 8-15: up rows); the last warp to finish sums the warp partials in warp
+// order and forms h.
+//   variant 1: one integer MMA per sub-block. A = q + 8 as unsigned bytes
+//     (one LOP3 per four weights: the low nibbles of a word are coordinates
+//     0,2,4,6, the high nibbles 1,3,5,7); B column p = digit plane p of the
+//     fixed-point x (p < 3), other columns 0. Per scale block the exact
+//     integer sums give sum(q M) = D0 + 256 D1 + 65536 D2 - 8 sum(M); the
+//     fp16 scale and 2^(E-21) are applied to that once.
+//   variant 0: fp16 MMAs on w = fp16(q * s) (backends/triton/core.py:17).
 template <int H, bool F>
 __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, uint8_t* st, SmemTail* t,
                                uint32_t s, int warp, int lane) {
     constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
     constexpr int CH = SBW < 4 ? SBW : 4;  // sub-blocks per scale block handled at once
-    constexpr int PG = H + 16;
-    constexpr int SPN = 2 * (H / 128);  // scale halves per neuron (gate, then up)
+    constexpr int PG = gateup_pitch<H, F>();
+    constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;  // staged scale row (gate, up, pad) in halves
     const int g = lane >> 2, tq = lane & 3;
     float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxPartials);  // [warp][8]
     __syncwarp();  // mma.sync is .aligned: enter converged whatever the caller's waits did
@@ -720,46 +849,107 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
         const uint8_t* rowg = st + g * PG + 4 * tq;
         const __half* sc = reinterpret_cast<const __half*>(st + kStageData) + g * SPN;
         float pg = 0.f, pu = 0.f;
+        if constexpr (F) {
+            // Chunks of CH sub-blocks (one scale block, or the warp's share
+            // of one), their MMA chains interleaved. Low nibbles give
+            // A = q + 8, high nibbles (masked in place, no shift) 16 (q + 8):
+            // two exact integer accumulators, combined as lo + hi / 16.
+            // B columns 3..7 are never read, so lanes g >= 3 load any plane.
+            constexpr int NC = SBW / CH;
+            int alo[NC][4], ahi[NC][4];
+            int ms[NC];
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                alo[c][0] = alo[c][1] = alo[c][2] = alo[c][3] = 0;
+                ahi[c][0] = ahi[c][1] = ahi[c][2] = ahi[c][3] = 0;
+            }
+            const uint8_t* xp = t->xarea + (g < 3 ? g : 0) * kXPlane;
+            if constexpr (CH >= 2) {
+                // 64-coordinate groups: lane t reads bytes 8t..8t+7 of a row
+                // (coordinates 16t..16t+15) with one 8-byte load, and the
+                // matching digits (two 8-coordinate units) with one 16-byte load.
+                constexpr int DC = CH / 2;
+                const uint8_t* row2 = st + g * PG + 8 * tq;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int d0 = (warp * SBW + c * CH) / 2;
+                    ms[c] = t->msum64[d0];
+                    if constexpr (DC == 2) ms[c] += t->msum64[d0 + 1];
+                }
+#pragma unroll
+                for (int dj = 0; dj < DC; ++dj) {
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        const int dg = (warp * SBW + c * CH) / 2 + dj;
+                        const uint2 wg = *reinterpret_cast<const uint2*>(row2 + 32 * dg);
+                        const uint2 wu = *reinterpret_cast<const uint2*>(row2 + H / 2 + 32 * dg);
+                        const uint4 xb = reinterpret_cast<const uint4*>(xp)[4 * dg + tq];
+                        // even coordinates of both units, then odd ones
+                        imma16832(alo[c], (wg.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wu.x & 0x0F0F0F0Fu) ^ 0x08080808u,
+                                  (wg.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wu.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
+                        imma16832(ahi[c], (wg.x & 0xF0F0F0F0u) ^ 0x80808080u, (wu.x & 0xF0F0F0F0u) ^ 0x80808080u,
+                                  (wg.y & 0xF0F0F0F0u) ^ 0x80808080u, (wu.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int sb = warp * SBW + c;
+                    const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
+                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
+                    const uint2 xb = reinterpret_cast<const uint2*>(xp)[sb * 4 + tq];
+                    ms[c] = t->msum[sb];
+                    imma16832(alo[c], (wg & 0x0F0F0F0Fu) ^ 0x08080808u, (wu & 0x0F0F0F0Fu) ^ 0x08080808u,
+                              ((wg >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wu >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                              xb.y);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int blk = (warp * SBW + c * CH) / 4;
+                // per digit plane p (B column p): lo + hi / 16 (exact in fp32);
+                // lane (g, 0) holds planes 0,1, lane (g, 1) plane 2
+                float dv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dv[e] = fmaf(0.0625f, float(ahi[c][e]), float(alo[c][e]));
+                const float dg2 = __shfl_down_sync(0xffffffffu, dv[0], 1);
+                const float du2 = __shfl_down_sync(0xffffffffu, dv[2], 1);
+                const float m8 = 8.f * float(ms[c]);
+                const float rg = fmaf(dg2, 65536.f, fmaf(dv[1], 256.f, dv[0])) - m8;
+                const float ru = fmaf(du2, 65536.f, fmaf(dv[3], 256.f, dv[2])) - m8;
+                pg = fmaf(__half2float(sc[blk]), rg, pg);
+                pu = fmaf(__half2float(sc[H / 128 + blk]), ru, pu);
+            }
+        }
 #pragma unroll
         for (int j0 = 0; j0 < SBW; j0 += CH) {
             const int blk = (warp * SBW + j0) / 4;
-            float al[4] = {0.f, 0.f, 0.f, 0.f}, ah[4] = {0.f, 0.f, 0.f, 0.f};
-            float X = 0.f;
-            __half2 sg2, su2;
-            if constexpr (!F) {
-                sg2 = __half2half2(sc[blk]);
-                su2 = __half2half2(sc[H / 128 + blk]);
-            }
+            if constexpr (F) {
+            } else {
+                float al[4] = {0.f, 0.f, 0.f, 0.f};
+                const __half2 sg2 = __half2half2(sc[blk]), su2 = __half2half2(sc[H / 128 + blk]);
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
-                const int sb = warp * SBW + j0 + j;
-                const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
-                const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
-                const uint4 xv = t->xf[sb * 4 + tq];
-                const uint32_t wg8 = wg >> 8, wu8 = wu >> 8;
-                if constexpr (F) {
-                    X += t->xs32[sb];
-                    // even coordinates (0,4),(2,6) and odd (1,5),(3,7) in separate sums
-                    mma16816(al, sub_lo(wg), sub_lo(wu), sub_lo(wg8), sub_lo(wu8), xv.x, xv.z);
-                    mma16816(ah, sub_hi(wg), sub_hi(wu), sub_hi(wg8), sub_hi(wu8), xv.y, xv.w);
-                } else {
+                for (int j = 0; j < CH; ++j) {
+                    const int sb = warp * SBW + j0 + j;
+                    const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
+                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
+                    const uint4 xv = reinterpret_cast<const uint4*>(t->xarea)[sb * 4 + tq];
+                    const uint32_t wg8 = wg >> 8, wu8 = wu >> 8;
                     const uint32_t g0 = h2_bits(__hmul2(int_lo(wg), sg2)), g1 = h2_bits(__hmul2(int_hi(wg), sg2));
                     const uint32_t g2 = h2_bits(__hmul2(int_lo(wg8), sg2)), g3 = h2_bits(__hmul2(int_hi(wg8), sg2));
                     const uint32_t u0 = h2_bits(__hmul2(int_lo(wu), su2)), u1 = h2_bits(__hmul2(int_hi(wu), su2));
                     const uint32_t u2 = h2_bits(__hmul2(int_lo(wu8), su2)), u3 = h2_bits(__hmul2(int_hi(wu8), su2));
+                    // pairs (0,4),(2,6) then (1,5),(3,7) of the 8 coordinates 8t..8t+7
                     mma16816(al, g0, u0, g2, u2, xv.x, xv.z);
                     mma16816(al, g1, u1, g3, u3, xv.y, xv.w);
                 }
-            }
-            if constexpr (F) {
-                const float sg = __half2float(sc[blk]), su = __half2float(sc[H / 128 + blk]);
-                // D = sum (q + 8) x  (even: x 2^-24, odd: x 16 * 2^-24)
-                pg = fmaf(sg, fmaf(16777216.f, al[0], fmaf(1048576.f, ah[0], -8.f * X)), pg);
-                pu = fmaf(su, fmaf(16777216.f, al[2], fmaf(1048576.f, ah[2], -8.f * X)), pu);
-            } else {
                 pg += al[0];
                 pu += al[2];
             }
+        }
+        if constexpr (F) {
+            pg *= t->xscale;
+            pu *= t->xscale;
         }
         if (tq == 0) part[warp * 8 + g] = make_float2(pg, pu);
     }
@@ -794,16 +984,18 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
 }
 
 // DOWN piece: warp w owns 64-column tiles [w*TPW, (w+1)*TPW); in each, lane
-// (g, t) reads the 8 columns 8g..8g+7 of neurons 2t, 2t+1, 2t+8, 2t+9, pairs
-// the two neurons of each column with PRMT and runs four 16-neuron MMAs
-// (MMA j: columns 8g+j and 8g+j+4). The slab's partial row goes to global
-// memory, 256 contiguous bytes per warp and tile.
+// (g, t) reads the 8 columns 8g..8g+7 of neurons 2t, 2t+1, 2t+8, 2t+9 and
+// pairs the two neurons of each column with PRMT. MMA j (columns 8g+j and
+// 8g+j+4 as rows g and g+8 of A) gets a B that is nonzero only in its own
+// columns 2j (the fp16 value of h * s, or h) and 2j+1 (the fp16 residual of
+// h * s), so the four MMAs of a tile share one accumulator and lane (g, t)
+// ends with columns 8g+t and 8g+t+4 -- every lane stores two tagged words.
 template <int H, bool F>
 __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8_t* st, const SmemTail* t, int warp,
                              int lane) {
     constexpr int NT = H / 64, DW = NT < kConsumerWarps ? NT : kConsumerWarps, TPW = NT / DW;
     constexpr int PD = H / 2 + 16;
-    constexpr int SPN = H / 128;  // down scale halves per neuron
+    constexpr int SPN = ScaleCopy<H>::kDownPitch / 2;  // staged down-scale row in halves
     if (warp >= DW) return;
     __syncwarp();  // mma.sync is .aligned: enter converged
     const int g = lane >> 2, tq = lane & 3;
@@ -813,9 +1005,11 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     const __half hv0 = uint32_t(n0) < cnt ? t->hs[n0] : zero, hv1 = uint32_t(n1) < cnt ? t->hs[n1] : zero;
     const __half hv2 = uint32_t(n2) < cnt ? t->hs[n2] : zero, hv3 = uint32_t(n3) < cnt ? t->hs[n3] : zero;
     const __half* sd = reinterpret_cast<const __half*>(st + kStageData);
-    float* out = P.partial + size_t(pc.row) * H;
-    uint32_t b0 = 0, b1 = 0, r0 = 0, r1 = 0, s01 = 0, s23 = 0;
-    float hsum = 0.f;
+    unsigned long long* out = P.partial + size_t(pc.row) * H;
+    const unsigned long long tag = static_cast<unsigned long long>(scratch_tag(P, pc.layer)) << 32;
+    const int mine = g >> 1;  // the MMA whose B column g this lane supplies
+    uint32_t bj0[4] = {0u, 0u, 0u, 0u}, bj1[4] = {0u, 0u, 0u, 0u}, s01 = 0, s23 = 0;
+    float hsum8 = 0.f;
 #pragma unroll
     for (int i = 0; i < TPW; ++i) {
         const int tile = warp * TPW + i;
@@ -825,31 +1019,36 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
             const __half c1 = uint32_t(n1) < cnt ? sd[n1 * SPN + blk] : zero;
             const __half c2 = uint32_t(n2) < cnt ? sd[n2 * SPN + blk] : zero;
             const __half c3 = uint32_t(n3) < cnt ? sd[n3 * SPN + blk] : zero;
+            uint32_t v0, v1;
             if constexpr (F) {
-                // B carries h * s (exact in fp32) as an fp16 value plus its
-                // fp16 residual, fed to two MMAs into the same accumulator;
-                // the +8 offset of A is removed with their sum over the slab.
+                // h * s is exact in fp32; split it into an fp16 value (even B
+                // columns) and an fp16 residual (odd B columns). The +8 offset
+                // of A is removed with their sum over the slab's 16 neurons.
                 const float f[4] = {__half2float(hv0) * __half2float(c0), __half2float(hv1) * __half2float(c1),
                                     __half2float(hv2) * __half2float(c2), __half2float(hv3) * __half2float(c3)};
                 __half hi[4], lo[4];
-                hsum = 0.f;
+                float hsum = 0.f;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     hi[e] = __float2half_rn(f[e]);
                     lo[e] = __float2half_rn(f[e] - __half2float(hi[e]));
                     hsum += __half2float(hi[e]) + __half2float(lo[e]);
                 }
-                b0 = h2_bits(__halves2half2(hi[0], hi[1]));
-                b1 = h2_bits(__halves2half2(hi[2], hi[3]));
-                r0 = h2_bits(__halves2half2(lo[0], lo[1]));
-                r1 = h2_bits(__halves2half2(lo[2], lo[3]));
+                v0 = (g & 1) ? h2_bits(__halves2half2(lo[0], lo[1])) : h2_bits(__halves2half2(hi[0], hi[1]));
+                v1 = (g & 1) ? h2_bits(__halves2half2(lo[2], lo[3])) : h2_bits(__halves2half2(hi[2], hi[3]));
                 hsum += __shfl_xor_sync(0xffffffffu, hsum, 1);
                 hsum += __shfl_xor_sync(0xffffffffu, hsum, 2);
+                hsum8 = -8.f * hsum;
             } else {
-                b0 = h2_bits(__halves2half2(hv0, hv1));
-                b1 = h2_bits(__halves2half2(hv2, hv3));
+                v0 = (g & 1) ? 0u : h2_bits(__halves2half2(hv0, hv1));
+                v1 = (g & 1) ? 0u : h2_bits(__halves2half2(hv2, hv3));
                 s01 = h2_bits(__halves2half2(c0, c1));
                 s23 = h2_bits(__halves2half2(c2, c3));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                bj0[j] = j == mine ? v0 : 0u;
+                bj1[j] = j == mine ? v1 : 0u;
             }
         }
         const uint8_t* base = st + 32 * tile + 4 * g;
@@ -863,7 +1062,9 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
         uint32_t a01[8], a23[8];  // column c: (neuron 2t, 2t+1) and (2t+8, 2t+9)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t x = p01[hh], x8 = x >> 8, y = p23[hh], y8 = y >> 8;
+            // bytes 1 and 3 moved down by one byte: (v * 2^24) >> 32 runs on the
+            // FMA pipe, leaving the integer pipe to the nibble masks
+            const uint32_t x = p01[hh], x8 = __umulhi(x, 1u << 24), y = p23[hh], y8 = __umulhi(y, 1u << 24);
             if constexpr (F) {
                 a01[4 * hh + 0] = sub_lo(x);
                 a01[4 * hh + 1] = sub_hi(x);
@@ -885,75 +1086,96 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
                 a23[4 * hh + 3] = h2_bits(__hmul2(int_hi(y8), t23));
             }
         }
-        float acc[4][4];
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-            mma16816(acc[j], a01[j], a01[j + 4], a23[j], a23[j + 4], b0, b1);
-            if constexpr (F) mma16816(acc[j], a01[j], a01[j + 4], a23[j], a23[j + 4], r0, r1);
-        }
-        // lane (g, t) stores columns 8g + 2t, 8g + 2t + 1
-        const bool hi_half = (tq & 2) != 0, odd = (tq & 1) != 0;
-        const float m0 = hi_half ? acc[0][2] : acc[0][0], m1 = hi_half ? acc[1][2] : acc[1][0];
-        const float m2 = hi_half ? acc[2][2] : acc[2][0], m3 = hi_half ? acc[3][2] : acc[3][0];
-        float v0 = odd ? m2 : m0, v1 = odd ? m3 : m1;
+        for (int j = 0; j < 4; ++j) mma16816(acc, a01[j], a01[j + 4], a23[j], a23[j + 4], bj0[j], bj1[j]);
+        // D[g][2t] + D[g][2t+1]: column 8g + t; D[g+8][2t] + D[g+8][2t+1]: column 8g + t + 4
+        float v0 = acc[0] + acc[1], v1 = acc[2] + acc[3];
         if constexpr (F) {
-            v0 = fmaf(16777216.f, v0, -8.f * hsum);  // even column: (q + 8) 2^-24
-            v1 = fmaf(1048576.f, v1, -8.f * hsum);   // odd column: 16 (q + 8) 2^-24
+            const float k = (tq & 1) ? 1048576.f : 16777216.f;  // odd column: 16 (q + 8) 2^-24; even: (q + 8) 2^-24
+            v0 = fmaf(k, v0, hsum8);
+            v1 = fmaf(k, v1, hsum8);
         }
-        *reinterpret_cast<float2*>(out + 64 * tile + 8 * g + 2 * tq) = make_float2(v0, v1);
+        unsigned long long* o = out + 64 * tile + 8 * g + tq;
+        st_volatile_u64(o, tag | __float_as_uint(v0));
+        st_volatile_u64(o + 4, tag | __float_as_uint(v1));
     }
 }
 
-// End of layer l: partial rows -> reduction -> epilogue. Canonical sum per
-// column: rows in chunks of 16 (row order inside a chunk), chunk c added to
-// warp c % 16's running sum in chunk order, then the 16 warp sums in warp
-// order (reduction.py:6-28, streaming_mlp.cu:80-84 sum rows in row order).
+// End of layer l: partial rows -> reduction -> epilogue, on CTAs 0..H/32-1
+// (one 32-column block each). Each warp polls its rows until they carry the
+// layer's tag, so the reduction starts without a grid-wide barrier.
+// Canonical sum per column: rows in chunks of 16 (row order inside a chunk),
+// chunk c added to warp c % 16's running sum in chunk order, then the 16 warp
+// sums in warp order (reduction.py:6-28, streaming_mlp.cu:80-84 sum rows in
+// row order). With `chain`, hidden_out is also published as tagged fp16 pairs
+// for the next layer of the launch.
 template <int H>
 __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t rows, bool good,
-                          SmemTail* t, uint32_t& cph, uint64_t limit, int tid) {
+                          SmemTail* t, uint32_t& cph, uint64_t limit, int tid, bool chain) {
     constexpr uint32_t NBLK = H / 32;
     const int warp = tid >> 5, lane = tid & 31;
-    uint32_t* wl = ws_layer(P, l);
-    __threadfence();  // this warp's partial rows are visible at gpu scope
-    csync(P, t, cph, limit, lane);
-    if (tid == 0) red_release_gpu(wl + 2, 1u);
     if (blockIdx.x >= NBLK) return;
-    if (tid == 0) {
-        const bool ready = wait_count(P, t, wl + 2, gridDim.x, limit, 5);
-        t->flag = (ready ? 1u : 0u) | ((ready && good && ld_acquire_gpu(P.ws + kWsErr) == 0) ? 2u : 0u);
-        trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
-    }
-    csync(P, t, cph, limit, lane);
-    const uint32_t flag = t->flag;
+    const uint32_t tag = scratch_tag(P, l);
     const uint32_t nch = (rows + 15) / 16;
     for (uint32_t blk = blockIdx.x; blk < NBLK; blk += gridDim.x) {
         float acc = 0.f;
-        if (flag & 1u) {
-            for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
-                const float* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
-                const uint32_t nr = rows - 16 * c;
-                float v[16];
+        for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
+            const unsigned long long* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
+            const uint32_t nr = rows - 16 * c < 16u ? rows - 16 * c : 16u;
+            unsigned long long w[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] = uint32_t(e) < nr ? __ldcg(p + size_t(e) * H) : 0.f;
-                float cs = v[0];
+            for (int e = 0; e < 16; ++e)
+                w[e] = uint32_t(e) < nr ? ld_volatile_u64(p + size_t(e) * H) : (static_cast<unsigned long long>(tag) << 32);
+            uint32_t spins = 0;
+            for (;;) {
+                bool ok = true;
 #pragma unroll
-                for (int e = 1; e < 16; ++e) cs += v[e];
-                acc += cs;
+                for (int e = 0; e < 16; ++e) ok &= uint32_t(w[e] >> 32) == tag;
+                if (__all_sync(0xffffffffu, ok)) break;
+                uint32_t late = 0;
+                if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit)) late = 1;
+                if (__shfl_sync(0xffffffffu, late, 0)) {
+                    if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 5);
+                    break;
+                }
+                __nanosleep(64);
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    if (uint32_t(w[e] >> 32) != tag) w[e] = ld_volatile_u64(p + size_t(e) * H);
             }
+            float cs = __uint_as_float(uint32_t(w[0]));
+#pragma unroll
+            for (int e = 1; e < 16; ++e) cs += __uint_as_float(uint32_t(w[e]));
+            acc += cs;
         }
         t->red2[warp][lane] = acc;
         csync(P, t, cph, limit, lane);
-        if (warp == 0 && (flag & 2u)) {
+        if (warp == 0) {
+            if (blk == blockIdx.x && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
             float y = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
             const uint32_t c = 32 * blk + lane;
-            if (L.y32) L.y32[c] = y;
+            uint32_t write = 0;
+            if (lane == 0) write = (good && !grid_failed(P)) ? 1u : 0u;
+            write = __shfl_sync(0xffffffffu, write, 0);
             const __half y16 = __float2half_rn(y);
-            if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
-            if (L.hidden_out && L.residual)
-                L.hidden_out[c] = __half_as_ushort(__float2half_rn(h2f(__ldcg(L.residual + c)) + __half2float(y16)));
+            __half hout = y16;
+            if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(__ldcg(L.residual + c)) + __half2float(y16));
+            if (write) {
+                if (L.y32) L.y32[c] = y;
+                if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
+                if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
+            }
+            if (chain) {
+                // published even after an error so that the next layer's
+                // readers never wait for it; the error is reported anyway
+                const uint32_t mine = __half_as_ushort(hout);
+                const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
+                if ((lane & 1) == 0)
+                    st_volatile_u64(P.xbuf + c / 2, (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
+            }
         }
         csync(P, t, cph, limit, lane);  // red2 is reused by the next block
     }
@@ -961,7 +1183,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         __threadfence();
         __syncwarp();
         if (lane == 0) {
-            red_release_gpu(wl + 3, 1u);
+            red_release_gpu(ws_layer(P, l) + 3, 1u);  // reduced blocks (unchained next layers wait on it)
             trace_layer(P, l, LS_B200_LTRACE_REDUCED);
         }
     }
@@ -975,7 +1197,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    stage_x<H>(P, *L, t, cph, limit, tid);
+    stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % kStages;
         const uint32_t parity = (idx / kStages) & 1u;
@@ -1027,6 +1249,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
                     ok = false;
                     break;
                 }
+                __nanosleep(32);  // leave issue slots to the warp that finalises h
             }
             __threadfence_block();
             const bool aborted = __shfl_sync(0xffffffffu, t->abort, 0) != 0;
@@ -1041,16 +1264,23 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         if (pc.kind != kPieceLayer) continue;
 
         // ---- end of layer l: partial rows -> reduction -> next activation.
-        end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid);
-        if (l + 1 >= P.nlayers) continue;  // the FINAL marker follows
-        if (tid == 0) {
-            wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
-            trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
+        // Chained layers (the next input is this layer's hidden_out) hand the
+        // activation over through tagged words; otherwise every CTA waits
+        // until all column blocks are reduced and reads the next input.
+        const LayerPlan* next = l + 1 < P.nlayers ? &plan_at(P, l + 1) : nullptr;
+        const bool chain = next && L->hidden_out && L->residual &&
+                           reinterpret_cast<const void*>(next->x) == reinterpret_cast<const void*>(L->hidden_out);
+        end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid, chain);
+        if (!next) continue;  // the FINAL marker follows
+        if (!chain) {
+            if (tid == 0) wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
+            csync(P, t, cph, limit, lane);
         }
-        csync(P, t, cph, limit, lane);
+        if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
+        const uint32_t tag = scratch_tag(P, l);
         ++l;
-        L = &plan_at(P, l);
-        stage_x<H>(P, *L, t, cph, limit, tid);
+        L = next;
+        stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag);
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
     }
 }
@@ -1079,7 +1309,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     __syncthreads();
 
     if (tid >= kConsumerThreads) {
-        run_producer<H>(P, stages, t, deadline);
+        run_producer<H, F>(P, stages, t, deadline);
     } else {
         run_consumers<H, F>(P, stages, t, deadline);
     }
