@@ -41,6 +41,11 @@ FMIN, FMAX = 0.2, 0.4
 GROUP_BYTES = G * 3 * H // 2                  # packed INT4 bytes per group
 SCALE_BYTES = G * 3 * (H // 128) * 2          # fp16 scale bytes per group
 ALG_BYTES_PER_GROUP = GROUP_BYTES + SCALE_BYTES  # 405,504 B (algorithmic bytes)
+# dram__bytes_read.sum + dram__bytes_write.sum of one fused_mlp_kernel launch
+# (8-layer stack, token 3: 183.23 MB + 7.13 MB) divided by that launch's
+# algorithmic bytes (449 groups x 405,504 B = 182.07 MB): weights are read
+# once, the excess is tagged scratch evicted from L2.
+TRAFFIC_PER_ALG_BYTE = 1.0455
 SEED = 3
 EPS = 1e-5
 WORKLOAD = "config3: 36-layer MLP stack, H4096/I12288, 192x64 groups, 20-40% active/layer, batch 1"
@@ -59,8 +64,11 @@ def active_sets(step: int):
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    polled from a thread every 2 ms (the timed region lasts milliseconds), or
+    nvidia-smi at its 100 ms floor when NVML is unavailable. Read-only."""
 
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -68,8 +76,38 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.samples, self.reasons, self.smax = [], set(), None
+        self.stop_flag = False
+
+    def _nvml_loop(self, nv, handle):
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        while not self.stop_flag:
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)))
+                active = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.reasons.update(name for name, bit in bits.items() if active & bit)
+            except Exception:  # a failed query ends sampling, it never stops the bench
+                break
+            time.sleep(0.002)
 
     def start(self):
+        try:
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            handle = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, handle), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -77,7 +115,17 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def mark(self):
+        """Drops the samples taken so far: only the timed region counts."""
+        self.samples = []
+        self.reasons = set()
+
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.smax,
+                    "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -88,7 +136,6 @@ class ClockSampler:
             out, _ = self.proc.communicate()
         rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             r = [x.strip() for x in r]
             if len(r) < 9:
@@ -98,11 +145,11 @@ class ClockSampler:
                 smax = float(r[2])
             except ValueError:
                 continue
-            for name, val in zip(names, r[5:9]):
+            for name, val in zip(self.NAMES, r[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # --------------------------------------------------------------------- GPU arm
@@ -318,14 +365,15 @@ def run_gpu(args, rank, world, local_rank):
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    clocks.mark()
     with torch.cuda.stream(stream):
         e0.record(stream)
         for s in range(args.warmup, steps_total):
             graphs[s].replay()
         e1.record(stream)
     torch.cuda.synchronize()
-    barrier()
     clock = clocks.stop()
+    barrier()
     ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -419,12 +467,10 @@ def run_gpu(args, rank, world, local_rank):
             pass
         peak = float(peaks.get("hbm_gbs", 6650.0))
         mean_active = float(np.mean([sum(c) for c in st.active_local[args.warmup:]])) / LAYERS
-        traffic = None
-        try:
-            prof = json.loads((ROOT / "profiles" / "traffic.json").read_text())
-            traffic = prof.get("bytes_per_group") and prof["bytes_per_group"] * mean_active / world
-        except (OSError, ValueError):
-            traffic = None
+        # DRAM bytes (read + write) of one launch, from the ncu capture of
+        # the same kernel on an 8-layer stack, scaled by the algorithmic
+        # bytes the launch processes (traffic grows with the active groups).
+        traffic = TRAFFIC_PER_ALG_BYTE * float(np.mean(kern_bytes))
         result = {
             "metric": METRIC,
             "value": args.steps / (ms * 1e-3),

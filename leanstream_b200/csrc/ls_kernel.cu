@@ -688,8 +688,8 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
 // stores it in the B-fragment order of the gate/up MMAs, thread u handling
 // coordinates 8u..8u+7 (sub-block u/4, lane quad position u%4):
 //   variant 1: x' as 22-bit fixed point, M = rint(x' * 2^(21-E)) with E the
-//     exponent of max|x'| (so |M| < 2^22, exact for every x' within 2^12 of
-//     the maximum and within 2^-22 * max|x'| otherwise), split into three
+//     exponent of an upper bound of max|x'| (|M| < 2^22; exact for every x'
+//     within 2^11 of the bound, within 2^-22 of it otherwise), split into three
 //     balanced signed 8-bit digits M = d0 + 256 d1 + 65536 d2; plane p holds,
 //     per unit, the digits of coordinates (0,2,4,6) and (1,3,5,7);
 //   variant 0: fp16 pairs (0,4) (1,5) (2,6) (3,7).
@@ -738,41 +738,62 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         }
     }
     const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
-    float inv = 1.f;
-    if (norm) {
-        ss = warp_sum(ss);
-        if (lane == 0) t->red[warp] = ss;
+    const bool weighted = norm && L.norm_w;
+    uint4 nw = make_uint4(0u, 0u, 0u, 0u);
+    if (weighted && tid < NU) nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + tid);
+    // One reduction round: sum of squares (RMSNorm) and, for variant 1, the
+    // maxima of |x| and |w| that bound max|x'| for the fixed-point exponent.
+    float mx = 0.f, mw = 0.f;
+    if constexpr (F) {
+        const __half* h = reinterpret_cast<const __half*>(&raw);
+        const __half* wh = reinterpret_cast<const __half*>(&nw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            mx = fmaxf(mx, fabsf(__half2float(h[e])));
+            mw = fmaxf(mw, fabsf(__half2float(wh[e])));
+        }
+    }
+    float inv = 1.f, xbound = 0.f;
+    if (norm || F) {
+        if (norm) ss = warp_sum(ss);
+        if constexpr (F) {
+#pragma unroll
+            for (int off = 16; off; off >>= 1) {
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, off));
+            }
+        }
+        if (lane == 0) {
+            t->red[warp] = ss;
+            t->red2[0][warp] = mx;
+            t->red2[1][warp] = mw;
+        }
         csync(P, t, cph, limit, lane);
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) tot += t->red[w];
-        inv = rsqrtf(tot / float(H) + P.eps);
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            tot += t->red[w];
+            mx = fmaxf(mx, t->red2[0][w]);
+            mw = fmaxf(mw, t->red2[1][w]);
+        }
+        if (norm) inv = rsqrtf(tot / float(H) + P.eps);
+        // |fp16(fp16(x inv) w)| <= |x| inv |w| (1 + 2^-11)^2 < max|x| inv max|w| (1 + 2^-9)
+        xbound = norm ? mx * inv * (weighted ? mw : 1.f) * (1.f + 0.001953125f) : mx;
     }
     __half v[8];
     {
         const __half* h = reinterpret_cast<const __half*>(&raw);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = norm ? __float2half_rn(__half2float(h[e]) * inv) : h[e];
-        if (norm && L.norm_w && tid < NU) {
-            const uint4 nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + tid);
+        if (weighted) {
             const __half* wh = reinterpret_cast<const __half*>(&nw);
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
         }
     }
     if constexpr (F) {
-        // block maximum of |x'| -> exponent E (the same in every CTA)
-        float mx = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(__half2float(v[e])));
-#pragma unroll
-        for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (lane == 0) t->red2[0][warp] = mx;
-        csync(P, t, cph, limit, lane);
-        mx = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, t->red2[0][w]);
-        const int E = mx > 0.f ? int((__float_as_uint(mx) >> 23) & 0xffu) - 127 : 0;
+        // exponent E of the bound on max|x'|: identical in every CTA
+        const int E = xbound > 0.f ? int((__float_as_uint(xbound) >> 23) & 0xffu) - 127 : 0;
         const float up = __uint_as_float(uint32_t(127 + 21 - E) << 23);    // 2^(21-E)
         if (tid == 0) t->xscale = __uint_as_float(uint32_t(127 - 21 + E) << 23);  // 2^(E-21)
         if (tid < NU) {
@@ -1119,6 +1140,9 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
     const uint32_t tag = scratch_tag(P, l);
     const uint32_t nch = (rows + 15) / 16;
     for (uint32_t blk = blockIdx.x; blk < NBLK; blk += gridDim.x) {
+        // the residual is read now, off the critical path of the last rows
+        uint16_t res = 0;
+        if (warp == 0 && L.hidden_out && L.residual) res = __ldcg(L.residual + 32 * blk + lane);
         float acc = 0.f;
         for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
             const unsigned long long* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
@@ -1162,7 +1186,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             write = __shfl_sync(0xffffffffu, write, 0);
             const __half y16 = __float2half_rn(y);
             __half hout = y16;
-            if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(__ldcg(L.residual + c)) + __half2float(y16));
+            if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
             if (write) {
                 if (L.y32) L.y32[c] = y;
                 if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
