@@ -233,6 +233,22 @@ void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket);
  * compilation or synchronisation. Replaces enqueue_streaming_mlp
  * (kernels/streaming_mlp.cu:85-93). */
 int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream);
+
+/* No counterpart in the reference. The launch of ls_b200_launch for callers
+ * that must not allocate device memory: no backend object, no cudaMalloc,
+ * no allocating library routine. The scratch is a fixed set of device
+ * arrays in the library (32 MiB of partial rows), one set per device.
+ * geometry: as for ls_b200_configure (max_layers is ignored). Returns
+ * E2BIG when group_count * ceil(group_size / 16) * hidden exceeds 2^22 or
+ * args->layer >= 256, EINVAL for the cases ls_b200_launch rejects. status:
+ * optional GPU-addressable [LS_B200_STATUS_WORDS] words that receive the
+ * launch's device status; NULL sends it to a word set in the library that
+ * no call reads. The first call on a device (that device current) does the
+ * set-up: symbol lookup, kernel attributes and zeroing on `stream`; make it
+ * before any stream capture. Calls whose launches overlap in time on one
+ * device race on the shared scratch: order them on one stream. */
+int ls_b200_launch_static(const ls_b200_geometry* geometry, const ls_b200_layer_args* args, uint32_t* status,
+                          void* stream);
 /* Multi-layer launch: `count` layers in ONE persistent launch, each layer
  * reading the previous layer's hidden_out as input (a decode stack with the
  * residual / RMSNorm epilogue fused). Plans are encoded on the host with

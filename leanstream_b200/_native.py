@@ -97,6 +97,7 @@ SIGNATURES = {
     "ls_b200_set_buffers": (C.c_int, [C.c_void_p, C.POINTER(LayerArgs)]),
     "ls_b200_set_state": (None, [C.c_void_p, C.c_uint32, C.c_uint32]),
     "ls_b200_launch": (C.c_int, [C.c_void_p, C.POINTER(LayerArgs), C.c_void_p]),
+    "ls_b200_launch_static": (C.c_int, [C.POINTER(Geometry), C.POINTER(LayerArgs), C.c_void_p, C.c_void_p]),
     "ls_b200_enqueue": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
     "ls_b200_plan_size": (C.c_uint32, []),
     "ls_b200_encode_plan": (C.c_int, [C.c_void_p, C.POINTER(LayerArgs), C.c_void_p]),

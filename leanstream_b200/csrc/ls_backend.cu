@@ -7,11 +7,13 @@
 // (Runtime / LayerStep / WeightManager) is not touched: it reaches this
 // backend through ls_b200_view, which fills a ComputeBackend
 // (include/leanstream/runtime.h:10-22).
+#include <atomic>
 #include <cerrno>
 #include <cstddef>
 #include <cstring>
-#include <new>
 #include <limits>
+#include <mutex>
+#include <new>
 #include <cuda_runtime.h>
 #include "ls_internal.h"
 
@@ -309,6 +311,143 @@ void view_cancel(void*, uint32_t, uint32_t) {
 }
 
 }  // namespace
+
+// ------------------------------------------------------------ static-scratch launch
+// ls_b200_launch_static is for callers that must not allocate device memory
+// on their launch path: an engine that has already given all of HBM to its
+// own pool (a cudaMalloc would fail, or take pages that pool counts on), a
+// layer driven from inside a region where an allocation would synchronise
+// the device and stall the pipeline, or a host that cannot own the lifetime
+// of a backend object. Such a caller gets the same kernel with its scratch
+// fixed at compile time in the arrays below, whose device addresses are
+// looked up once per device.
+//
+// Limits: the partial rows (group_count * ceil(G/16) * hidden tagged words)
+// must fit kStaticPartialWords (32 MiB; H 4096 with G 64 allows 256 groups),
+// and args.layer must be below kStaticLayers. One scratch set per device:
+// two calls whose launches overlap in time on one device race on it.
+constexpr size_t kStaticPartialWords = size_t(1) << 22;
+constexpr uint32_t kStaticLayers = 256;
+constexpr uint32_t kStaticWsWords = 64;
+constexpr int kStaticDevices = 64;
+static_assert(kWsHeader + kWsPerLayer <= kStaticWsWords, "workspace of a one-layer launch");
+
+static __device__ __align__(256) unsigned long long g_static_partial[kStaticPartialWords];
+static __device__ __align__(256) unsigned long long g_static_xbuf[kMaxHidden / 2];
+static __device__ __align__(256) uint32_t g_static_ws[kStaticWsWords];
+static __device__ __align__(256) uint32_t g_static_status[LS_B200_STATUS_WORDS];
+static __device__ __align__(256) uint32_t g_static_done[kStaticLayers];
+
+namespace {
+
+struct StaticScratch {
+    std::atomic<bool> ready{false};
+    int sms = 0;
+    unsigned long long* partial = nullptr;
+    unsigned long long* xbuf = nullptr;
+    uint32_t* ws = nullptr;
+    uint32_t* status = nullptr;
+    uint32_t* done = nullptr;
+    uint32_t seq = 0;  // launches on this device, for the scratch tags
+};
+StaticScratch g_static[kStaticDevices];
+std::mutex g_static_setup;
+
+template <typename T>
+int symbol_address(T** out, const void* symbol) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, symbol);
+    if (e != cudaSuccess) return cuda_rc(e);
+    if (!p) return EIO;
+    *out = static_cast<T*>(p);
+    return 0;
+}
+
+// First call on a device (that device current): kernel attributes, symbol
+// addresses, and zeroing on `stream` of everything that must start at zero:
+// the workspace (exit counter, error word, claims), the tagged scratch (a
+// zero word carries no tag any launch issues), status and completion words.
+int static_setup(StaticScratch& s, int dev, cudaStream_t stream) {
+    std::lock_guard<std::mutex> lock(g_static_setup);
+    if (s.ready.load(std::memory_order_acquire)) return 0;
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return ENODEV;
+    if (major != 10) return ENOTSUP;
+    int rc = prepare_kernels();
+    if (rc) return cuda_rc(cudaError_t(rc));
+    if ((rc = symbol_address(&s.partial, g_static_partial)) || (rc = symbol_address(&s.xbuf, g_static_xbuf)) ||
+        (rc = symbol_address(&s.ws, g_static_ws)) || (rc = symbol_address(&s.status, g_static_status)) ||
+        (rc = symbol_address(&s.done, g_static_done)))
+        return rc;
+    cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.ws, 0, sizeof(g_static_ws), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.status, 0, sizeof(g_static_status), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.done, 0, sizeof(g_static_done), stream);
+    if (e != cudaSuccess) return cuda_rc(e);
+    s.sms = sms;
+    s.ready.store(true, std::memory_order_release);
+    return 0;
+}
+
+int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32_t* status,
+                  cudaStream_t stream) {
+    // Host-only checks first: nothing below runs for a rejected call.
+    const uint32_t H = g.hidden, G = g.group_size, N = g.group_count;
+    const uint32_t sb = H / 256;
+    if (!H || H % 256 || (sb & (sb - 1)) || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N)
+        return EINVAL;
+    if (size_t(N) * slabs_per_group(G) * H > kStaticPartialWords || a.layer >= kStaticLayers) return E2BIG;
+    Backend b;  // host view for validation and candidate choice; owns nothing
+    b.configured = true;
+    b.geo = g;
+    b.geo.max_layers = kStaticLayers;
+    if (!b.geo.timeout_us) b.geo.timeout_us = 5000000;
+    LayerPlan plan;
+    int rc = encode(b, a, &plan);
+    if (rc) return rc;
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticDevices) return ENODEV;
+    StaticScratch& s = g_static[dev];
+    if (!s.ready.load(std::memory_order_acquire) && (rc = static_setup(s, dev, stream))) return rc;
+    b.sms = s.sms;
+
+    KernelParams p{};
+    p.H = H;
+    p.G = G;
+    p.N = N;
+    p.cache_slots = g.cache_slots;
+    p.staging_slots = g.staging_slots;
+    p.phys_groups = g.physical_groups;
+    p.group_bytes = uint64_t(G) * 3 * H / 2;
+    p.timeout_ns = uint64_t(b.geo.timeout_us) * 1000ull;
+    p.eps = g.rms_eps;
+    p.nlayers = 1;
+    p.max_layers = kStaticLayers;
+    p.seq = ++s.seq & kSeqMask;
+    if (p.seq == 0) {  // tag wrap: clear the tagged scratch on the stream
+        cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
+        if (e != cudaSuccess) return cuda_rc(e);
+        p.seq = ++s.seq & kSeqMask;
+    }
+    p.partial = s.partial;
+    p.xbuf = s.xbuf;
+    p.ws = s.ws;
+    p.status = status ? status : s.status;
+    p.done = s.done;
+    p.trace = a.trace;
+    p.plans = nullptr;
+    p.first = plan;
+    const int grid = grid_for(b, a.candidate, &p.variant);
+    rc = launch_fused(p, grid, stream);
+    return rc ? cuda_rc(cudaError_t(rc)) : 0;
+}
+
+}  // namespace
 }  // namespace lsb
 
 using lsb::Backend;
@@ -351,6 +490,12 @@ void ls_b200_set_state(void* backend, uint32_t layer, uint32_t io_bucket) {
 int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream) {
     if (!backend || !args) return EINVAL;
     return lsb::launch(*static_cast<Backend*>(backend), *args, static_cast<cudaStream_t>(stream));
+}
+
+int ls_b200_launch_static(const ls_b200_geometry* geometry, const ls_b200_layer_args* args, uint32_t* status,
+                          void* stream) {
+    if (!geometry || !args) return EINVAL;
+    return lsb::launch_static(*geometry, *args, status, static_cast<cudaStream_t>(stream));
 }
 
 uint32_t ls_b200_plan_size(void) { return uint32_t(sizeof(lsb::LayerPlan)); }
