@@ -167,6 +167,11 @@ __device__ __forceinline__ void st_volatile_v2u64(unsigned long long* p, unsigne
 __device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long a) {
     asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
 }
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void red_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -1181,36 +1186,40 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
             const uint32_t c = 32 * blk + lane;
-            uint32_t write = 0;
-            if (lane == 0) write = (good && !grid_failed(P)) ? 1u : 0u;
-            write = __shfl_sync(0xffffffffu, write, 0);
             const __half y16 = __float2half_rn(y);
             __half hout = y16;
             if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
-            if (write) {
-                if (L.y32) L.y32[c] = y;
-                if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
-                if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
-            }
             if (chain) {
-                // published even after an error so that the next layer's
-                // readers never wait for it; the error is reported anyway
+                // the next layer's input first: it is on the critical path.
+                // Published even after an error so that the next layer's
+                // readers never wait for it; the error is reported anyway.
                 const uint32_t mine = __half_as_ushort(hout);
                 const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
                 if ((lane & 1) == 0)
                     st_volatile_u64(P.xbuf + c / 2, (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
             }
+            // outputs are skipped once any CTA reported an error (a relaxed
+            // read: the check is best effort, the error word is the verdict)
+            uint32_t write = 0;
+            if (lane == 0) write = (good && ld_relaxed_gpu(P.ws + kWsErr) == 0u) ? 1u : 0u;
+            write = __shfl_sync(0xffffffffu, write, 0);
+            if (write) {
+                if (L.y32) L.y32[c] = y;
+                if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
+                if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
+            }
         }
         csync(P, t, cph, limit, lane);  // red2 is reused by the next block
     }
-    if (warp == 0) {
+    // Reduced blocks: an unchained next layer (or the host's view of the
+    // layer outputs) waits on this count. A chained next layer reads the
+    // tagged words instead, so the fence stays off its critical path.
+    if (warp == 0 && !chain) {
         __threadfence();
         __syncwarp();
-        if (lane == 0) {
-            red_release_gpu(ws_layer(P, l) + 3, 1u);  // reduced blocks (unchained next layers wait on it)
-            trace_layer(P, l, LS_B200_LTRACE_REDUCED);
-        }
+        if (lane == 0) red_release_gpu(ws_layer(P, l) + 3, 1u);
     }
+    if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
 }
 
 template <int H, bool F>
