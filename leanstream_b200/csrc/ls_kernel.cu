@@ -59,7 +59,11 @@
 namespace lsb {
 
 enum : uint32_t { kPieceFinal = 0, kPieceGateUp = 1, kPieceDown = 2, kPieceLayer = 3 };
-enum : uint32_t { kCompletes = 4u, kLayerGood = 8u };
+// Piece flags. kPaired: a GATEUP piece whose slab's second GATEUP piece
+// is the next stage (both are consumed in one pass). kHsBuf: the h buffer
+// of the piece's slab (slabs alternate, so that the next slab's GATEUP can
+// finalise h while this slab's DOWN still reads it).
+enum : uint32_t { kCompletes = 4u, kLayerGood = 8u, kPaired = 16u, kHsBuf = 32u };
 constexpr uint32_t kPathFast = 1, kPathProgressive = 2, kPathAbort = 3;
 
 // Wait bounds, ordered so that a stalled launch always drains its ring:
@@ -107,7 +111,7 @@ struct SmemTail {
     float xscale;               // variant 1: x = fixed-point value * xscale
     float red[kConsumerWarps];             // RMSNorm warp sums
     float red2[kConsumerWarps][32];        // reduction warp sums
-    __half hs[kSlab];                      // h of the slab being computed
+    __half hs[2][kSlab];                   // h of the last two slabs (kHsBuf)
     volatile uint32_t octets_done;         // GATEUP pieces finalised (monotonic)
     volatile uint32_t abort;
     volatile uint32_t flag;                // CTA-uniform decision broadcast by thread 0
@@ -332,6 +336,7 @@ __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_
 struct Producer {
     uint32_t idx;     // pieces issued so far (stage = idx % kStages)
     uint32_t octets;  // GATEUP pieces issued so far
+    uint32_t slabs;   // slabs issued so far (h buffer = slabs & 1)
     uint32_t lane;
     uint8_t* stages;
     SmemTail* t;
@@ -414,7 +419,7 @@ __host__ __device__ constexpr int gateup_pitch() { return F ? H + 32 : H + 16; }
 // GATEUP piece: gate+up records of neurons [n0, n0+cnt) (cnt <= 8).
 template <int H, bool F>
 __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                                uint32_t layer, uint32_t n0, uint32_t cnt) {
+                                uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t flags) {
     if (!producer_acquire_stage(pr, P)) return false;
     const uint32_t s = pr.idx % kStages;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
@@ -427,7 +432,7 @@ __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const Layer
         pc.dest = d.dest;
         pc.n0 = n0;
         pc.count = cnt;
-        pc.flags = 0;
+        pc.flags = flags;
         trace_piece(P, pr.idx, 0);
         mbar_arrive_expect_tx(bar, cnt * H);
         for (uint32_t k = 0; k < cnt; ++k)
@@ -450,7 +455,7 @@ __device__ bool producer_gateup(Producer& pr, const KernelParams& P, const Layer
 // DOWN piece: down rows of neurons [n0, n0+cnt) (one slab, cnt <= 16).
 template <int H>
 __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                              uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t row, uint32_t flags) {
+                              uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t row, uint32_t flags, uint32_t need) {
     if (!producer_acquire_stage(pr, P)) return false;
     const uint32_t s = pr.idx % kStages;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
@@ -464,7 +469,7 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
         pc.dest = d.dest;
         pc.n0 = n0;
         pc.count = cnt;
-        pc.need = pr.octets;
+        pc.need = need;
         pc.flags = flags;
         trace_piece(P, pr.idx, 0);
         mbar_arrive_expect_tx(bar, cnt * (H / 2));
@@ -485,17 +490,57 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
     return true;
 }
 
-// All pieces of slab `slab` of one descriptor.
+// The GATEUP pieces of slab `slab` of one descriptor (variant 1 pairs the
+// two halves of a 16-neuron slab so that they are consumed in one pass).
 template <int H, bool F>
-__device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                              uint32_t layer, uint32_t slab) {
-    const uint32_t spg = slabs_per_group(P.G);
+__device__ bool producer_slab_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
+                                     uint32_t layer, uint32_t slab, uint32_t buf) {
     const uint32_t n0 = slab * kSlab;
     const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
-    if (!producer_gateup<H, F>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u) || pr.t->abort) return false;
-    if (cnt > 8u && (!producer_gateup<H, F>(pr, P, L, d, layer, n0 + 8, cnt - 8) || pr.t->abort)) return false;
-    const uint32_t flags = slab + 1 == spg ? kCompletes : 0u;
-    return producer_down<H>(pr, P, L, d, layer, n0, cnt, d.row * spg + slab, flags) && !pr.t->abort;
+    const uint32_t first = (F && cnt > 8u) ? (buf | kPaired) : buf;
+    if (!producer_gateup<H, F>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u, first) || pr.t->abort) return false;
+    if (cnt > 8u && (!producer_gateup<H, F>(pr, P, L, d, layer, n0 + 8, cnt - 8, buf) || pr.t->abort)) return false;
+    return true;
+}
+
+// A slab whose GATEUP pieces are issued and whose DOWN piece is not yet.
+struct PendingDown {
+    DescView d;
+    uint32_t slab, need, buf;
+    bool valid;
+};
+
+// The DOWN piece of a pending slab. It is issued after the next slab's
+// GATEUP pieces, so that the consumers compute those while the last warp
+// of this slab's GATEUP finalises h.
+template <int H>
+__device__ bool producer_slab_down(Producer& pr, const KernelParams& P, const LayerPlan& L, PendingDown& pd,
+                                   uint32_t layer) {
+    if (!pd.valid) return true;
+    pd.valid = false;
+    const uint32_t spg = slabs_per_group(P.G);
+    const uint32_t n0 = pd.slab * kSlab;
+    const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
+    const uint32_t flags = (pd.slab + 1 == spg ? kCompletes : 0u) | pd.buf;
+    return producer_down<H>(pr, P, L, pd.d, layer, n0, cnt, pd.d.row * spg + pd.slab, flags, pd.need) &&
+           !pr.t->abort;
+}
+
+// Issues the GATEUP pieces of a slab and the DOWN piece of the previous one.
+template <int H, bool F>
+__device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
+                              uint32_t layer, uint32_t slab, PendingDown& pd) {
+    const uint32_t buf = (pr.slabs & 1u) ? kHsBuf : 0u;
+    if (!producer_slab_gateup<H, F>(pr, P, L, d, layer, slab, buf)) return false;
+    const uint32_t need = pr.octets;
+    ++pr.slabs;
+    if (!producer_slab_down<H>(pr, P, L, pd, layer)) return false;
+    pd.d = d;
+    pd.slab = slab;
+    pd.need = need;
+    pd.buf = buf;
+    pd.valid = true;
+    return true;
 }
 
 // Loads the descriptor window [base, base+32) into shared memory, one
@@ -577,6 +622,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
     Producer pr;
     pr.idx = 0;
     pr.octets = 0;
+    pr.slabs = 0;
     pr.lane = threadIdx.x & 31u;
     pr.stages = stages;
     pr.t = t;
@@ -596,6 +642,8 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         const uint32_t D = L.core_count + total;
         const uint32_t NS = D * spg;
         pr.wbase = pr.wlayer = 0xffffffffu;
+        PendingDown pd;
+        pd.valid = false;
         if (path == kPathFast) {
             // Static balanced split of the layer's slab positions.
             const uint32_t b = blockIdx.x, grid = gridDim.x;
@@ -606,7 +654,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 if (!ok) break;
                 const DescView dv = t->dtab[d - pr.wbase];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
-                ok = producer_slab<H, F>(pr, P, L, dv, l, slab);
+                ok = producer_slab<H, F>(pr, P, L, dv, l, slab, pd);
             }
         } else {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(L.q.control);
@@ -639,10 +687,11 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                 if (!ok) break;
                 const DescView dv = t->dtab[0];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
-                ok = producer_slab<H, F>(pr, P, L, dv, l, slab);
+                ok = producer_slab<H, F>(pr, P, L, dv, l, slab, pd);
             }
             if (t->abort) ok = false;
         }
+        if (ok) ok = producer_slab_down<H>(pr, P, L, pd, l);
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_ISSUED);
         if (ok) ok = producer_marker(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
     }
@@ -998,7 +1047,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
         const float g16 = round16(gsum), u16 = round16(usum);
         const float sl = round16(g16 / (1.f + expf(-g16)));
         const __half h = __float2half_rn(sl * u16);
-        t->hs[(pc.n0 & (kSlab - 1)) + lane] = h;
+        t->hs[(pc.flags & kHsBuf) ? 1 : 0][(pc.n0 & (kSlab - 1)) + lane] = h;
         if (L.act) L.act[size_t(pc.dest) * P.G + pc.n0 + lane] = __half_as_ushort(h);
     }
     __syncwarp();
@@ -1006,6 +1055,150 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
     if (lane == 0) {
         t->gcnt[s] = 0;
         t->octets_done = t->octets_done + 1;
+    }
+}
+
+// Variant-1 sums of one GATEUP tile's scale block: per digit plane p (B
+// column p), lo + hi / 16 is exact in fp32; lane (g, 0) holds planes 0 and 1
+// and takes plane 2 from lane (g, 1). Returns the scaled gate and up terms.
+__device__ __forceinline__ void gateup_block_terms(const int (&alo)[4], const int (&ahi)[4], int ms, float sg, float su,
+                                                   float& pg, float& pu) {
+    float dv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dv[e] = fmaf(0.0625f, float(ahi[e]), float(alo[e]));
+    const float dg2 = __shfl_down_sync(0xffffffffu, dv[0], 1);
+    const float du2 = __shfl_down_sync(0xffffffffu, dv[2], 1);
+    const float m8 = 8.f * float(ms);
+    const float rg = fmaf(dg2, 65536.f, fmaf(dv[1], 256.f, dv[0])) - m8;
+    const float ru = fmaf(du2, 65536.f, fmaf(dv[3], 256.f, dv[2])) - m8;
+    pg = fmaf(sg, rg, pg);
+    pu = fmaf(su, ru, pu);
+}
+
+// Both GATEUP pieces of a 16-neuron slab in one pass (variant 1): stage A
+// holds neurons 0-7, stage B neurons 8-15. Each warp reads an activation
+// fragment once for the two 16-row tiles, and the last warp to finish
+// forms the 16 values of h. The arithmetic of each tile, and the order of
+// the warp partials, are those of consume_gateup.
+template <int H>
+__device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, const Piece& pa, const Piece& pb,
+                                    uint8_t* sa, uint8_t* sb, SmemTail* t, uint32_t s, int warp, int lane) {
+    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
+    constexpr int CH = SBW < 4 ? SBW : 4;
+    constexpr int NC = SBW / CH;
+    constexpr int PG = gateup_pitch<H, true>();
+    constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;
+    const int g = lane >> 2, tq = lane & 3;
+    float2* parta = reinterpret_cast<float2*>(sa + kStageData + kAuxPartials);  // [warp][8]
+    float2* partb = reinterpret_cast<float2*>(sb + kStageData + kAuxPartials);
+    __syncwarp();  // mma.sync is .aligned: enter converged
+    if (warp < AW) {
+        const __half* sca = reinterpret_cast<const __half*>(sa + kStageData) + g * SPN;
+        const __half* scb = reinterpret_cast<const __half*>(sb + kStageData) + g * SPN;
+        float pga = 0.f, pua = 0.f, pgb = 0.f, pub = 0.f;
+        int aloa[NC][4], ahia[NC][4], alob[NC][4], ahib[NC][4];
+        int ms[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) aloa[c][e] = ahia[c][e] = alob[c][e] = ahib[c][e] = 0;
+        const uint8_t* xp = t->xarea + (g < 3 ? g : 0) * kXPlane;
+        if constexpr (CH >= 2) {
+            constexpr int DC = CH / 2;
+            const uint8_t* rowa = sa + g * PG + 8 * tq;
+            const uint8_t* rowb = sb + g * PG + 8 * tq;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int d0 = (warp * SBW + c * CH) / 2;
+                ms[c] = t->msum64[d0];
+                if constexpr (DC == 2) ms[c] += t->msum64[d0 + 1];
+            }
+#pragma unroll
+            for (int dj = 0; dj < DC; ++dj) {
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int dg = (warp * SBW + c * CH) / 2 + dj;
+                    const uint4 xb = reinterpret_cast<const uint4*>(xp)[4 * dg + tq];
+                    const uint2 wga = *reinterpret_cast<const uint2*>(rowa + 32 * dg);
+                    const uint2 wua = *reinterpret_cast<const uint2*>(rowa + H / 2 + 32 * dg);
+                    const uint2 wgb = *reinterpret_cast<const uint2*>(rowb + 32 * dg);
+                    const uint2 wub = *reinterpret_cast<const uint2*>(rowb + H / 2 + 32 * dg);
+                    imma16832(aloa[c], (wga.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wua.x & 0x0F0F0F0Fu) ^ 0x08080808u,
+                              (wga.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wua.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
+                    imma16832(ahia[c], (wga.x & 0xF0F0F0F0u) ^ 0x80808080u, (wua.x & 0xF0F0F0F0u) ^ 0x80808080u,
+                              (wga.y & 0xF0F0F0F0u) ^ 0x80808080u, (wua.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
+                    imma16832(alob[c], (wgb.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wub.x & 0x0F0F0F0Fu) ^ 0x08080808u,
+                              (wgb.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wub.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
+                    imma16832(ahib[c], (wgb.x & 0xF0F0F0F0u) ^ 0x80808080u, (wub.x & 0xF0F0F0F0u) ^ 0x80808080u,
+                              (wgb.y & 0xF0F0F0F0u) ^ 0x80808080u, (wub.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
+                }
+            }
+        } else {
+            const uint8_t* rowa = sa + g * PG + 4 * tq;
+            const uint8_t* rowb = sb + g * PG + 4 * tq;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int sbk = warp * SBW + c;
+                const uint2 xb = reinterpret_cast<const uint2*>(xp)[sbk * 4 + tq];
+                ms[c] = t->msum[sbk];
+                const uint32_t wga = *reinterpret_cast<const uint32_t*>(rowa + 16 * sbk);
+                const uint32_t wua = *reinterpret_cast<const uint32_t*>(rowa + H / 2 + 16 * sbk);
+                const uint32_t wgb = *reinterpret_cast<const uint32_t*>(rowb + 16 * sbk);
+                const uint32_t wub = *reinterpret_cast<const uint32_t*>(rowb + H / 2 + 16 * sbk);
+                imma16832(aloa[c], (wga & 0x0F0F0F0Fu) ^ 0x08080808u, (wua & 0x0F0F0F0Fu) ^ 0x08080808u,
+                          ((wga >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wua >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                          xb.y);
+                imma16832(alob[c], (wgb & 0x0F0F0F0Fu) ^ 0x08080808u, (wub & 0x0F0F0F0Fu) ^ 0x08080808u,
+                          ((wgb >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wub >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                          xb.y);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int blk = (warp * SBW + c * CH) / 4;
+            gateup_block_terms(aloa[c], ahia[c], ms[c], __half2float(sca[blk]), __half2float(sca[H / 128 + blk]), pga,
+                               pua);
+            gateup_block_terms(alob[c], ahib[c], ms[c], __half2float(scb[blk]), __half2float(scb[H / 128 + blk]), pgb,
+                               pub);
+        }
+        const float xs = t->xscale;
+        if (tq == 0) {
+            parta[warp * 8 + g] = make_float2(pga * xs, pua * xs);
+            partb[warp * 8 + g] = make_float2(pgb * xs, pub * xs);
+        }
+    }
+    // Last warp to finish combines the partial sums of both tiles.
+    __syncwarp();
+    __threadfence_block();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(&t->gcnt[s], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != uint32_t(kConsumerWarps) - 1) return;
+    __threadfence_block();
+    const bool second = lane >= 8;
+    const uint32_t li = uint32_t(lane) & 7u;
+    const uint32_t cnt = second ? pb.count : pa.count;
+    if (lane < 16 && li < cnt) {
+        const float2* pp = second ? partb : parta;
+        float gsum = 0.f, usum = 0.f;
+#pragma unroll
+        for (int w = 0; w < AW; ++w) {
+            const float2 v = pp[w * 8 + li];
+            gsum += v.x;
+            usum += v.y;
+        }
+        const float g16 = round16(gsum), u16 = round16(usum);
+        const float sl = round16(g16 / (1.f + expf(-g16)));
+        const __half h = __float2half_rn(sl * u16);
+        const uint32_t n0 = second ? pb.n0 : pa.n0;
+        t->hs[(pa.flags & kHsBuf) ? 1 : 0][(n0 & (kSlab - 1)) + li] = h;
+        if (L.act) L.act[size_t(pa.dest) * P.G + n0 + li] = __half_as_ushort(h);
+    }
+    __syncwarp();
+    __threadfence_block();
+    if (lane == 0) {
+        t->gcnt[s] = 0;
+        t->octets_done = t->octets_done + 2;
     }
 }
 
@@ -1028,8 +1221,10 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     const uint32_t cnt = pc.count;
     const int n0 = 2 * tq, n1 = n0 + 1, n2 = n0 + 8, n3 = n0 + 9;
     const __half zero = __float2half_rn(0.f);
-    const __half hv0 = uint32_t(n0) < cnt ? t->hs[n0] : zero, hv1 = uint32_t(n1) < cnt ? t->hs[n1] : zero;
-    const __half hv2 = uint32_t(n2) < cnt ? t->hs[n2] : zero, hv3 = uint32_t(n3) < cnt ? t->hs[n3] : zero;
+    const __half* hb = t->hs[(pc.flags & kHsBuf) ? 1 : 0];
+    const __half hv0 = uint32_t(n0) < cnt ? hb[n0] : zero, hv1 = uint32_t(n1) < cnt ? hb[n1] : zero;
+    const __half hv2 = uint32_t(n2) < cnt ? hb[n2] : zero, hv3 = uint32_t(n3) < cnt ? hb[n3] : zero;
+    const __half2 h01 = __halves2half2(hv0, hv1), h23 = __halves2half2(hv2, hv3);
     const __half* sd = reinterpret_cast<const __half*>(st + kStageData);
     unsigned long long* out = P.partial + size_t(pc.row) * H;
     const unsigned long long tag = static_cast<unsigned long long>(scratch_tag(P, pc.layer)) << 32;
@@ -1047,21 +1242,23 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
             const __half c3 = uint32_t(n3) < cnt ? sd[n3 * SPN + blk] : zero;
             uint32_t v0, v1;
             if constexpr (F) {
-                // h * s is exact in fp32; split it into an fp16 value (even B
-                // columns) and an fp16 residual (odd B columns). The +8 offset
-                // of A is removed with their sum over the slab's 16 neurons.
-                const float f[4] = {__half2float(hv0) * __half2float(c0), __half2float(hv1) * __half2float(c1),
-                                    __half2float(hv2) * __half2float(c2), __half2float(hv3) * __half2float(c3)};
-                __half hi[4], lo[4];
-                float hsum = 0.f;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    hi[e] = __float2half_rn(f[e]);
-                    lo[e] = __float2half_rn(f[e] - __half2float(hi[e]));
-                    hsum += __half2float(hi[e]) + __half2float(lo[e]);
-                }
-                v0 = (g & 1) ? h2_bits(__halves2half2(lo[0], lo[1])) : h2_bits(__halves2half2(hi[0], hi[1]));
-                v1 = (g & 1) ? h2_bits(__halves2half2(lo[2], lo[3])) : h2_bits(__halves2half2(hi[2], hi[3]));
+                // h * s split into an fp16 value (even B columns) and the fp16
+                // residual (odd B columns): hi = fp16(h s), lo = fp16(h s - hi),
+                // the product and the difference exact before their one
+                // rounding (packed fp16 multiply and fused multiply-add). The
+                // +8 offset of A is removed with their sum over the slab's 16
+                // neurons.
+                const __half2 c01 = __halves2half2(c0, c1), c23 = __halves2half2(c2, c3);
+                const __half2 hi01 = __hmul2(h01, c01), hi23 = __hmul2(h23, c23);
+                const __half2 lo01 = __hfma2(h01, c01, __hneg2(hi01)), lo23 = __hfma2(h23, c23, __hneg2(hi23));
+                const float2 fh01 = __half22float2(hi01), fl01 = __half22float2(lo01);
+                const float2 fh23 = __half22float2(hi23), fl23 = __half22float2(lo23);
+                float hsum = fh01.x + fl01.x;
+                hsum += fh01.y + fl01.y;
+                hsum += fh23.x + fl23.x;
+                hsum += fh23.y + fl23.y;
+                v0 = (g & 1) ? h2_bits(lo01) : h2_bits(hi01);
+                v1 = (g & 1) ? h2_bits(lo23) : h2_bits(hi23);
                 hsum += __shfl_xor_sync(0xffffffffu, hsum, 1);
                 hsum += __shfl_xor_sync(0xffffffffu, hsum, 2);
                 hsum8 = -8.f * hsum;
@@ -1222,6 +1419,22 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
     if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
 }
 
+// Warp-uniform bounded wait until piece `idx`'s stage is full (acquire of
+// the TMA-written data). False when the producer stopped without a FINAL
+// marker.
+__device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane) {
+    const uint32_t bar = smem_u32(&t->full_bar[idx % kStages]);
+    const uint32_t parity = (idx / kStages) & 1u;
+    uint32_t spins = 0;
+    for (;;) {
+        const bool ready = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ready)) return true;
+        uint32_t late = 0;
+        if (lane == 0 && (++spins & 255u) == 0 && gtimer() > deadline + kConsumerGraceNs) late = 1;
+        if (__shfl_sync(0xffffffffu, late, 0)) return false;
+    }
+}
+
 template <int H, bool F>
 __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     constexpr uint32_t NBLK = H / 32;
@@ -1233,23 +1446,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % kStages;
-        const uint32_t parity = (idx / kStages) & 1u;
-        const uint32_t bar = smem_u32(&t->full_bar[s]);
-        // Warp-uniform bounded wait on the stage's mbarrier (acquire of the
-        // TMA-written data).
-        uint32_t spins = 0;
-        bool timed_out = false;
-        for (;;) {
-            const bool ready = mbar_try_wait(bar, parity);
-            if (__all_sync(0xffffffffu, ready)) break;
-            uint32_t late = 0;
-            if (lane == 0 && (++spins & 255u) == 0 && gtimer() > deadline + kConsumerGraceNs) late = 1;
-            if (__shfl_sync(0xffffffffu, late, 0)) {
-                timed_out = true;
-                break;
-            }
-        }
-        if (timed_out) {
+        if (!wait_full(t, idx, deadline, lane)) {
             // The producer stopped without a FINAL marker; nothing is in
             // flight for this stage.
             if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 4);
@@ -1265,6 +1462,30 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         }
         uint8_t* st = stages + size_t(s) * kStageBytes;
         if (pc.kind == kPieceGateUp) {
+            if constexpr (F) {
+                if (pc.flags & kPaired) {
+                    // the slab's second GATEUP piece is the next stage
+                    if (!wait_full(t, idx + 1, deadline, lane)) {
+                        if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 4);
+                        break;
+                    }
+                    const uint32_t s2 = (idx + 1) % kStages;
+                    const Piece pc2 = t->piece[s2];
+                    if (tid == 0) trace_piece(P, idx + 1, 2);
+                    consume_gateup_pair<H>(P, *L, pc, pc2, st, stages + size_t(s2) * kStageBytes, t, s, warp, lane);
+                    __syncwarp();
+                    if (tid == 0) {
+                        trace_piece(P, idx, 3);
+                        trace_piece(P, idx + 1, 3);
+                    }
+                    if (lane == 0) {
+                        mbar_arrive(smem_u32(&t->empty_bar[s]));
+                        mbar_arrive(smem_u32(&t->empty_bar[s2]));
+                    }
+                    ++idx;
+                    continue;
+                }
+            }
             // every warp takes part (the last one finalises h)
             consume_gateup<H, F>(P, *L, pc, st, t, s, warp, lane);
         } else if (pc.kind == kPieceDown) {
