@@ -10,7 +10,7 @@ namespace lsb {
 // CTA shape: sixteen consumer warps plus one TMA producer warp, one CTA per SM.
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kThreads = kConsumerThreads + 64;  // + producer warp + epilogue warp
 
 // Work unit: a slab of up to 16 consecutive neurons of one descriptor. One
 // CTA computes a slab's gate/up rows, its h values and its down rows, and

@@ -100,7 +100,7 @@ struct SmemTail {
     unsigned long long cbar;  // consumer-warp barrier (16 arrivals per phase)
     Piece piece[kStages];
     DescView dtab[32];        // producer's descriptor window
-    uint32_t gcnt[kStages];   // warps done with a GATEUP piece (per stage)
+    unsigned long long pbar[kStages];  // GATEUP warp partials written (16 arrivals per phase)
     // Activation of the current layer in B-fragment order (see stage_x):
     // variant 1: three planes of signed 8-bit digits, uint2 per 8 coordinates,
     //            planes kXPlane bytes apart (8 banks apart);
@@ -901,8 +901,8 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
 
 // GATEUP piece: warp w reduces sub-blocks [w*SBW, (w+1)*SBW) (32 hidden
 // coordinates each) for the piece's 8 neurons (MMA rows 0-7: gate rows,
-// 8-15: up rows); the last warp to finish sums the warp partials in warp
-// order and forms h.
+// 8-15: up rows); the epilogue warp sums the warp partials in warp order and
+// forms h.
 //   variant 1: one integer MMA per sub-block. A = q + 8 as unsigned bytes
 //     (one LOP3 per four weights: the low nibbles of a word are coordinates
 //     0,2,4,6, the high nibbles 1,3,5,7); B column p = digit plane p of the
@@ -1028,34 +1028,9 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
         }
         if (tq == 0) part[warp * 8 + g] = make_float2(pg, pu);
     }
-    // Last warp to finish this piece combines the partial sums.
+    // The epilogue warp forms h once every consumer warp has arrived.
     __syncwarp();
-    __threadfence_block();
-    uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(&t->gcnt[s], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != uint32_t(kConsumerWarps) - 1) return;
-    __threadfence_block();
-    if (uint32_t(lane) < pc.count) {
-        float gsum = 0.f, usum = 0.f;
-#pragma unroll
-        for (int w = 0; w < AW; ++w) {
-            const float2 v = part[w * 8 + lane];
-            gsum += v.x;
-            usum += v.y;
-        }
-        const float g16 = round16(gsum), u16 = round16(usum);
-        const float sl = round16(g16 / (1.f + expf(-g16)));
-        const __half h = __float2half_rn(sl * u16);
-        t->hs[(pc.flags & kHsBuf) ? 1 : 0][(pc.n0 & (kSlab - 1)) + lane] = h;
-        if (L.act) L.act[size_t(pc.dest) * P.G + pc.n0 + lane] = __half_as_ushort(h);
-    }
-    __syncwarp();
-    __threadfence_block();
-    if (lane == 0) {
-        t->gcnt[s] = 0;
-        t->octets_done = t->octets_done + 1;
-    }
+    if (lane == 0) mbar_arrive(smem_u32(&t->pbar[s]));
 }
 
 // Variant-1 sums of one GATEUP tile's scale block: per digit plane p (B
@@ -1077,9 +1052,9 @@ __device__ __forceinline__ void gateup_block_terms(const int (&alo)[4], const in
 
 // Both GATEUP pieces of a 16-neuron slab in one pass (variant 1): stage A
 // holds neurons 0-7, stage B neurons 8-15. Each warp reads an activation
-// fragment once for the two 16-row tiles, and the last warp to finish
-// forms the 16 values of h. The arithmetic of each tile, and the order of
-// the warp partials, are those of consume_gateup.
+// fragment once for the two 16-row tiles; the epilogue warp forms the 16
+// values of h. The arithmetic of each tile, and the order of the warp
+// partials, are those of consume_gateup.
 template <int H>
 __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, const Piece& pa, const Piece& pb,
                                     uint8_t* sa, uint8_t* sb, SmemTail* t, uint32_t s, int warp, int lane) {
@@ -1167,39 +1142,9 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
             partb[warp * 8 + g] = make_float2(pgb * xs, pub * xs);
         }
     }
-    // Last warp to finish combines the partial sums of both tiles.
+    // The epilogue warp forms h once every consumer warp has arrived.
     __syncwarp();
-    __threadfence_block();
-    uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(&t->gcnt[s], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != uint32_t(kConsumerWarps) - 1) return;
-    __threadfence_block();
-    const bool second = lane >= 8;
-    const uint32_t li = uint32_t(lane) & 7u;
-    const uint32_t cnt = second ? pb.count : pa.count;
-    if (lane < 16 && li < cnt) {
-        const float2* pp = second ? partb : parta;
-        float gsum = 0.f, usum = 0.f;
-#pragma unroll
-        for (int w = 0; w < AW; ++w) {
-            const float2 v = pp[w * 8 + li];
-            gsum += v.x;
-            usum += v.y;
-        }
-        const float g16 = round16(gsum), u16 = round16(usum);
-        const float sl = round16(g16 / (1.f + expf(-g16)));
-        const __half h = __float2half_rn(sl * u16);
-        const uint32_t n0 = second ? pb.n0 : pa.n0;
-        t->hs[(pa.flags & kHsBuf) ? 1 : 0][(n0 & (kSlab - 1)) + li] = h;
-        if (L.act) L.act[size_t(pa.dest) * P.G + n0 + li] = __half_as_ushort(h);
-    }
-    __syncwarp();
-    __threadfence_block();
-    if (lane == 0) {
-        t->gcnt[s] = 0;
-        t->octets_done = t->octets_done + 2;
-    }
+    if (lane == 0) mbar_arrive(smem_u32(&t->pbar[s]));
 }
 
 // DOWN piece: warp w owns 64-column tiles [w*TPW, (w+1)*TPW); in each, lane
@@ -1419,6 +1364,46 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
     if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
 }
 
+// h of the neurons of one GATEUP stage from its warp partials ([warp][8]
+// float2 in the stage's aux area): the sums in warp order, each rounded to
+// fp16, then fp16(fp16(silu(g)) * u) (kernels/streaming_mlp.cu:34-37,
+// backends/triton/core.py:49-52). Lane i < count handles neuron n0 + i.
+template <int H>
+__device__ __forceinline__ void form_h(const KernelParams& P, const LayerPlan& L, const Piece& pc, const uint8_t* st,
+                                       SmemTail* t, uint32_t buf, uint32_t i) {
+    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps;
+    if (i >= pc.count) return;
+    const float2* part = reinterpret_cast<const float2*>(st + kStageData + kAuxPartials);
+    float gsum = 0.f, usum = 0.f;
+#pragma unroll
+    for (int w = 0; w < AW; ++w) {
+        const float2 v = part[w * 8 + i];
+        gsum += v.x;
+        usum += v.y;
+    }
+    const float g16 = round16(gsum), u16 = round16(usum);
+    const float sl = round16(g16 / (1.f + expf(-g16)));
+    const __half h = __float2half_rn(sl * u16);
+    t->hs[buf][(pc.n0 & (kSlab - 1)) + i] = h;
+    if (L.act) L.act[size_t(pc.dest) * P.G + pc.n0 + i] = __half_as_ushort(h);
+}
+
+// Bounded wait of a warp on an mbarrier phase; false on abort or deadline.
+__device__ bool wait_phase(const KernelParams& P, SmemTail* t, uint32_t bar, uint32_t parity, uint64_t limit,
+                           int lane, uint32_t detail) {
+    uint32_t spins = 0;
+    for (;;) {
+        const bool ready = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ready)) return true;
+        uint32_t late = 0;
+        if (lane == 0 && (t->abort || ((++spins & 255u) == 0 && gtimer() > limit))) late = 1;
+        if (__shfl_sync(0xffffffffu, late, 0)) {
+            if (lane == 0 && !t->abort) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, detail);
+            return false;
+        }
+    }
+}
+
 // Warp-uniform bounded wait until piece `idx`'s stage is full (acquire of
 // the TMA-written data). False when the producer stopped without a FINAL
 // marker.
@@ -1539,6 +1524,55 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     }
 }
 
+// Epilogue warp: follows the pieces in ring order and, for each GATEUP
+// piece (or pair), waits until the 16 consumer warps have written their
+// partials, forms h and publishes it to the DOWN piece through octets_done.
+// It is the stage's 17th release, so a stage is refilled only after its
+// partials were read. Keeping this off the consumer warps removes a serial
+// step from whichever warp finished a GATEUP piece last.
+template <int H, bool F>
+__device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t limit = deadline + kSyncGraceNs;
+    uint32_t phases = 0;  // completed-phase parity of each stage's pbar
+    for (uint32_t idx = 0;; ++idx) {
+        const uint32_t s = idx % kStages;
+        if (!wait_full(t, idx, deadline, lane)) break;  // the consumers report it
+        const Piece pc = t->piece[s];
+        if (pc.kind == kPieceFinal) break;
+        if (pc.kind == kPieceGateUp) {
+            if (!wait_phase(P, t, smem_u32(&t->pbar[s]), (phases >> s) & 1u, limit, lane, 10)) break;
+            phases ^= 1u << s;
+            const LayerPlan& L = plan_at(P, pc.layer);
+            const uint32_t buf = (pc.flags & kHsBuf) ? 1u : 0u;
+            const uint8_t* st = stages + size_t(s) * kStageBytes;
+            if (F && (pc.flags & kPaired)) {
+                // the consumers saw the second stage full before writing
+                // their partials; this wait returns at once
+                if (!wait_full(t, idx + 1, deadline, lane)) break;
+                const uint32_t s2 = (idx + 1) % kStages;
+                const Piece pc2 = t->piece[s2];
+                if (lane < 8) form_h<H>(P, L, pc, st, t, buf, uint32_t(lane));
+                else if (lane < 16) form_h<H>(P, L, pc2, stages + size_t(s2) * kStageBytes, t, buf, uint32_t(lane - 8));
+                __syncwarp();
+                __threadfence_block();
+                if (lane == 0) {
+                    t->octets_done = t->octets_done + 2;
+                    mbar_arrive(smem_u32(&t->empty_bar[s]));
+                    mbar_arrive(smem_u32(&t->empty_bar[s2]));
+                }
+                ++idx;
+                continue;
+            }
+            form_h<H>(P, L, pc, st, t, buf, uint32_t(lane));
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) t->octets_done = t->octets_done + 1;
+        }
+        if (lane == 0) mbar_arrive(smem_u32(&t->empty_bar[s]));
+    }
+}
+
 template <int H, bool F>
 __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_constant__ KernelParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1550,8 +1584,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
         trace(P, LS_B200_TRACE_ENTRY);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&t->full_bar[s]), 34);                // lane 0 expect_tx + 32 cp.async + lane 0 close
-            mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps);  // one arrive per consumer warp
-            t->gcnt[s] = 0;
+            mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps + 1);  // consumer warps + epilogue warp
+            mbar_init(smem_u32(&t->pbar[s]), kConsumerWarps);
         }
         mbar_init(smem_u32(&t->cbar), kConsumerWarps);
         t->octets_done = 0;
@@ -1562,7 +1596,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
     }
     __syncthreads();
 
-    if (tid >= kConsumerThreads) {
+    if (tid >= kConsumerThreads + 32) {
+        run_epilogue<H, F>(P, stages, t, deadline);
+    } else if (tid >= kConsumerThreads) {
         run_producer<H, F>(P, stages, t, deadline);
     } else {
         run_consumers<H, F>(P, stages, t, deadline);
