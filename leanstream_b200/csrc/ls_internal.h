@@ -54,7 +54,7 @@ struct alignas(16) LayerPlan {
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
-constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, (unused), reduced column blocks
+constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, reduction-block claim, reduced column blocks
 constexpr uint32_t kSeqMask = 0xFFFFFFu;  // launch sequence bits inside scratch tags
 __host__ __device__ inline uint32_t ws_words(uint32_t max_layers) { return kWsHeader + kWsPerLayer * max_layers; }
 

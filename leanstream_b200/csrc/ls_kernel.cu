@@ -267,7 +267,7 @@ __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
-    return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] claim [2] partial-rows-done CTAs [3] reduced blocks
+    return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] slab claim [2] block claim [3] reduced blocks
 }
 // Tag of the scratch words written by launch-local layer l (never 0: seq >= 1).
 // A 64-bit word (tag << 32 | value) is written by one store, so a reader that
@@ -1283,13 +1283,26 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                           SmemTail* t, uint32_t& cph, uint64_t limit, int tid, bool chain) {
     constexpr uint32_t NBLK = H / 32;
     const int warp = tid >> 5, lane = tid & 31;
-    if (blockIdx.x >= NBLK) return;
+    uint32_t blk0 = blockIdx.x, step = gridDim.x;
+    if (gridDim.x >= NBLK) {
+        // One column block per CTA, handed out in the order in which the CTAs
+        // reach the end of the layer: a CTA still busy with its last pieces
+        // does not hold up a block's reduction.
+        if (tid == 0) t->flag = atomicAdd(ws_layer(P, l) + 2, 1u);
+        csync(P, t, cph, limit, lane);
+        blk0 = t->flag;
+        step = NBLK;
+    }
+    if (blk0 >= NBLK) return;
     const uint32_t tag = scratch_tag(P, l);
     const uint32_t nch = (rows + 15) / 16;
-    for (uint32_t blk = blockIdx.x; blk < NBLK; blk += gridDim.x) {
-        // the residual is read now, off the critical path of the last rows
+    for (uint32_t blk = blk0; blk < NBLK; blk += step) {
+        // the residual and the error word are read now, off the critical
+        // path of the last rows
         uint16_t res = 0;
+        uint32_t err = 0;
         if (warp == 0 && L.hidden_out && L.residual) res = __ldcg(L.residual + 32 * blk + lane);
+        if (warp == 0 && lane == 0) err = ld_relaxed_gpu(P.ws + kWsErr);
         float acc = 0.f;
         for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
             const unsigned long long* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
@@ -1323,7 +1336,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         t->red2[warp][lane] = acc;
         csync(P, t, cph, limit, lane);
         if (warp == 0) {
-            if (blk == blockIdx.x && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
+            if (blk == blk0 && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
             float y = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
@@ -1340,10 +1353,10 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                 if ((lane & 1) == 0)
                     st_volatile_u64(P.xbuf + c / 2, (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
             }
-            // outputs are skipped once any CTA reported an error (a relaxed
-            // read: the check is best effort, the error word is the verdict)
+            // outputs are skipped once any CTA had reported an error when
+            // the reduction started (best effort: the error word is the verdict)
             uint32_t write = 0;
-            if (lane == 0) write = (good && ld_relaxed_gpu(P.ws + kWsErr) == 0u) ? 1u : 0u;
+            if (lane == 0) write = (good && err == 0u && !t->abort) ? 1u : 0u;
             write = __shfl_sync(0xffffffffu, write, 0);
             if (write) {
                 if (L.y32) L.y32[c] = y;
