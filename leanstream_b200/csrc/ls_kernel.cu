@@ -102,10 +102,13 @@ struct SmemTail {
     DescView dtab[32];        // producer's descriptor window
     unsigned long long pbar[kStages];  // GATEUP warp partials written (16 arrivals per phase)
     // Activation of the current layer in B-fragment order (see stage_x):
-    // variant 1: three planes of signed 8-bit digits, uint2 per 8 coordinates,
-    //            planes kXPlane bytes apart (8 banks apart);
+    // variant 1: three planes of signed 8-bit digits, 16 bytes per two
+    //            8-coordinate units u, u+1 (even digits of u, of u+1, odd
+    //            digits of u, of u+1), planes kXPlane bytes apart (8 banks);
     // variant 0: uint4 of four fp16 pairs per 8 coordinates.
     alignas(16) uint8_t xarea[3 * kXPlane];
+    alignas(16) uint32_t zero16[4];        // read by lanes whose B operand is zero
+    alignas(16) uint32_t nib[8];           // nibble masks and offsets (NibMasks), see and_xor
     int msum[kMaxHidden / 32];  // variant 1: sum of the fixed-point x over each 32-coordinate sub-block
     int msum64[kMaxHidden / 64];  // variant 1: the same over each 64-coordinate group
     float xscale;               // variant 1: x = fixed-point value * xscale
@@ -247,8 +250,26 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t v) {
 // backends/triton/core.py:14-15).
 // Subnormal form: (q + 8) * 2^-24 (low nibble) or 16 (q + 8) * 2^-24 (high
 // nibble), exact fp16 values built by one LOP3.
-__device__ __forceinline__ uint32_t sub_lo(uint32_t w) { return (w & 0x000F000Fu) ^ 0x00080008u; }
-__device__ __forceinline__ uint32_t sub_hi(uint32_t w) { return (w & 0x00F000F0u) ^ 0x00800080u; }
+// (w & m) ^ x as one three-input logic instruction. The masks live in
+// registers loaded from shared memory (NibMasks): written as two 32-bit
+// immediates, the expression takes two instructions, one per immediate.
+__device__ __forceinline__ uint32_t and_xor(uint32_t w, uint32_t m, uint32_t x) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(r) : "r"(w), "r"(m), "r"(x));
+    return r;
+}
+// Nibble masks: q + 8 of the low (high, times 16) nibble of every byte, and
+// of the low byte of every 16-bit half (fp16 subnormal operands).
+struct NibMasks {
+    uint32_t lo_m, lo_x, hi_m, hi_x;    // 0x0F0F0F0F 0x08080808 0xF0F0F0F0 0x80808080
+    uint32_t hlo_m, hlo_x, hhi_m, hhi_x;  // 0x000F000F 0x00080008 0x00F000F0 0x00800080
+};
+__device__ __forceinline__ NibMasks load_nib(const SmemTail* t) {
+    const uint4 a = *reinterpret_cast<const uint4*>(t->nib), b = *reinterpret_cast<const uint4*>(t->nib + 4);
+    return NibMasks{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+}
+__device__ __forceinline__ uint32_t sub_lo(uint32_t w, const NibMasks& k) { return and_xor(w, k.hlo_m, k.hlo_x); }
+__device__ __forceinline__ uint32_t sub_hi(uint32_t w, const NibMasks& k) { return and_xor(w, k.hhi_m, k.hhi_x); }
 // Exact-integer form: q as fp16.
 __device__ __forceinline__ __half2 int_lo(uint32_t w) {
     return __hsub2(bits_h2((w & 0x000F000Fu) ^ 0x64086408u), __float2half2_rn(1032.f));  // 1024 + (q + 8)
@@ -868,8 +889,11 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
                 dst[2] |= uint32_t(d2 & 0xff) << sh;
             }
 #pragma unroll
-            for (int p = 0; p < 3; ++p)
-                reinterpret_cast<uint2*>(t->xarea + p * kXPlane)[tid] = make_uint2(pe[p], po[p]);
+            for (int p = 0; p < 3; ++p) {
+                uint32_t* plane = reinterpret_cast<uint32_t*>(t->xarea + p * kXPlane);
+                plane[4 * (tid >> 1) + (tid & 1)] = pe[p];
+                plane[4 * (tid >> 1) + 2 + (tid & 1)] = po[p];
+            }
             msum += __shfl_xor_sync(0xffffffffu, msum, 1);
             msum += __shfl_xor_sync(0xffffffffu, msum, 2);
             if ((tid & 3) == 0) t->msum[tid >> 2] = msum;
@@ -887,6 +911,12 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         }
     }
     csync(P, t, cph, limit, lane);
+}
+
+// (even, odd) digits of 8-coordinate unit u in one plane (layout of SmemTail::xarea).
+__device__ __forceinline__ uint2 x_unit(const uint8_t* plane, int u) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(plane) + 4 * (u >> 1) + (u & 1);
+    return make_uint2(w[0], w[2]);
 }
 
 // Tensor-core step on 8-bit integers: D(16x8,s32) += A(16x32,u8) * B(32x8,s8).
@@ -918,6 +948,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
     constexpr int PG = gateup_pitch<H, F>();
     constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;  // staged scale row (gate, up, pad) in halves
     const int g = lane >> 2, tq = lane & 3;
+    const NibMasks nk = load_nib(t);
     float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxPartials);  // [warp][8]
     __syncwarp();  // mma.sync is .aligned: enter converged whatever the caller's waits did
     if (warp < AW) {
@@ -960,10 +991,10 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                         const uint2 wu = *reinterpret_cast<const uint2*>(row2 + H / 2 + 32 * dg);
                         const uint4 xb = reinterpret_cast<const uint4*>(xp)[4 * dg + tq];
                         // even coordinates of both units, then odd ones
-                        imma16832(alo[c], (wg.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wu.x & 0x0F0F0F0Fu) ^ 0x08080808u,
-                                  (wg.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wu.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
-                        imma16832(ahi[c], (wg.x & 0xF0F0F0F0u) ^ 0x80808080u, (wu.x & 0xF0F0F0F0u) ^ 0x80808080u,
-                                  (wg.y & 0xF0F0F0F0u) ^ 0x80808080u, (wu.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
+                        imma16832(alo[c], and_xor(wg.x, nk.lo_m, nk.lo_x), and_xor(wu.x, nk.lo_m, nk.lo_x),
+                                  and_xor(wg.y, nk.lo_m, nk.lo_x), and_xor(wu.y, nk.lo_m, nk.lo_x), xb.x, xb.y);
+                        imma16832(ahi[c], and_xor(wg.x, nk.hi_m, nk.hi_x), and_xor(wu.x, nk.hi_m, nk.hi_x),
+                                  and_xor(wg.y, nk.hi_m, nk.hi_x), and_xor(wu.y, nk.hi_m, nk.hi_x), xb.z, xb.w);
                     }
                 }
             } else {
@@ -972,10 +1003,10 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                     const int sb = warp * SBW + c;
                     const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
                     const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
-                    const uint2 xb = reinterpret_cast<const uint2*>(xp)[sb * 4 + tq];
+                    const uint2 xb = x_unit(xp, sb * 4 + tq);
                     ms[c] = t->msum[sb];
-                    imma16832(alo[c], (wg & 0x0F0F0F0Fu) ^ 0x08080808u, (wu & 0x0F0F0F0Fu) ^ 0x08080808u,
-                              ((wg >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wu >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                    imma16832(alo[c], and_xor(wg, nk.lo_m, nk.lo_x), and_xor(wu, nk.lo_m, nk.lo_x),
+                              and_xor(wg >> 4, nk.lo_m, nk.lo_x), and_xor(wu >> 4, nk.lo_m, nk.lo_x), xb.x,
                               xb.y);
                 }
             }
@@ -1050,6 +1081,69 @@ __device__ __forceinline__ void gateup_block_terms(const int (&alo)[4], const in
     pu = fmaf(su, ru, pu);
 }
 
+// Two scale blocks per warp (H 4096): one 16-row tile's gate and up terms
+// over the warp's blocks b0 = 2w and b1 = 2w + 1 with one accumulator pair.
+// An MMA of block b0 has a nonzero B only in columns 0-2 (digit planes 0-2,
+// supplied by lanes g < 3: x0), one of block b1 only in columns 3-5 (lanes
+// 3 <= g < 6: x1); every other lane reads zeros. Each B operand is a pair
+// of adjacent registers of one 16-byte load.
+template <int H>
+__device__ __forceinline__ void gateup_tile2(const uint8_t* row, const uint4 (&x0)[2], const uint4 (&x1)[2], int b0,
+                                             int b1, const NibMasks& nk, int (&lo)[4], int (&hi)[4]) {
+#pragma unroll
+    for (int dj = 0; dj < 2; ++dj) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const int dg = 2 * (c ? b1 : b0) + dj;
+            const uint4 xb = c ? x1[dj] : x0[dj];
+            const uint2 wg = *reinterpret_cast<const uint2*>(row + 32 * dg);
+            const uint2 wu = *reinterpret_cast<const uint2*>(row + H / 2 + 32 * dg);
+            imma16832(lo, and_xor(wg.x, nk.lo_m, nk.lo_x), and_xor(wu.x, nk.lo_m, nk.lo_x),
+                      and_xor(wg.y, nk.lo_m, nk.lo_x), and_xor(wu.y, nk.lo_m, nk.lo_x), xb.x, xb.y);
+            imma16832(hi, and_xor(wg.x, nk.hi_m, nk.hi_x), and_xor(wu.x, nk.hi_m, nk.hi_x),
+                      and_xor(wg.y, nk.hi_m, nk.hi_x), and_xor(wu.y, nk.hi_m, nk.hi_x), xb.z, xb.w);
+        }
+    }
+}
+
+// Per-lane coefficients of the two-block epilogue: the lane's term for a row
+// is s_b0 * (kA f0 + kB f1 - mA) + s_b1 * (kC f0 + kD f1 - mB), f the lane's two
+// accumulator columns (each 16 times the digit-plane sum), m = 128 * sum(M)
+// of the block (8 sum(M) at the same scale).
+struct Tile2Coef {
+    float kA, kB, kC, kD, mA, mB;
+};
+__device__ __forceinline__ Tile2Coef tile2_coef(int tq, int ms0, int ms1) {
+    Tile2Coef c{0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (tq == 0) {
+        c.kA = 1.f;
+        c.kB = 256.f;
+        c.mA = 128.f * float(ms0);
+    } else if (tq == 1) {
+        c.kA = 65536.f;
+        c.kD = 1.f;
+        c.mB = 128.f * float(ms1);
+    } else if (tq == 2) {
+        c.kC = 256.f;
+        c.kD = 65536.f;
+    }
+    return c;
+}
+__device__ __forceinline__ void tile2_terms(const int (&lo)[4], const int (&hi)[4], const Tile2Coef& k, float sg0,
+                                            float sg1, float su0, float su1, float& pg, float& pu) {
+    float f[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f[e] = float(16 * lo[e] + hi[e]);  // exact: |16 lo + hi| < 2^23
+    float tg = sg0 * (fmaf(k.kB, f[1], k.kA * f[0]) - k.mA) + sg1 * (fmaf(k.kD, f[1], k.kC * f[0]) - k.mB);
+    float tu = su0 * (fmaf(k.kB, f[3], k.kA * f[2]) - k.mA) + su1 * (fmaf(k.kD, f[3], k.kC * f[2]) - k.mB);
+    tg += __shfl_xor_sync(0xffffffffu, tg, 1);
+    tu += __shfl_xor_sync(0xffffffffu, tu, 1);
+    tg += __shfl_xor_sync(0xffffffffu, tg, 2);
+    tu += __shfl_xor_sync(0xffffffffu, tu, 2);
+    pg = tg;
+    pu = tu;
+}
+
 // Both GATEUP pieces of a 16-neuron slab in one pass (variant 1): stage A
 // holds neurons 0-7, stage B neurons 8-15. Each warp reads an activation
 // fragment once for the two 16-row tiles; the epilogue warp forms the 16
@@ -1064,10 +1158,42 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
     constexpr int PG = gateup_pitch<H, true>();
     constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;
     const int g = lane >> 2, tq = lane & 3;
+    const NibMasks nk = load_nib(t);
     float2* parta = reinterpret_cast<float2*>(sa + kStageData + kAuxPartials);  // [warp][8]
     float2* partb = reinterpret_cast<float2*>(sb + kStageData + kAuxPartials);
     __syncwarp();  // mma.sync is .aligned: enter converged
-    if (warp < AW) {
+    if constexpr (SBW == 8) {
+        // two scale blocks per warp: one accumulator pair per tile
+        const int b0 = 2 * warp, b1 = b0 + 1;
+        // digits of units 8 dg + 2t, 8 dg + 2t + 1 of the lane's plane, or zeros
+        const uint8_t* z = reinterpret_cast<const uint8_t*>(t->zero16);
+        const uint8_t* p0 = g < 3 ? t->xarea + g * kXPlane + 64 * (2 * b0) + 16 * tq : z;
+        const uint8_t* p1 = (g >= 3 && g < 6) ? t->xarea + (g - 3) * kXPlane + 64 * (2 * b1) + 16 * tq : z;
+        const int step0 = g < 3 ? 64 : 0, step1 = (g >= 3 && g < 6) ? 64 : 0;
+        uint4 x0[2], x1[2];
+#pragma unroll
+        for (int dj = 0; dj < 2; ++dj) {
+            x0[dj] = *reinterpret_cast<const uint4*>(p0 + dj * step0);
+            x1[dj] = *reinterpret_cast<const uint4*>(p1 + dj * step1);
+        }
+        const Tile2Coef k = tile2_coef(tq, t->msum64[2 * b0] + t->msum64[2 * b0 + 1],
+                                       t->msum64[2 * b1] + t->msum64[2 * b1 + 1]);
+        int loa[4] = {0, 0, 0, 0}, hia[4] = {0, 0, 0, 0}, lob[4] = {0, 0, 0, 0}, hib[4] = {0, 0, 0, 0};
+        gateup_tile2<H>(sa + g * PG + 8 * tq, x0, x1, b0, b1, nk, loa, hia);
+        gateup_tile2<H>(sb + g * PG + 8 * tq, x0, x1, b0, b1, nk, lob, hib);
+        const __half* sca = reinterpret_cast<const __half*>(sa + kStageData) + g * SPN;
+        const __half* scb = reinterpret_cast<const __half*>(sb + kStageData) + g * SPN;
+        float pga, pua, pgb, pub;
+        tile2_terms(loa, hia, k, __half2float(sca[b0]), __half2float(sca[b1]), __half2float(sca[H / 128 + b0]),
+                    __half2float(sca[H / 128 + b1]), pga, pua);
+        tile2_terms(lob, hib, k, __half2float(scb[b0]), __half2float(scb[b1]), __half2float(scb[H / 128 + b0]),
+                    __half2float(scb[H / 128 + b1]), pgb, pub);
+        const float xs = t->xscale * 0.0625f;  // the accumulator columns are 16 times the plane sums
+        if (tq == 0) {
+            parta[warp * 8 + g] = make_float2(pga * xs, pua * xs);
+            partb[warp * 8 + g] = make_float2(pgb * xs, pub * xs);
+        }
+    } else if (warp < AW) {
         const __half* sca = reinterpret_cast<const __half*>(sa + kStageData) + g * SPN;
         const __half* scb = reinterpret_cast<const __half*>(sb + kStageData) + g * SPN;
         float pga = 0.f, pua = 0.f, pgb = 0.f, pub = 0.f;
@@ -1098,14 +1224,14 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
                     const uint2 wua = *reinterpret_cast<const uint2*>(rowa + H / 2 + 32 * dg);
                     const uint2 wgb = *reinterpret_cast<const uint2*>(rowb + 32 * dg);
                     const uint2 wub = *reinterpret_cast<const uint2*>(rowb + H / 2 + 32 * dg);
-                    imma16832(aloa[c], (wga.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wua.x & 0x0F0F0F0Fu) ^ 0x08080808u,
-                              (wga.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wua.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
-                    imma16832(ahia[c], (wga.x & 0xF0F0F0F0u) ^ 0x80808080u, (wua.x & 0xF0F0F0F0u) ^ 0x80808080u,
-                              (wga.y & 0xF0F0F0F0u) ^ 0x80808080u, (wua.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
-                    imma16832(alob[c], (wgb.x & 0x0F0F0F0Fu) ^ 0x08080808u, (wub.x & 0x0F0F0F0Fu) ^ 0x08080808u,
-                              (wgb.y & 0x0F0F0F0Fu) ^ 0x08080808u, (wub.y & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x, xb.z);
-                    imma16832(ahib[c], (wgb.x & 0xF0F0F0F0u) ^ 0x80808080u, (wub.x & 0xF0F0F0F0u) ^ 0x80808080u,
-                              (wgb.y & 0xF0F0F0F0u) ^ 0x80808080u, (wub.y & 0xF0F0F0F0u) ^ 0x80808080u, xb.y, xb.w);
+                    imma16832(aloa[c], and_xor(wga.x, nk.lo_m, nk.lo_x), and_xor(wua.x, nk.lo_m, nk.lo_x),
+                              and_xor(wga.y, nk.lo_m, nk.lo_x), and_xor(wua.y, nk.lo_m, nk.lo_x), xb.x, xb.y);
+                    imma16832(ahia[c], and_xor(wga.x, nk.hi_m, nk.hi_x), and_xor(wua.x, nk.hi_m, nk.hi_x),
+                              and_xor(wga.y, nk.hi_m, nk.hi_x), and_xor(wua.y, nk.hi_m, nk.hi_x), xb.z, xb.w);
+                    imma16832(alob[c], and_xor(wgb.x, nk.lo_m, nk.lo_x), and_xor(wub.x, nk.lo_m, nk.lo_x),
+                              and_xor(wgb.y, nk.lo_m, nk.lo_x), and_xor(wub.y, nk.lo_m, nk.lo_x), xb.x, xb.y);
+                    imma16832(ahib[c], and_xor(wgb.x, nk.hi_m, nk.hi_x), and_xor(wub.x, nk.hi_m, nk.hi_x),
+                              and_xor(wgb.y, nk.hi_m, nk.hi_x), and_xor(wub.y, nk.hi_m, nk.hi_x), xb.z, xb.w);
                 }
             }
         } else {
@@ -1114,17 +1240,17 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const int sbk = warp * SBW + c;
-                const uint2 xb = reinterpret_cast<const uint2*>(xp)[sbk * 4 + tq];
+                const uint2 xb = x_unit(xp, sbk * 4 + tq);
                 ms[c] = t->msum[sbk];
                 const uint32_t wga = *reinterpret_cast<const uint32_t*>(rowa + 16 * sbk);
                 const uint32_t wua = *reinterpret_cast<const uint32_t*>(rowa + H / 2 + 16 * sbk);
                 const uint32_t wgb = *reinterpret_cast<const uint32_t*>(rowb + 16 * sbk);
                 const uint32_t wub = *reinterpret_cast<const uint32_t*>(rowb + H / 2 + 16 * sbk);
-                imma16832(aloa[c], (wga & 0x0F0F0F0Fu) ^ 0x08080808u, (wua & 0x0F0F0F0Fu) ^ 0x08080808u,
-                          ((wga >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wua >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                imma16832(aloa[c], and_xor(wga, nk.lo_m, nk.lo_x), and_xor(wua, nk.lo_m, nk.lo_x),
+                          and_xor(wga >> 4, nk.lo_m, nk.lo_x), and_xor(wua >> 4, nk.lo_m, nk.lo_x), xb.x,
                           xb.y);
-                imma16832(alob[c], (wgb & 0x0F0F0F0Fu) ^ 0x08080808u, (wub & 0x0F0F0F0Fu) ^ 0x08080808u,
-                          ((wgb >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((wub >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, xb.x,
+                imma16832(alob[c], and_xor(wgb, nk.lo_m, nk.lo_x), and_xor(wub, nk.lo_m, nk.lo_x),
+                          and_xor(wgb >> 4, nk.lo_m, nk.lo_x), and_xor(wub >> 4, nk.lo_m, nk.lo_x), xb.x,
                           xb.y);
             }
         }
@@ -1163,6 +1289,7 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     if (warp >= DW) return;
     __syncwarp();  // mma.sync is .aligned: enter converged
     const int g = lane >> 2, tq = lane & 3;
+    const NibMasks nk = load_nib(t);
     const uint32_t cnt = pc.count;
     const int n0 = 2 * tq, n1 = n0 + 1, n2 = n0 + 8, n3 = n0 + 9;
     const __half zero = __float2half_rn(0.f);
@@ -1234,14 +1361,14 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
             // FMA pipe, leaving the integer pipe to the nibble masks
             const uint32_t x = p01[hh], x8 = __umulhi(x, 1u << 24), y = p23[hh], y8 = __umulhi(y, 1u << 24);
             if constexpr (F) {
-                a01[4 * hh + 0] = sub_lo(x);
-                a01[4 * hh + 1] = sub_hi(x);
-                a01[4 * hh + 2] = sub_lo(x8);
-                a01[4 * hh + 3] = sub_hi(x8);
-                a23[4 * hh + 0] = sub_lo(y);
-                a23[4 * hh + 1] = sub_hi(y);
-                a23[4 * hh + 2] = sub_lo(y8);
-                a23[4 * hh + 3] = sub_hi(y8);
+                a01[4 * hh + 0] = sub_lo(x, nk);
+                a01[4 * hh + 1] = sub_hi(x, nk);
+                a01[4 * hh + 2] = sub_lo(x8, nk);
+                a01[4 * hh + 3] = sub_hi(x8, nk);
+                a23[4 * hh + 0] = sub_lo(y, nk);
+                a23[4 * hh + 1] = sub_hi(y, nk);
+                a23[4 * hh + 2] = sub_lo(y8, nk);
+                a23[4 * hh + 3] = sub_hi(y8, nk);
             } else {
                 const __half2 t01 = bits_h2(s01), t23 = bits_h2(s23);
                 a01[4 * hh + 0] = h2_bits(__hmul2(int_lo(x), t01));
@@ -1420,7 +1547,7 @@ __device__ bool wait_phase(const KernelParams& P, SmemTail* t, uint32_t bar, uin
 // Warp-uniform bounded wait until piece `idx`'s stage is full (acquire of
 // the TMA-written data). False when the producer stopped without a FINAL
 // marker.
-__device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane) {
+__device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane, uint32_t backoff_ns = 0) {
     const uint32_t bar = smem_u32(&t->full_bar[idx % kStages]);
     const uint32_t parity = (idx / kStages) & 1u;
     uint32_t spins = 0;
@@ -1430,6 +1557,7 @@ __device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane
         uint32_t late = 0;
         if (lane == 0 && (++spins & 255u) == 0 && gtimer() > deadline + kConsumerGraceNs) late = 1;
         if (__shfl_sync(0xffffffffu, late, 0)) return false;
+        if (backoff_ns) __nanosleep(backoff_ns);
     }
 }
 
@@ -1603,6 +1731,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
         mbar_init(smem_u32(&t->cbar), kConsumerWarps);
         t->octets_done = 0;
         t->abort = 0;
+        t->zero16[0] = t->zero16[1] = t->zero16[2] = t->zero16[3] = 0u;
+        const uint32_t nib[8] = {0x0F0F0F0Fu, 0x08080808u, 0xF0F0F0F0u, 0x80808080u,
+                                 0x000F000Fu, 0x00080008u, 0x00F000F0u, 0x00800080u};
+        for (int i = 0; i < 8; ++i) t->nib[i] = nib[i];
         t->flag = 0;
         t->last = 0;
         fence_mbar_init();
