@@ -437,54 +437,26 @@ struct ScaleCopy {
 template <int H, bool F>
 __host__ __device__ constexpr int gateup_pitch() { return F ? H + 32 : H + 16; }
 
-// GATEUP piece: gate+up records of neurons [n0, n0+cnt) (cnt <= 8).
+// One GATEUP piece (gate+up records of neurons [n0, n0+cnt), cnt <= 8) or
+// DOWN piece (down rows of one slab, cnt <= 16): lane k issues the bulk copy
+// of neuron k, every lane up to two 16-byte scale copies. No unrolled loops:
+// the producer's code shares the instruction caches with the consumers'
+// piece loops. (Out of line, the call costs more than the code it saves.)
 template <int H, bool F>
-__device__ bool producer_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                                uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t flags) {
+__device__ __forceinline__ bool producer_piece(Producer& pr, const KernelParams& P, const LayerPlan& L,
+                                            const DescView& d, uint32_t kind, uint32_t layer, uint32_t n0,
+                                            uint32_t cnt, uint32_t row, uint32_t flags, uint32_t need) {
     if (!producer_acquire_stage(pr, P)) return false;
+    const bool gu = kind == kPieceGateUp;
     const uint32_t s = pr.idx % kStages;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
     const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
     constexpr uint64_t rec = uint64_t(3) * H / 2;  // bytes per neuron record
+    const uint32_t bytes = gu ? uint32_t(H) : uint32_t(H / 2);
+    const uint32_t pitch = gu ? uint32_t(gateup_pitch<H, F>()) : uint32_t(H / 2 + 16);
     if (pr.lane == 0) {
         Piece& pc = pr.t->piece[s];
-        pc.kind = kPieceGateUp;
-        pc.layer = layer;
-        pc.dest = d.dest;
-        pc.n0 = n0;
-        pc.count = cnt;
-        pc.flags = flags;
-        trace_piece(P, pr.idx, 0);
-        mbar_arrive_expect_tx(bar, cnt * H);
-        for (uint32_t k = 0; k < cnt; ++k)
-            bulk_g2s(smem_u32(st + size_t(k) * gateup_pitch<H, F>()), d.src + (n0 + k) * rec, H, bar);
-    }
-    using SC = ScaleCopy<H>;
-    constexpr uint32_t upn = SC::kGateUp / SC::kUnit;
-    const uint8_t* sbase = reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow;
-    const uint32_t sdst = smem_u32(st + kStageData);
-    for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
-        const uint32_t k = i / upn, o = i % upn;
-        cp_async<SC::kUnit>(sdst + k * SC::kGateUpPitch + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
-    }
-    producer_close(pr, P, s);
-    ++pr.idx;
-    ++pr.octets;
-    return true;
-}
-
-// DOWN piece: down rows of neurons [n0, n0+cnt) (one slab, cnt <= 16).
-template <int H>
-__device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
-                              uint32_t layer, uint32_t n0, uint32_t cnt, uint32_t row, uint32_t flags, uint32_t need) {
-    if (!producer_acquire_stage(pr, P)) return false;
-    const uint32_t s = pr.idx % kStages;
-    uint8_t* st = pr.stages + size_t(s) * kStageBytes;
-    const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
-    constexpr uint64_t rec = uint64_t(3) * H / 2;
-    if (pr.lane == 0) {
-        Piece& pc = pr.t->piece[s];
-        pc.kind = kPieceDown;
+        pc.kind = kind;
         pc.layer = layer;
         pc.row = row;
         pc.dest = d.dest;
@@ -493,22 +465,42 @@ __device__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPl
         pc.need = need;
         pc.flags = flags;
         trace_piece(P, pr.idx, 0);
-        mbar_arrive_expect_tx(bar, cnt * (H / 2));
-        for (uint32_t r = 0; r < cnt; ++r)
-            bulk_g2s(smem_u32(st + size_t(r) * (H / 2 + 16)), d.src + (n0 + r) * rec + H, H / 2, bar);
+        mbar_arrive_expect_tx(bar, cnt * bytes);
     }
+    __syncwarp();
+    if (pr.lane < cnt)
+        bulk_g2s(smem_u32(st + size_t(pr.lane) * pitch), d.src + (n0 + pr.lane) * rec + (gu ? 0u : uint32_t(H)),
+                 bytes, bar);
     using SC = ScaleCopy<H>;
-    constexpr uint32_t upn = SC::kDown / SC::kUnit;
-    const uint8_t* sbase =
-        reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow + SC::kGateUp;
+    const uint32_t unit_bytes = gu ? SC::kGateUp : SC::kDown;  // scale bytes of one neuron in this piece
+    const uint32_t upn = unit_bytes / SC::kUnit;
+    const uint32_t spitch = gu ? SC::kGateUpPitch : SC::kDownPitch;
+    const uint8_t* sbase = reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow +
+                           (gu ? 0u : SC::kGateUp);
     const uint32_t sdst = smem_u32(st + kStageData);
+#pragma unroll 1
     for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
-        const uint32_t r = i / upn, o = i % upn;
-        cp_async<SC::kUnit>(sdst + r * SC::kDownPitch + o * SC::kUnit, sbase + r * SC::kRow + o * SC::kUnit);
+        const uint32_t k = i / upn, o = i % upn;
+        cp_async<SC::kUnit>(sdst + k * spitch + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
     }
     producer_close(pr, P, s);
     ++pr.idx;
+    if (gu) ++pr.octets;
     return true;
+}
+
+template <int H, bool F>
+__device__ __forceinline__ bool producer_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L,
+                                                const DescView& d, uint32_t layer, uint32_t n0, uint32_t cnt,
+                                                uint32_t flags) {
+    return producer_piece<H, F>(pr, P, L, d, kPieceGateUp, layer, n0, cnt, 0u, flags, 0u);
+}
+
+template <int H, bool F>
+__device__ __forceinline__ bool producer_down(Producer& pr, const KernelParams& P, const LayerPlan& L,
+                                              const DescView& d, uint32_t layer, uint32_t n0, uint32_t cnt,
+                                              uint32_t row, uint32_t flags, uint32_t need) {
+    return producer_piece<H, F>(pr, P, L, d, kPieceDown, layer, n0, cnt, row, flags, need);
 }
 
 // The GATEUP pieces of slab `slab` of one descriptor (variant 1 pairs the
@@ -534,7 +526,7 @@ struct PendingDown {
 // The DOWN piece of a pending slab. It is issued after the next slab's
 // GATEUP pieces, so that the consumers compute those while the last warp
 // of this slab's GATEUP finalises h.
-template <int H>
+template <int H, bool F>
 __device__ bool producer_slab_down(Producer& pr, const KernelParams& P, const LayerPlan& L, PendingDown& pd,
                                    uint32_t layer) {
     if (!pd.valid) return true;
@@ -543,7 +535,7 @@ __device__ bool producer_slab_down(Producer& pr, const KernelParams& P, const La
     const uint32_t n0 = pd.slab * kSlab;
     const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
     const uint32_t flags = (pd.slab + 1 == spg ? kCompletes : 0u) | pd.buf;
-    return producer_down<H>(pr, P, L, pd.d, layer, n0, cnt, pd.d.row * spg + pd.slab, flags, pd.need) &&
+    return producer_down<H, F>(pr, P, L, pd.d, layer, n0, cnt, pd.d.row * spg + pd.slab, flags, pd.need) &&
            !pr.t->abort;
 }
 
@@ -555,7 +547,7 @@ __device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPl
     if (!producer_slab_gateup<H, F>(pr, P, L, d, layer, slab, buf)) return false;
     const uint32_t need = pr.octets;
     ++pr.slabs;
-    if (!producer_slab_down<H>(pr, P, L, pd, layer)) return false;
+    if (!producer_slab_down<H, F>(pr, P, L, pd, layer)) return false;
     pd.d = d;
     pd.slab = slab;
     pd.need = need;
@@ -712,7 +704,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
             }
             if (t->abort) ok = false;
         }
-        if (ok) ok = producer_slab_down<H>(pr, P, L, pd, l);
+        if (ok) ok = producer_slab_down<H, F>(pr, P, L, pd, l);
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_ISSUED);
         if (ok) ok = producer_marker(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
     }
