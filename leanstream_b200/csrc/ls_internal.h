@@ -84,6 +84,8 @@ struct KernelParams {
 
 // Host-side launchers implemented in ls_kernel.cu.
 int launch_fused(const KernelParams& p, int grid, cudaStream_t stream);
+int launch_fused_traced(const KernelParams& p, int grid, cudaStream_t stream);  // p.trace set
+int prepare_kernels_traced();
 int prepare_kernels();  // raise the dynamic shared-memory limit once
 size_t kernel_smem_bytes();
 

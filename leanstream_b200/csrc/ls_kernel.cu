@@ -7,7 +7,7 @@
 // residual + RMSNorm glue (reduction.py:17-20;
 // examples/ministral/native/predictor_shared_input.cu:16-33).
 //
-// CTA = 16 consumer warps + 1 producer warp, one CTA per SM.
+// CTA = 16 consumer warps + a producer warp + an epilogue warp, one CTA per SM.
 //
 // Work unit: a slab = up to 16 consecutive neurons of one descriptor (group).
 // The CTA that owns a slab computes its gate/up rows, its h values and its
@@ -18,45 +18,55 @@
 //
 // Producer warp: streams each slab into a 6-stage shared-memory ring as
 // three pieces -- GATEUP (gate+up records of 8 neurons, one cp.async.bulk
-// per neuron, pitch H+16), GATEUP (the next 8) and DOWN (the slab's down
-// rows, pitch H/2+16) -- plus their fp16 scales (cp.async), completing one
-// mbarrier per stage. Weights do not depend on activations, so the producer
-// runs ahead across layer boundaries while the consumers synchronise.
+// per neuron), GATEUP (the next 8) and DOWN (the slab's down rows) -- plus
+// their fp16 scales (cp.async), completing one mbarrier per stage. A slab's
+// DOWN piece follows the next slab's GATEUP pieces. Weights do not depend on
+// activations, so the producer runs ahead across layer boundaries while the
+// consumers synchronise.
 //
-// Consumers (tensor cores, mma.sync m16n8k16, fp32 accumulation):
-//   GATEUP: A = 8 gate rows + 8 up rows of the piece's neurons, B = x; the
-//           hidden dimension is split over the warps; the last warp to
-//           finish sums the warp partials in warp order and forms
+// Consumers (tensor cores, mma.sync):
+//   GATEUP: 16 rows = the gate and up rows of 8 neurons; the hidden dimension
+//           is split over the warps. Variant 1: integer MMAs on q + 8 and the
+//           three 8-bit digit planes of x as 22-bit fixed point, the fp16
+//           scale applied per 128-block to the exact sums. Variant 0: fp16
+//           MMAs on w = fp16(q * s) (backends/triton/core.py:17). The
+//           epilogue warp sums the warp partials in warp order and forms
 //           h = fp16(fp16(SiLU(fp16 g)) * fp16 u).
-//   DOWN:   A = down weights with neurons along K (nibbles of two neurons
-//           interleaved with PRMT), B = h; one 16-neuron MMA per 16 columns.
-//   Two arithmetic variants (identical data flow):
-//     variant 1 (default): nibbles become exact fp16 subnormals
-//       (q + 8) * 2^-24 with one LOP3 per pair; the per-128 fp16 scale is
-//       applied once per block after the tensor-core sum (gate/up) or folded
-//       into B as h * s, carried as an fp16 value plus its fp16 residual
-//       (down), and the +8 offset is removed with the block sum of B.
-//       Products and sums are fp32, so outputs stay within the fp32-reference
-//       tolerance, but w is never rounded to fp16.
-//     variant 0: w = fp16(q * s) exactly as backends/triton/core.py:17
-//       before the MMA; B = x or h.
+//   DOWN:   fp16 MMAs, A = down weights with neurons along K (nibbles of two
+//           neurons paired with PRMT, exact fp16 subnormals (q + 8) 2^-24),
+//           B = h * s as an fp16 value plus its fp16 residual (variant 1) or
+//           h with w = fp16(q * s) (variant 0).
 //   Canonical arithmetic (identical for both schedules, so BatchCompat and
 //   Progressive outputs are bit-identical, tests/persistent_mlp_test.cu:65):
 //   a slab's h and partial row depend only on the slab; y sums the partial
 //   rows (row = descriptor row * slabs-per-group + slab) in a fixed tree of
 //   16-row chunks.
-// End of layer: every CTA counts itself done; CTAs 0..H/32-1 reduce one
-// 32-column block each and apply the epilogue (fp16 output, fp32 output,
-// residual add); then every CTA loads the next layer's input (RMSNorm).
+// End of layer: H/32 CTAs each reduce one 32-column block and apply the
+// epilogue (fp16 output, fp32 output, residual add); the next layer's input
+// is handed over through tagged words, without a grid-wide barrier.
 //
 // Every wait is bounded by a %globaltimer deadline and records an error;
 // consumer warps synchronise through an mbarrier with bounded waits (never
 // bar.sync), so a warp that gives up cannot strand the others.
+//
+// The file is compiled twice: ls_kernel_traced.cu includes it with
+// LS_KERNEL_TRACE 1 for the kernels that write phase stamps, which run only
+// for launches that ask for stamps; the other kernels carry no stamp code.
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include "ls_internal.h"
 
+#ifndef LS_KERNEL_TRACE
+#define LS_KERNEL_TRACE 0
+#endif
+#if LS_KERNEL_TRACE
+#define LS_KERNEL_NS traced
+#else
+#define LS_KERNEL_NS plain
+#endif
+
 namespace lsb {
+namespace LS_KERNEL_NS {
 
 enum : uint32_t { kPieceFinal = 0, kPieceGateUp = 1, kPieceDown = 2, kPieceLayer = 3 };
 // Piece flags. kPaired: a GATEUP piece whose slab's second GATEUP piece
@@ -298,17 +308,20 @@ __device__ __forceinline__ uint32_t scratch_tag(const KernelParams& P, uint32_t 
 }
 __device__ __forceinline__ bool grid_failed(const KernelParams& P) { return ld_acquire_gpu(P.ws + kWsErr) != 0; }
 __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
+    if (!LS_KERNEL_TRACE) return;
     if (P.trace) P.trace[size_t(blockIdx.x) * LS_B200_TRACE_WORDS + word] = gtimer();
 }
 // Per-piece stamps of CTAs 0..3 after the per-layer block:
 // [4][LS_B200_PIECE_TRACE_PIECES][4] = issued, closed (producer), ready, done (consumer warp 0).
 __device__ __forceinline__ void trace_piece(const KernelParams& P, uint32_t piece, uint32_t word) {
+    if (!LS_KERNEL_TRACE) return;
     if (P.trace && blockIdx.x < 4 && piece < LS_B200_PIECE_TRACE_PIECES)
         P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(gridDim.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
                 (size_t(blockIdx.x) * LS_B200_PIECE_TRACE_PIECES + piece) * 4 + word] = gtimer();
 }
 // Per-layer stamps after the launch-level block: [grid][nlayers][LS_B200_LAYER_TRACE_WORDS].
 __device__ __forceinline__ void trace_layer(const KernelParams& P, uint32_t l, uint32_t word) {
+    if (!LS_KERNEL_TRACE) return;
     if (P.trace)
         P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS +
                 (size_t(blockIdx.x) * P.nlayers + l) * LS_B200_LAYER_TRACE_WORDS + word] = gtimer();
@@ -1786,7 +1799,7 @@ static cudaError_t raise_smem(int bytes) {
     return cudaFuncSetAttribute(fused_mlp_kernel<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-int prepare_kernels() {
+int prepare() {
     const int bytes = int(kernel_smem_bytes());
     const cudaError_t errs[] = {raise_smem<256, false>(bytes),  raise_smem<512, false>(bytes),
                                 raise_smem<1024, false>(bytes), raise_smem<2048, false>(bytes),
@@ -1799,7 +1812,7 @@ int prepare_kernels() {
 }
 
 // H in {256, 512, 1024, 2048, 4096}.
-int launch_fused(const KernelParams& p, int grid, cudaStream_t stream) {
+int launch(const KernelParams& p, int grid, cudaStream_t stream) {
     const bool f = p.variant != 0;
     switch (p.H) {
         case 256: return f ? launch_t<256, true>(p, grid, stream) : launch_t<256, false>(p, grid, stream);
@@ -1810,5 +1823,23 @@ int launch_fused(const KernelParams& p, int grid, cudaStream_t stream) {
         default: return int(cudaErrorInvalidValue);
     }
 }
+
+}  // namespace LS_KERNEL_NS
+
+#if LS_KERNEL_TRACE
+int prepare_kernels_traced() { return traced::prepare(); }
+int launch_fused_traced(const KernelParams& p, int grid, cudaStream_t stream) {
+    return traced::launch(p, grid, stream);
+}
+#else
+size_t kernel_smem_bytes() { return plain::kernel_smem_bytes(); }
+int prepare_kernels() {
+    const int rc = plain::prepare();
+    return rc ? rc : prepare_kernels_traced();
+}
+int launch_fused(const KernelParams& p, int grid, cudaStream_t stream) {
+    return p.trace ? launch_fused_traced(p, grid, stream) : plain::launch(p, grid, stream);
+}
+#endif
 
 }  // namespace lsb
