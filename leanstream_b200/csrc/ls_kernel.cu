@@ -1308,7 +1308,7 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     const int mine = g >> 1;  // the MMA whose B column g this lane supplies
     uint32_t bj0[4] = {0u, 0u, 0u, 0u}, bj1[4] = {0u, 0u, 0u, 0u}, s01 = 0, s23 = 0;
     float hsum8 = 0.f;
-#pragma unroll
+#pragma unroll 2  // two tiles in flight; full unrolling costs instruction-cache space
     for (int i = 0; i < TPW; ++i) {
         const int tile = warp * TPW + i;
         const int blk = tile >> 1;  // 128-column scale block
