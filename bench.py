@@ -324,9 +324,19 @@ def run_gpu(args, rank, world, local_rank):
     if world > 1:
         from datetime import timedelta
 
+        # The per-layer allreduce is 16 KB: NVLink SHARP buys nothing at that
+        # size, and a rank that dies while bound to an NVLink multicast
+        # object can fault the other GPUs, so it stays off.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     steps_total = args.warmup + args.steps
+    t_start = time.time()
+
+    def progress(msg):  # phase marks on stderr (the JSON line is stdout's only content)
+        print(f"[bench rank {rank}/{world} {time.time() - t_start:7.2f}s] {msg}", file=sys.stderr, flush=True)
+
     st = Stack(rank, world, steps_total)
+    progress("weights and plans resident")
     stream = torch.cuda.Stream()
     N = st.N
     lib = N.load()
@@ -353,6 +363,7 @@ def run_gpu(args, rank, world, local_rank):
         graphs.append(g)
     torch.cuda.synchronize()
     barrier()
+    progress(f"{len(graphs)} token graphs captured")
 
     # ---- value: device-resident inputs, K graph replays
     with torch.cuda.stream(stream):
@@ -360,6 +371,7 @@ def run_gpu(args, rank, world, local_rank):
             graphs[s].replay()
     barrier()
     assert st.backend.status()[N.STATUS_ERROR] == 0, st.backend.status()
+    progress("warm-up done")
     clocks = ClockSampler(local_rank)
     clocks.start()
     time.sleep(0.3)
@@ -383,6 +395,7 @@ def run_gpu(args, rank, world, local_rank):
     if status[N.STATUS_ERROR]:
         raise RuntimeError(f"device status {status}")
     ms_per_step = ms / args.steps
+    progress(f"timed region: {ms_per_step:.3f} ms per token")
 
     # ---- kernel-only durations: pre-queued, event-bracketed launches of the
     # dominant kernel (one GPU: the multi-layer launch; N GPUs: the layer kernel)
@@ -415,6 +428,7 @@ def run_gpu(args, rank, world, local_rank):
         kern_bytes = [n * ALG_BYTES_PER_GROUP for n in st.active_local[args.warmup]]
         kernel_name = "fused_mlp_kernel (one layer, per-rank shard)"
     achieved_gbs = sum(kern_bytes) / (sum(kern_ms) * 1e-3) / 1e9
+    progress("kernel-only timing done")
     if args.trace and world == 1:
         trace_report(st, encoded[args.warmup], stream)
 
@@ -447,6 +461,7 @@ def run_gpu(args, rank, world, local_rank):
         f1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
+    progress("end-to-end timing done")
     if world > 1:
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -503,12 +518,20 @@ def run_gpu(args, rank, world, local_rank):
             "gpu_launches": launches_per_token * args.steps,
             "clocks": clock,
         }
-    # release graphs before tearing down the process group
-    del graphs, e2e_graph
+    # Release every graph before tearing down the process group: a graph that
+    # still holds NCCL work keeps destroy_process_group waiting for good (the
+    # capture loop's own variable referenced the last token graph).
     torch.cuda.synchronize()
+    for gr in graphs:
+        gr.reset()
+    e2e_graph.reset()
+    del graphs, e2e_graph, g
+    torch.cuda.synchronize()
+    progress("graphs released")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    progress("done")
     return result
 
 
