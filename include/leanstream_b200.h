@@ -187,7 +187,7 @@ enum {
     LS_B200_STATUS_ERROR = 0,       /* LS_B200_DEV_* code of the latest failed launch */
     LS_B200_STATUS_ERROR_EPOCH = 1, /* epoch (first layer) of that launch */
     LS_B200_STATUS_ERROR_DETAIL = 2,/* position / slot / wait site involved */
-    LS_B200_STATUS_LAUNCHES = 3,    /* sequence number (mod 2^24) of the latest completed launch */
+    LS_B200_STATUS_LAUNCHES = 3,    /* layers executed by this backend's launches (mod 0xFFFF0000) */
     LS_B200_STATUS_WORDS = 4
 };
 enum {

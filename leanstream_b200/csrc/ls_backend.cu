@@ -72,7 +72,8 @@ struct Backend {
     unsigned long long* xbuf = nullptr;     // tagged layer output handed to the next layer
     size_t partial_bytes = 0, xbuf_bytes = 0;
     uint32_t* ws = nullptr;
-    uint32_t seq = 0;
+    uint64_t layers_issued = 0;  // layers of the launches issued through this backend
+    bool clear_tags = false;     // the tag counter wrapped: clear the tagged scratch first
     uint32_t* status_host = nullptr;
     uint32_t* status_dev = nullptr;
     uint32_t* done_host = nullptr;
@@ -229,15 +230,18 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace, cudaStre
     p.eps = b.geo.rms_eps;
     p.nlayers = nlayers;
     p.max_layers = b.geo.max_layers;
-    // Scratch words carry tag (seq mod 2^24) << 8 | layer. When the sequence
-    // wraps, the scratch is cleared on the stream (no allocation) so that no
-    // word written 2^24 launches earlier can carry a current tag.
-    p.seq = ++b.seq & kSeqMask;
-    if (p.seq == 0) {
+    // The device tag counter advances by nlayers per launch and wraps below
+    // kTagWrap. After a launch that crossed a wrap, the scratch is cleared on
+    // the stream (no allocation) so that no word of the previous cycle can
+    // carry a current tag.
+    if (b.clear_tags) {
         cudaMemsetAsync(b.partial, 0, b.partial_bytes, stream);
         cudaMemsetAsync(b.xbuf, 0, b.xbuf_bytes, stream);
-        p.seq = ++b.seq & kSeqMask;
+        b.clear_tags = false;
     }
+    const uint64_t before = b.layers_issued;
+    b.layers_issued += nlayers;
+    if (before / kTagWrap != b.layers_issued / kTagWrap) b.clear_tags = true;
     p.partial = b.partial;
     p.xbuf = b.xbuf;
     p.ws = b.ws;
@@ -348,7 +352,8 @@ struct StaticScratch {
     uint32_t* ws = nullptr;
     uint32_t* status = nullptr;
     uint32_t* done = nullptr;
-    uint32_t seq = 0;  // launches on this device, for the scratch tags
+    uint64_t layers_issued = 0;  // layers launched on this device (tag counter wraps)
+    bool clear_tags = false;
 };
 StaticScratch g_static[kStaticDevices];
 std::mutex g_static_setup;
@@ -427,13 +432,13 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.eps = g.rms_eps;
     p.nlayers = 1;
     p.max_layers = kStaticLayers;
-    p.seq = ++s.seq & kSeqMask;
-    if (p.seq == 0) {  // tag wrap: clear the tagged scratch on the stream
+    if (s.clear_tags) {  // the tag counter wrapped: clear the tagged scratch on the stream
         cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
         if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
         if (e != cudaSuccess) return cuda_rc(e);
-        p.seq = ++s.seq & kSeqMask;
+        s.clear_tags = false;
     }
+    if (++s.layers_issued % kTagWrap == 0) s.clear_tags = true;
     p.partial = s.partial;
     p.xbuf = s.xbuf;
     p.ws = s.ws;

@@ -53,9 +53,15 @@ struct alignas(16) LayerPlan {
 
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
-constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsHeader = 8;
+constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsHeader = 8;
 constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, reduction-block claim, reduced column blocks
-constexpr uint32_t kSeqMask = 0xFFFFFFu;  // launch sequence bits inside scratch tags
+// Scratch tags: tag = 1 + base + l for launch-local layer l, where base is a
+// device counter (ws[kWsTag]) advanced by the layers of every launch at its
+// end, so CUDA-graph replays get fresh tags too. It wraps below kTagWrap;
+// the host clears the tagged scratch when its own count of issued layers
+// crosses a wrap (launches it did not issue, such as graph replays, are not
+// counted). Tag 0 never occurs: zeroed scratch holds no current word.
+constexpr uint32_t kTagWrap = 0xFFFF0000u;
 __host__ __device__ inline uint32_t ws_words(uint32_t max_layers) { return kWsHeader + kWsPerLayer * max_layers; }
 
 // Slabs per group and partial rows of the scratch buffer.
@@ -70,7 +76,6 @@ struct KernelParams {
     float eps;
     uint32_t nlayers;     // layers executed by this launch
     uint32_t max_layers;  // workspace capacity
-    uint32_t seq;         // launch sequence number (status word)
     uint32_t variant;     // 1: scales applied per 128-block after the tensor-core sums; 0: fp16(q*s) weights
     unsigned long long* partial;  // [N * slabs_per_group(G)][H] tagged fp32 slab partial rows
     unsigned long long* xbuf;     // [H/2] tagged fp16 pairs: a layer's hidden_out for the next layer

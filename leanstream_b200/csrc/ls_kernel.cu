@@ -126,6 +126,7 @@ struct SmemTail {
     float red2[kConsumerWarps][32];        // reduction warp sums
     __half hs[2][kSlab];                   // h of the last two slabs (kHsBuf)
     volatile uint32_t octets_done;         // GATEUP pieces finalised (monotonic)
+    uint32_t tagbase;                      // ws[kWsTag] at launch entry (scratch tags)
     volatile uint32_t abort;
     volatile uint32_t flag;                // CTA-uniform decision broadcast by thread 0
     uint32_t last;
@@ -300,12 +301,11 @@ __device__ __forceinline__ float round16(float v) { return __half2float(__float2
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
     return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] slab claim [2] block claim [3] reduced blocks
 }
-// Tag of the scratch words written by launch-local layer l (never 0: seq >= 1).
-// A 64-bit word (tag << 32 | value) is written by one store, so a reader that
-// sees the current tag also sees the value: no fence or counter is needed.
-__device__ __forceinline__ uint32_t scratch_tag(const KernelParams& P, uint32_t l) {
-    return (P.seq << 8) | (l & 0xffu);
-}
+// Tag of the scratch words written by launch-local layer l: 1 + the device
+// tag counter at launch entry + l (never 0). A 64-bit word (tag << 32 | value)
+// is written by one store, so a reader that sees the current tag also sees
+// the value: no fence or counter is needed.
+__device__ __forceinline__ uint32_t scratch_tag(const SmemTail* t, uint32_t l) { return 1u + t->tagbase + l; }
 __device__ __forceinline__ bool grid_failed(const KernelParams& P) { return ld_acquire_gpu(P.ws + kWsErr) != 0; }
 __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
     if (!LS_KERNEL_TRACE) return;
@@ -1304,7 +1304,7 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     const __half2 h01 = __halves2half2(hv0, hv1), h23 = __halves2half2(hv2, hv3);
     const __half* sd = reinterpret_cast<const __half*>(st + kStageData);
     unsigned long long* out = P.partial + size_t(pc.row) * H;
-    const unsigned long long tag = static_cast<unsigned long long>(scratch_tag(P, pc.layer)) << 32;
+    const unsigned long long tag = static_cast<unsigned long long>(scratch_tag(t, pc.layer)) << 32;
     const int mine = g >> 1;  // the MMA whose B column g this lane supplies
     uint32_t bj0[4] = {0u, 0u, 0u, 0u}, bj1[4] = {0u, 0u, 0u, 0u}, s01 = 0, s23 = 0;
     float hsum8 = 0.f;
@@ -1426,7 +1426,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         step = NBLK;
     }
     if (blk0 >= NBLK) return;
-    const uint32_t tag = scratch_tag(P, l);
+    const uint32_t tag = scratch_tag(t, l);
     const uint32_t nch = (rows + 15) / 16;
     for (uint32_t blk = blk0; blk < NBLK; blk += step) {
         // the residual and the error word are read now, off the critical
@@ -1509,15 +1509,11 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
     if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
 }
 
-// h of the neurons of one GATEUP stage from its warp partials ([warp][8]
-// float2 in the stage's aux area): the sums in warp order, each rounded to
-// fp16, then fp16(fp16(silu(g)) * u) (kernels/streaming_mlp.cu:34-37,
-// backends/triton/core.py:49-52). Lane i < count handles neuron n0 + i.
+// Sums of neuron i's gate and up warp partials ([warp][8] float2 in a
+// GATEUP stage's aux area), in warp order.
 template <int H>
-__device__ __forceinline__ void form_h(const KernelParams& P, const LayerPlan& L, const Piece& pc, const uint8_t* st,
-                                       SmemTail* t, uint32_t buf, uint32_t i) {
+__device__ __forceinline__ float2 sum_partials(const uint8_t* st, uint32_t i) {
     constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps;
-    if (i >= pc.count) return;
     const float2* part = reinterpret_cast<const float2*>(st + kStageData + kAuxPartials);
     float gsum = 0.f, usum = 0.f;
 #pragma unroll
@@ -1526,11 +1522,19 @@ __device__ __forceinline__ void form_h(const KernelParams& P, const LayerPlan& L
         gsum += v.x;
         usum += v.y;
     }
-    const float g16 = round16(gsum), u16 = round16(usum);
+    return make_float2(gsum, usum);
+}
+
+// h from the gate and up sums, each rounded to fp16, then
+// fp16(fp16(silu(g)) * u) (kernels/streaming_mlp.cu:34-37,
+// backends/triton/core.py:49-52), for neuron n of the slab.
+__device__ __forceinline__ void finish_h(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t buf,
+                                         uint32_t dest, uint32_t n, float2 gu) {
+    const float g16 = round16(gu.x), u16 = round16(gu.y);
     const float sl = round16(g16 / (1.f + expf(-g16)));
     const __half h = __float2half_rn(sl * u16);
-    t->hs[buf][(pc.n0 & (kSlab - 1)) + i] = h;
-    if (L.act) L.act[size_t(pc.dest) * P.G + pc.n0 + i] = __half_as_ushort(h);
+    t->hs[buf][n & (kSlab - 1)] = h;
+    if (L.act) L.act[size_t(dest) * P.G + n] = __half_as_ushort(h);
 }
 
 // Bounded wait of a warp on an mbarrier phase; false on abort or deadline.
@@ -1662,7 +1666,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             csync(P, t, cph, limit, lane);
         }
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
-        const uint32_t tag = scratch_tag(P, l);
+        const uint32_t tag = scratch_tag(t, l);
         ++l;
         L = next;
         stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag);
@@ -1691,29 +1695,36 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
             phases ^= 1u << s;
             const LayerPlan& L = plan_at(P, pc.layer);
             const uint32_t buf = (pc.flags & kHsBuf) ? 1u : 0u;
-            const uint8_t* st = stages + size_t(s) * kStageBytes;
-            if (F && (pc.flags & kPaired)) {
+            const bool paired = F && (pc.flags & kPaired);
+            uint32_t s2 = s, cnt = pc.count, n0 = pc.n0, i = uint32_t(lane);
+            const uint8_t* sq = stages + size_t(s) * kStageBytes;
+            if (paired) {
                 // the consumers saw the second stage full before writing
                 // their partials; this wait returns at once
                 if (!wait_full(t, idx + 1, deadline, lane)) break;
-                const uint32_t s2 = (idx + 1) % kStages;
-                const Piece pc2 = t->piece[s2];
-                if (lane < 8) form_h<H>(P, L, pc, st, t, buf, uint32_t(lane));
-                else if (lane < 16) form_h<H>(P, L, pc2, stages + size_t(s2) * kStageBytes, t, buf, uint32_t(lane - 8));
-                __syncwarp();
-                __threadfence_block();
-                if (lane == 0) {
-                    t->octets_done = t->octets_done + 2;
-                    mbar_arrive(smem_u32(&t->empty_bar[s]));
-                    mbar_arrive(smem_u32(&t->empty_bar[s2]));
+                s2 = (idx + 1) % kStages;
+                i = uint32_t(lane) & 7u;
+                if (lane >= 8) {
+                    cnt = lane < 16 ? t->piece[s2].count : 0u;
+                    n0 = t->piece[s2].n0;
+                    sq = stages + size_t(s2) * kStageBytes;
                 }
-                ++idx;
-                continue;
             }
-            form_h<H>(P, L, pc, st, t, buf, uint32_t(lane));
+            const bool mine = i < cnt;
+            const float2 gu = mine ? sum_partials<H>(sq, i) : make_float2(0.f, 0.f);
+            // The partials are in registers: the stages may be refilled while
+            // h is formed.
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_u32(&t->empty_bar[s]));
+                if (paired) mbar_arrive(smem_u32(&t->empty_bar[s2]));
+            }
+            if (mine) finish_h(P, L, t, buf, pc.dest, n0 + i, gu);
             __syncwarp();
             __threadfence_block();
-            if (lane == 0) t->octets_done = t->octets_done + 1;
+            if (lane == 0) t->octets_done = t->octets_done + (paired ? 2u : 1u);
+            if (paired) ++idx;
+            continue;
         }
         if (lane == 0) mbar_arrive(smem_u32(&t->empty_bar[s]));
     }
@@ -1736,6 +1747,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
         mbar_init(smem_u32(&t->cbar), kConsumerWarps);
         t->octets_done = 0;
         t->abort = 0;
+        t->tagbase = ld_relaxed_gpu(P.ws + kWsTag);  // advanced by the previous launch's last CTA
         t->zero16[0] = t->zero16[1] = t->zero16[2] = t->zero16[3] = 0u;
         const uint32_t nib[8] = {0x0F0F0F0Fu, 0x08080808u, 0xF0F0F0F0u, 0x80808080u,
                                  0x000F000Fu, 0x00080008u, 0x00F000F0u, 0x00800080u};
@@ -1777,12 +1789,15 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
             P.ws[kWsErr] = 0;
             P.ws[kWsDetail] = 0;
             P.ws[kWsExit] = 0;
+            uint32_t next_base = t->tagbase + nl;
+            if (next_base >= kTagWrap) next_base -= kTagWrap;
+            P.ws[kWsTag] = next_base;
             __threadfence();
             for (uint32_t l = 0; l < nl; ++l) {
                 const LayerPlan& L = plan_at(P, l);
                 st_release_sys(P.done + L.layer, L.epoch);
             }
-            st_relaxed_sys(P.status + LS_B200_STATUS_LAUNCHES, P.seq);
+            st_relaxed_sys(P.status + LS_B200_STATUS_LAUNCHES, next_base);
         }
     }
     if (tid == 0) trace(P, LS_B200_TRACE_EXIT);
