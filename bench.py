@@ -234,17 +234,25 @@ class Stack:
         return self.N.DeviceExecQueue(base, base + 4 * self.d_words, base + 4 * (self.d_words + self.i_words),
                                       max(self.nloc, 1))
 
+    def connect(self):
+        """Tensor parallel: exchange the ranks' IPC handles of their exchange
+        buffers (host collective, once); the data path is inside the kernel."""
+        import torch.distributed as dist
+
+        mine = self.backend.tp_setup(self.rank, self.world)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine)
+        self.backend.tp_connect(handles)
+
     def layer_args(self, layer: int, plan_words):
         N = self.N
-        tp = self.world > 1
         return self.backend.layer_args(
-            input=self.xs[layer], output=None if tp else self.y, cache=self.cache[layer], scales=self.scales[layer],
+            input=self.xs[layer], output=self.y, cache=self.cache[layer], scales=self.scales[layer],
             epoch=1, queue=self.queue_view(plan_words), mode=N.MODE_BATCH_COMPAT, layer=layer,
-            flags=N.NORM_INPUT | (N.NO_OUTPUT if tp else 0), residual=None if tp else self.xs[layer],
-            hidden_out=None if tp else self.xs[layer + 1], output_f32=self.y32 if tp else None)
+            flags=N.NORM_INPUT, residual=self.xs[layer], hidden_out=self.xs[layer + 1])
 
     def encode_token(self, plan_rows, base_dev):
-        """Encoded plans of one token for the multi-layer launch (one GPU)."""
+        """Encoded plans of one token for the multi-layer launch."""
         import torch
 
         blobs = [self.backend.encode_plan(self.layer_args(layer, plan_rows[layer])) for layer in range(LAYERS)]
@@ -252,28 +260,14 @@ class Stack:
         dev = host.to(base_dev)
         return host, dev
 
-    def enqueue_token(self, plan_rows, stream, encoded=None):
-        """Enqueues one token (all layers) on `stream`; returns launches of ours.
-        One GPU: one persistent multi-layer launch. N GPUs: per layer, the
-        fused layer kernel, an NCCL allreduce of the fp32 partial and the
-        epilogue kernel."""
-        import torch.distributed as dist
-
-        lib = self.N.load()
-        if self.world == 1:
-            host, dev = encoded
-            self.backend.launch_plans(dev, LAYERS, host, stream=stream)
-            return 1
-        launches = 0
-        for layer in range(LAYERS):
-            self.backend.launch(self.layer_args(layer, plan_rows[layer]), stream)
-            launches += 1
-            dist.all_reduce(self.y32)
-            rc = lib.ls_b200_tp_epilogue(self.y32.data_ptr(), self.xs[layer].data_ptr(), self.y.data_ptr(),
-                                         self.xs[layer + 1].data_ptr(), H, stream.cuda_stream)
-            assert rc == 0
-            launches += 1
-        return launches
+    def enqueue_token(self, plan_rows, stream, encoded):
+        """Enqueues one token (all layers) on `stream` as one persistent
+        multi-layer launch; returns launches of ours. N GPUs: every rank issues
+        the same launch over its own groups, and the kernel exchanges the fp32
+        partial outputs of each layer over NVLink peer memory."""
+        host, dev = encoded
+        self.backend.launch_plans(dev, LAYERS, host, stream=stream)
+        return 1
 
 
 def trace_report(st, encoded, stream):
@@ -324,9 +318,9 @@ def run_gpu(args, rank, world, local_rank):
     if world > 1:
         from datetime import timedelta
 
-        # The per-layer allreduce is 16 KB: NVLink SHARP buys nothing at that
-        # size, and a rank that dies while bound to an NVLink multicast
-        # object can fault the other GPUs, so it stays off.
+        # NCCL carries only host-side setup and the timing reduction; a rank
+        # that dies while bound to an NVLink multicast object can fault the
+        # other GPUs, so NVLS stays off.
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     steps_total = args.warmup + args.steps
@@ -336,6 +330,8 @@ def run_gpu(args, rank, world, local_rank):
         print(f"[bench rank {rank}/{world} {time.time() - t_start:7.2f}s] {msg}", file=sys.stderr, flush=True)
 
     st = Stack(rank, world, steps_total)
+    if world > 1:
+        st.connect()
     progress("weights and plans resident")
     stream = torch.cuda.Stream()
     N = st.N
@@ -349,13 +345,9 @@ def run_gpu(args, rank, world, local_rank):
     # ---- capture one CUDA graph per token (kernel params point at that token's plans)
     st.xs[0].copy_(st.x0)
     torch.cuda.synchronize()
-    if world > 1:  # NCCL warm-up before capture
-        with torch.cuda.stream(stream):
-            dist.all_reduce(st.y32)
-        torch.cuda.synchronize()
     graphs = []
     launches_per_token = 0
-    encoded = [st.encode_token(st.plans_dev[s], st.dev) if world == 1 else None for s in range(steps_total)]
+    encoded = [st.encode_token(st.plans_dev[s], st.dev) for s in range(steps_total)]
     for s in range(steps_total):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -397,37 +389,28 @@ def run_gpu(args, rank, world, local_rank):
     ms_per_step = ms / args.steps
     progress(f"timed region: {ms_per_step:.3f} ms per token")
 
-    # ---- kernel-only durations: pre-queued, event-bracketed launches of the
-    # dominant kernel (one GPU: the multi-layer launch; N GPUs: the layer kernel)
+    # ---- kernel-only durations: pre-queued, event-bracketed multi-layer
+    # launches (N GPUs: each rank's launch over its own groups, including the
+    # in-kernel exchange)
     barrier()
-    if world == 1:
-        reps = min(args.steps, 8)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * reps)]
-        with torch.cuda.stream(stream):
-            lib.ls_b200_spin(2_000_000, stream.cuda_stream)
-            for i in range(reps):
-                s = args.warmup + i
-                ev[2 * i].record(stream)
-                st.enqueue_token(st.plans_dev[s], stream, encoded[s])
-                ev[2 * i + 1].record(stream)
-        torch.cuda.synchronize()
-        kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps)]
-        kern_bytes = [sum(st.active_local[args.warmup + i]) * ALG_BYTES_PER_GROUP for i in range(reps)]
-        kernel_name = "fused_mlp_kernel (36-layer persistent launch)"
-    else:
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * LAYERS)]
-        with torch.cuda.stream(stream):
-            s = args.warmup
-            lib.ls_b200_spin(2_000_000, stream.cuda_stream)  # queue everything behind a 2 ms delay
-            for layer in range(LAYERS):
-                ev[2 * layer].record(stream)
-                st.backend.launch(st.layer_args(layer, st.plans_dev[s][layer]), stream)
-                ev[2 * layer + 1].record(stream)
-        torch.cuda.synchronize()
-        kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(LAYERS)]
-        kern_bytes = [n * ALG_BYTES_PER_GROUP for n in st.active_local[args.warmup]]
-        kernel_name = "fused_mlp_kernel (one layer, per-rank shard)"
+    reps = min(args.steps, 8)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * reps)]
+    with torch.cuda.stream(stream):
+        lib.ls_b200_spin(2_000_000, stream.cuda_stream)  # queue everything behind a 2 ms delay
+        for i in range(reps):
+            s = args.warmup + i
+            ev[2 * i].record(stream)
+            st.enqueue_token(st.plans_dev[s], stream, encoded[s])
+            ev[2 * i + 1].record(stream)
+    torch.cuda.synchronize()
+    kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps)]
+    kern_bytes = [sum(st.active_local[args.warmup + i]) * ALG_BYTES_PER_GROUP for i in range(reps)]
+    kernel_name = "fused_mlp_kernel (36-layer persistent launch" + (", per-rank shard)" if world > 1 else ")")
     achieved_gbs = sum(kern_bytes) / (sum(kern_ms) * 1e-3) / 1e9
+    if world > 1:  # the slowest rank's HBM rate
+        t = torch.tensor([-achieved_gbs], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        achieved_gbs = -float(t.item())
     progress("kernel-only timing done")
     if args.trace and world == 1:
         trace_report(st, encoded[args.warmup], stream)
@@ -435,7 +418,7 @@ def run_gpu(args, rank, world, local_rank):
     # ---- e2e: host plans + host x in, host y out, through the C ABI each step
     barrier()
     e2e_graph = torch.cuda.CUDAGraph()
-    slot_encoded = st.encode_token(st.slot_dev, st.dev) if world == 1 else None
+    slot_encoded = st.encode_token(st.slot_dev, st.dev)
     with torch.cuda.graph(e2e_graph, stream=stream):
         st.enqueue_token(st.slot_dev, torch.cuda.current_stream(), slot_encoded)
     x_host = st.x0.cpu().pin_memory()
@@ -503,7 +486,8 @@ def run_gpu(args, rank, world, local_rank):
             "config": {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
                        "group_size": G, "active_fraction": [FMIN, FMAX], "batch": 1,
                        "mean_active_groups_per_layer": mean_active,
-                       "parallelism": f"tp{world} (groups round-robin, fp32 NCCL allreduce per layer)",
+                       "parallelism": f"tp{world} (groups round-robin; fp32 partials exchanged over NVLink peer memory "
+                                      "inside the persistent launch)" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: ~841 MB of distinct weights per token",
                        "timing": "CUDA graph per token, CUDA events on the launching stream, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",

@@ -274,6 +274,26 @@ int ls_b200_view(void* backend, ls_compute_backend* out);
  * This is the Done epoch of backends/triton/primitives.py:10-14. */
 int ls_b200_completed_epoch(void* backend, uint32_t layer, uint32_t* epoch);
 
+/* Tensor parallel inside one launch (no counterpart in the reference, whose
+ * multi-GPU step is an allreduce between launches). Each rank computes the
+ * fp32 partial output of its own groups; at the end of every layer its
+ * reducer CTAs store their columns into every rank's exchange buffer over
+ * NVLink peer memory, and every rank forms y = the sum over ranks in rank
+ * order, fp16(y) and fp16(residual + fp16(y)) -- the arithmetic of an
+ * allreduce followed by ls_b200_tp_epilogue -- inside the same persistent
+ * launch, so a whole stack of layers is one launch per rank.
+ * ls_b200_tp_setup allocates and zeroes this rank's exchange buffer and
+ * writes its CUDA IPC handle (LS_B200_TP_HANDLE_BYTES) to handle_out; the
+ * host gathers the handles of all ranks (rank order) and passes them to
+ * ls_b200_tp_connect, which maps the peers' buffers and resets the tag
+ * counter. Afterwards every launch through the backend is a collective:
+ * all ranks issue the same launches in the same order. Consecutive layers
+ * of one launch must chain (next input = hidden_out) and a hidden_out's
+ * residual must be its layer's input, else EINVAL. world <= 8. */
+enum { LS_B200_TP_HANDLE_BYTES = 64 };
+int ls_b200_tp_setup(void* backend, uint32_t rank, uint32_t world, void* handle_out);
+int ls_b200_tp_connect(void* backend, const void* handles);
+
 /* Tensor-parallel layer epilogue (one rank): after the fp32 partial outputs
  * of all ranks are summed (NCCL allreduce of output_f32), round once to fp16
  * and add the residual -- the single-GPU epilogue of

@@ -14,6 +14,7 @@ SOURCE_CACHE, SOURCE_STAGING = 0, 1
 MODE_BATCH_COMPAT, MODE_PROGRESSIVE, MODE_AUTO = 0, 1, 2
 NORM_INPUT, NO_OUTPUT = 1, 2
 STATUS_ERROR, STATUS_ERROR_EPOCH, STATUS_ERROR_DETAIL, STATUS_LAUNCHES, STATUS_WORDS = 0, 1, 2, 3, 4
+TP_HANDLE_BYTES = 64
 DEV_OK, DEV_QUEUE_ERROR, DEV_TIMEOUT_EPOCH, DEV_TIMEOUT_READY, DEV_TIMEOUT_SYNC, DEV_BAD_DESCRIPTOR, DEV_BAD_PLAN = range(7)
 
 
@@ -124,6 +125,8 @@ SIGNATURES = {
     "ls_b200_queue_fail": (C.c_int, [C.POINTER(Queue), C.c_uint32]),
     "ls_b200_build_info": (C.c_char_p, []),
     "ls_b200_tp_epilogue": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "ls_b200_tp_setup": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "ls_b200_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "ls_b200_spin": (C.c_int, [C.c_uint64, C.c_void_p]),
 }
 

@@ -207,6 +207,21 @@ class B200Backend:
         _check(self.lib.ls_b200_launch_plans(self.context, _ptr(device_plans), count, hp, candidate, _ptr(trace),
                                              _stream(stream)), "ls_b200_launch_plans")
 
+    # -- tensor parallel inside one launch
+    def tp_setup(self, rank: int, world: int) -> bytes:
+        """Allocates this rank's exchange buffer; returns its IPC handle."""
+        h = (C.c_uint8 * N.TP_HANDLE_BYTES)()
+        _check(self.lib.ls_b200_tp_setup(self.context, rank, world, h), "ls_b200_tp_setup")
+        return bytes(h)
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Maps the peers' exchange buffers (handles in rank order). Every
+        launch afterwards is a collective of the ranks."""
+        if any(len(h) != N.TP_HANDLE_BYTES for h in handles):
+            raise ValueError("IPC handles of the wrong size")
+        blob = (C.c_uint8 * (N.TP_HANDLE_BYTES * len(handles))).from_buffer_copy(b"".join(handles))
+        _check(self.lib.ls_b200_tp_connect(self.context, blob), "ls_b200_tp_connect")
+
     def enqueue(self, layer: int, io_bucket: int, epoch: int, stream=None) -> None:
         _check(self.lib.ls_b200_enqueue(self.context, layer, io_bucket, epoch, _stream(stream)), "ls_b200_enqueue")
 

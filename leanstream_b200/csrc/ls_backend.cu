@@ -80,6 +80,13 @@ struct Backend {
     uint32_t* done_dev = nullptr;
     uint32_t* last_epoch = nullptr;  // host: epoch of the last enqueue per layer
     uint64_t scratch_bytes = 0;
+    // tensor parallel inside one launch (ls_b200_tp_setup / ls_b200_tp_connect)
+    uint32_t tp_world = 1, tp_rank = 0;
+    bool tp_connected = false;
+    unsigned long long* exch = nullptr;  // this rank's exchange buffer [2][world][H]
+    size_t exch_bytes = 0;
+    unsigned long long* peers[kMaxRanks] = {};
+    bool opened[kMaxRanks] = {};
 
     ls_kernel_candidate candidate(uint32_t id) const {
         // kernel_selector.cpp:9-16: invalid/unavailable ids fall back.
@@ -99,7 +106,21 @@ struct Backend {
         const uint32_t id = lut[size_t(layer) * lut_buckets + bucket];
         return candidate(id).id;
     }
+    void release_tp() {
+        for (uint32_t r = 0; r < uint32_t(kMaxRanks); ++r) {
+            if (opened[r]) cudaIpcCloseMemHandle(peers[r]);
+            opened[r] = false;
+            peers[r] = nullptr;
+        }
+        if (exch) cudaFree(exch);
+        exch = nullptr;
+        exch_bytes = 0;
+        tp_world = 1;
+        tp_rank = 0;
+        tp_connected = false;
+    }
     void release() {
+        release_tp();
         if (partial) cudaFree(partial);
         if (xbuf) cudaFree(xbuf);
         if (ws) cudaFree(ws);
@@ -248,7 +269,22 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace, cudaStre
     p.status = b.status_dev;
     p.done = b.done_dev;
     p.trace = trace;
+    p.world = b.tp_connected ? b.tp_world : 1u;
+    p.rank = b.tp_connected ? b.tp_rank : 0u;
+    for (uint32_t r = 0; r < p.world; ++r) p.xpeer[r] = b.peers[r];
     return p;
+}
+
+// A tensor-parallel launch forms each layer's outputs and the next input from
+// the layer input (the residual) and the ranks' partials: consecutive layers
+// must chain (next input = hidden_out) and a hidden_out's residual must be
+// its layer's input.
+bool tp_plans_ok(const LayerPlan* hp, uint32_t count) {
+    for (uint32_t i = 0; i < count; ++i) {
+        if (hp[i].hidden_out && hp[i].residual != hp[i].x) return false;
+        if (i + 1 < count && (!hp[i].hidden_out || hp[i + 1].x != hp[i].hidden_out)) return false;
+    }
+    return true;
 }
 
 int grid_for(const Backend& b, int32_t candidate, uint32_t* variant) {
@@ -265,6 +301,7 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     LayerPlan plan;
     int rc = encode(b, a, &plan);
     if (rc) return rc;
+    if (b.tp_connected && !tp_plans_ok(&plan, 1)) return EINVAL;
     KernelParams p = base_params(b, 1, a.trace, stream);
     p.plans = nullptr;
     p.first = plan;
@@ -275,6 +312,67 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------- ComputeBackend
+// Tensor parallel inside one launch. Setup allocates and zeroes this rank's
+// exchange buffer ([2 slots][world][H] tagged fp32 words) and exports it as
+// a CUDA IPC handle; connect maps every peer's buffer (NVLink peer memory),
+// resets the tag counter and clears the tagged scratch, so that all ranks
+// start from the same tags. From then on every launch through this backend
+// is a collective of the `world` ranks: they must issue the same launches
+// (same layers, in the same order), as for an allreduce.
+int tp_setup(Backend& b, uint32_t rank, uint32_t world, void* handle_out) {
+    if (!b.configured || world < 2 || world > uint32_t(kMaxRanks) || rank >= world) return EINVAL;
+    b.release_tp();
+    const size_t bytes = size_t(2) * world * b.geo.hidden * sizeof(unsigned long long);
+    cudaError_t e = cudaMalloc(&b.exch, bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.exch, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b.exch);
+    if (e != cudaSuccess) {
+        b.release_tp();
+        return cuda_rc(e);
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == LS_B200_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    b.exch_bytes = bytes;
+    b.tp_world = world;
+    b.tp_rank = rank;
+    return 0;
+}
+
+int tp_connect(Backend& b, const void* handles) {
+    if (!b.exch || b.tp_connected) return EINVAL;
+    const auto* hs = static_cast<const uint8_t*>(handles);
+    cudaError_t e = cudaSuccess;
+    for (uint32_t r = 0; r < b.tp_world && e == cudaSuccess; ++r) {
+        if (r == b.tp_rank) {
+            b.peers[r] = b.exch;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + size_t(r) * LS_B200_TP_HANDLE_BYTES, sizeof(h));
+        void* ptr = nullptr;
+        e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e == cudaSuccess) {
+            b.peers[r] = static_cast<unsigned long long*>(ptr);
+            b.opened[r] = true;
+        }
+    }
+    // same starting tags on every rank
+    if (e == cudaSuccess) e = cudaMemset(b.ws, 0, size_t(ws_words(b.geo.max_layers)) * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(b.partial, 0, b.partial_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.xbuf, 0, b.xbuf_bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        b.release_tp();
+        return cuda_rc(e);
+    }
+    b.layers_issued = 0;
+    b.clear_tags = false;
+    b.tp_connected = true;
+    return 0;
+}
+
 int view_enqueue(void* ctx, uint32_t layer, const void* input, void* output, void* stream, ls_exec_span core,
                  ls_device_exec_queue queue, uint32_t epoch, uint8_t mode) {
     // TritonBackend::submit (enqueue.cpp:38-43), all three modes accepted.
@@ -432,6 +530,7 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.eps = g.rms_eps;
     p.nlayers = 1;
     p.max_layers = kStaticLayers;
+    p.world = 1;  // one GPU: no exchange
     if (s.clear_tags) {  // the tag counter wrapped: clear the tagged scratch on the stream
         cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
         if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
@@ -503,6 +602,16 @@ int ls_b200_launch_static(const ls_b200_geometry* geometry, const ls_b200_layer_
     return lsb::launch_static(*geometry, *args, status, static_cast<cudaStream_t>(stream));
 }
 
+int ls_b200_tp_setup(void* backend, uint32_t rank, uint32_t world, void* handle_out) {
+    if (!backend || !handle_out) return EINVAL;
+    return lsb::tp_setup(*static_cast<Backend*>(backend), rank, world, handle_out);
+}
+
+int ls_b200_tp_connect(void* backend, const void* handles) {
+    if (!backend || !handles) return EINVAL;
+    return lsb::tp_connect(*static_cast<Backend*>(backend), handles);
+}
+
 uint32_t ls_b200_plan_size(void) { return uint32_t(sizeof(lsb::LayerPlan)); }
 
 int ls_b200_encode_plan(void* backend, const ls_b200_layer_args* args, void* plan) {
@@ -522,10 +631,10 @@ int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count
     if (!b->configured || count > b->geo.max_layers) return EINVAL;
     if ((reinterpret_cast<uintptr_t>(device_plans) & 15u) != 0) return EINVAL;
     const auto* hp = static_cast<const lsb::LayerPlan*>(host_plans);
-    for (uint32_t i = 0; i < count; ++i) {
+    for (uint32_t i = 0; i < count; ++i)
         if (hp[i].layer >= b->geo.max_layers || !hp[i].epoch) return EINVAL;
-        b->last_epoch[hp[i].layer] = hp[i].epoch;
-    }
+    if (b->tp_connected && !lsb::tp_plans_ok(hp, count)) return EINVAL;
+    for (uint32_t i = 0; i < count; ++i) b->last_epoch[hp[i].layer] = hp[i].epoch;
     lsb::KernelParams p = lsb::base_params(*b, count, trace, static_cast<cudaStream_t>(stream));
     p.plans = static_cast<const lsb::LayerPlan*>(device_plans);
     p.first = hp[0];

@@ -29,6 +29,7 @@ constexpr int kAuxPartials = 1280;  // aux offset of the GATEUP warp partials
 constexpr int kStageBytes = kStageData + kStageAux;
 constexpr int kMaxGroupSize = 256;
 constexpr int kMaxHidden = 4096;
+constexpr int kMaxRanks = 8;       // tensor-parallel ranks of one in-kernel exchange
 
 // One MLP layer of a launch (POD, copied into kernel parameters or read from
 // a device array for multi-layer launches).
@@ -54,7 +55,9 @@ struct alignas(16) LayerPlan {
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsHeader = 8;
-constexpr uint32_t kWsPerLayer = 4;  // path, slab claim, reduction-block claim, reduced column blocks
+// path, slab claim, reduction-block claim, reduced column blocks, CTAs past the
+// tensor-parallel gather of the layer's input
+constexpr uint32_t kWsPerLayer = 5;
 // Scratch tags: tag = 1 + base + l for launch-local layer l, where base is a
 // device counter (ws[kWsTag]) advanced by the layers of every launch at its
 // end, so CUDA-graph replays get fresh tags too. It wraps below kTagWrap;
@@ -85,6 +88,10 @@ struct KernelParams {
     uint64_t* trace;      // optional phase stamps
     const LayerPlan* plans;  // device array for nlayers > 1, else nullptr
     LayerPlan first;         // layer 0 when plans == nullptr
+    // Tensor parallel inside one launch (world > 1): rank r's exchange buffer
+    // [2 slots][world][H] tagged fp32 words, mapped on every rank (xpeer[r]).
+    uint32_t world, rank;
+    unsigned long long* xpeer[kMaxRanks];
 };
 
 // Host-side launchers implemented in ls_kernel.cu.

@@ -299,7 +299,8 @@ __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
-    return P.ws + kWsHeader + kWsPerLayer * l;  // [0] path [1] slab claim [2] block claim [3] reduced blocks
+    // [0] path [1] slab claim [2] block claim [3] reduced blocks [4] CTAs past the TP gather
+    return P.ws + kWsHeader + kWsPerLayer * l;
 }
 // Tag of the scratch words written by launch-local layer l: 1 + the device
 // tag counter at launch entry + l (never 0). A 64-bit word (tag << 32 | value)
@@ -762,6 +763,71 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
     return true;
 }
 
+// Tensor parallel (world > 1): the next layer's input from every rank's
+// fp32 partial of the finished layer, read from this rank's exchange buffer
+// (slot by the tag's parity) as soon as the words carry `tag`: y = the sum
+// over ranks in rank order, y16 = fp16(y), x = fp16(x_prev + y16), the single
+// rounding that ls_b200_tp_epilogue applies after an allreduce. Thread u
+// handles coordinates 8u..8u+7 (x_prev: its own copy of the finished layer's
+// input, which is that layer's residual); with `write` it also stores the
+// finished layer's outputs.
+template <int H>
+__device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail* t, uint64_t limit, int tid,
+                           uint32_t tag, uint4 xprev, bool write) {
+    const int lane = tid & 31;
+    const uint32_t slot = (tag - 1u) & 1u;
+    const unsigned long long* base = P.xpeer[P.rank] + size_t(slot) * P.world * H + 8 * tid;
+    float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (uint32_t r = 0; r < P.world; ++r) {
+        const unsigned long long* src = base + size_t(r) * H;
+        ulonglong2 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
+        uint32_t spins = 0;
+        for (;;) {
+            bool ok = true;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ok &= uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag;
+            if (__all_sync(0xffffffffu, ok)) break;
+            uint32_t late = 0;
+            if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit)) late = 1;
+            if (__shfl_sync(0xffffffffu, late, 0)) {
+                if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
+                break;
+            }
+            __nanosleep(32);
+            if (!ok) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            y[2 * k] += __uint_as_float(uint32_t(v[k].x));
+            y[2 * k + 1] += __uint_as_float(uint32_t(v[k].y));
+        }
+    }
+    const __half* xp = reinterpret_cast<const __half*>(&xprev);
+    uint4 out, y16v;
+    __half* o = reinterpret_cast<__half*>(&out);
+    __half* yh = reinterpret_cast<__half*>(&y16v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        yh[e] = __float2half_rn(y[e]);
+        o[e] = __float2half_rn(__half2float(xp[e]) + __half2float(yh[e]));
+    }
+    if (write) {
+        if (Lp.y32) {
+            float4* d = reinterpret_cast<float4*>(Lp.y32 + 8 * tid);
+            d[0] = make_float4(y[0], y[1], y[2], y[3]);
+            d[1] = make_float4(y[4], y[5], y[6], y[7]);
+        }
+        if (Lp.y && !(Lp.flags & LS_B200_NO_OUTPUT)) reinterpret_cast<uint4*>(Lp.y)[tid] = y16v;
+        if (Lp.hidden_out) reinterpret_cast<uint4*>(Lp.hidden_out)[tid] = out;
+    }
+    return out;
+}
+
 // Loads the layer's input, applies the HF RMSNorm of
 // predictor_shared_input.cu:16-33 when flagged
 // (inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv))), and
@@ -779,13 +845,15 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
 // grid-wide barrier between layers.
 template <int H, bool F>
 __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t& cph, uint64_t limit,
-                        int tid, bool tagged, uint32_t tag) {
+                        int tid, bool tagged, uint32_t tag, const LayerPlan* prev, uint4& xkeep) {
     constexpr int NU = H / 8;  // one 8-coordinate unit per thread (H <= 4096)
     const int warp = tid >> 5, lane = tid & 31;
     uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     float ss = 0.f;
     if (tid < NU) {
-        if (tagged) {
+        if (tagged && P.world > 1) {
+            raw = tp_gather<H>(P, *prev, t, limit, tid, tag, xkeep, blockIdx.x == 0);
+        } else if (tagged) {
             const unsigned long long* src = P.xbuf + 4 * tid;
             ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
             uint32_t spins = 0;
@@ -809,6 +877,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         } else {
             raw = __ldcg(reinterpret_cast<const uint4*>(L.x) + tid);
         }
+        xkeep = raw;  // this layer's input: the residual of a tensor-parallel gather
         const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1466,6 +1535,13 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             acc += cs;
         }
         t->red2[warp][lane] = acc;
+        // Tensor parallel: the exchange slot of layer l still holds layer
+        // l-2 until every CTA of each reading rank has gathered it. A rank
+        // publishes layer l only after all of its own CTAs gathered layer
+        // l-1, and every rank's CTAs gathered layer l-1 only after all ranks
+        // published it, hence after all CTAs had gathered layer l-2.
+        if (P.world > 1 && l > 0 && blk == blk0 && tid == 0)
+            wait_count(P, t, ws_layer(P, l) + 4, gridDim.x, limit, 12);
         csync(P, t, cph, limit, lane);
         if (warp == 0) {
             if (blk == blk0 && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
@@ -1473,27 +1549,39 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
             const uint32_t c = 32 * blk + lane;
-            const __half y16 = __float2half_rn(y);
-            __half hout = y16;
-            if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
-            if (chain) {
-                // the next layer's input first: it is on the critical path.
-                // Published even after an error so that the next layer's
-                // readers never wait for it; the error is reported anyway.
-                const uint32_t mine = __half_as_ushort(hout);
-                const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
-                if ((lane & 1) == 0)
-                    st_volatile_u64(P.xbuf + c / 2, (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
-            }
-            // outputs are skipped once any CTA had reported an error when
-            // the reduction started (best effort: the error word is the verdict)
-            uint32_t write = 0;
-            if (lane == 0) write = (good && err == 0u && !t->abort) ? 1u : 0u;
-            write = __shfl_sync(0xffffffffu, write, 0);
-            if (write) {
-                if (L.y32) L.y32[c] = y;
-                if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
-                if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
+            if (P.world > 1) {
+                // Tensor parallel: this rank's fp32 partial of the column goes
+                // to every rank's exchange buffer over NVLink (peer stores);
+                // the sum over ranks, its fp16 rounding and the residual are
+                // formed by the readers (tp_gather), identically on all ranks.
+                const uint32_t slot = (tag - 1u) & 1u;
+                const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(y);
+                const size_t at = (size_t(slot) * P.world + P.rank) * H + c;
+                for (uint32_t r = 0; r < P.world; ++r) st_volatile_u64(P.xpeer[r] + at, w);
+            } else {
+                const __half y16 = __float2half_rn(y);
+                __half hout = y16;
+                if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
+                if (chain) {
+                    // the next layer's input first: it is on the critical path.
+                    // Published even after an error so that the next layer's
+                    // readers never wait for it; the error is reported anyway.
+                    const uint32_t mine = __half_as_ushort(hout);
+                    const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
+                    if ((lane & 1) == 0)
+                        st_volatile_u64(P.xbuf + c / 2,
+                                        (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
+                }
+                // outputs are skipped once any CTA had reported an error when
+                // the reduction started (best effort: the error word is the verdict)
+                uint32_t write = 0;
+                if (lane == 0) write = (good && err == 0u && !t->abort) ? 1u : 0u;
+                write = __shfl_sync(0xffffffffu, write, 0);
+                if (write) {
+                    if (L.y32) L.y32[c] = y;
+                    if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
+                    if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
+                }
             }
         }
         csync(P, t, cph, limit, lane);  // red2 is reused by the next block
@@ -1578,7 +1666,8 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0);
+    uint4 xkeep = make_uint4(0u, 0u, 0u, 0u);
+    stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0, nullptr, xkeep);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % kStages;
         if (!wait_full(t, idx, deadline, lane)) {
@@ -1660,16 +1749,24 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         const bool chain = next && L->hidden_out && L->residual &&
                            reinterpret_cast<const void*>(next->x) == reinterpret_cast<const void*>(L->hidden_out);
         end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid, chain);
-        if (!next) continue;  // the FINAL marker follows
+        if (!next) {
+            // Tensor parallel: the launch's last layer has no next input to
+            // gather; CTA 0 forms its outputs from the ranks' partials.
+            if (P.world > 1 && blockIdx.x == 0 && tid < int(H / 8))
+                tp_gather<H>(P, *L, t, limit, tid, scratch_tag(t, l), xkeep, true);
+            continue;  // the FINAL marker follows
+        }
         if (!chain) {
             if (tid == 0) wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
             csync(P, t, cph, limit, lane);
         }
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
         const uint32_t tag = scratch_tag(t, l);
+        const LayerPlan* prev = L;
         ++l;
         L = next;
-        stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag);
+        stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag, prev, xkeep);
+        if (P.world > 1 && tid == 0) red_release_gpu(ws_layer(P, l) + 4, 1u);  // gathered (stage_x ends in a CTA barrier)
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
     }
 }

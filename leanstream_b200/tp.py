@@ -2,10 +2,16 @@
 
 Logical group g lives on rank g mod R at local slot g // R (static,
 round-robin residency: 1/R of each layer's weights per GPU). The active set
-is chosen globally; every rank enqueues only its own descriptors, computes
-an fp32 partial of y (LS_B200_NO_OUTPUT + output_f32), the partials are
-summed with an NCCL allreduce, and ls_b200_tp_epilogue rounds once to fp16
-and adds the residual, so every rank holds the same next hidden state.
+is chosen globally; every rank enqueues only its own descriptors and
+computes an fp32 partial of y. Two ways to combine the partials, with the
+same arithmetic (sum over ranks, one fp16 rounding, the residual), so every
+rank holds the same next hidden state:
+- inside the persistent launch (ls_b200_tp_setup / ls_b200_tp_connect): the
+  reducer CTAs store each layer's partial into every rank's exchange buffer
+  over NVLink peer memory and every CTA forms the next input from them --
+  one launch per token per rank, no collective library on the data path;
+- between launches: LS_B200_NO_OUTPUT + output_f32, an allreduce of the
+  partials, and ls_b200_tp_epilogue.
 """
 from __future__ import annotations
 

@@ -4,6 +4,7 @@ types, the kernel selector follows src/runtime/kernel_selector.cpp and
 tests/kernel_selector_test.cpp, and the host producer follows
 src/runtime/execution_queue.cpp. No compute call is made."""
 import ctypes as C
+import errno
 import re
 import subprocess
 from pathlib import Path
@@ -170,6 +171,11 @@ def test_view_and_unconfigured_errors(native_lib):
                          queue=N.DeviceExecQueue(1 << 24, 1 << 25, 1 << 26, 4))
     assert be.launch_rc(args, 0) != 0
     assert native_lib.ls_b200_status(be.context, (C.c_uint32 * 4)(), 4) != 0
+    # tensor-parallel setup needs a configured backend; connect needs a setup
+    handle = (C.c_uint8 * N.TP_HANDLE_BYTES)()
+    assert native_lib.ls_b200_tp_setup(be.context, 0, 2, handle) == errno.EINVAL
+    assert native_lib.ls_b200_tp_connect(be.context, handle) == errno.EINVAL
+    assert native_lib.ls_b200_tp_setup(None, 0, 2, handle) == errno.EINVAL
     be.close()
 
 
