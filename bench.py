@@ -18,7 +18,11 @@ scales U(0.005,0.02), hidden N(0,1)).
 Each token streams ~841 MB of distinct weights, far more than the 126 MB L2,
 so no L2 flush is needed between steps.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+Configuration 5 (--config 5): an 80-layer stack at 8192/28672 (448 groups
+of 64, 20 % active: 90 groups per layer), batch 1 -- ~5.8 GB of weights per
+token.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 3|5]
 """
 from __future__ import annotations
 
@@ -50,6 +54,23 @@ SEED = 3
 EPS = 1e-5
 WORKLOAD = "config3: 36-layer MLP stack, H4096/I12288, 192x64 groups, 20-40% active/layer, batch 1"
 METRIC = "MLP-stack tokens/s (batch-1 decode, 36 layers, H4096/I12288, 20-40% active INT4 groups)"
+CONFIG = 3
+
+
+def set_config(config: int) -> None:
+    """Geometry of BASELINE.json configuration 3 (the headline) or 5."""
+    global H, I, NGROUPS, LAYERS, FMIN, FMAX, GROUP_BYTES, SCALE_BYTES, ALG_BYTES_PER_GROUP
+    global TRAFFIC_PER_ALG_BYTE, WORKLOAD, METRIC, CONFIG
+    CONFIG = config
+    if config == 5:
+        H, I, NGROUPS, LAYERS = 8192, 28672, 448, 80
+        FMIN = FMAX = 0.2  # k = round(0.2 * 448) = 90 groups per layer
+        TRAFFIC_PER_ALG_BYTE = None  # no ncu capture of this geometry
+        WORKLOAD = "config5: 80-layer MLP stack, H8192/I28672, 448x64 groups, 20% active/layer, batch 1"
+        METRIC = "MLP-stack tokens/s (batch-1 decode, 80 layers, H8192/I28672, 20% active INT4 groups)"
+    GROUP_BYTES = G * 3 * H // 2
+    SCALE_BYTES = G * 3 * (H // 128) * 2
+    ALG_BYTES_PER_GROUP = GROUP_BYTES + SCALE_BYTES
 
 
 def active_sets(step: int):
@@ -405,7 +426,7 @@ def run_gpu(args, rank, world, local_rank):
     torch.cuda.synchronize()
     kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps)]
     kern_bytes = [sum(st.active_local[args.warmup + i]) * ALG_BYTES_PER_GROUP for i in range(reps)]
-    kernel_name = "fused_mlp_kernel (36-layer persistent launch" + (", per-rank shard)" if world > 1 else ")")
+    kernel_name = f"fused_mlp_kernel ({LAYERS}-layer persistent launch" + (", per-rank shard)" if world > 1 else ")")
     achieved_gbs = sum(kern_bytes) / (sum(kern_ms) * 1e-3) / 1e9
     if world > 1:  # the slowest rank's HBM rate
         t = torch.tensor([-achieved_gbs], device="cuda")
@@ -468,7 +489,7 @@ def run_gpu(args, rank, world, local_rank):
         # DRAM bytes (read + write) of one launch, from the ncu capture of
         # the same kernel on an 8-layer stack, scaled by the algorithmic
         # bytes the launch processes (traffic grows with the active groups).
-        traffic = TRAFFIC_PER_ALG_BYTE * float(np.mean(kern_bytes))
+        traffic = TRAFFIC_PER_ALG_BYTE * float(np.mean(kern_bytes)) if TRAFFIC_PER_ALG_BYTE else None
         result = {
             "metric": METRIC,
             "value": args.steps / (ms * 1e-3),
@@ -545,7 +566,7 @@ def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
     per_layer = elapsed / done
     return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": int(nthreads), "kind": "port",
             "sample": f"{done} of {LAYERS} layers of token 0 (same shapes and active fractions), "
-                      f"{elapsed:.1f} s of CPU work; tokens/s = 1/(36 x mean layer time)"}
+                      f"{elapsed:.1f} s of CPU work; tokens/s = 1/({LAYERS} x mean layer time)"}
 
 
 def run_reference(args, rank, world):
@@ -576,7 +597,7 @@ def run_reference(args, rank, world):
     t = [one(s) for s in range(args.steps)]
     per_layer = float(np.mean(t))
     value = 1.0 / (per_layer * LAYERS)
-    sample = f"each step = 1 MLP layer of the stack ({args.steps} steps); tokens/s = 1/(36 x mean layer time)"
+    sample = f"each step = 1 MLP layer of the stack ({args.steps} steps); tokens/s = 1/({LAYERS} x mean layer time)"
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3 * LAYERS,
@@ -596,13 +617,18 @@ def main():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--trace", action="store_true", help="print per-CTA phase stamps of one launch to stderr")
-    p.add_argument("--layers", type=int, default=36,
-                   help="stack depth; smaller values only for profiling captures (the metric is quoted at 36)")
+    p.add_argument("--config", type=int, choices=[3, 5], default=3,
+                   help="BASELINE.json configuration: 3 (headline, H 4096, 36 layers) or 5 (H 8192, 80 layers)")
+    p.add_argument("--layers", type=int, default=0,
+                   help="stack depth; smaller values only for profiling captures (the metric is quoted at the "
+                        "configuration's depth)")
     args = p.parse_args()
     global LAYERS
-    if not 1 <= args.layers <= 36:
-        p.error("--layers must be in [1, 36]")
-    LAYERS = args.layers
+    set_config(args.config)
+    if args.layers:
+        if not 1 <= args.layers <= LAYERS:
+            p.error(f"--layers must be in [1, {LAYERS}]")
+        LAYERS = args.layers
     if args.warmup < 3:
         p.error("--warmup must be at least 3")
     rank = int(os.environ.get("RANK", "0"))

@@ -143,7 +143,7 @@ int cuda_rc(cudaError_t e) { return e == cudaSuccess ? 0 : (int(e) > 0 ? int(e) 
 int configure(Backend& b, const ls_b200_geometry& g) {
     if (b.configured) return EBUSY;
     const uint32_t H = g.hidden, G = g.group_size, N = g.group_count;
-    // H = 256 * {1, 2, 4, 8, 16}: the kernel is instantiated per hidden size
+    // H = 256 * {1, 2, 4, 8, 16, 32}: the kernel is instantiated per hidden size
     const uint32_t sb = H / 256;
     if (!H || H % 256 || (sb & (sb - 1)) || H > uint32_t(kMaxHidden) || !G || G > uint32_t(kMaxGroupSize) || !N)
         return EINVAL;
@@ -290,7 +290,9 @@ bool tp_plans_ok(const LayerPlan* hp, uint32_t count) {
 int grid_for(const Backend& b, int32_t candidate, uint32_t* variant) {
     const uint32_t id = candidate >= 0 ? uint32_t(candidate) : b.select(b.state_layer, b.state_bucket);
     const ls_kernel_candidate c = b.candidate(id);
-    *variant = c.entry_point;
+    // variant 0 is built up to one piece's hidden extent; above it the
+    // candidate's grid runs variant 1
+    *variant = b.geo.hidden > uint32_t(kMaxPieceHidden) ? 1u : c.entry_point;
     int grid = int(c.cta_count);
     return grid > b.sms ? b.sms : grid;
 }

@@ -28,7 +28,8 @@ constexpr int kStageAux = 2304;
 constexpr int kAuxPartials = 1280;  // aux offset of the GATEUP warp partials
 constexpr int kStageBytes = kStageData + kStageAux;
 constexpr int kMaxGroupSize = 256;
-constexpr int kMaxHidden = 4096;
+constexpr int kMaxHidden = 8192;
+constexpr int kMaxPieceHidden = 4096;  // hidden extent of one staged piece
 constexpr int kMaxRanks = 8;       // tensor-parallel ranks of one in-kernel exchange
 
 // One MLP layer of a launch (POD, copied into kernel parameters or read from
@@ -99,6 +100,5 @@ int launch_fused(const KernelParams& p, int grid, cudaStream_t stream);
 int launch_fused_traced(const KernelParams& p, int grid, cudaStream_t stream);  // p.trace set
 int prepare_kernels_traced();
 int prepare_kernels();  // raise the dynamic shared-memory limit once
-size_t kernel_smem_bytes();
 
 }  // namespace lsb

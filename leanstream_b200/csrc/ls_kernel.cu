@@ -72,8 +72,10 @@ enum : uint32_t { kPieceFinal = 0, kPieceGateUp = 1, kPieceDown = 2, kPieceLayer
 // Piece flags. kPaired: a GATEUP piece whose slab's second GATEUP piece
 // is the next stage (both are consumed in one pass). kHsBuf: the h buffer
 // of the piece's slab (slabs alternate, so that the next slab's GATEUP can
-// finalise h while this slab's DOWN still reads it).
-enum : uint32_t { kCompletes = 4u, kLayerGood = 8u, kPaired = 16u, kHsBuf = 32u };
+// finalise h while this slab's DOWN still reads it). kPart1: the piece
+// covers the second K part (GATEUP) or column part (DOWN) of its slab
+// (hidden sizes above one piece's extent).
+enum : uint32_t { kCompletes = 4u, kLayerGood = 8u, kPaired = 16u, kHsBuf = 32u, kPart1 = 64u };
 constexpr uint32_t kPathFast = 1, kPathProgressive = 2, kPathAbort = 3;
 
 // Wait bounds, ordered so that a stalled launch always drains its ring:
@@ -102,25 +104,31 @@ struct DescView {
     uint32_t phys, dest, row, ok;
 };
 
-constexpr int kXPlane = kMaxHidden + 32;  // bytes per digit plane of the fixed-point activation
+// Piece geometry per hidden size. A piece covers at most 4096 hidden
+// coordinates: above that (H 8192) a slab's gate/up records are split into
+// KS parts along K and its down rows into KS parts along the output columns,
+// so that every piece has the stage layout of H 4096; the ring then holds
+// five stages (the activation planes take the sixth's space).
+template <int H>
+struct Geo {
+    static constexpr int HP = H > kMaxPieceHidden ? kMaxPieceHidden : H;  // hidden extent of one piece
+    static constexpr int KS = H / HP;                                    // parts per slab
+    static constexpr int NS = H > kMaxPieceHidden ? 5 : 6;               // ring stages
+    static constexpr int XPL = H + 32;  // bytes per digit plane of the fixed-point activation (8 banks apart)
+    static constexpr int XBYTES = 3 * XPL + 4 * (H / 32) + 4 * (H / 64);
+    static constexpr int UPT = (H / 8 + kConsumerThreads - 1) / kConsumerThreads;  // activation units per thread
+    static_assert(NS <= kStages, "ring stages");
+};
 
-struct SmemTail {
+struct alignas(16) SmemTail {
     unsigned long long full_bar[kStages];
     unsigned long long empty_bar[kStages];
     unsigned long long cbar;  // consumer-warp barrier (16 arrivals per phase)
     Piece piece[kStages];
     DescView dtab[32];        // producer's descriptor window
     unsigned long long pbar[kStages];  // GATEUP warp partials written (16 arrivals per phase)
-    // Activation of the current layer in B-fragment order (see stage_x):
-    // variant 1: three planes of signed 8-bit digits, 16 bytes per two
-    //            8-coordinate units u, u+1 (even digits of u, of u+1, odd
-    //            digits of u, of u+1), planes kXPlane bytes apart (8 banks);
-    // variant 0: uint4 of four fp16 pairs per 8 coordinates.
-    alignas(16) uint8_t xarea[3 * kXPlane];
     alignas(16) uint32_t zero16[4];        // read by lanes whose B operand is zero
     alignas(16) uint32_t nib[8];           // nibble masks and offsets (NibMasks), see and_xor
-    int msum[kMaxHidden / 32];  // variant 1: sum of the fixed-point x over each 32-coordinate sub-block
-    int msum64[kMaxHidden / 64];  // variant 1: the same over each 64-coordinate group
     float xscale;               // variant 1: x = fixed-point value * xscale
     float red[kConsumerWarps];             // RMSNorm warp sums
     float red2[kConsumerWarps][32];        // reduction warp sums
@@ -132,7 +140,36 @@ struct SmemTail {
     uint32_t last;
 };
 
-size_t kernel_smem_bytes() { return size_t(kStages) * kStageBytes + sizeof(SmemTail); }
+// Activation of the current layer, after the tail (Geo<H>::XBYTES):
+// variant 1: three planes of signed 8-bit digits, 16 bytes per two
+//            8-coordinate units u, u+1 (even digits of u, of u+1, odd digits
+//            of u, of u+1), planes Geo<H>::XPL bytes apart; then the sums of
+//            the fixed-point x over each 32-coordinate sub-block and over
+//            each 64-coordinate group;
+// variant 0: uint4 of four fp16 pairs per 8 coordinates.
+template <int H>
+__device__ __forceinline__ uint8_t* xarea(SmemTail* t) { return reinterpret_cast<uint8_t*>(t + 1); }
+template <int H>
+__device__ __forceinline__ int* xsum32(SmemTail* t) { return reinterpret_cast<int*>(xarea<H>(t) + 3 * Geo<H>::XPL); }
+template <int H>
+__device__ __forceinline__ int* xsum64(SmemTail* t) { return xsum32<H>(t) + H / 32; }
+
+// The part of the activation one GATEUP piece reduces over (K part kp).
+struct XPart {
+    const uint8_t* x;  // digit plane 0 at the part's first coordinate
+    const int* m32;    // sub-block sums of the part
+    const int* m64;    // 64-coordinate group sums of the part
+};
+template <int H>
+__device__ __forceinline__ XPart xpart(SmemTail* t, uint32_t kp) {
+    constexpr int HP = Geo<H>::HP;
+    return XPart{xarea<H>(t) + kp * HP, xsum32<H>(t) + kp * (HP / 32), xsum64<H>(t) + kp * (HP / 64)};
+}
+
+template <int H>
+__host__ __device__ constexpr size_t kernel_smem_bytes() {
+    return size_t(Geo<H>::NS) * kStageBytes + sizeof(SmemTail) + Geo<H>::XBYTES;
+}
 
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ uint64_t gtimer() {
@@ -369,7 +406,7 @@ __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_
 
 // ------------------------------------------------------------ producer side
 struct Producer {
-    uint32_t idx;     // pieces issued so far (stage = idx % kStages)
+    uint32_t idx;     // pieces issued so far (stage = idx % Geo<H>::NS)
     uint32_t octets;  // GATEUP pieces issued so far
     uint32_t slabs;   // slabs issued so far (h buffer = slabs & 1)
     uint32_t lane;
@@ -381,9 +418,11 @@ struct Producer {
 };
 
 // Waits until the next stage is free.
+template <int H>
 __device__ bool producer_acquire_stage(Producer& pr, const KernelParams& P) {
-    const uint32_t s = pr.idx % kStages;
-    const uint32_t parity = ((pr.idx / kStages) & 1u) ^ 1u;
+    constexpr uint32_t NS = Geo<H>::NS;
+    const uint32_t s = pr.idx % NS;
+    const uint32_t parity = ((pr.idx / NS) & 1u) ^ 1u;
     const uint32_t bar = smem_u32(&pr.t->empty_bar[s]);
     uint32_t spins = 0;
     for (;;) {
@@ -414,10 +453,11 @@ __device__ __forceinline__ void producer_close(Producer& pr, const KernelParams&
 }
 
 // A data-less piece (LAYER or FINAL marker).
+template <int H>
 __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t kind, uint32_t layer, uint32_t rows,
                                 uint32_t flags) {
-    if (!producer_acquire_stage(pr, P)) return false;
-    const uint32_t s = pr.idx % kStages;
+    if (!producer_acquire_stage<H>(pr, P)) return false;
+    const uint32_t s = pr.idx % Geo<H>::NS;
     if (pr.lane == 0) {
         Piece& pc = pr.t->piece[s];
         pc.kind = kind;
@@ -435,13 +475,17 @@ __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t ki
 // Scale copy granule: 16 bytes when every scale row and segment is 16-byte
 // aligned (H >= 1024: row pitch 3H/64 bytes), else the segment size.
 // Staged scale rows are padded by 16 bytes so that consecutive neurons' rows
-// start 4 banks apart (conflict-free reads by the MMA lane layout).
+// start 4 banks apart (conflict-free reads by the MMA lane layout). A staged
+// row holds the scales of the piece's part: gate then up (GATEUP) or down.
 template <int H>
 struct ScaleCopy {
+    static constexpr int HP = Geo<H>::HP;
     static constexpr int kUnit = H >= 1024 ? 16 : H / 64;
-    static constexpr uint32_t kRow = 3 * H / 64;   // bytes of one neuron's scales
-    static constexpr uint32_t kGateUp = H / 32;    // gate + up scale bytes of one neuron
-    static constexpr uint32_t kDown = H / 64;      // down scale bytes of one neuron
+    static constexpr uint32_t kRow = 3 * H / 64;   // bytes of one neuron's scales in HBM
+    static constexpr uint32_t kGateUp = HP / 32;   // staged gate + up scale bytes of one neuron
+    static constexpr uint32_t kDown = HP / 64;     // staged down scale bytes of one neuron
+    static constexpr uint32_t kPart = HP / 64;     // offset of part kp+1's gate (or down) scales
+    static constexpr uint32_t kUpSkip = (H - HP) / 64;  // the gate scales of the other parts
     static constexpr uint32_t kGateUpPitch = kGateUp + 16;
     static constexpr uint32_t kDownPitch = kDown + 16;
 };
@@ -452,22 +496,26 @@ template <int H, bool F>
 __host__ __device__ constexpr int gateup_pitch() { return F ? H + 32 : H + 16; }
 
 // One GATEUP piece (gate+up records of neurons [n0, n0+cnt), cnt <= 8) or
-// DOWN piece (down rows of one slab, cnt <= 16): lane k issues the bulk copy
-// of neuron k, every lane up to two 16-byte scale copies. No unrolled loops:
-// the producer's code shares the instruction caches with the consumers'
-// piece loops. (Out of line, the call costs more than the code it saves.)
+// DOWN piece (down rows of one slab, cnt <= 16) of part kp: lane k issues
+// the bulk copy of neuron k (parts of a split slab: lanes 0-7 the gate and
+// 8-15 the up part of neuron k & 7), every lane up to two 16-byte scale
+// copies. No unrolled loops: the producer's code shares the instruction
+// caches with the consumers' piece loops. (Out of line, the call costs more
+// than the code it saves.)
 template <int H, bool F>
 __device__ __forceinline__ bool producer_piece(Producer& pr, const KernelParams& P, const LayerPlan& L,
                                             const DescView& d, uint32_t kind, uint32_t layer, uint32_t n0,
                                             uint32_t cnt, uint32_t row, uint32_t flags, uint32_t need) {
-    if (!producer_acquire_stage(pr, P)) return false;
+    constexpr int HP = Geo<H>::HP, KS = Geo<H>::KS;
+    if (!producer_acquire_stage<H>(pr, P)) return false;
     const bool gu = kind == kPieceGateUp;
-    const uint32_t s = pr.idx % kStages;
+    const uint32_t kp = (flags & kPart1) ? 1u : 0u;
+    const uint32_t s = pr.idx % Geo<H>::NS;
     uint8_t* st = pr.stages + size_t(s) * kStageBytes;
     const uint32_t bar = smem_u32(&pr.t->full_bar[s]);
     constexpr uint64_t rec = uint64_t(3) * H / 2;  // bytes per neuron record
-    const uint32_t bytes = gu ? uint32_t(H) : uint32_t(H / 2);
-    const uint32_t pitch = gu ? uint32_t(gateup_pitch<H, F>()) : uint32_t(H / 2 + 16);
+    const uint32_t bytes = gu ? uint32_t(HP) : uint32_t(HP / 2);
+    const uint32_t pitch = gu ? uint32_t(gateup_pitch<HP, F>()) : uint32_t(HP / 2 + 16);
     if (pr.lane == 0) {
         Piece& pc = pr.t->piece[s];
         pc.kind = kind;
@@ -482,24 +530,35 @@ __device__ __forceinline__ bool producer_piece(Producer& pr, const KernelParams&
         mbar_arrive_expect_tx(bar, cnt * bytes);
     }
     __syncwarp();
-    if (pr.lane < cnt)
-        bulk_g2s(smem_u32(st + size_t(pr.lane) * pitch), d.src + (n0 + pr.lane) * rec + (gu ? 0u : uint32_t(H)),
-                 bytes, bar);
+    if constexpr (KS == 1) {
+        if (pr.lane < cnt)
+            bulk_g2s(smem_u32(st + size_t(pr.lane) * pitch), d.src + (n0 + pr.lane) * rec + (gu ? 0u : uint32_t(H)),
+                     bytes, bar);
+    } else {
+        // gate part kp at kp*HP/2 of the record, up part at H/2 + kp*HP/2,
+        // down part at H + kp*HP/2; each HP/2 bytes
+        const uint32_t k = gu ? (pr.lane & 7u) : pr.lane, half = gu ? (pr.lane >> 3) : 0u;
+        if ((gu ? pr.lane < 16u : true) && k < cnt)
+            bulk_g2s(smem_u32(st + size_t(k) * pitch + half * (HP / 2)),
+                     d.src + (n0 + k) * rec + (gu ? half * uint32_t(H / 2) : uint32_t(H)) + kp * uint32_t(HP / 2),
+                     uint32_t(HP / 2), bar);
+    }
     using SC = ScaleCopy<H>;
     const uint32_t unit_bytes = gu ? SC::kGateUp : SC::kDown;  // scale bytes of one neuron in this piece
     const uint32_t upn = unit_bytes / SC::kUnit;
     const uint32_t spitch = gu ? SC::kGateUpPitch : SC::kDownPitch;
     const uint8_t* sbase = reinterpret_cast<const uint8_t*>(L.scales) + (size_t(d.phys) * P.G + n0) * SC::kRow +
-                           (gu ? 0u : SC::kGateUp);
+                           (gu ? 0u : uint32_t(H / 32)) + kp * SC::kPart;
     const uint32_t sdst = smem_u32(st + kStageData);
 #pragma unroll 1
     for (uint32_t i = pr.lane; i < cnt * upn; i += 32) {
         const uint32_t k = i / upn, o = i % upn;
-        cp_async<SC::kUnit>(sdst + k * spitch + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit);
+        const uint32_t skip = (KS > 1 && gu && 2 * o >= upn) ? SC::kUpSkip : 0u;  // up scales of part kp
+        cp_async<SC::kUnit>(sdst + k * spitch + o * SC::kUnit, sbase + k * SC::kRow + o * SC::kUnit + skip);
     }
     producer_close(pr, P, s);
     ++pr.idx;
-    if (gu) ++pr.octets;
+    if (gu && (KS == 1 || kp == KS - 1)) ++pr.octets;  // h of the octet is formed after its last part
     return true;
 }
 
@@ -518,15 +577,21 @@ __device__ __forceinline__ bool producer_down(Producer& pr, const KernelParams& 
 }
 
 // The GATEUP pieces of slab `slab` of one descriptor (variant 1 pairs the
-// two halves of a 16-neuron slab so that they are consumed in one pass).
+// two halves of a 16-neuron slab so that they are consumed in one pass),
+// for each K part in order.
 template <int H, bool F>
 __device__ bool producer_slab_gateup(Producer& pr, const KernelParams& P, const LayerPlan& L, const DescView& d,
                                      uint32_t layer, uint32_t slab, uint32_t buf) {
     const uint32_t n0 = slab * kSlab;
     const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
-    const uint32_t first = (F && cnt > 8u) ? (buf | kPaired) : buf;
-    if (!producer_gateup<H, F>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u, first) || pr.t->abort) return false;
-    if (cnt > 8u && (!producer_gateup<H, F>(pr, P, L, d, layer, n0 + 8, cnt - 8, buf) || pr.t->abort)) return false;
+#pragma unroll 1
+    for (uint32_t kp = 0; kp < uint32_t(Geo<H>::KS); ++kp) {
+        const uint32_t part = kp ? kPart1 : 0u;
+        const uint32_t first = (F && cnt > 8u) ? (buf | part | kPaired) : (buf | part);
+        if (!producer_gateup<H, F>(pr, P, L, d, layer, n0, cnt < 8u ? cnt : 8u, first) || pr.t->abort) return false;
+        if (cnt > 8u && (!producer_gateup<H, F>(pr, P, L, d, layer, n0 + 8, cnt - 8, buf | part) || pr.t->abort))
+            return false;
+    }
     return true;
 }
 
@@ -548,9 +613,15 @@ __device__ bool producer_slab_down(Producer& pr, const KernelParams& P, const La
     const uint32_t spg = slabs_per_group(P.G);
     const uint32_t n0 = pd.slab * kSlab;
     const uint32_t cnt = (P.G - n0) < kSlab ? (P.G - n0) : kSlab;
-    const uint32_t flags = (pd.slab + 1 == spg ? kCompletes : 0u) | pd.buf;
-    return producer_down<H, F>(pr, P, L, pd.d, layer, n0, cnt, pd.d.row * spg + pd.slab, flags, pd.need) &&
-           !pr.t->abort;
+#pragma unroll 1
+    for (uint32_t kp = 0; kp < uint32_t(Geo<H>::KS); ++kp) {
+        const bool last = kp + 1 == uint32_t(Geo<H>::KS);
+        const uint32_t flags = (last && pd.slab + 1 == spg ? kCompletes : 0u) | pd.buf | (kp ? kPart1 : 0u);
+        if (!producer_down<H, F>(pr, P, L, pd.d, layer, n0, cnt, pd.d.row * spg + pd.slab, flags, pd.need) ||
+            pr.t->abort)
+            return false;
+    }
+    return true;
 }
 
 // Issues the GATEUP pieces of a slab and the DOWN piece of the previous one.
@@ -720,9 +791,9 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         }
         if (ok) ok = producer_slab_down<H, F>(pr, P, L, pd, l);
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_ISSUED);
-        if (ok) ok = producer_marker(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
+        if (ok) ok = producer_marker<H>(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
     }
-    producer_marker(pr, P, kPieceFinal, 0, 0, 0);
+    producer_marker<H>(pr, P, kPieceFinal, 0, 0, 0);
     if (pr.lane == 0) trace(P, LS_B200_TRACE_PRODUCED);
 }
 
@@ -767,16 +838,16 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
 // fp32 partial of the finished layer, read from this rank's exchange buffer
 // (slot by the tag's parity) as soon as the words carry `tag`: y = the sum
 // over ranks in rank order, y16 = fp16(y), x = fp16(x_prev + y16), the single
-// rounding that ls_b200_tp_epilogue applies after an allreduce. Thread u
-// handles coordinates 8u..8u+7 (x_prev: its own copy of the finished layer's
-// input, which is that layer's residual); with `write` it also stores the
-// finished layer's outputs.
+// rounding that ls_b200_tp_epilogue applies after an allreduce, for the
+// coordinates 8u..8u+7 of unit u (x_prev: the thread's own copy of the
+// finished layer's input, which is that layer's residual); with `write` it
+// also stores the finished layer's outputs.
 template <int H>
-__device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail* t, uint64_t limit, int tid,
+__device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail* t, uint64_t limit, int u,
                            uint32_t tag, uint4 xprev, bool write) {
-    const int lane = tid & 31;
+    const int lane = threadIdx.x & 31;
     const uint32_t slot = (tag - 1u) & 1u;
-    const unsigned long long* base = P.xpeer[P.rank] + size_t(slot) * P.world * H + 8 * tid;
+    const unsigned long long* base = P.xpeer[P.rank] + size_t(slot) * P.world * H + 8 * u;
     float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (uint32_t r = 0; r < P.world; ++r) {
         const unsigned long long* src = base + size_t(r) * H;
@@ -818,12 +889,12 @@ __device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail*
     }
     if (write) {
         if (Lp.y32) {
-            float4* d = reinterpret_cast<float4*>(Lp.y32 + 8 * tid);
+            float4* d = reinterpret_cast<float4*>(Lp.y32 + 8 * u);
             d[0] = make_float4(y[0], y[1], y[2], y[3]);
             d[1] = make_float4(y[4], y[5], y[6], y[7]);
         }
-        if (Lp.y && !(Lp.flags & LS_B200_NO_OUTPUT)) reinterpret_cast<uint4*>(Lp.y)[tid] = y16v;
-        if (Lp.hidden_out) reinterpret_cast<uint4*>(Lp.hidden_out)[tid] = out;
+        if (Lp.y && !(Lp.flags & LS_B200_NO_OUTPUT)) reinterpret_cast<uint4*>(Lp.y)[u] = y16v;
+        if (Lp.hidden_out) reinterpret_cast<uint4*>(Lp.hidden_out)[u] = out;
     }
     return out;
 }
@@ -845,16 +916,20 @@ __device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail*
 // grid-wide barrier between layers.
 template <int H, bool F>
 __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t& cph, uint64_t limit,
-                        int tid, bool tagged, uint32_t tag, const LayerPlan* prev, uint4& xkeep) {
-    constexpr int NU = H / 8;  // one 8-coordinate unit per thread (H <= 4096)
+                        int tid, bool tagged, uint32_t tag, const LayerPlan* prev, uint4 (&xkeep)[Geo<H>::UPT]) {
+    constexpr int NU = H / 8, UPT = Geo<H>::UPT;  // units u = tid + j * 512, j < UPT
     const int warp = tid >> 5, lane = tid & 31;
-    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    uint4 raw[UPT];
     float ss = 0.f;
-    if (tid < NU) {
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+        const int u = tid + j * kConsumerThreads;
+        raw[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (u >= NU) continue;  // warp-uniform: NU is a multiple of 32
         if (tagged && P.world > 1) {
-            raw = tp_gather<H>(P, *prev, t, limit, tid, tag, xkeep, blockIdx.x == 0);
+            raw[j] = tp_gather<H>(P, *prev, t, limit, u, tag, xkeep[j], blockIdx.x == 0);
         } else if (tagged) {
-            const unsigned long long* src = P.xbuf + 4 * tid;
+            const unsigned long long* src = P.xbuf + 4 * u;
             ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
             uint32_t spins = 0;
             for (;;) {
@@ -873,12 +948,12 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
                     b = ld_volatile_v2u64(src + 2);
                 }
             }
-            raw = make_uint4(uint32_t(a.x), uint32_t(a.y), uint32_t(b.x), uint32_t(b.y));
+            raw[j] = make_uint4(uint32_t(a.x), uint32_t(a.y), uint32_t(b.x), uint32_t(b.y));
         } else {
-            raw = __ldcg(reinterpret_cast<const uint4*>(L.x) + tid);
+            raw[j] = __ldcg(reinterpret_cast<const uint4*>(L.x) + u);
         }
-        xkeep = raw;  // this layer's input: the residual of a tensor-parallel gather
-        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+        xkeep[j] = raw[j];  // this layer's input: the residual of a tensor-parallel gather
+        const __half2* h = reinterpret_cast<const __half2*>(&raw[j]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const float2 v = __half22float2(h[e]);
@@ -888,18 +963,26 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
     }
     const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
     const bool weighted = norm && L.norm_w;
-    uint4 nw = make_uint4(0u, 0u, 0u, 0u);
-    if (weighted && tid < NU) nw = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + tid);
+    uint4 nw[UPT];
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+        const int u = tid + j * kConsumerThreads;
+        nw[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (weighted && u < NU) nw[j] = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + u);
+    }
     // One reduction round: sum of squares (RMSNorm) and, for variant 1, the
     // maxima of |x| and |w| that bound max|x'| for the fixed-point exponent.
     float mx = 0.f, mw = 0.f;
     if constexpr (F) {
-        const __half* h = reinterpret_cast<const __half*>(&raw);
-        const __half* wh = reinterpret_cast<const __half*>(&nw);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            mx = fmaxf(mx, fabsf(__half2float(h[e])));
-            mw = fmaxf(mw, fabsf(__half2float(wh[e])));
+        for (int j = 0; j < UPT; ++j) {
+            const __half* h = reinterpret_cast<const __half*>(&raw[j]);
+            const __half* wh = reinterpret_cast<const __half*>(&nw[j]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                mx = fmaxf(mx, fabsf(__half2float(h[e])));
+                mw = fmaxf(mw, fabsf(__half2float(wh[e])));
+            }
         }
     }
     float inv = 1.f, xbound = 0.f;
@@ -929,23 +1012,26 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         // |fp16(fp16(x inv) w)| <= |x| inv |w| (1 + 2^-11)^2 < max|x| inv max|w| (1 + 2^-9)
         xbound = norm ? mx * inv * (weighted ? mw : 1.f) * (1.f + 0.001953125f) : mx;
     }
-    __half v[8];
-    {
-        const __half* h = reinterpret_cast<const __half*>(&raw);
+    // exponent E of the bound on max|x'|: identical in every CTA
+    const int E = xbound > 0.f ? int((__float_as_uint(xbound) >> 23) & 0xffu) - 127 : 0;
+    const float up = __uint_as_float(uint32_t(127 + 21 - E) << 23);  // 2^(21-E)
+    if (F && tid == 0) t->xscale = __uint_as_float(uint32_t(127 - 21 + E) << 23);  // 2^(E-21)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = norm ? __float2half_rn(__half2float(h[e]) * inv) : h[e];
-        if (weighted) {
-            const __half* wh = reinterpret_cast<const __half*>(&nw);
+    for (int j = 0; j < UPT; ++j) {
+        const int u = tid + j * kConsumerThreads;
+        if (u >= NU) continue;
+        __half v[8];
+        {
+            const __half* h = reinterpret_cast<const __half*>(&raw[j]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
+            for (int e = 0; e < 8; ++e) v[e] = norm ? __float2half_rn(__half2float(h[e]) * inv) : h[e];
+            if (weighted) {
+                const __half* wh = reinterpret_cast<const __half*>(&nw[j]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __hmul(wh[e], v[e]);
+            }
         }
-    }
-    if constexpr (F) {
-        // exponent E of the bound on max|x'|: identical in every CTA
-        const int E = xbound > 0.f ? int((__float_as_uint(xbound) >> 23) & 0xffu) - 127 : 0;
-        const float up = __uint_as_float(uint32_t(127 + 21 - E) << 23);    // 2^(21-E)
-        if (tid == 0) t->xscale = __uint_as_float(uint32_t(127 - 21 + E) << 23);  // 2^(E-21)
-        if (tid < NU) {
+        if constexpr (F) {
             uint32_t pe[3] = {0u, 0u, 0u}, po[3] = {0u, 0u, 0u};
             int msum = 0;
 #pragma unroll
@@ -964,30 +1050,28 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
             }
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
-                uint32_t* plane = reinterpret_cast<uint32_t*>(t->xarea + p * kXPlane);
-                plane[4 * (tid >> 1) + (tid & 1)] = pe[p];
-                plane[4 * (tid >> 1) + 2 + (tid & 1)] = po[p];
+                uint32_t* plane = reinterpret_cast<uint32_t*>(xarea<H>(t) + p * Geo<H>::XPL);
+                plane[4 * (u >> 1) + (u & 1)] = pe[p];
+                plane[4 * (u >> 1) + 2 + (u & 1)] = po[p];
             }
             msum += __shfl_xor_sync(0xffffffffu, msum, 1);
             msum += __shfl_xor_sync(0xffffffffu, msum, 2);
-            if ((tid & 3) == 0) t->msum[tid >> 2] = msum;
+            if ((u & 3) == 0) xsum32<H>(t)[u >> 2] = msum;
             msum += __shfl_xor_sync(0xffffffffu, msum, 4);
-            if ((tid & 7) == 0) t->msum64[tid >> 3] = msum;
-        }
-    } else {
-        if (tid < NU) {
+            if ((u & 7) == 0) xsum64<H>(t)[u >> 3] = msum;
+        } else {
             uint4 f;
             f.x = h2_bits(__halves2half2(v[0], v[4]));
             f.y = h2_bits(__halves2half2(v[1], v[5]));
             f.z = h2_bits(__halves2half2(v[2], v[6]));
             f.w = h2_bits(__halves2half2(v[3], v[7]));
-            reinterpret_cast<uint4*>(t->xarea)[tid] = f;
+            reinterpret_cast<uint4*>(xarea<H>(t))[u] = f;
         }
     }
     csync(P, t, cph, limit, lane);
 }
 
-// (even, odd) digits of 8-coordinate unit u in one plane (layout of SmemTail::xarea).
+// (even, odd) digits of 8-coordinate unit u in one plane (layout of xarea<H>).
 __device__ __forceinline__ uint2 x_unit(const uint8_t* plane, int u) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(plane) + 4 * (u >> 1) + (u & 1);
     return make_uint2(w[0], w[2]);
@@ -1017,12 +1101,13 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
 template <int H, bool F>
 __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const Piece& pc, uint8_t* st, SmemTail* t,
                                uint32_t s, int warp, int lane) {
-    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
+    constexpr int HP = Geo<H>::HP, NSB = HP / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
     constexpr int CH = SBW < 4 ? SBW : 4;  // sub-blocks per scale block handled at once
-    constexpr int PG = gateup_pitch<H, F>();
+    constexpr int PG = gateup_pitch<HP, F>();
     constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;  // staged scale row (gate, up, pad) in halves
     const int g = lane >> 2, tq = lane & 3;
     const NibMasks nk = load_nib(t);
+    const XPart xq = xpart<H>(t, (Geo<H>::KS > 1 && (pc.flags & kPart1)) ? 1u : 0u);
     float2* part = reinterpret_cast<float2*>(st + kStageData + kAuxPartials);  // [warp][8]
     __syncwarp();  // mma.sync is .aligned: enter converged whatever the caller's waits did
     if (warp < AW) {
@@ -1043,7 +1128,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                 alo[c][0] = alo[c][1] = alo[c][2] = alo[c][3] = 0;
                 ahi[c][0] = ahi[c][1] = ahi[c][2] = ahi[c][3] = 0;
             }
-            const uint8_t* xp = t->xarea + (g < 3 ? g : 0) * kXPlane;
+            const uint8_t* xp = xq.x + (g < 3 ? g : 0) * Geo<H>::XPL;
             if constexpr (CH >= 2) {
                 // 64-coordinate groups: lane t reads bytes 8t..8t+7 of a row
                 // (coordinates 16t..16t+15) with one 8-byte load, and the
@@ -1053,8 +1138,8 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
                     const int d0 = (warp * SBW + c * CH) / 2;
-                    ms[c] = t->msum64[d0];
-                    if constexpr (DC == 2) ms[c] += t->msum64[d0 + 1];
+                    ms[c] = xq.m64[d0];
+                    if constexpr (DC == 2) ms[c] += xq.m64[d0 + 1];
                 }
 #pragma unroll
                 for (int dj = 0; dj < DC; ++dj) {
@@ -1062,7 +1147,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                     for (int c = 0; c < NC; ++c) {
                         const int dg = (warp * SBW + c * CH) / 2 + dj;
                         const uint2 wg = *reinterpret_cast<const uint2*>(row2 + 32 * dg);
-                        const uint2 wu = *reinterpret_cast<const uint2*>(row2 + H / 2 + 32 * dg);
+                        const uint2 wu = *reinterpret_cast<const uint2*>(row2 + HP / 2 + 32 * dg);
                         const uint4 xb = reinterpret_cast<const uint4*>(xp)[4 * dg + tq];
                         // even coordinates of both units, then odd ones
                         imma16832(alo[c], and_xor(wg.x, nk.lo_m, nk.lo_x), and_xor(wu.x, nk.lo_m, nk.lo_x),
@@ -1076,9 +1161,9 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                 for (int c = 0; c < NC; ++c) {
                     const int sb = warp * SBW + c;
                     const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
-                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
+                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + HP / 2 + 16 * sb);
                     const uint2 xb = x_unit(xp, sb * 4 + tq);
-                    ms[c] = t->msum[sb];
+                    ms[c] = xq.m32[sb];
                     imma16832(alo[c], and_xor(wg, nk.lo_m, nk.lo_x), and_xor(wu, nk.lo_m, nk.lo_x),
                               and_xor(wg >> 4, nk.lo_m, nk.lo_x), and_xor(wu >> 4, nk.lo_m, nk.lo_x), xb.x,
                               xb.y);
@@ -1098,7 +1183,7 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
                 const float rg = fmaf(dg2, 65536.f, fmaf(dv[1], 256.f, dv[0])) - m8;
                 const float ru = fmaf(du2, 65536.f, fmaf(dv[3], 256.f, dv[2])) - m8;
                 pg = fmaf(__half2float(sc[blk]), rg, pg);
-                pu = fmaf(__half2float(sc[H / 128 + blk]), ru, pu);
+                pu = fmaf(__half2float(sc[HP / 128 + blk]), ru, pu);
             }
         }
 #pragma unroll
@@ -1107,13 +1192,13 @@ __device__ void consume_gateup(const KernelParams& P, const LayerPlan& L, const 
             if constexpr (F) {
             } else {
                 float al[4] = {0.f, 0.f, 0.f, 0.f};
-                const __half2 sg2 = __half2half2(sc[blk]), su2 = __half2half2(sc[H / 128 + blk]);
+                const __half2 sg2 = __half2half2(sc[blk]), su2 = __half2half2(sc[HP / 128 + blk]);
 #pragma unroll
                 for (int j = 0; j < CH; ++j) {
                     const int sb = warp * SBW + j0 + j;
                     const uint32_t wg = *reinterpret_cast<const uint32_t*>(rowg + 16 * sb);
-                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + H / 2 + 16 * sb);
-                    const uint4 xv = reinterpret_cast<const uint4*>(t->xarea)[sb * 4 + tq];
+                    const uint32_t wu = *reinterpret_cast<const uint32_t*>(rowg + HP / 2 + 16 * sb);
+                    const uint4 xv = reinterpret_cast<const uint4*>(xq.x)[sb * 4 + tq];
                     const uint32_t wg8 = wg >> 8, wu8 = wu >> 8;
                     const uint32_t g0 = h2_bits(__hmul2(int_lo(wg), sg2)), g1 = h2_bits(__hmul2(int_hi(wg), sg2));
                     const uint32_t g2 = h2_bits(__hmul2(int_lo(wg8), sg2)), g3 = h2_bits(__hmul2(int_hi(wg8), sg2));
@@ -1226,13 +1311,14 @@ __device__ __forceinline__ void tile2_terms(const int (&lo)[4], const int (&hi)[
 template <int H>
 __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, const Piece& pa, const Piece& pb,
                                     uint8_t* sa, uint8_t* sb, SmemTail* t, uint32_t s, int warp, int lane) {
-    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
+    constexpr int HP = Geo<H>::HP, NSB = HP / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps, SBW = NSB / AW;
     constexpr int CH = SBW < 4 ? SBW : 4;
     constexpr int NC = SBW / CH;
-    constexpr int PG = gateup_pitch<H, true>();
+    constexpr int PG = gateup_pitch<HP, true>();
     constexpr int SPN = ScaleCopy<H>::kGateUpPitch / 2;
     const int g = lane >> 2, tq = lane & 3;
     const NibMasks nk = load_nib(t);
+    const XPart xq = xpart<H>(t, (Geo<H>::KS > 1 && (pa.flags & kPart1)) ? 1u : 0u);
     float2* parta = reinterpret_cast<float2*>(sa + kStageData + kAuxPartials);  // [warp][8]
     float2* partb = reinterpret_cast<float2*>(sb + kStageData + kAuxPartials);
     __syncwarp();  // mma.sync is .aligned: enter converged
@@ -1241,8 +1327,8 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
         const int b0 = 2 * warp, b1 = b0 + 1;
         // digits of units 8 dg + 2t, 8 dg + 2t + 1 of the lane's plane, or zeros
         const uint8_t* z = reinterpret_cast<const uint8_t*>(t->zero16);
-        const uint8_t* p0 = g < 3 ? t->xarea + g * kXPlane + 64 * (2 * b0) + 16 * tq : z;
-        const uint8_t* p1 = (g >= 3 && g < 6) ? t->xarea + (g - 3) * kXPlane + 64 * (2 * b1) + 16 * tq : z;
+        const uint8_t* p0 = g < 3 ? xq.x + g * Geo<H>::XPL + 64 * (2 * b0) + 16 * tq : z;
+        const uint8_t* p1 = (g >= 3 && g < 6) ? xq.x + (g - 3) * Geo<H>::XPL + 64 * (2 * b1) + 16 * tq : z;
         const int step0 = g < 3 ? 64 : 0, step1 = (g >= 3 && g < 6) ? 64 : 0;
         uint4 x0[2], x1[2];
 #pragma unroll
@@ -1250,18 +1336,17 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
             x0[dj] = *reinterpret_cast<const uint4*>(p0 + dj * step0);
             x1[dj] = *reinterpret_cast<const uint4*>(p1 + dj * step1);
         }
-        const Tile2Coef k = tile2_coef(tq, t->msum64[2 * b0] + t->msum64[2 * b0 + 1],
-                                       t->msum64[2 * b1] + t->msum64[2 * b1 + 1]);
+        const Tile2Coef k = tile2_coef(tq, xq.m64[2 * b0] + xq.m64[2 * b0 + 1], xq.m64[2 * b1] + xq.m64[2 * b1 + 1]);
         int loa[4] = {0, 0, 0, 0}, hia[4] = {0, 0, 0, 0}, lob[4] = {0, 0, 0, 0}, hib[4] = {0, 0, 0, 0};
-        gateup_tile2<H>(sa + g * PG + 8 * tq, x0, x1, b0, b1, nk, loa, hia);
-        gateup_tile2<H>(sb + g * PG + 8 * tq, x0, x1, b0, b1, nk, lob, hib);
+        gateup_tile2<HP>(sa + g * PG + 8 * tq, x0, x1, b0, b1, nk, loa, hia);
+        gateup_tile2<HP>(sb + g * PG + 8 * tq, x0, x1, b0, b1, nk, lob, hib);
         const __half* sca = reinterpret_cast<const __half*>(sa + kStageData) + g * SPN;
         const __half* scb = reinterpret_cast<const __half*>(sb + kStageData) + g * SPN;
         float pga, pua, pgb, pub;
-        tile2_terms(loa, hia, k, __half2float(sca[b0]), __half2float(sca[b1]), __half2float(sca[H / 128 + b0]),
-                    __half2float(sca[H / 128 + b1]), pga, pua);
-        tile2_terms(lob, hib, k, __half2float(scb[b0]), __half2float(scb[b1]), __half2float(scb[H / 128 + b0]),
-                    __half2float(scb[H / 128 + b1]), pgb, pub);
+        tile2_terms(loa, hia, k, __half2float(sca[b0]), __half2float(sca[b1]), __half2float(sca[HP / 128 + b0]),
+                    __half2float(sca[HP / 128 + b1]), pga, pua);
+        tile2_terms(lob, hib, k, __half2float(scb[b0]), __half2float(scb[b1]), __half2float(scb[HP / 128 + b0]),
+                    __half2float(scb[HP / 128 + b1]), pgb, pub);
         const float xs = t->xscale * 0.0625f;  // the accumulator columns are 16 times the plane sums
         if (tq == 0) {
             parta[warp * 8 + g] = make_float2(pga * xs, pua * xs);
@@ -1277,7 +1362,7 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
         for (int c = 0; c < NC; ++c)
 #pragma unroll
             for (int e = 0; e < 4; ++e) aloa[c][e] = ahia[c][e] = alob[c][e] = ahib[c][e] = 0;
-        const uint8_t* xp = t->xarea + (g < 3 ? g : 0) * kXPlane;
+        const uint8_t* xp = xq.x + (g < 3 ? g : 0) * Geo<H>::XPL;
         if constexpr (CH >= 2) {
             constexpr int DC = CH / 2;
             const uint8_t* rowa = sa + g * PG + 8 * tq;
@@ -1285,8 +1370,8 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const int d0 = (warp * SBW + c * CH) / 2;
-                ms[c] = t->msum64[d0];
-                if constexpr (DC == 2) ms[c] += t->msum64[d0 + 1];
+                ms[c] = xq.m64[d0];
+                if constexpr (DC == 2) ms[c] += xq.m64[d0 + 1];
             }
 #pragma unroll
             for (int dj = 0; dj < DC; ++dj) {
@@ -1295,9 +1380,9 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
                     const int dg = (warp * SBW + c * CH) / 2 + dj;
                     const uint4 xb = reinterpret_cast<const uint4*>(xp)[4 * dg + tq];
                     const uint2 wga = *reinterpret_cast<const uint2*>(rowa + 32 * dg);
-                    const uint2 wua = *reinterpret_cast<const uint2*>(rowa + H / 2 + 32 * dg);
+                    const uint2 wua = *reinterpret_cast<const uint2*>(rowa + HP / 2 + 32 * dg);
                     const uint2 wgb = *reinterpret_cast<const uint2*>(rowb + 32 * dg);
-                    const uint2 wub = *reinterpret_cast<const uint2*>(rowb + H / 2 + 32 * dg);
+                    const uint2 wub = *reinterpret_cast<const uint2*>(rowb + HP / 2 + 32 * dg);
                     imma16832(aloa[c], and_xor(wga.x, nk.lo_m, nk.lo_x), and_xor(wua.x, nk.lo_m, nk.lo_x),
                               and_xor(wga.y, nk.lo_m, nk.lo_x), and_xor(wua.y, nk.lo_m, nk.lo_x), xb.x, xb.y);
                     imma16832(ahia[c], and_xor(wga.x, nk.hi_m, nk.hi_x), and_xor(wua.x, nk.hi_m, nk.hi_x),
@@ -1315,11 +1400,11 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
             for (int c = 0; c < NC; ++c) {
                 const int sbk = warp * SBW + c;
                 const uint2 xb = x_unit(xp, sbk * 4 + tq);
-                ms[c] = t->msum[sbk];
+                ms[c] = xq.m32[sbk];
                 const uint32_t wga = *reinterpret_cast<const uint32_t*>(rowa + 16 * sbk);
-                const uint32_t wua = *reinterpret_cast<const uint32_t*>(rowa + H / 2 + 16 * sbk);
+                const uint32_t wua = *reinterpret_cast<const uint32_t*>(rowa + HP / 2 + 16 * sbk);
                 const uint32_t wgb = *reinterpret_cast<const uint32_t*>(rowb + 16 * sbk);
-                const uint32_t wub = *reinterpret_cast<const uint32_t*>(rowb + H / 2 + 16 * sbk);
+                const uint32_t wub = *reinterpret_cast<const uint32_t*>(rowb + HP / 2 + 16 * sbk);
                 imma16832(aloa[c], and_xor(wga, nk.lo_m, nk.lo_x), and_xor(wua, nk.lo_m, nk.lo_x),
                           and_xor(wga >> 4, nk.lo_m, nk.lo_x), and_xor(wua >> 4, nk.lo_m, nk.lo_x), xb.x,
                           xb.y);
@@ -1331,9 +1416,9 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const int blk = (warp * SBW + c * CH) / 4;
-            gateup_block_terms(aloa[c], ahia[c], ms[c], __half2float(sca[blk]), __half2float(sca[H / 128 + blk]), pga,
+            gateup_block_terms(aloa[c], ahia[c], ms[c], __half2float(sca[blk]), __half2float(sca[HP / 128 + blk]), pga,
                                pua);
-            gateup_block_terms(alob[c], ahib[c], ms[c], __half2float(scb[blk]), __half2float(scb[H / 128 + blk]), pgb,
+            gateup_block_terms(alob[c], ahib[c], ms[c], __half2float(scb[blk]), __half2float(scb[HP / 128 + blk]), pgb,
                                pub);
         }
         const float xs = t->xscale;
@@ -1357,8 +1442,8 @@ __device__ void consume_gateup_pair(const KernelParams& P, const LayerPlan& L, c
 template <int H, bool F>
 __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8_t* st, const SmemTail* t, int warp,
                              int lane) {
-    constexpr int NT = H / 64, DW = NT < kConsumerWarps ? NT : kConsumerWarps, TPW = NT / DW;
-    constexpr int PD = H / 2 + 16;
+    constexpr int HP = Geo<H>::HP, NT = HP / 64, DW = NT < kConsumerWarps ? NT : kConsumerWarps, TPW = NT / DW;
+    constexpr int PD = HP / 2 + 16;
     constexpr int SPN = ScaleCopy<H>::kDownPitch / 2;  // staged down-scale row in halves
     if (warp >= DW) return;
     __syncwarp();  // mma.sync is .aligned: enter converged
@@ -1372,7 +1457,8 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     const __half hv2 = uint32_t(n2) < cnt ? hb[n2] : zero, hv3 = uint32_t(n3) < cnt ? hb[n3] : zero;
     const __half2 h01 = __halves2half2(hv0, hv1), h23 = __halves2half2(hv2, hv3);
     const __half* sd = reinterpret_cast<const __half*>(st + kStageData);
-    unsigned long long* out = P.partial + size_t(pc.row) * H;
+    // columns [kp HP, (kp + 1) HP) of the slab's partial row
+    unsigned long long* out = P.partial + size_t(pc.row) * H + ((Geo<H>::KS > 1 && (pc.flags & kPart1)) ? HP : 0);
     const unsigned long long tag = static_cast<unsigned long long>(scratch_tag(t, pc.layer)) << 32;
     const int mine = g >> 1;  // the MMA whose B column g this lane supplies
     uint32_t bj0[4] = {0u, 0u, 0u, 0u}, bj1[4] = {0u, 0u, 0u, 0u}, s01 = 0, s23 = 0;
@@ -1601,7 +1687,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
 // GATEUP stage's aux area), in warp order.
 template <int H>
 __device__ __forceinline__ float2 sum_partials(const uint8_t* st, uint32_t i) {
-    constexpr int NSB = H / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps;
+    constexpr int NSB = Geo<H>::HP / 32, AW = NSB < kConsumerWarps ? NSB : kConsumerWarps;
     const float2* part = reinterpret_cast<const float2*>(st + kStageData + kAuxPartials);
     float gsum = 0.f, usum = 0.f;
 #pragma unroll
@@ -1644,9 +1730,11 @@ __device__ bool wait_phase(const KernelParams& P, SmemTail* t, uint32_t bar, uin
 // Warp-uniform bounded wait until piece `idx`'s stage is full (acquire of
 // the TMA-written data). False when the producer stopped without a FINAL
 // marker.
+template <int H>
 __device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane, uint32_t backoff_ns = 0) {
-    const uint32_t bar = smem_u32(&t->full_bar[idx % kStages]);
-    const uint32_t parity = (idx / kStages) & 1u;
+    constexpr uint32_t NS = Geo<H>::NS;
+    const uint32_t bar = smem_u32(&t->full_bar[idx % NS]);
+    const uint32_t parity = (idx / NS) & 1u;
     uint32_t spins = 0;
     for (;;) {
         const bool ready = mbar_try_wait(bar, parity);
@@ -1666,11 +1754,11 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    uint4 xkeep = make_uint4(0u, 0u, 0u, 0u);
+    uint4 xkeep[Geo<H>::UPT];
     stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0, nullptr, xkeep);
     for (uint32_t idx = 0;; ++idx) {
-        const uint32_t s = idx % kStages;
-        if (!wait_full(t, idx, deadline, lane)) {
+        const uint32_t s = idx % Geo<H>::NS;
+        if (!wait_full<H>(t, idx, deadline, lane)) {
             // The producer stopped without a FINAL marker; nothing is in
             // flight for this stage.
             if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 4);
@@ -1689,11 +1777,11 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             if constexpr (F) {
                 if (pc.flags & kPaired) {
                     // the slab's second GATEUP piece is the next stage
-                    if (!wait_full(t, idx + 1, deadline, lane)) {
+                    if (!wait_full<H>(t, idx + 1, deadline, lane)) {
                         if (lane == 0) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 4);
                         break;
                     }
-                    const uint32_t s2 = (idx + 1) % kStages;
+                    const uint32_t s2 = (idx + 1) % Geo<H>::NS;
                     const Piece pc2 = t->piece[s2];
                     if (tid == 0) trace_piece(P, idx + 1, 2);
                     consume_gateup_pair<H>(P, *L, pc, pc2, st, stages + size_t(s2) * kStageBytes, t, s, warp, lane);
@@ -1752,8 +1840,13 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         if (!next) {
             // Tensor parallel: the launch's last layer has no next input to
             // gather; CTA 0 forms its outputs from the ranks' partials.
-            if (P.world > 1 && blockIdx.x == 0 && tid < int(H / 8))
-                tp_gather<H>(P, *L, t, limit, tid, scratch_tag(t, l), xkeep, true);
+            if (P.world > 1 && blockIdx.x == 0) {
+#pragma unroll
+                for (int j = 0; j < Geo<H>::UPT; ++j) {
+                    const int u = tid + j * kConsumerThreads;
+                    if (u < H / 8) tp_gather<H>(P, *L, t, limit, u, scratch_tag(t, l), xkeep[j], true);
+                }
+            }
             continue;  // the FINAL marker follows
         }
         if (!chain) {
@@ -1782,9 +1875,10 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
     const int lane = threadIdx.x & 31;
     const uint64_t limit = deadline + kSyncGraceNs;
     uint32_t phases = 0;  // completed-phase parity of each stage's pbar
+    float2 carry = make_float2(0.f, 0.f);  // gate/up sums of a slab's first K part
     for (uint32_t idx = 0;; ++idx) {
-        const uint32_t s = idx % kStages;
-        if (!wait_full(t, idx, deadline, lane)) break;  // the consumers report it
+        const uint32_t s = idx % Geo<H>::NS;
+        if (!wait_full<H>(t, idx, deadline, lane)) break;  // the consumers report it
         const Piece pc = t->piece[s];
         if (pc.kind == kPieceFinal) break;
         if (pc.kind == kPieceGateUp) {
@@ -1798,8 +1892,8 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
             if (paired) {
                 // the consumers saw the second stage full before writing
                 // their partials; this wait returns at once
-                if (!wait_full(t, idx + 1, deadline, lane)) break;
-                s2 = (idx + 1) % kStages;
+                if (!wait_full<H>(t, idx + 1, deadline, lane)) break;
+                s2 = (idx + 1) % Geo<H>::NS;
                 i = uint32_t(lane) & 7u;
                 if (lane >= 8) {
                     cnt = lane < 16 ? t->piece[s2].count : 0u;
@@ -1808,13 +1902,23 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
                 }
             }
             const bool mine = i < cnt;
-            const float2 gu = mine ? sum_partials<H>(sq, i) : make_float2(0.f, 0.f);
+            float2 gu = mine ? sum_partials<H>(sq, i) : make_float2(0.f, 0.f);
             // The partials are in registers: the stages may be refilled while
             // h is formed.
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(smem_u32(&t->empty_bar[s]));
                 if (paired) mbar_arrive(smem_u32(&t->empty_bar[s2]));
+            }
+            if constexpr (Geo<H>::KS > 1) {
+                // K parts of a slab follow each other: the first part's sums
+                // wait in registers for the second's
+                if (!(pc.flags & kPart1)) {
+                    carry = gu;
+                    if (paired) ++idx;
+                    continue;
+                }
+                gu = make_float2(carry.x + gu.x, carry.y + gu.y);
             }
             if (mine) finish_h(P, L, t, buf, pc.dest, n0 + i, gu);
             __syncwarp();
@@ -1831,12 +1935,12 @@ template <int H, bool F>
 __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_constant__ KernelParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
-    SmemTail* t = reinterpret_cast<SmemTail*>(smem + size_t(kStages) * kStageBytes);
+    SmemTail* t = reinterpret_cast<SmemTail*>(smem + size_t(Geo<H>::NS) * kStageBytes);
     const int tid = threadIdx.x;
     const uint64_t deadline = gtimer() + P.timeout_ns;
     if (tid == 0) {
         trace(P, LS_B200_TRACE_ENTRY);
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < Geo<H>::NS; ++s) {
             mbar_init(smem_u32(&t->full_bar[s]), 34);                // lane 0 expect_tx + 32 cp.async + lane 0 close
             mbar_init(smem_u32(&t->empty_bar[s]), kConsumerWarps + 1);  // consumer warps + epilogue warp
             mbar_init(smem_u32(&t->pbar[s]), kConsumerWarps);
@@ -1902,28 +2006,29 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
 
 template <int H, bool F>
 static int launch_t(const KernelParams& p, int grid, cudaStream_t stream) {
-    fused_mlp_kernel<H, F><<<grid, kThreads, kernel_smem_bytes(), stream>>>(p);
+    fused_mlp_kernel<H, F><<<grid, kThreads, kernel_smem_bytes<H>(), stream>>>(p);
     return int(cudaGetLastError());
 }
 
 template <int H, bool F>
-static cudaError_t raise_smem(int bytes) {
-    return cudaFuncSetAttribute(fused_mlp_kernel<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+static cudaError_t raise_smem() {
+    static_assert(kernel_smem_bytes<H>() <= 232448, "dynamic shared memory of one CTA");
+    return cudaFuncSetAttribute(fused_mlp_kernel<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kernel_smem_bytes<H>()));
 }
 
 int prepare() {
-    const int bytes = int(kernel_smem_bytes());
-    const cudaError_t errs[] = {raise_smem<256, false>(bytes),  raise_smem<512, false>(bytes),
-                                raise_smem<1024, false>(bytes), raise_smem<2048, false>(bytes),
-                                raise_smem<4096, false>(bytes), raise_smem<256, true>(bytes),
-                                raise_smem<512, true>(bytes),   raise_smem<1024, true>(bytes),
-                                raise_smem<2048, true>(bytes),  raise_smem<4096, true>(bytes)};
+    const cudaError_t errs[] = {raise_smem<256, false>(),  raise_smem<512, false>(), raise_smem<1024, false>(),
+                                raise_smem<2048, false>(), raise_smem<4096, false>(), raise_smem<256, true>(),
+                                raise_smem<512, true>(),   raise_smem<1024, true>(),  raise_smem<2048, true>(),
+                                raise_smem<4096, true>(),  raise_smem<8192, true>()};
     for (cudaError_t e : errs)
         if (e != cudaSuccess) return int(e);
     return 0;
 }
 
-// H in {256, 512, 1024, 2048, 4096}.
+// H in {256, 512, 1024, 2048, 4096, 8192}; variant 0 up to 4096 (the
+// backend selects variant 1 above).
 int launch(const KernelParams& p, int grid, cudaStream_t stream) {
     const bool f = p.variant != 0;
     switch (p.H) {
@@ -1932,6 +2037,7 @@ int launch(const KernelParams& p, int grid, cudaStream_t stream) {
         case 1024: return f ? launch_t<1024, true>(p, grid, stream) : launch_t<1024, false>(p, grid, stream);
         case 2048: return f ? launch_t<2048, true>(p, grid, stream) : launch_t<2048, false>(p, grid, stream);
         case 4096: return f ? launch_t<4096, true>(p, grid, stream) : launch_t<4096, false>(p, grid, stream);
+        case 8192: return f ? launch_t<8192, true>(p, grid, stream) : int(cudaErrorInvalidValue);
         default: return int(cudaErrorInvalidValue);
     }
 }
@@ -1944,7 +2050,6 @@ int launch_fused_traced(const KernelParams& p, int grid, cudaStream_t stream) {
     return traced::launch(p, grid, stream);
 }
 #else
-size_t kernel_smem_bytes() { return plain::kernel_smem_bytes(); }
 int prepare_kernels() {
     const int rc = plain::prepare();
     return rc ? rc : prepare_kernels_traced();

@@ -149,3 +149,41 @@ def test_config2_parity(native_lib, cuda_device, candidate):
     ids = seeded_selection(2, 192, 0.3)
     assert len(ids) == 58
     _seeded_parity(4096, 192, ids, 2, candidate=candidate)
+
+
+@pytest.mark.parametrize("candidate", [0, 4])
+def test_config5_parity(native_lib, cuda_device, candidate):
+    """Config 5 geometry: H 8192 (each slab split into two K parts for gate/up
+    and two column parts for down), 20% of 40 groups active; candidate 0
+    (4 CTAs) wraps every CTA's stage ring many times."""
+    ids = np.random.default_rng(11).permutation(40)[:8]
+    _seeded_parity(8192, 40, ids, 5, candidate=candidate)
+
+
+def test_config5_ragged_slabs_and_variant_fallback(native_lib, cuda_device):
+    """H 8192 with G 24 (a full slab and an 8-neuron one: the unpaired GATEUP
+    path in both K parts); candidate 5 (variant 0, built up to H 4096) runs
+    the default arithmetic and must equal candidate 4 bit for bit."""
+    from gpu_harness import LayerBuffers, make_backend, run_layer, wait_stream
+    from leanstream_b200 import _native as N
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    H, G, n = 8192, 24, 12
+    L = make_layer(9, H, n, G)
+    rows = descriptors(np.array([1, 4, 5, 9, 11]))
+    y_ref16, _, _ = O.mlp(H, G, L.x, L.packed, L.scales, rows)
+    outs = []
+    for cand in (4, 5):
+        buf = LayerBuffers(H, G, n, L.packed, L.scales, L.x)
+        be = make_backend(H, G, n)
+        run_layer(be, buf, [], rows, mode=N.MODE_PROGRESSIVE, candidate=cand)
+        wait_stream()
+        assert be.status()[N.STATUS_ERROR] == 0, be.status()
+        y = buf.y.cpu().numpy()
+        ref = y_ref16.astype(np.float32)
+        assert np.abs(y.astype(np.float32) - ref).max() <= TOL * np.abs(ref).max()
+        assert np.all(buf.execs.cpu().numpy()[: len(rows)] == 1)
+        outs.append(y.view(np.uint16).copy())
+        be.close()
+    assert np.array_equal(outs[0], outs[1])

@@ -36,7 +36,7 @@ def test_norm_residual_single_layer(native_lib, cuda_device):
     be.close()
 
 
-@pytest.mark.parametrize("H", [1024, 4096])
+@pytest.mark.parametrize("H", [1024, 4096, 8192])
 def test_stack_chain(native_lib, cuda_device, H):
     import torch
     from gpu_harness import to_dev, wait_stream

@@ -122,7 +122,7 @@ def _spawn(world, H, out, limit_s=240.0):
             raise AssertionError("tensor-parallel ranks did not finish in time")
 
 
-@pytest.mark.parametrize("H", [1024, 4096])
+@pytest.mark.parametrize("H", [1024, 4096, 8192])
 def test_two_gpu_exchange_matches_oracle(native_lib, cuda_device, tmp_path, H):
     import torch
 
