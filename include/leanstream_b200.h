@@ -107,7 +107,7 @@ typedef struct ls_kernel_candidate {
 /* ------------------------------------------------------------------ */
 
 typedef struct ls_b200_geometry {
-    uint32_t hidden;        /* H: 256, 512, 1024, 2048 or 4096 */
+    uint32_t hidden;        /* H: 256, 512, 1024, 2048, 4096 or 8192 */
     uint32_t group_size;    /* G: neurons per logical group, 1..256 */
     uint32_t group_count;   /* N: logical groups = dest slots = partial rows */
     uint32_t max_layers;    /* number of per-layer completion words (0 -> 256) */
@@ -344,6 +344,84 @@ int ls_b200_queue_seal(ls_b200_queue* queue, uint32_t total);
 int ls_b200_queue_publish_all(ls_b200_queue* queue);
 int ls_b200_queue_publish(ls_b200_queue* queue, uint32_t index);
 int ls_b200_queue_fail(ls_b200_queue* queue, uint32_t error);
+
+/* ------------------------------------------------------------------ */
+/* Streaming IO: IOBackend (include/leanstream/weight_manager.h:8-24)  */
+/* over pinned host memory -> HBM staging copies.                      */
+/* ------------------------------------------------------------------ */
+
+/* IOCompletion (weight_manager.h:8-11) and its callback; the reference
+ * passes the completion by const reference, i.e. by address. */
+typedef struct ls_io_completion {
+    uint32_t epoch;
+    int32_t logical_group;
+    int32_t staging_slot;
+    int32_t error;
+    uint64_t slot_sequence;
+} ls_io_completion;
+typedef void (*ls_io_completion_fn)(void* arg, const ls_io_completion* completion);
+
+/* IOBackend (weight_manager.h:14-24): the table a WeightManager borrows
+ * through ManagerConfig::io_backend. */
+typedef struct ls_io_backend {
+    void* context;
+    int (*begin)(void* context, ls_io_completion_fn callback, void* arg, uint32_t epoch);
+    int (*update)(void* context, ls_group_span priority);
+    int (*consume)(void* context, ls_group_span final_reads);
+    int (*retire)(void* context);
+    int32_t (*ready_slot)(void* context, int32_t group);
+    uint64_t (*requests)(void* context);
+    int (*wait)(void* context, int timeout_ms);
+} ls_io_backend;
+
+/* io_states words, as the reference stream engine publishes them
+ * (src/io/stream_io.h:6); io_states[group_count] holds a terminal errno. */
+enum { LS_IO_EMPTY = 0, LS_IO_INFLIGHT = 1, LS_IO_READY = 2, LS_IO_ERROR = 3 };
+
+typedef struct ls_b200_stream_config {
+    const void* host_base;         /* pinned host memory (cudaHostAlloc / cudaHostRegister) */
+    const uint64_t* host_offsets;  /* [group_count]: byte offset of logical group g in host_base */
+    void* staging;                 /* device memory: group g lands at staging + g * staging_stride */
+    uint64_t staging_stride;
+    uint64_t group_bytes;          /* bytes copied per group (<= staging_stride) */
+    uint32_t* io_states;           /* [group_count + 1] host words shared with the caller */
+    uint32_t group_count;
+    uint32_t queue_depth;          /* copies in flight, 1..32 (ManagerConfig::qd) */
+    int32_t device;                /* CUDA device of the staging memory */
+    float delay_mean_us;           /* emulated IO latency: each landed group becomes READY after an
+                                    * extra delay ~ Exp(mean) (seeded); 0 = none */
+    uint64_t delay_seed;
+} ls_b200_stream_config;
+
+typedef struct ls_b200_stream_counters {
+    uint64_t admissions;    /* copies issued (IOBackend::requests) */
+    uint64_t completions;   /* groups published READY */
+    uint64_t bytes;         /* bytes copied host -> HBM */
+    uint64_t first_issue_ns, last_land_ns;  /* CLOCK_MONOTONIC of the first copy issue / last landing */
+    uint64_t copy_ns;       /* sum over copies of issue -> landing as the worker observed it */
+    int32_t error;          /* first error (CUDA error code or errno), 0 if none */
+    uint32_t outstanding;   /* copies in flight now */
+} ls_b200_stream_counters;
+
+/* (new; the reference transport reads an O_DIRECT file into host memory the
+ * GPU maps, src/io/stream_io.cpp:75-148, which a discrete GPU cannot use as
+ * staging) Creates the engine: one worker thread, one CUDA stream and
+ * `queue_depth` events on `device`. Returns NULL (errno EINVAL / ENOMEM /
+ * ENODEV) on failure. The worker admits groups in the priority order of the
+ * last update (then, after consume, the committed final reads), one
+ * cudaMemcpyAsync per group, never preempting a started copy; a landed
+ * group's io_states word turns READY (release) before its completion
+ * callback runs on the worker thread. */
+void* ls_b200_stream_create(const ls_b200_stream_config* config);
+/* Fills the IOBackend table for this engine. */
+int ls_b200_stream_view(void* engine, ls_io_backend* out);
+int ls_b200_stream_stats(void* engine, ls_b200_stream_counters* out);
+/* Admission order of the current session (logical ids), up to `capacity`;
+ * returns the number written. Tests and diagnostics. */
+uint32_t ls_b200_stream_issue_log(void* engine, int32_t* out, uint32_t capacity);
+/* Stops the worker after draining in-flight copies; the caller has retired
+ * the session. */
+void ls_b200_stream_destroy(void* engine);
 
 /* Library build identity: "sm_100a" plus the kernel revision. */
 const char* ls_b200_build_info(void);

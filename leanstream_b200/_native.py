@@ -87,6 +87,37 @@ class Queue(C.Structure):
     _fields_ = [("view", DeviceExecQueue), ("tail", C.c_uint32), ("epoch", C.c_uint32), ("total", C.c_uint32)]
 
 
+class IOCompletion(C.Structure):
+    """IOCompletion, include/leanstream/weight_manager.h:8-11."""
+    _fields_ = [("epoch", C.c_uint32), ("logical_group", C.c_int32), ("staging_slot", C.c_int32),
+                ("error", C.c_int32), ("slot_sequence", C.c_uint64)]
+
+
+IO_COMPLETION_FN = C.CFUNCTYPE(None, C.c_void_p, C.POINTER(IOCompletion))
+
+
+class IOBackend(C.Structure):
+    """IOBackend, include/leanstream/weight_manager.h:14-24."""
+    _fields_ = [("context", C.c_void_p), ("begin", C.c_void_p), ("update", C.c_void_p), ("consume", C.c_void_p),
+                ("retire", C.c_void_p), ("ready_slot", C.c_void_p), ("requests", C.c_void_p), ("wait", C.c_void_p)]
+
+
+class StreamConfig(C.Structure):
+    _fields_ = [("host_base", C.c_void_p), ("host_offsets", C.c_void_p), ("staging", C.c_void_p),
+                ("staging_stride", C.c_uint64), ("group_bytes", C.c_uint64), ("io_states", C.c_void_p),
+                ("group_count", C.c_uint32), ("queue_depth", C.c_uint32), ("device", C.c_int32),
+                ("delay_mean_us", C.c_float), ("delay_seed", C.c_uint64)]
+
+
+class StreamStats(C.Structure):
+    _fields_ = [("admissions", C.c_uint64), ("completions", C.c_uint64), ("bytes", C.c_uint64),
+                ("first_issue_ns", C.c_uint64), ("last_land_ns", C.c_uint64), ("copy_ns", C.c_uint64),
+                ("error", C.c_int32), ("outstanding", C.c_uint32)]
+
+
+IO_EMPTY, IO_INFLIGHT, IO_READY, IO_ERROR = 0, 1, 2, 3
+
+assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 72
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32
 
 # name -> (restype, argtypes); every entry point declared in include/leanstream_b200.h
@@ -128,6 +159,11 @@ SIGNATURES = {
     "ls_b200_tp_setup": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "ls_b200_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "ls_b200_spin": (C.c_int, [C.c_uint64, C.c_void_p]),
+    "ls_b200_stream_create": (C.c_void_p, [C.POINTER(StreamConfig)]),
+    "ls_b200_stream_view": (C.c_int, [C.c_void_p, C.POINTER(IOBackend)]),
+    "ls_b200_stream_stats": (C.c_int, [C.c_void_p, C.POINTER(StreamStats)]),
+    "ls_b200_stream_issue_log": (C.c_uint32, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "ls_b200_stream_destroy": (None, [C.c_void_p]),
 }
 
 _lib = None
@@ -139,7 +175,7 @@ def load() -> C.CDLL:
     if _lib is None:
         if not LIBRARY.exists():
             raise RuntimeError(f"{LIBRARY} is missing: run `python -m leanstream_b200.build` (no CPU fallback)")
-        lib = C.CDLL(str(LIBRARY))
+        lib = C.CDLL(str(LIBRARY), use_errno=True)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.restype = res
