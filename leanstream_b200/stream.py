@@ -99,8 +99,13 @@ class IOBackendView:
             v = c.contents
             on_completion(v.epoch, v.logical_group, v.staging_slot, v.error, v.slot_sequence)
 
-        self._callback = N.IO_COMPLETION_FN(trampoline)  # kept alive for the session
-        return self._begin(self.ctx, self._callback, None, epoch)
+        callback = N.IO_COMPLETION_FN(trampoline)
+        rc = self._begin(self.ctx, callback, None, epoch)
+        if rc == 0:
+            # the engine calls it until the session retires: keep it alive (a
+            # refused begin leaves the running session's callback in place)
+            self._callback = callback
+        return rc
 
     @staticmethod
     def _span(ids):
