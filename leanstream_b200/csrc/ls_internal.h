@@ -55,10 +55,12 @@ struct alignas(16) LayerPlan {
 
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
-constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsHeader = 8;
+// kWsPollClock: %globaltimer (low 32 bits) of the last host-queue poll.
+constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsHeader = 8;
 // path, slab claim, reduction-block claim, reduced column blocks, CTAs past the
-// tensor-parallel gather of the layer's input
-constexpr uint32_t kWsPerLayer = 5;
+// tensor-parallel gather of the layer's input, device mirror of the queue's
+// ready_count, device mirror of the queue state (1 activated, 2 failed)
+constexpr uint32_t kWsPerLayer = 7;
 // Scratch tags: tag = 1 + base + l for launch-local layer l, where base is a
 // device counter (ws[kWsTag]) advanced by the layers of every launch at its
 // end, so CUDA-graph replays get fresh tags too. It wraps below kTagWrap;

@@ -230,6 +230,12 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
 __device__ __forceinline__ void red_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_max_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -337,6 +343,7 @@ __device__ __forceinline__ float round16(float v) { return __half2float(__float2
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
     // [0] path [1] slab claim [2] block claim [3] reduced blocks [4] CTAs past the TP gather
+    // [5] mirror of ready_count [6] mirror of the queue state
     return P.ws + kWsHeader + kWsPerLayer * l;
 }
 // Tag of the scratch words written by launch-local layer l: 1 + the device
@@ -663,6 +670,19 @@ __device__ bool producer_window(Producer& pr, const KernelParams& P, const Layer
     return true;
 }
 
+// The queue's control words may be mapped host memory: a grid whose 148
+// producers all polled them over PCIe would starve the copy engine that
+// streams the weights. So one thread of the grid at a time polls the host
+// (a lease of kHostPollNs on a device clock word) and publishes what it saw
+// to device mirrors, which every CTA reads.
+constexpr uint32_t kHostPollNs = 1000;
+constexpr uint32_t kQueueActive = 1, kQueueFailed = 2;
+__device__ __forceinline__ bool take_poll_lease(const KernelParams& P) {
+    const uint32_t now = uint32_t(gtimer());
+    const uint32_t last = ld_relaxed_gpu(P.ws + kWsPollClock);
+    return now - last >= kHostPollNs && atomicCAS(P.ws + kWsPollClock, last, now) == last;
+}
+
 // Per-CTA path decision for one layer (streaming_mlp.cu:49-56,
 // persistent.py:46-55). BatchCompat / Auto wait for the batch epoch and take
 // the fast path; Progressive proposes a path and agrees with the other CTAs
@@ -672,15 +692,28 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
                            uint32_t* total_out) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(L.q.control);
     const bool batch = L.mode != LS_MODE_PROGRESSIVE;  // Auto follows BatchCompat (streaming_mlp.cu:90)
+    uint32_t* state = ws_layer(P, l) + 6;
     uint32_t code = 0;
     for (;;) {
-        const uint4 a = ld_relaxed_sys_v4(w);
-        const uint4 b = ld_relaxed_sys_v4(w + 4);
-        if (b.y) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-        if (a.w == L.epoch && (!batch || b.x == L.epoch)) {
+        const uint32_t m = ld_acquire_gpu(state);  // another CTA saw the queue
+        if (m == kQueueActive) break;
+        if (m == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }
+        if (take_poll_lease(P)) {
+            const uint4 a = ld_relaxed_sys_v4(w);
+            const uint4 b = ld_relaxed_sys_v4(w + 4);
+            if (b.y) {
+                st_release_gpu(state, kQueueFailed);
+                code = LS_B200_DEV_QUEUE_ERROR;
+                break;
+            }
             // Acquire the deciding word (a system-scope acquire load is ~0.2 us;
-            // a system-scope fence is ~4 us on this part).
-            if (ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) break;
+            // a system-scope fence is ~4 us on this part), then release the
+            // mirror: the CTAs that acquire it are ordered after the plan.
+            if (a.w == L.epoch && (!batch || b.x == L.epoch) && ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) {
+                if (!batch) red_max_release_gpu(ws_layer(P, l) + 5, a.x);
+                st_release_gpu(state, kQueueActive);
+                break;
+            }
         }
         if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_EPOCH; break; }
         __nanosleep(100);
@@ -766,11 +799,26 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                         code = 0xffffffffu;  // exhausted
                     } else if (d >= L.core_count) {
                         // Wait until the descriptor of the claimed slab is
-                        // published (persistent.py:71-90; streaming_mlp.cu:63-75).
+                        // published (persistent.py:71-90; streaming_mlp.cu:63-75):
+                        // the device mirror of ready_count, refreshed from the
+                        // host queue under the polling lease.
                         const uint32_t q = d - L.core_count;
+                        uint32_t* mirror = ws_layer(P, l) + 5;
+                        uint32_t* state = ws_layer(P, l) + 6;
                         for (;;) {
-                            if (ld_acquire_sys(words + 5)) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-                            if (ld_acquire_sys(words + 0) > q) break;
+                            const uint32_t seen = ld_acquire_gpu(mirror);
+                            if (seen > q) break;
+                            if (ld_relaxed_gpu(state) == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }
+                            if (take_poll_lease(P)) {
+                                if (ld_acquire_sys(words + 5)) {
+                                    st_release_gpu(state, kQueueFailed);
+                                    code = LS_B200_DEV_QUEUE_ERROR;
+                                    break;
+                                }
+                                const uint32_t ready = ld_acquire_sys(words + 0);
+                                if (ready > seen) red_max_release_gpu(mirror, ready);
+                                if (ready > q) break;
+                            }
                             if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_READY; break; }
                             __nanosleep(128);
                         }

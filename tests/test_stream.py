@@ -132,8 +132,9 @@ def _config4_inputs(tmp_path, H=1024, G=64, N=64, seed=0):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("delay_us", [0, 20])
 @pytest.mark.parametrize("candidate", [0, 1, 2, 3, 4])
-def test_reference_runtime_streams_config4(native_lib, cuda_device, tmp_path, candidate):
+def test_reference_runtime_streams_config4(native_lib, cuda_device, tmp_path, candidate, delay_us):
     from leanstream_b200.synthetic import descriptors
     from oracle import oracle as O
 
@@ -141,10 +142,11 @@ def test_reference_runtime_streams_config4(native_lib, cuda_device, tmp_path, ca
         pytest.fail(f"{DRIVER} is missing: build it with `make -C oracle ref` where the reference is mounted")
     H, G, N = 1024, 64, 64
     L, final = _config4_inputs(tmp_path, H, G, N)
-    out = subprocess.run([str(DRIVER), str(tmp_path), str(H), str(G), str(N), "8", "20", str(candidate), "4"],
+    out = subprocess.run([str(DRIVER), str(tmp_path), str(H), str(G), str(N), "8", str(delay_us), str(candidate), "8"],
                          capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stdout + out.stderr
     rep = json.loads(out.stdout.strip().splitlines()[-1])
+    print("config4", json.dumps(rep))  # timings of the step, shown with pytest -s
     assert rep["final_groups"] == len(final) and rep["h2d_bytes"] >= len(final) * G * 3 * H // 2
     y = np.fromfile(tmp_path / "y.bin", dtype=np.float16).astype(np.float32)
     y_ref, _, _ = O.mlp(H, G, L.x, L.packed, L.scales, descriptors(final))
