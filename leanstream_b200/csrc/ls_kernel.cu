@@ -670,6 +670,15 @@ __device__ bool producer_window(Producer& pr, const KernelParams& P, const Layer
     return true;
 }
 
+// Sleep between polls of a global word that has not changed yet: short for
+// the first few microseconds of a wait (the layer hand-off), then growing to
+// 1 us, so that a long wait (weights still streaming in) does not flood L2
+// with polling loads while the copy engine writes into it.
+__device__ __forceinline__ void poll_backoff(uint32_t spins, uint32_t base_ns) {
+    const uint32_t shift = spins >> 6;
+    __nanosleep(shift >= 5 ? 1024u : (base_ns << shift < 1024u ? base_ns << shift : 1024u));
+}
+
 // The queue's control words may be mapped host memory: a grid whose 148
 // producers all polled them over PCIe would starve the copy engine that
 // streams the weights. So one thread of the grid at a time polls the host
@@ -902,7 +911,7 @@ __device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail*
         ulonglong2 v[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
-        uint32_t spins = 0;
+        uint32_t spins = 0, polls = 0;
         for (;;) {
             bool ok = true;
 #pragma unroll
@@ -914,7 +923,7 @@ __device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail*
                 if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
                 break;
             }
-            __nanosleep(32);
+            poll_backoff(polls++, 32);
             if (!ok) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
@@ -979,7 +988,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         } else if (tagged) {
             const unsigned long long* src = P.xbuf + 4 * u;
             ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
-            uint32_t spins = 0;
+            uint32_t spins = 0, polls = 0;
             for (;;) {
                 const bool ok = uint32_t(a.x >> 32) == tag && uint32_t(a.y >> 32) == tag &&
                                 uint32_t(b.x >> 32) == tag && uint32_t(b.y >> 32) == tag;
@@ -990,7 +999,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
                     if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 6);
                     break;
                 }
-                __nanosleep(32);
+                poll_backoff(polls++, 32);
                 if (!ok) {
                     a = ld_volatile_v2u64(src);
                     b = ld_volatile_v2u64(src + 2);
@@ -1646,7 +1655,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
 #pragma unroll
             for (int e = 0; e < 16; ++e)
                 w[e] = uint32_t(e) < nr ? ld_volatile_u64(p + size_t(e) * H) : (static_cast<unsigned long long>(tag) << 32);
-            uint32_t spins = 0;
+            uint32_t spins = 0, polls = 0;
             for (;;) {
                 bool ok = true;
 #pragma unroll
@@ -1658,7 +1667,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                     if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 5);
                     break;
                 }
-                __nanosleep(64);
+                poll_backoff(polls++, 64);
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
                     if (uint32_t(w[e] >> 32) != tag) w[e] = ld_volatile_u64(p + size_t(e) * H);
