@@ -73,6 +73,8 @@ struct Backend {
     size_t partial_bytes = 0, xbuf_bytes = 0;
     uint32_t* ws = nullptr;
     uint64_t layers_issued = 0;  // layers of the launches issued through this backend
+    mutable const void* last_control = nullptr;  // host_memory() cache
+    mutable bool last_control_host = false;
     bool clear_tags = false;     // the tag counter wrapped: clear the tagged scratch first
     uint32_t* status_host = nullptr;
     uint32_t* status_dev = nullptr;
@@ -196,8 +198,22 @@ int configure(Backend& b, const ls_b200_geometry& g) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Whether the queue's control words are host memory (mapped pinned or
+// registered): the kernel then polls them under a grid-wide lease. One
+// pointer query per new control address (cached).
+bool host_memory(const Backend& b, const void* control) {
+    if (control != b.last_control) {
+        cudaPointerAttributes at{};
+        const cudaError_t e = cudaPointerGetAttributes(&at, control);
+        if (e != cudaSuccess) cudaGetLastError();  // not a CUDA pointer: plain host memory
+        b.last_control_host = e != cudaSuccess || at.type != cudaMemoryTypeDevice;
+        b.last_control = control;
+    }
+    return b.last_control_host;
+}
+
 // Validates one layer's arguments and encodes its plan. Host only, no
-// CUDA calls.
+// device work (one cached pointer query).
 int encode(const Backend& b, const ls_b200_layer_args& a, LayerPlan* out) {
     if (!b.configured) return EINVAL;
     if (!a.epoch || !a.input || !a.scales || !a.queue.control || !a.queue.descriptors || !a.queue.ready_indices)
@@ -231,7 +247,7 @@ int encode(const Backend& b, const ls_b200_layer_args& a, LayerPlan* out) {
     p.norm_w = static_cast<const uint16_t*>(a.norm_weight);
     p.epoch = a.epoch;
     p.mode = a.mode;
-    p.flags = a.flags;
+    p.flags = (a.flags & ~kPlanHostQueue) | (host_memory(b, a.queue.control) ? kPlanHostQueue : 0u);
     p.layer = a.layer;
     p.core_count = a.core_count;
     *out = p;

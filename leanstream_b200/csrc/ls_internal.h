@@ -61,6 +61,10 @@ constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollCl
 // tensor-parallel gather of the layer's input, device mirror of the queue's
 // ready_count, device mirror of the queue state (1 activated, 2 failed)
 constexpr uint32_t kWsPerLayer = 7;
+// LayerPlan::flags bit set by the host when the queue's control words are in
+// host memory (polled under the grid-wide lease); the public flags use the
+// low bits.
+constexpr uint32_t kPlanHostQueue = 1u << 31;
 // Scratch tags: tag = 1 + base + l for launch-local layer l, where base is a
 // device counter (ws[kWsTag]) advanced by the layers of every launch at its
 // end, so CUDA-graph replays get fresh tags too. It wraps below kTagWrap;

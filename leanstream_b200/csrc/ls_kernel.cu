@@ -702,16 +702,17 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
     const uint32_t* w = reinterpret_cast<const uint32_t*>(L.q.control);
     const bool batch = L.mode != LS_MODE_PROGRESSIVE;  // Auto follows BatchCompat (streaming_mlp.cu:90)
     uint32_t* state = ws_layer(P, l) + 6;
+    const bool host_queue = (L.flags & kPlanHostQueue) != 0;
     uint32_t code = 0;
     for (;;) {
-        const uint32_t m = ld_acquire_gpu(state);  // another CTA saw the queue
+        const uint32_t m = host_queue ? ld_acquire_gpu(state) : 0u;  // another CTA saw the queue
         if (m == kQueueActive) break;
         if (m == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-        if (take_poll_lease(P)) {
+        if (!host_queue || take_poll_lease(P)) {  // device-memory queue: every CTA reads it
             const uint4 a = ld_relaxed_sys_v4(w);
             const uint4 b = ld_relaxed_sys_v4(w + 4);
             if (b.y) {
-                st_release_gpu(state, kQueueFailed);
+                if (host_queue) st_release_gpu(state, kQueueFailed);
                 code = LS_B200_DEV_QUEUE_ERROR;
                 break;
             }
@@ -719,8 +720,10 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
             // a system-scope fence is ~4 us on this part), then release the
             // mirror: the CTAs that acquire it are ordered after the plan.
             if (a.w == L.epoch && (!batch || b.x == L.epoch) && ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) {
-                if (!batch) red_max_release_gpu(ws_layer(P, l) + 5, a.x);
-                st_release_gpu(state, kQueueActive);
+                if (host_queue) {
+                    if (!batch) red_max_release_gpu(ws_layer(P, l) + 5, a.x);
+                    st_release_gpu(state, kQueueActive);
+                }
                 break;
             }
         }
@@ -814,7 +817,15 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                         const uint32_t q = d - L.core_count;
                         uint32_t* mirror = ws_layer(P, l) + 5;
                         uint32_t* state = ws_layer(P, l) + 6;
+                        const bool host_queue = (L.flags & kPlanHostQueue) != 0;
                         for (;;) {
+                            if (!host_queue) {  // device-memory queue: read it directly
+                                if (ld_acquire_sys(words + 5)) { code = LS_B200_DEV_QUEUE_ERROR; break; }
+                                if (ld_acquire_sys(words + 0) > q) break;
+                                if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_READY; break; }
+                                __nanosleep(128);
+                                continue;
+                            }
                             const uint32_t seen = ld_acquire_gpu(mirror);
                             if (seen > q) break;
                             if (ld_relaxed_gpu(state) == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }

@@ -15,6 +15,7 @@
 // writes DIR/y.bin (fp16 y of the last step) and prints one JSON line of timings.
 #include <cuda_runtime.h>
 #include <time.h>
+#include <unistd.h>
 
 #include <cerrno>
 #include <cstdio>
@@ -79,6 +80,8 @@ int main(int argc, char** argv) {
     const float delay_us = float(std::atof(argv[6]));
     const int candidate = std::atoi(argv[7]), steps = std::atoi(argv[8]);
     const uint64_t group_bytes = uint64_t(G) * 3 * H / 2;
+    const char* basic_env = std::getenv("LS_DRIVER_BASIC");
+    const bool basic = basic_env && basic_env[0] == '1';
 
     const std::vector<char> packed = slurp(dir + "/packed.bin"), scales = slurp(dir + "/scales.bin"),
                             x = slurp(dir + "/x.bin");
@@ -165,7 +168,7 @@ int main(int argc, char** argv) {
 
     cudaStream_t stream;
     CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-    double sum_step = 0, sum_tail = 0, sum_gbs = 0, sum_io = 0;
+    double sum_step = 0, sum_tail = 0, sum_gbs = 0, sum_io = 0, sum_copy = 0;
     uint64_t bytes = 0, requests = 0;
     int measured = 0;
     for (int s = 0; s < steps; ++s) {
@@ -173,9 +176,17 @@ int main(int argc, char** argv) {
         const uint64_t t0 = now_ns();
         CHECK(runtime.begin_layer(0, storage, &step));
         CHECK(step.update_prediction({p0.data(), p0.size()}));
-        CHECK(step.enqueue_compute(dx, dy, stream));
-        CHECK(step.update_prediction({p1.data(), p1.size()}));
-        CHECK(step.finalize({fin.data(), fin.size()}));
+        if (basic) {
+            // the reference's basic mode: finalize, wait for the reads, then launch
+            CHECK(step.update_prediction({p1.data(), p1.size()}));
+            CHECK(step.finalize({fin.data(), fin.size()}));
+            CHECK(runtime.weights(0).wait_io(5000));
+            CHECK(step.enqueue_compute(dx, dy, stream));
+        } else {
+            CHECK(step.enqueue_compute(dx, dy, stream));
+            CHECK(step.update_prediction({p1.data(), p1.size()}));
+            CHECK(step.finalize({fin.data(), fin.size()}));
+        }
         CHECK(cudaStreamSynchronize(stream));
         const uint64_t t1 = now_ns();
         uint32_t status[4] = {0, 0, 0, 0};
@@ -194,6 +205,7 @@ int main(int argc, char** argv) {
             sum_tail += double(t1 - st.last_land_ns);
             sum_io += io_ns;
             sum_gbs += io_ns > 0 ? double(st.bytes) / io_ns : 0.0;
+            sum_copy += st.admissions ? double(st.copy_ns) / double(st.admissions) : 0.0;
             bytes = st.bytes;
             ++measured;
         }
@@ -204,9 +216,11 @@ int main(int argc, char** argv) {
     std::printf(
         "{\"candidate\": %d, \"queue_depth\": %u, \"delay_mean_us\": %.1f, \"steps\": %d, \"step_us\": %.2f, "
         "\"io_span_us\": %.2f, \"h2d_gbs\": %.3f, \"tail_after_last_landing_us\": %.2f, \"h2d_bytes\": %llu, "
-        "\"read_requests\": %llu, \"final_groups\": %zu}\n",
+        "\"read_requests\": %llu, \"final_groups\": %zu, \"copy_issue_to_land_us\": %.2f, \"mode\": \"%s\", "
+        "\"host_cores\": %ld}\n",
         candidate, qd, delay_us, measured, sum_step / measured / 1e3, sum_io / measured / 1e3, sum_gbs / measured,
-        sum_tail / measured / 1e3, (unsigned long long)bytes, (unsigned long long)requests, fin.size());
+        sum_tail / measured / 1e3, (unsigned long long)bytes, (unsigned long long)requests, fin.size(),
+        sum_copy / measured / 1e3, basic ? "basic" : "progressive", sysconf(_SC_NPROCESSORS_ONLN));
     CHECK(runtime.drain());
     ls_b200_stream_destroy(engine);
     ls_b200_destroy(backend);
