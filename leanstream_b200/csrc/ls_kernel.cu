@@ -686,6 +686,14 @@ __device__ __forceinline__ void poll_backoff(uint32_t spins, uint32_t base_ns) {
 // to device mirrors, which every CTA reads.
 constexpr uint32_t kHostPollNs = 1000;
 constexpr uint32_t kQueueActive = 1, kQueueFailed = 2;
+// Waits on a host-memory queue back off quickly to 2 us between polls of the
+// device mirrors: the mirror, state and lease words share one L2 line, and
+// 148 CTAs polling it every ~150 ns made that L2 slice a hot spot that
+// stalled the copy engine's writes of the streamed weights (copies 6x slower).
+__device__ __forceinline__ void mirror_backoff(uint32_t polls) {
+    const uint32_t shift = polls >> 3;
+    __nanosleep(shift >= 4 ? 2048u : 128u << shift);
+}
 __device__ __forceinline__ bool take_poll_lease(const KernelParams& P) {
     const uint32_t now = uint32_t(gtimer());
     const uint32_t last = ld_relaxed_gpu(P.ws + kWsPollClock);
@@ -703,7 +711,7 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
     const bool batch = L.mode != LS_MODE_PROGRESSIVE;  // Auto follows BatchCompat (streaming_mlp.cu:90)
     uint32_t* state = ws_layer(P, l) + 6;
     const bool host_queue = (L.flags & kPlanHostQueue) != 0;
-    uint32_t code = 0;
+    uint32_t code = 0, polls = 0;
     for (;;) {
         const uint32_t m = host_queue ? ld_acquire_gpu(state) : 0u;  // another CTA saw the queue
         if (m == kQueueActive) break;
@@ -728,7 +736,10 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
             }
         }
         if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_EPOCH; break; }
-        __nanosleep(100);
+        if (host_queue)
+            mirror_backoff(polls++);
+        else
+            __nanosleep(100);
     }
     uint32_t path = kPathAbort, total = 0;
     if (!code) {
@@ -818,6 +829,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                         uint32_t* mirror = ws_layer(P, l) + 5;
                         uint32_t* state = ws_layer(P, l) + 6;
                         const bool host_queue = (L.flags & kPlanHostQueue) != 0;
+                        uint32_t polls = 0;
                         for (;;) {
                             if (!host_queue) {  // device-memory queue: read it directly
                                 if (ld_acquire_sys(words + 5)) { code = LS_B200_DEV_QUEUE_ERROR; break; }
@@ -840,7 +852,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                                 if (ready > q) break;
                             }
                             if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_READY; break; }
-                            __nanosleep(128);
+                            mirror_backoff(polls++);
                         }
                     }
                     if (code && code != 0xffffffffu) raise_error(P, t, code, pos);
