@@ -802,9 +802,12 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
             // Static balanced split of the layer's slab positions.
             const uint32_t b = blockIdx.x, grid = gridDim.x;
             const uint32_t u1 = uint32_t(uint64_t(NS) * (b + 1) / grid);
+            // only the descriptors of this CTA's slabs: a host-memory queue
+            // costs a PCIe round trip per word read
+            const uint32_t dend = u1 ? (u1 - 1) / spg + 1 : 0;
             for (uint32_t u = uint32_t(uint64_t(NS) * b / grid); ok && u < u1; ++u) {
                 const uint32_t d = u / spg, slab = u % spg;
-                if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32) ok = producer_window(pr, P, L, l, d, D);
+                if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32) ok = producer_window(pr, P, L, l, d, dend);
                 if (!ok) break;
                 const DescView dv = t->dtab[d - pr.wbase];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);

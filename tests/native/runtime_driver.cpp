@@ -92,6 +92,8 @@ int main(int argc, char** argv) {
         return 2;
     }
 
+    const char* blocking_env = std::getenv("LS_DRIVER_BLOCKING_SYNC");
+    if (blocking_env && blocking_env[0] == '1') CHECK(cudaSetDeviceFlags(cudaDeviceScheduleBlockingSync));
     CHECK(cudaSetDevice(0));
     // weights in pinned host memory; staging, scales, x and y on the device
     void* host = nullptr;
@@ -217,10 +219,11 @@ int main(int argc, char** argv) {
         "{\"candidate\": %d, \"queue_depth\": %u, \"delay_mean_us\": %.1f, \"steps\": %d, \"step_us\": %.2f, "
         "\"io_span_us\": %.2f, \"h2d_gbs\": %.3f, \"tail_after_last_landing_us\": %.2f, \"h2d_bytes\": %llu, "
         "\"read_requests\": %llu, \"final_groups\": %zu, \"copy_issue_to_land_us\": %.2f, \"mode\": \"%s\", "
-        "\"host_cores\": %ld}\n",
+        "\"host_cores\": %ld, \"blocking_sync\": %d}\n",
         candidate, qd, delay_us, measured, sum_step / measured / 1e3, sum_io / measured / 1e3, sum_gbs / measured,
         sum_tail / measured / 1e3, (unsigned long long)bytes, (unsigned long long)requests, fin.size(),
-        sum_copy / measured / 1e3, basic ? "basic" : "progressive", sysconf(_SC_NPROCESSORS_ONLN));
+        sum_copy / measured / 1e3, basic ? "basic" : "progressive", sysconf(_SC_NPROCESSORS_ONLN),
+        blocking_env && blocking_env[0] == '1' ? 1 : 0);
     CHECK(runtime.drain());
     ls_b200_stream_destroy(engine);
     ls_b200_destroy(backend);
