@@ -70,6 +70,7 @@ struct Backend {
     // scratch (device) and mapped words (host)
     unsigned long long* partial = nullptr;  // tagged slab partial rows
     unsigned long long* xbuf = nullptr;     // tagged layer output handed to the next layer
+    uint4* qmirror = nullptr;               // device copy of host-memory queues' descriptors
     size_t partial_bytes = 0, xbuf_bytes = 0;
     uint32_t* ws = nullptr;
     uint64_t layers_issued = 0;  // layers of the launches issued through this backend
@@ -125,6 +126,8 @@ struct Backend {
         release_tp();
         if (partial) cudaFree(partial);
         if (xbuf) cudaFree(xbuf);
+        if (qmirror) cudaFree(qmirror);
+        qmirror = nullptr;
         if (ws) cudaFree(ws);
         if (status_host) cudaFreeHost(status_host);
         if (done_host) cudaFreeHost(done_host);
@@ -166,8 +169,11 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     const size_t partial_bytes = size_t(N) * slabs_per_group(G) * H * sizeof(unsigned long long);
     const size_t xbuf_bytes = size_t(H / 2) * sizeof(unsigned long long);
     const size_t ws_bytes = size_t(ws_words(b.geo.max_layers)) * sizeof(uint32_t);
+    // device copy of a host-memory queue's descriptors, per layer (32 B each)
+    const size_t qmirror_bytes = size_t(b.geo.max_layers) * N * 2 * sizeof(uint4);
     cudaError_t e = cudaMalloc(&b.partial, partial_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.xbuf, xbuf_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&b.qmirror, qmirror_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
@@ -191,7 +197,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
         b.release();
         return ENOMEM;
     }
-    b.scratch_bytes = partial_bytes + xbuf_bytes + ws_bytes;
+    b.scratch_bytes = partial_bytes + xbuf_bytes + ws_bytes + qmirror_bytes;
     b.configured = true;
     return 0;
 }
@@ -281,6 +287,7 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace, cudaStre
     if (before / kTagWrap != b.layers_issued / kTagWrap) b.clear_tags = true;
     p.partial = b.partial;
     p.xbuf = b.xbuf;
+    p.qmirror = b.qmirror;
     p.ws = b.ws;
     p.status = b.status_dev;
     p.done = b.done_dev;
@@ -457,6 +464,10 @@ static __device__ __align__(256) unsigned long long g_static_xbuf[kMaxHidden / 2
 static __device__ __align__(256) uint32_t g_static_ws[kStaticWsWords];
 static __device__ __align__(256) uint32_t g_static_status[LS_B200_STATUS_WORDS];
 static __device__ __align__(256) uint32_t g_static_done[kStaticLayers];
+// device copy of a host-memory queue: N <= kStaticPartialWords / 256 groups
+// (H >= 256, one slab per group at least)
+constexpr size_t kStaticMirror = kStaticPartialWords / 256;
+static __device__ __align__(256) uint4 g_static_qmirror[kStaticMirror * 2];
 
 namespace {
 
@@ -468,6 +479,7 @@ struct StaticScratch {
     uint32_t* ws = nullptr;
     uint32_t* status = nullptr;
     uint32_t* done = nullptr;
+    uint4* qmirror = nullptr;
     uint64_t layers_issued = 0;  // layers launched on this device (tag counter wraps)
     bool clear_tags = false;
 };
@@ -500,7 +512,7 @@ int static_setup(StaticScratch& s, int dev, cudaStream_t stream) {
     if (rc) return cuda_rc(cudaError_t(rc));
     if ((rc = symbol_address(&s.partial, g_static_partial)) || (rc = symbol_address(&s.xbuf, g_static_xbuf)) ||
         (rc = symbol_address(&s.ws, g_static_ws)) || (rc = symbol_address(&s.status, g_static_status)) ||
-        (rc = symbol_address(&s.done, g_static_done)))
+        (rc = symbol_address(&s.done, g_static_done)) || (rc = symbol_address(&s.qmirror, g_static_qmirror)))
         return rc;
     cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
@@ -558,6 +570,7 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     if (++s.layers_issued % kTagWrap == 0) s.clear_tags = true;
     p.partial = s.partial;
     p.xbuf = s.xbuf;
+    p.qmirror = s.qmirror;
     p.ws = s.ws;
     p.status = status ? status : s.status;
     p.done = s.done;

@@ -58,9 +58,10 @@ struct alignas(16) LayerPlan {
 // kWsPollClock: %globaltimer (low 32 bits) of the last host-queue poll.
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsHeader = 8;
 // path, slab claim, reduction-block claim, reduced column blocks, CTAs past the
-// tensor-parallel gather of the layer's input, device mirror of the queue's
-// ready_count, device mirror of the queue state (1 activated, 2 failed)
-constexpr uint32_t kWsPerLayer = 7;
+// tensor-parallel gather of the layer's input, and for a host-memory queue:
+// queue positions mirrored into device memory, queue state (1 activated,
+// 2 failed), total_count at activation
+constexpr uint32_t kWsPerLayer = 8;
 // LayerPlan::flags bit set by the host when the queue's control words are in
 // host memory (polled under the grid-wide lease); the public flags use the
 // low bits.
@@ -93,6 +94,7 @@ struct KernelParams {
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
     uint32_t* done;       // mapped host per-layer completion epochs
     uint64_t* trace;      // optional phase stamps
+    uint4* qmirror;       // [max_layers][N][2]: device copy of a host queue's core + published descriptors
     const LayerPlan* plans;  // device array for nlayers > 1, else nullptr
     LayerPlan first;         // layer 0 when plans == nullptr
     // Tensor parallel inside one launch (world > 1): rank r's exchange buffer

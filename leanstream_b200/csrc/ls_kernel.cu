@@ -233,6 +233,9 @@ __device__ __forceinline__ void red_release_gpu(uint32_t* p, uint32_t v) {
 __device__ __forceinline__ void red_max_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -386,9 +389,26 @@ __device__ __forceinline__ const LayerPlan& plan_at(const KernelParams& P, uint3
 // queue descriptor published at ready position d - core_count
 // (streaming_mlp.cu:60, persistent.py:80). Descriptor row: d for core, else
 // core_count + descriptor index (custom_triton.md:54).
-__device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_t d) {
+__device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t d) {
     const uint32_t* c;
     uint32_t row;
+    if (L.flags & kPlanHostQueue) {
+        // the device copy made under the polling lease (mirror_queue)
+        const uint4* e = P.qmirror + (size_t(l) * P.N + d) * 2;
+        const uint4 a = e[0];
+        const uint32_t kind = e[1].x;
+        const uint32_t idx = a.x;
+        DescView v;
+        row = d < L.core_count ? d : L.core_count + idx;
+        v.ok = idx != 0xffffffffu && kind <= 1u && a.w < P.N && row < P.N &&
+               (P.phys_groups == 0 || a.y < P.phys_groups) &&
+               (kind == 0 ? (P.cache_slots == 0 || a.z < P.cache_slots) : (P.staging_slots == 0 || a.z < P.staging_slots));
+        v.src = (kind == 0 ? L.cache : L.staging) + size_t(a.z) * P.group_bytes;
+        v.phys = a.y;
+        v.dest = a.w;
+        v.row = row;
+        return v;
+    }
     if (d < L.core_count) {
         c = reinterpret_cast<const uint32_t*>(L.core + d);
         row = d;
@@ -655,7 +675,7 @@ __device__ bool producer_window(Producer& pr, const KernelParams& P, const Layer
     const uint32_t d = base + pr.lane;
     uint32_t bad = 0;
     if (d < D) {
-        const DescView v = load_desc(P, L, d);
+        const DescView v = load_desc(P, L, layer, d);
         pr.t->dtab[pr.lane] = v;
         bad = v.ok ? 0u : 1u;
     }
@@ -700,70 +720,124 @@ __device__ __forceinline__ bool take_poll_lease(const KernelParams& P) {
     return now - last >= kHostPollNs && atomicCAS(P.ws + kWsPollClock, last, now) == last;
 }
 
+// Warp-wide: copies descriptors [from, to) of layer l (core descriptors
+// first, then queue positions through ready_indices) from host memory into
+// the device mirror, one descriptor per lane in flight, then publishes the
+// number of mirrored queue positions (lane 0, release). Entries of published
+// positions never change, so overlapping copies by successive lease holders
+// write the same values.
+__device__ void mirror_queue(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t from, uint32_t to,
+                             uint32_t lane, bool publish_count) {
+    for (uint32_t d = from + lane; d < to; d += 32) {
+        uint32_t idx, w[4] = {0u, 0u, 0u, 0xffffffffu};
+        const uint32_t* c = nullptr;
+        if (d < L.core_count) {
+            idx = d;
+            c = reinterpret_cast<const uint32_t*>(L.core + d);
+        } else {
+            idx = ld_relaxed_sys(L.q.ready_indices + (d - L.core_count));
+            if (idx < L.q.capacity) c = reinterpret_cast<const uint32_t*>(L.q.descriptors + idx);
+            else idx = 0xffffffffu;
+        }
+        if (c) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w[k] = ld_relaxed_sys(c + 1 + k);
+        }
+        uint4* e = P.qmirror + (size_t(l) * P.N + d) * 2;
+        e[0] = make_uint4(idx, w[0], w[1], w[2]);
+        e[1] = make_uint4(w[3], 0u, 0u, 0u);
+    }
+    __threadfence();
+    __syncwarp();
+    if (publish_count && lane == 0) red_max_release_gpu(ws_layer(P, l) + 5, to - L.core_count);
+}
+
 // Per-CTA path decision for one layer (streaming_mlp.cu:49-56,
-// persistent.py:46-55). BatchCompat / Auto wait for the batch epoch and take
-// the fast path; Progressive proposes a path and agrees with the other CTAs
-// through a device-memory CAS (QueueControl.consumer_path stays untouched:
-// a discrete GPU has no host-native atomics).
+// persistent.py:46-55), by the producer warp. BatchCompat / Auto wait for the
+// batch epoch and take the fast path; Progressive proposes a path and agrees
+// with the other CTAs through a device-memory CAS (QueueControl.consumer_path
+// stays untouched: a discrete GPU has no host-native atomics). A queue in
+// host memory is read by the lease holder alone, who mirrors the plan into
+// device memory before the other CTAs see it activated.
 __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l, SmemTail* t, uint64_t deadline,
-                           uint32_t* total_out) {
+                           uint32_t lane, uint32_t* total_out) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(L.q.control);
     const bool batch = L.mode != LS_MODE_PROGRESSIVE;  // Auto follows BatchCompat (streaming_mlp.cu:90)
-    uint32_t* state = ws_layer(P, l) + 6;
     const bool host_queue = (L.flags & kPlanHostQueue) != 0;
-    uint32_t code = 0, polls = 0;
+    uint32_t* state = ws_layer(P, l) + 6;
+    uint32_t code = 0, polls = 0, total = 0, ready = 0;
     for (;;) {
-        const uint32_t m = host_queue ? ld_acquire_gpu(state) : 0u;  // another CTA saw the queue
-        if (m == kQueueActive) break;
-        if (m == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-        if (!host_queue || take_poll_lease(P)) {  // device-memory queue: every CTA reads it
-            const uint4 a = ld_relaxed_sys_v4(w);
-            const uint4 b = ld_relaxed_sys_v4(w + 4);
-            if (b.y) {
-                if (host_queue) st_release_gpu(state, kQueueFailed);
-                code = LS_B200_DEV_QUEUE_ERROR;
-                break;
-            }
-            // Acquire the deciding word (a system-scope acquire load is ~0.2 us;
-            // a system-scope fence is ~4 us on this part), then release the
-            // mirror: the CTAs that acquire it are ordered after the plan.
-            if (a.w == L.epoch && (!batch || b.x == L.epoch) && ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) {
-                if (host_queue) {
-                    if (!batch) red_max_release_gpu(ws_layer(P, l) + 5, a.x);
-                    st_release_gpu(state, kQueueActive);
+        // lane 0 polls; 0 wait, 1 activated (seen in the mirror), 2 failed,
+        // 3 activated now (read from the queue), 4 deadline
+        uint32_t st = 0;
+        if (lane == 0) {
+            const uint32_t m = host_queue ? ld_acquire_gpu(state) : 0u;
+            if (m == kQueueActive) {
+                st = 1;
+            } else if (m == kQueueFailed) {
+                st = 2;
+            } else if (!host_queue || take_poll_lease(P)) {  // device-memory queue: every CTA reads it
+                const uint4 a = ld_relaxed_sys_v4(w);
+                const uint4 b = ld_relaxed_sys_v4(w + 4);
+                if (b.y) {
+                    if (host_queue) st_release_gpu(state, kQueueFailed);
+                    st = 2;
+                } else if (a.w == L.epoch && (!batch || b.x == L.epoch) &&
+                           ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) {
+                    // Acquire of the deciding word (a system-scope acquire load
+                    // is ~0.2 us; a system-scope fence ~4 us on this part).
+                    const uint4 a2 = ld_relaxed_sys_v4(w);  // ordered after the acquire
+                    total = a2.z;
+                    ready = batch ? total : a2.x;
+                    st = 3;
                 }
-                break;
             }
+            if (st == 0 && gtimer() > deadline) st = 4;
         }
-        if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_EPOCH; break; }
-        if (host_queue)
-            mirror_backoff(polls++);
-        else
-            __nanosleep(100);
-    }
-    uint32_t path = kPathAbort, total = 0;
-    if (!code) {
-        const uint4 a = ld_relaxed_sys_v4(w);  // ordered after the acquire above
-        total = a.z;
-        const uint32_t ready = batch ? total : a.x;
-        if (total > L.q.capacity || L.core_count + total > P.N || ready > total) {
+        st = __shfl_sync(0xffffffffu, st, 0);
+        if (st == 0) {
+            if (host_queue)
+                mirror_backoff(polls++);
+            else
+                __nanosleep(100);
+            continue;
+        }
+        if (st == 2) code = LS_B200_DEV_QUEUE_ERROR;
+        if (st == 4) code = LS_B200_DEV_TIMEOUT_EPOCH;
+        if (st == 1 && lane == 0) {
+            total = ld_relaxed_gpu(ws_layer(P, l) + 7);
+            ready = batch ? total : ld_acquire_gpu(ws_layer(P, l) + 5);
+        }
+        total = __shfl_sync(0xffffffffu, total, 0);
+        ready = __shfl_sync(0xffffffffu, ready, 0);
+        if ((st == 1 || st == 3) && (total > L.q.capacity || L.core_count + total > P.N || ready > total)) {
             code = LS_B200_DEV_BAD_PLAN;
-        } else {
-            const uint32_t proposal = ready == total ? kPathFast : kPathProgressive;
-            if (batch) {
-                path = proposal;
-            } else {
-                const uint32_t old = atomicCAS(ws_layer(P, l) + 0, 0u, proposal);
-                path = old ? old : proposal;
+            if (host_queue && lane == 0) st_release_gpu(state, kQueueFailed);
+        }
+        if (st == 3 && host_queue && !code) {
+            // core descriptors and the published prefix into device memory,
+            // then the activation for the other CTAs
+            mirror_queue(P, L, l, 0, L.core_count + ready, lane, true);
+            if (lane == 0) {
+                st_relaxed_gpu(ws_layer(P, l) + 7, total);
+                st_release_gpu(state, kQueueActive);
             }
         }
+        break;
     }
-    if (code) {
-        raise_error(P, t, code, l);
-        path = kPathAbort;
+    uint32_t path = kPathAbort;
+    if (!code && lane == 0) {
+        const uint32_t proposal = ready == total ? kPathFast : kPathProgressive;
+        if (batch) {
+            path = proposal;
+        } else {
+            const uint32_t old = atomicCAS(ws_layer(P, l) + 0, 0u, proposal);
+            path = old ? old : proposal;
+        }
     }
+    if (code && lane == 0) raise_error(P, t, code, l);
     *total_out = total;
-    return path;
+    return __shfl_sync(0xffffffffu, path, 0);
 }
 
 __device__ void stamp(const LayerPlan& L, const DescView& d) {
@@ -786,10 +860,8 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
     bool ok = true;
     for (uint32_t l = 0; ok && l < P.nlayers; ++l) {
         const LayerPlan& L = plan_at(P, l);
-        uint32_t path = 0, total = 0;
-        if (pr.lane == 0) path = decide(P, L, l, t, deadline, &total);
-        path = __shfl_sync(0xffffffffu, path, 0);
-        total = __shfl_sync(0xffffffffu, total, 0);
+        uint32_t total = 0;
+        const uint32_t path = decide(P, L, l, t, deadline, pr.lane, &total);
         if (pr.lane == 0 && l == 0) trace(P, LS_B200_TRACE_DECIDED);
         if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_DECIDED);
         if (path == kPathAbort) break;
@@ -816,53 +888,76 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         } else {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(L.q.control);
             uint32_t* claim = ws_layer(P, l) + 1;
+            const bool host_queue = (L.flags & kPlanHostQueue) != 0;
+            uint32_t* mirror = ws_layer(P, l) + 5;
+            uint32_t* state = ws_layer(P, l) + 6;
             while (ok && !t->abort) {
                 uint32_t pos = 0, code = 0;
                 if (pr.lane == 0) {
                     pos = atomicAdd(claim, 1u);
-                    const uint32_t d = pos / spg;
-                    if (pos >= NS) {
-                        code = 0xffffffffu;  // exhausted
-                    } else if (d >= L.core_count) {
-                        // Wait until the descriptor of the claimed slab is
-                        // published (persistent.py:71-90; streaming_mlp.cu:63-75):
-                        // the device mirror of ready_count, refreshed from the
-                        // host queue under the polling lease.
-                        const uint32_t q = d - L.core_count;
-                        uint32_t* mirror = ws_layer(P, l) + 5;
-                        uint32_t* state = ws_layer(P, l) + 6;
-                        const bool host_queue = (L.flags & kPlanHostQueue) != 0;
-                        uint32_t polls = 0;
-                        for (;;) {
-                            if (!host_queue) {  // device-memory queue: read it directly
-                                if (ld_acquire_sys(words + 5)) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-                                if (ld_acquire_sys(words + 0) > q) break;
-                                if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_READY; break; }
-                                __nanosleep(128);
-                                continue;
-                            }
-                            const uint32_t seen = ld_acquire_gpu(mirror);
-                            if (seen > q) break;
-                            if (ld_relaxed_gpu(state) == kQueueFailed) { code = LS_B200_DEV_QUEUE_ERROR; break; }
-                            if (take_poll_lease(P)) {
-                                if (ld_acquire_sys(words + 5)) {
-                                    st_release_gpu(state, kQueueFailed);
-                                    code = LS_B200_DEV_QUEUE_ERROR;
-                                    break;
-                                }
-                                const uint32_t ready = ld_acquire_sys(words + 0);
-                                if (ready > seen) red_max_release_gpu(mirror, ready);
-                                if (ready > q) break;
-                            }
-                            if (gtimer() > deadline) { code = LS_B200_DEV_TIMEOUT_READY; break; }
-                            mirror_backoff(polls++);
-                        }
-                    }
-                    if (code && code != 0xffffffffu) raise_error(P, t, code, pos);
+                    if (pos >= NS) code = 0xffffffffu;  // exhausted
                 }
-                code = __shfl_sync(0xffffffffu, code, 0);
                 pos = __shfl_sync(0xffffffffu, pos, 0);
+                code = __shfl_sync(0xffffffffu, code, 0);
                 if (code) break;
+                if (pos / spg >= L.core_count) {
+                    // Wait until the descriptor of the claimed slab is published
+                    // (persistent.py:71-90; streaming_mlp.cu:63-75). A host
+                    // queue is read by the lease holder, whose warp copies the
+                    // newly published descriptors into the device mirror.
+                    const uint32_t q = pos / spg - L.core_count;
+                    uint32_t polls = 0;
+                    for (;;) {
+                        // lane 0: 0 wait, 1 ready, 2 queue error, 3 mirror [from, to), 4 deadline
+                        uint32_t st = 0, from = 0, to = 0;
+                        if (pr.lane == 0) {
+                            if (!host_queue) {  // device-memory queue: read it directly
+                                if (ld_acquire_sys(words + 5)) st = 2;
+                                else if (ld_acquire_sys(words + 0) > q) st = 1;
+                            } else {
+                                const uint32_t seen = ld_acquire_gpu(mirror);
+                                if (seen > q) {
+                                    st = 1;
+                                } else if (ld_relaxed_gpu(state) == kQueueFailed) {
+                                    st = 2;
+                                } else if (take_poll_lease(P)) {
+                                    if (ld_acquire_sys(words + 5)) {
+                                        st_release_gpu(state, kQueueFailed);
+                                        st = 2;
+                                    } else {
+                                        uint32_t ready = ld_acquire_sys(words + 0);
+                                        if (ready > total) ready = total;  // bounded by the plan
+                                        if (ready > seen) {
+                                            st = 3;
+                                            from = seen;
+                                            to = ready;
+                                        }
+                                    }
+                                }
+                            }
+                            if (st == 0 && gtimer() > deadline) st = 4;
+                        }
+                        st = __shfl_sync(0xffffffffu, st, 0);
+                        if (st == 3) {
+                            from = __shfl_sync(0xffffffffu, from, 0);
+                            to = __shfl_sync(0xffffffffu, to, 0);
+                            mirror_queue(P, L, l, L.core_count + from, L.core_count + to, pr.lane, true);
+                            if (to > q) break;
+                            continue;
+                        }
+                        if (st == 1) break;
+                        if (st == 2 || st == 4) {
+                            code = st == 2 ? LS_B200_DEV_QUEUE_ERROR : LS_B200_DEV_TIMEOUT_READY;
+                            if (pr.lane == 0) raise_error(P, t, code, pos);
+                            break;
+                        }
+                        if (host_queue)
+                            mirror_backoff(polls++);
+                        else
+                            __nanosleep(128);
+                    }
+                    if (code) break;
+                }
                 const uint32_t d = pos / spg, slab = pos % spg;
                 ok = producer_window(pr, P, L, l, d, d + 1);  // one descriptor, lane 0
                 if (!ok) break;
