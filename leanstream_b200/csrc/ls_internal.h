@@ -55,8 +55,10 @@ struct alignas(16) LayerPlan {
 
 // Workspace words (device memory, zero at rest; the last CTA of every
 // launch restores the words it used).
-// kWsPollClock: %globaltimer (low 32 bits) of the last host-queue poll.
-constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsHeader = 8;
+// kWsPollClock: %globaltimer (low 32 bits) of the last host-queue poll;
+// kWsPollLock: 1 while one thread of the grid reads a host-memory queue.
+constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsPollLock = 5,
+                   kWsHeader = 8;
 // path, slab claim, reduction-block claim, reduced column blocks, CTAs past the
 // tensor-parallel gather of the layer's input, and for a host-memory queue:
 // queue positions mirrored into device memory, queue state (1 activated,

@@ -195,6 +195,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ uint4 ld_acquire_sys_v4(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.acquire.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -714,11 +722,17 @@ __device__ __forceinline__ void mirror_backoff(uint32_t polls) {
     const uint32_t shift = polls >> 3;
     __nanosleep(shift >= 4 ? 2048u : 128u << shift);
 }
+// The lease is exclusive until released (a read of host memory takes ~10 us
+// here, far longer than the polling interval) and is taken at most every
+// kHostPollNs.
 __device__ __forceinline__ bool take_poll_lease(const KernelParams& P) {
     const uint32_t now = uint32_t(gtimer());
-    const uint32_t last = ld_relaxed_gpu(P.ws + kWsPollClock);
-    return now - last >= kHostPollNs && atomicCAS(P.ws + kWsPollClock, last, now) == last;
+    if (now - ld_relaxed_gpu(P.ws + kWsPollClock) < kHostPollNs) return false;
+    if (atomicCAS(P.ws + kWsPollLock, 0u, 1u) != 0u) return false;
+    st_relaxed_gpu(P.ws + kWsPollClock, now);
+    return true;
 }
+__device__ __forceinline__ void release_poll_lease(const KernelParams& P) { st_release_gpu(P.ws + kWsPollLock, 0u); }
 
 // Warp-wide: copies descriptors [from, to) of layer l (core descriptors
 // first, then queue positions through ready_indices) from host memory into
@@ -777,20 +791,30 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
             } else if (m == kQueueFailed) {
                 st = 2;
             } else if (!host_queue || take_poll_lease(P)) {  // device-memory queue: every CTA reads it
-                const uint4 a = ld_relaxed_sys_v4(w);
-                const uint4 b = ld_relaxed_sys_v4(w + 4);
+                // The word that decides is read with acquire semantics (a
+                // system-scope acquire load is ~0.2 us; a system-scope fence
+                // ~4 us): Progressive reads the epoch word (in a), BatchCompat
+                // the batch epoch (in b). The other vector is read first, so
+                // both loads are in flight together; BatchCompat re-reads the
+                // counts after its acquire.
+                uint4 a, b;
+                if (batch) {
+                    a = ld_relaxed_sys_v4(w);
+                    b = ld_acquire_sys_v4(w + 4);
+                } else {
+                    b = ld_relaxed_sys_v4(w + 4);
+                    a = ld_acquire_sys_v4(w);
+                }
                 if (b.y) {
                     if (host_queue) st_release_gpu(state, kQueueFailed);
                     st = 2;
-                } else if (a.w == L.epoch && (!batch || b.x == L.epoch) &&
-                           ld_acquire_sys(w + (batch ? 4 : 3)) == L.epoch) {
-                    // Acquire of the deciding word (a system-scope acquire load
-                    // is ~0.2 us; a system-scope fence ~4 us on this part).
-                    const uint4 a2 = ld_relaxed_sys_v4(w);  // ordered after the acquire
-                    total = a2.z;
-                    ready = batch ? total : a2.x;
+                } else if (a.w == L.epoch && (!batch || b.x == L.epoch)) {
+                    if (batch) a = ld_relaxed_sys_v4(w);  // ordered after the acquire
+                    total = a.z;
+                    ready = batch ? total : a.x;
                     st = 3;
                 }
+                if (host_queue && st != 3) release_poll_lease(P);  // st 3: released after the mirror
             }
             if (st == 0 && gtimer() > deadline) st = 4;
         }
@@ -814,13 +838,16 @@ __device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l
             code = LS_B200_DEV_BAD_PLAN;
             if (host_queue && lane == 0) st_release_gpu(state, kQueueFailed);
         }
-        if (st == 3 && host_queue && !code) {
+        if (st == 3 && host_queue) {
             // core descriptors and the published prefix into device memory,
             // then the activation for the other CTAs
-            mirror_queue(P, L, l, 0, L.core_count + ready, lane, true);
+            if (!code) mirror_queue(P, L, l, 0, L.core_count + ready, lane, true);
             if (lane == 0) {
-                st_relaxed_gpu(ws_layer(P, l) + 7, total);
-                st_release_gpu(state, kQueueActive);
+                if (!code) {
+                    st_relaxed_gpu(ws_layer(P, l) + 7, total);
+                    st_release_gpu(state, kQueueActive);
+                }
+                release_poll_lease(P);
             }
         }
         break;
@@ -921,11 +948,14 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                                 } else if (ld_relaxed_gpu(state) == kQueueFailed) {
                                     st = 2;
                                 } else if (take_poll_lease(P)) {
-                                    if (ld_acquire_sys(words + 5)) {
+                                    // error word first (relaxed), then ready_count
+                                    // (acquire): both reads in flight together
+                                    const uint32_t err = ld_relaxed_sys(words + 5);
+                                    uint32_t ready = ld_acquire_sys(words + 0);
+                                    if (err) {
                                         st_release_gpu(state, kQueueFailed);
                                         st = 2;
                                     } else {
-                                        uint32_t ready = ld_acquire_sys(words + 0);
                                         if (ready > total) ready = total;  // bounded by the plan
                                         if (ready > seen) {
                                             st = 3;
@@ -933,6 +963,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                                             to = ready;
                                         }
                                     }
+                                    if (st != 3) release_poll_lease(P);
                                 }
                             }
                             if (st == 0 && gtimer() > deadline) st = 4;
@@ -942,6 +973,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                             from = __shfl_sync(0xffffffffu, from, 0);
                             to = __shfl_sync(0xffffffffu, to, 0);
                             mirror_queue(P, L, l, L.core_count + from, L.core_count + to, pr.lane, true);
+                            if (pr.lane == 0) release_poll_lease(P);
                             if (to > q) break;
                             continue;
                         }
@@ -2168,6 +2200,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
             P.ws[kWsErr] = 0;
             P.ws[kWsDetail] = 0;
             P.ws[kWsExit] = 0;
+            P.ws[kWsPollLock] = 0;  // every holder has released it; no CTA is left
             uint32_t next_base = t->tagbase + nl;
             if (next_base >= kTagWrap) next_base -= kTagWrap;
             P.ws[kWsTag] = next_base;

@@ -17,6 +17,7 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cerrno>
 #include <cstdio>
 #include <cstdlib>
@@ -127,6 +128,17 @@ int main(int argc, char** argv) {
     bound.staging = static_cast<const uint8_t*>(staging);
     bound.scales = dscales;
     bound.candidate = -1;
+    // optional phase stamps of the kernel (LS_DRIVER_TRACE=1): per CTA and per layer
+    const char* trace_env = std::getenv("LS_DRIVER_TRACE");
+    const bool tracing = trace_env && trace_env[0] == '1';
+    const size_t trace_words = 148 * LS_B200_TRACE_WORDS + 148 * LS_B200_LAYER_TRACE_WORDS +
+                               4 * LS_B200_PIECE_TRACE_PIECES * 4;
+    uint64_t* dtrace = nullptr;
+    if (tracing) {
+        CHECK(cudaMalloc(&dtrace, trace_words * 8));
+        CHECK(cudaMemset(dtrace, 0, trace_words * 8));
+        bound.trace = dtrace;
+    }
     CHECK(ls_b200_set_buffers(backend, &bound));
     ls_b200_set_state(backend, 0, 0);
     ls_compute_backend cview{};
@@ -210,6 +222,24 @@ int main(int argc, char** argv) {
             sum_copy += st.admissions ? double(st.copy_ns) / double(st.admissions) : 0.0;
             bytes = st.bytes;
             ++measured;
+        }
+    }
+    if (tracing) {
+        // stamps of the last step: per CTA, relative to the earliest entry (us)
+        std::vector<uint64_t> tr(trace_words);
+        CHECK(cudaMemcpy(tr.data(), dtrace, trace_words * 8, cudaMemcpyDeviceToHost));
+        const char* names[8] = {"entry", "decided", "first", "pieces", "produced", "barrier", "reduced", "exit"};
+        uint64_t t0 = ~0ull;
+        for (int c = 0; c < 148; ++c)
+            if (tr[c * 8] && tr[c * 8] < t0) t0 = tr[c * 8];
+        for (int k = 0; k < 8; ++k) {
+            std::vector<double> v;
+            for (int c = 0; c < 148; ++c)
+                if (tr[c * 8 + k]) v.push_back(double(tr[c * 8 + k] - t0) / 1e3);
+            if (v.empty()) continue;
+            std::sort(v.begin(), v.end());
+            std::fprintf(stderr, "trace %-9s n=%3zu min %8.1f med %8.1f max %8.1f us\n", names[k], v.size(), v.front(),
+                         v[v.size() / 2], v.back());
         }
     }
     std::vector<uint16_t> y(H);
