@@ -91,7 +91,7 @@ def test_engine_priority_order_reorder_and_bytes(native_lib, cuda_device):
     k = 0
     while k < len(issued) and issued[k] == p0[k]:
         k += 1
-    assert 1 <= k <= 4, issued[:6]  # the first update started at most a few reads
+    assert k <= 4, issued[:6]  # the first update started at most a few reads (none if the second came first)
     second = [g for g in p1 if g not in issued[:k]]
     assert issued[k:k + len(second)] == second
     third = [g for g in final if g not in issued[:k + len(second)]]
