@@ -740,8 +740,8 @@ __device__ __forceinline__ void release_poll_lease(const KernelParams& P) { st_r
 // number of mirrored queue positions (lane 0, release). Entries of published
 // positions never change, so overlapping copies by successive lease holders
 // write the same values.
-__device__ void mirror_queue(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t from, uint32_t to,
-                             uint32_t lane, bool publish_count) {
+__device__ __noinline__ void mirror_queue(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t from,
+                                          uint32_t to, uint32_t lane, bool publish_count) {
     for (uint32_t d = from + lane; d < to; d += 32) {
         uint32_t idx, w[4] = {0u, 0u, 0u, 0xffffffffu};
         const uint32_t* c = nullptr;
@@ -773,8 +773,10 @@ __device__ void mirror_queue(const KernelParams& P, const LayerPlan& L, uint32_t
 // stays untouched: a discrete GPU has no host-native atomics). A queue in
 // host memory is read by the lease holder alone, who mirrors the plan into
 // device memory before the other CTAs see it activated.
-__device__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l, SmemTail* t, uint64_t deadline,
-                           uint32_t lane, uint32_t* total_out) {
+// Out of line: once per layer, and kept out of the instruction-cache
+// footprint of the producer's per-piece code.
+__device__ __noinline__ uint32_t decide(const KernelParams& P, const LayerPlan& L, uint32_t l, SmemTail* t,
+                                        uint64_t deadline, uint32_t lane, uint32_t* total_out) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(L.q.control);
     const bool batch = L.mode != LS_MODE_PROGRESSIVE;  // Auto follows BatchCompat (streaming_mlp.cu:90)
     const bool host_queue = (L.flags & kPlanHostQueue) != 0;
