@@ -167,7 +167,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     // one tagged fp32 partial output row per slab of every descriptor row,
     // and one tagged fp16 pair per two hidden coordinates; tag 0 never occurs
     const size_t partial_bytes = size_t(N) * slabs_per_group(G) * H * sizeof(unsigned long long);
-    const size_t xbuf_bytes = size_t(H / 2) * sizeof(unsigned long long);
+    const size_t xbuf_bytes = size_t(kXbufReplicas) * (H / 2) * sizeof(unsigned long long);
     const size_t ws_bytes = size_t(ws_words(b.geo.max_layers)) * sizeof(uint32_t);
     // device copy of a host-memory queue's descriptors, per layer (32 B each)
     const size_t qmirror_bytes = size_t(b.geo.max_layers) * N * 2 * sizeof(uint4);
@@ -460,7 +460,7 @@ constexpr int kStaticDevices = 64;
 static_assert(kWsHeader + kWsPerLayer <= kStaticWsWords, "workspace of a one-layer launch");
 
 static __device__ __align__(256) unsigned long long g_static_partial[kStaticPartialWords];
-static __device__ __align__(256) unsigned long long g_static_xbuf[kMaxHidden / 2];
+static __device__ __align__(256) unsigned long long g_static_xbuf[kXbufReplicas * (kMaxHidden / 2)];
 static __device__ __align__(256) uint32_t g_static_ws[kStaticWsWords];
 static __device__ __align__(256) uint32_t g_static_status[LS_B200_STATUS_WORDS];
 static __device__ __align__(256) uint32_t g_static_done[kStaticLayers];

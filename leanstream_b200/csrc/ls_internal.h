@@ -68,6 +68,9 @@ constexpr uint32_t kWsPerLayer = 8;
 // host memory (polled under the grid-wide lease); the public flags use the
 // low bits.
 constexpr uint32_t kPlanHostQueue = 1u << 31;
+// Copies of the tagged layer hand-off (xbuf): CTA b polls copy b % 4, so 148
+// CTAs spread their polling over four sets of L2 lines.
+constexpr uint32_t kXbufReplicas = 4;
 // Scratch tags: tag = 1 + base + l for launch-local layer l, where base is a
 // device counter (ws[kWsTag]) advanced by the layers of every launch at its
 // end, so CUDA-graph replays get fresh tags too. It wraps below kTagWrap;
@@ -91,7 +94,7 @@ struct KernelParams {
     uint32_t max_layers;  // workspace capacity
     uint32_t variant;     // 1: scales applied per 128-block after the tensor-core sums; 0: fp16(q*s) weights
     unsigned long long* partial;  // [N * slabs_per_group(G)][H] tagged fp32 slab partial rows
-    unsigned long long* xbuf;     // [H/2] tagged fp16 pairs: a layer's hidden_out for the next layer
+    unsigned long long* xbuf;     // [kXbufReplicas][H/2] tagged fp16 pairs: a layer's hidden_out for the next layer
     uint32_t* ws;         // workspace words
     uint32_t* status;     // mapped host words (LS_B200_STATUS_*)
     uint32_t* done;       // mapped host per-layer completion epochs

@@ -1141,7 +1141,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         if (tagged && P.world > 1) {
             raw[j] = tp_gather<H>(P, *prev, t, limit, u, tag, xkeep[j], blockIdx.x == 0);
         } else if (tagged) {
-            const unsigned long long* src = P.xbuf + 4 * u;
+            const unsigned long long* src = P.xbuf + (blockIdx.x % kXbufReplicas) * uint32_t(H / 2) + 4 * u;
             ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
             uint32_t spins = 0, polls = 0;
             for (;;) {
@@ -1864,11 +1864,15 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                     // the next layer's input first: it is on the critical path.
                     // Published even after an error so that the next layer's
                     // readers never wait for it; the error is reported anyway.
+                    // pair word of columns (c & ~1, c | 1) on both lanes of the
+                    // pair; the even lane writes copies 0 and 1, the odd lane 2 and 3
                     const uint32_t mine = __half_as_ushort(hout);
                     const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
-                    if ((lane & 1) == 0)
-                        st_volatile_u64(P.xbuf + c / 2,
-                                        (static_cast<unsigned long long>(tag) << 32) | (odd << 16) | mine);
+                    const uint32_t pair = __shfl_sync(0xffffffffu, (odd << 16) | mine, lane & ~1);
+                    const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | pair;
+                    const uint32_t r0 = (lane & 1) * 2;
+                    st_volatile_u64(P.xbuf + r0 * uint32_t(H / 2) + c / 2, word);
+                    st_volatile_u64(P.xbuf + (r0 + 1) * uint32_t(H / 2) + c / 2, word);
                 }
                 // outputs are skipped once any CTA had reported an error when
                 // the reduction started (best effort: the error word is the verdict)
