@@ -291,10 +291,11 @@ class Stack:
         return 1
 
 
-def trace_report(st, encoded, stream):
+def trace_report(st, encoded, stream, rank=0):
     """Phase stamps (LS_B200_TRACE_*, LS_B200_LTRACE_*) of one multi-layer
     launch, summarised to stderr: per layer, the median over CTAs of each
-    stamp relative to the first CTA's entry."""
+    stamp relative to the first CTA's entry. With N GPUs every rank issues
+    the traced launch (it is a collective); rank 0 prints its own stamps."""
     import torch
 
     grid = torch.cuda.get_device_properties(0).multi_processor_count
@@ -305,6 +306,8 @@ def trace_report(st, encoded, stream):
         st.N.load().ls_b200_spin(1_000_000, stream.cuda_stream)
         st.backend.launch_plans(dev, LAYERS, host, trace=trace, stream=stream)
     torch.cuda.synchronize()
+    if rank != 0:
+        return
     t = trace.cpu().numpy().astype(np.int64)
     cta = t[: grid * 8].reshape(grid, 8)
     lay = t[grid * 8: grid * 8 + grid * LAYERS * 8].reshape(grid, LAYERS, 8)
@@ -433,8 +436,9 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         achieved_gbs = -float(t.item())
     progress("kernel-only timing done")
-    if args.trace and world == 1:
-        trace_report(st, encoded[args.warmup], stream)
+    if args.trace:
+        barrier()
+        trace_report(st, encoded[args.warmup], stream, rank)
 
     # ---- e2e: host plans + host x in, host y out, through the C ABI each step
     barrier()
