@@ -59,8 +59,8 @@ struct alignas(16) LayerPlan {
 // kWsPollLock: 1 while one thread of the grid reads a host-memory queue.
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsPollLock = 5,
                    kWsHeader = 8;
-// path, slab claim, reduction-block claim, reduced column blocks, CTAs past the
-// tensor-parallel gather of the layer's input, and for a host-memory queue:
+// path, slab claim, reduction-block claim, reduced column blocks, (unused),
+// and for a host-memory queue:
 // queue positions mirrored into device memory, queue state (1 activated,
 // 2 failed), total_count at activation
 constexpr uint32_t kWsPerLayer = 8;

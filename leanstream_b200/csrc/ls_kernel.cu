@@ -353,7 +353,7 @@ __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
-    // [0] path [1] slab claim [2] block claim [3] reduced blocks [4] CTAs past the TP gather
+    // [0] path [1] slab claim [2] block claim [3] reduced blocks [4] unused
     // [5] mirror of ready_count [6] mirror of the queue state
     return P.ws + kWsHeader + kWsPerLayer * l;
 }
@@ -1046,71 +1046,6 @@ __device__ bool wait_count(const KernelParams& P, SmemTail* t, const uint32_t* c
     return true;
 }
 
-// Tensor parallel (world > 1): the next layer's input from every rank's
-// fp32 partial of the finished layer, read from this rank's exchange buffer
-// (slot by the tag's parity) as soon as the words carry `tag`: y = the sum
-// over ranks in rank order, y16 = fp16(y), x = fp16(x_prev + y16), the single
-// rounding that ls_b200_tp_epilogue applies after an allreduce, for the
-// coordinates 8u..8u+7 of unit u (x_prev: the thread's own copy of the
-// finished layer's input, which is that layer's residual); with `write` it
-// also stores the finished layer's outputs.
-template <int H>
-__device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail* t, uint64_t limit, int u,
-                           uint32_t tag, uint4 xprev, bool write) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t slot = (tag - 1u) & 1u;
-    const unsigned long long* base = P.xpeer[P.rank] + size_t(slot) * P.world * H + 8 * u;
-    float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (uint32_t r = 0; r < P.world; ++r) {
-        const unsigned long long* src = base + size_t(r) * H;
-        ulonglong2 v[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
-        uint32_t spins = 0, polls = 0;
-        for (;;) {
-            bool ok = true;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) ok &= uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag;
-            if (__all_sync(0xffffffffu, ok)) break;
-            uint32_t late = 0;
-            if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit)) late = 1;
-            if (__shfl_sync(0xffffffffu, late, 0)) {
-                if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
-                break;
-            }
-            poll_backoff(polls++, 32);
-            if (!ok) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) v[k] = ld_volatile_v2u64(src + 2 * k);
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            y[2 * k] += __uint_as_float(uint32_t(v[k].x));
-            y[2 * k + 1] += __uint_as_float(uint32_t(v[k].y));
-        }
-    }
-    const __half* xp = reinterpret_cast<const __half*>(&xprev);
-    uint4 out, y16v;
-    __half* o = reinterpret_cast<__half*>(&out);
-    __half* yh = reinterpret_cast<__half*>(&y16v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        yh[e] = __float2half_rn(y[e]);
-        o[e] = __float2half_rn(__half2float(xp[e]) + __half2float(yh[e]));
-    }
-    if (write) {
-        if (Lp.y32) {
-            float4* d = reinterpret_cast<float4*>(Lp.y32 + 8 * u);
-            d[0] = make_float4(y[0], y[1], y[2], y[3]);
-            d[1] = make_float4(y[4], y[5], y[6], y[7]);
-        }
-        if (Lp.y && !(Lp.flags & LS_B200_NO_OUTPUT)) reinterpret_cast<uint4*>(Lp.y)[u] = y16v;
-        if (Lp.hidden_out) reinterpret_cast<uint4*>(Lp.hidden_out)[u] = out;
-    }
-    return out;
-}
-
 // Loads the layer's input, applies the HF RMSNorm of
 // predictor_shared_input.cu:16-33 when flagged
 // (inv = rsqrt(sum(x^2)/H + eps); x' = fp16(weight * fp16(x * inv))), and
@@ -1128,7 +1063,7 @@ __device__ uint4 tp_gather(const KernelParams& P, const LayerPlan& Lp, SmemTail*
 // grid-wide barrier between layers.
 template <int H, bool F>
 __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t& cph, uint64_t limit,
-                        int tid, bool tagged, uint32_t tag, const LayerPlan* prev, uint4 (&xkeep)[Geo<H>::UPT]) {
+                        int tid, bool tagged, uint32_t tag) {
     constexpr int NU = H / 8, UPT = Geo<H>::UPT;  // units u = tid + j * 512, j < UPT
     const int warp = tid >> 5, lane = tid & 31;
     uint4 raw[UPT];
@@ -1138,9 +1073,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         const int u = tid + j * kConsumerThreads;
         raw[j] = make_uint4(0u, 0u, 0u, 0u);
         if (u >= NU) continue;  // warp-uniform: NU is a multiple of 32
-        if (tagged && P.world > 1) {
-            raw[j] = tp_gather<H>(P, *prev, t, limit, u, tag, xkeep[j], blockIdx.x == 0);
-        } else if (tagged) {
+        if (tagged) {
             const unsigned long long* src = P.xbuf + (blockIdx.x % kXbufReplicas) * uint32_t(H / 2) + 4 * u;
             ulonglong2 a = ld_volatile_v2u64(src), b = ld_volatile_v2u64(src + 2);
             uint32_t spins = 0, polls = 0;
@@ -1164,7 +1097,6 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
         } else {
             raw[j] = __ldcg(reinterpret_cast<const uint4*>(L.x) + u);
         }
-        xkeep[j] = raw[j];  // this layer's input: the residual of a tensor-parallel gather
         const __half2* h = reinterpret_cast<const __half2*>(&raw[j]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1833,13 +1765,6 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             acc += cs;
         }
         t->red2[warp][lane] = acc;
-        // Tensor parallel: the exchange slot of layer l still holds layer
-        // l-2 until every CTA of each reading rank has gathered it. A rank
-        // publishes layer l only after all of its own CTAs gathered layer
-        // l-1, and every rank's CTAs gathered layer l-1 only after all ranks
-        // published it, hence after all CTAs had gathered layer l-2.
-        if (P.world > 1 && l > 0 && blk == blk0 && tid == 0)
-            wait_count(P, t, ws_layer(P, l) + 4, gridDim.x, limit, 12);
         csync(P, t, cph, limit, lane);
         if (warp == 0) {
             if (blk == blk0 && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
@@ -1850,13 +1775,42 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             if (P.world > 1) {
                 // Tensor parallel: this rank's fp32 partial of the column goes
                 // to every rank's exchange buffer over NVLink (peer stores);
-                // the sum over ranks, its fp16 rounding and the residual are
-                // formed by the readers (tp_gather), identically on all ranks.
+                // then this block's columns of every rank are read from the
+                // local exchange buffer as soon as they carry the tag and
+                // summed in rank order (the allreduce), identically on all
+                // ranks, and the block continues as on one GPU.
+                // Slot reuse: slot (tag-1)&1 of rank q still holds layer l-2
+                // until q's reducers of l-2 have read it. A rank publishes
+                // layer l only after its CTAs computed layer l, which needs
+                // the whole input of layer l, hence every rank's layer l-1
+                // partials; a rank publishes those only after its own CTAs
+                // loaded the input of layer l-1, which its reducers of layer
+                // l-2 had formed from the slot.
                 const uint32_t slot = (tag - 1u) & 1u;
                 const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(y);
                 const size_t at = (size_t(slot) * P.world + P.rank) * H + c;
                 for (uint32_t r = 0; r < P.world; ++r) st_volatile_u64(P.xpeer[r] + at, w);
-            } else {
+                const unsigned long long* mine = P.xpeer[P.rank] + size_t(slot) * P.world * H + c;
+                float sum = 0.f;
+                for (uint32_t r = 0; r < P.world; ++r) {
+                    unsigned long long v = ld_volatile_u64(mine + size_t(r) * H);
+                    uint32_t spins = 0, polls = 0;
+                    while (!__all_sync(0xffffffffu, uint32_t(v >> 32) == tag)) {
+                        uint32_t late = 0;
+                        if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit))
+                            late = 1;
+                        if (__shfl_sync(0xffffffffu, late, 0)) {
+                            if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
+                            break;
+                        }
+                        poll_backoff(polls++, 32);
+                        if (uint32_t(v >> 32) != tag) v = ld_volatile_u64(mine + size_t(r) * H);
+                    }
+                    sum += __uint_as_float(uint32_t(v));
+                }
+                y = sum;
+            }
+            {
                 const __half y16 = __float2half_rn(y);
                 __half hout = y16;
                 if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
@@ -1970,8 +1924,7 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
     uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
     const LayerPlan* L = &plan_at(P, 0);
-    uint4 xkeep[Geo<H>::UPT];
-    stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0, nullptr, xkeep);
+    stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % Geo<H>::NS;
         if (!wait_full<H>(t, idx, deadline, lane)) {
@@ -2053,29 +2006,16 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         const bool chain = next && L->hidden_out && L->residual &&
                            reinterpret_cast<const void*>(next->x) == reinterpret_cast<const void*>(L->hidden_out);
         end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid, chain);
-        if (!next) {
-            // Tensor parallel: the launch's last layer has no next input to
-            // gather; CTA 0 forms its outputs from the ranks' partials.
-            if (P.world > 1 && blockIdx.x == 0) {
-#pragma unroll
-                for (int j = 0; j < Geo<H>::UPT; ++j) {
-                    const int u = tid + j * kConsumerThreads;
-                    if (u < H / 8) tp_gather<H>(P, *L, t, limit, u, scratch_tag(t, l), xkeep[j], true);
-                }
-            }
-            continue;  // the FINAL marker follows
-        }
+        if (!next) continue;  // the FINAL marker follows
         if (!chain) {
             if (tid == 0) wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
             csync(P, t, cph, limit, lane);
         }
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
         const uint32_t tag = scratch_tag(t, l);
-        const LayerPlan* prev = L;
         ++l;
         L = next;
-        stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag, prev, xkeep);
-        if (P.world > 1 && tid == 0) red_release_gpu(ws_layer(P, l) + 4, 1u);  // gathered (stage_x ends in a CTA barrier)
+        stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag);
         if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
     }
 }
