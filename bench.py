@@ -46,10 +46,10 @@ GROUP_BYTES = G * 3 * H // 2                  # packed INT4 bytes per group
 SCALE_BYTES = G * 3 * (H // 128) * 2          # fp16 scale bytes per group
 ALG_BYTES_PER_GROUP = GROUP_BYTES + SCALE_BYTES  # 405,504 B (algorithmic bytes)
 # dram__bytes_read.sum + dram__bytes_write.sum of one fused_mlp_kernel launch
-# (8-layer stack, token 3: 183.05 MB + 6.60 MB) divided by that launch's
+# (8-layer stack, token 3: 183.12 MB + 6.43 MB) divided by that launch's
 # algorithmic bytes (449 groups x 405,504 B = 182.07 MB): weights are read
 # once, the excess is tagged scratch evicted from L2.
-TRAFFIC_PER_ALG_BYTE = 1.0416
+TRAFFIC_PER_ALG_BYTE = 1.0411
 SEED = 3
 EPS = 1e-5
 WORKLOAD = "config3: 36-layer MLP stack, H4096/I12288, 192x64 groups, 20-40% active/layer, batch 1"
