@@ -1819,14 +1819,16 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                     // Published even after an error so that the next layer's
                     // readers never wait for it; the error is reported anyway.
                     // pair word of columns (c & ~1, c | 1) on both lanes of the
-                    // pair; the even lane writes copies 0 and 1, the odd lane 2 and 3
+                    // pair; the even lane writes the first half of the copies, the odd lane the rest
                     const uint32_t mine = __half_as_ushort(hout);
                     const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
                     const uint32_t pair = __shfl_sync(0xffffffffu, (odd << 16) | mine, lane & ~1);
                     const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | pair;
-                    const uint32_t r0 = (lane & 1) * 2;
-                    st_volatile_u64(P.xbuf + r0 * uint32_t(H / 2) + c / 2, word);
-                    st_volatile_u64(P.xbuf + (r0 + 1) * uint32_t(H / 2) + c / 2, word);
+                    constexpr uint32_t kHalf = kXbufReplicas / 2;
+                    const uint32_t r0 = (lane & 1) * kHalf;
+#pragma unroll
+                    for (uint32_t r = 0; r < kHalf; ++r)
+                        st_volatile_u64(P.xbuf + (r0 + r) * uint32_t(H / 2) + c / 2, word);
                 }
                 // outputs are skipped once any CTA had reported an error when
                 // the reduction started (best effort: the error word is the verdict)
