@@ -1701,6 +1701,42 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
     }
 }
 
+// One reduced column c of a layer (warp 0 of a reducer, lane = c % 32): y16 =
+// fp16(y), hidden_out = fp16(residual + y16); with `chain` the pair word of
+// hidden_out goes to every copy of the tagged hand-off first (the next
+// layer's input is on the critical path, and it is published even after an
+// error so that no reader waits for it), then the outputs are written unless
+// an error had been reported when the reduction started (best effort: the
+// error word is the verdict).
+template <int H>
+__device__ __forceinline__ void emit_column(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t c,
+                                            float y, uint16_t res, uint32_t err, bool good, uint32_t tag, bool chain,
+                                            int lane) {
+    const __half y16 = __float2half_rn(y);
+    __half hout = y16;
+    if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
+    if (chain) {
+        // pair word of columns (c & ~1, c | 1) on both lanes of the pair; the
+        // even lane writes the first half of the copies, the odd lane the rest
+        const uint32_t mine = __half_as_ushort(hout);
+        const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
+        const uint32_t pair = __shfl_sync(0xffffffffu, (odd << 16) | mine, lane & ~1);
+        const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | pair;
+        constexpr uint32_t kHalf = kXbufReplicas / 2;
+        const uint32_t r0 = (lane & 1) * kHalf;
+#pragma unroll
+        for (uint32_t r = 0; r < kHalf; ++r) st_volatile_u64(P.xbuf + (r0 + r) * uint32_t(H / 2) + c / 2, word);
+    }
+    uint32_t write = 0;
+    if (lane == 0) write = (good && err == 0u && !t->abort) ? 1u : 0u;
+    write = __shfl_sync(0xffffffffu, write, 0);
+    if (write) {
+        if (L.y32) L.y32[c] = y;
+        if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
+        if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
+    }
+}
+
 // End of layer l: partial rows -> reduction -> epilogue, on CTAs 0..H/32-1
 // (one 32-column block each). Each warp polls its rows until they carry the
 // layer's tag, so the reduction starts without a grid-wide barrier.
@@ -1775,74 +1811,55 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             if (P.world > 1) {
                 // Tensor parallel: this rank's fp32 partial of the column goes
                 // to every rank's exchange buffer over NVLink (peer stores);
-                // then this block's columns of every rank are read from the
-                // local exchange buffer as soon as they carry the tag and
-                // summed in rank order (the allreduce), identically on all
-                // ranks, and the block continues as on one GPU.
-                // Slot reuse: slot (tag-1)&1 of rank q still holds layer l-2
-                // until q's reducers of l-2 have read it. A rank publishes
-                // layer l only after its CTAs computed layer l, which needs
-                // the whole input of layer l, hence every rank's layer l-1
-                // partials; a rank publishes those only after its own CTAs
-                // loaded the input of layer l-1, which its reducers of layer
-                // l-2 had formed from the slot.
+                // the ranks' partials are summed in the gather pass below.
                 const uint32_t slot = (tag - 1u) & 1u;
                 const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(y);
                 const size_t at = (size_t(slot) * P.world + P.rank) * H + c;
                 for (uint32_t r = 0; r < P.world; ++r) st_volatile_u64(P.xpeer[r] + at, w);
-                const unsigned long long* mine = P.xpeer[P.rank] + size_t(slot) * P.world * H + c;
-                float sum = 0.f;
-                for (uint32_t r = 0; r < P.world; ++r) {
-                    unsigned long long v = ld_volatile_u64(mine + size_t(r) * H);
-                    uint32_t spins = 0, polls = 0;
-                    while (!__all_sync(0xffffffffu, uint32_t(v >> 32) == tag)) {
-                        uint32_t late = 0;
-                        if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit))
-                            late = 1;
-                        if (__shfl_sync(0xffffffffu, late, 0)) {
-                            if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
-                            break;
-                        }
-                        poll_backoff(polls++, 32);
-                        if (uint32_t(v >> 32) != tag) v = ld_volatile_u64(mine + size_t(r) * H);
-                    }
-                    sum += __uint_as_float(uint32_t(v));
-                }
-                y = sum;
-            }
-            {
-                const __half y16 = __float2half_rn(y);
-                __half hout = y16;
-                if (L.hidden_out && L.residual) hout = __float2half_rn(h2f(res) + __half2float(y16));
-                if (chain) {
-                    // the next layer's input first: it is on the critical path.
-                    // Published even after an error so that the next layer's
-                    // readers never wait for it; the error is reported anyway.
-                    // pair word of columns (c & ~1, c | 1) on both lanes of the
-                    // pair; the even lane writes the first half of the copies, the odd lane the rest
-                    const uint32_t mine = __half_as_ushort(hout);
-                    const uint32_t odd = __shfl_down_sync(0xffffffffu, mine, 1);
-                    const uint32_t pair = __shfl_sync(0xffffffffu, (odd << 16) | mine, lane & ~1);
-                    const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | pair;
-                    constexpr uint32_t kHalf = kXbufReplicas / 2;
-                    const uint32_t r0 = (lane & 1) * kHalf;
-#pragma unroll
-                    for (uint32_t r = 0; r < kHalf; ++r)
-                        st_volatile_u64(P.xbuf + (r0 + r) * uint32_t(H / 2) + c / 2, word);
-                }
-                // outputs are skipped once any CTA had reported an error when
-                // the reduction started (best effort: the error word is the verdict)
-                uint32_t write = 0;
-                if (lane == 0) write = (good && err == 0u && !t->abort) ? 1u : 0u;
-                write = __shfl_sync(0xffffffffu, write, 0);
-                if (write) {
-                    if (L.y32) L.y32[c] = y;
-                    if (L.y && !(L.flags & LS_B200_NO_OUTPUT)) L.y[c] = __half_as_ushort(y16);
-                    if (L.hidden_out && L.residual) L.hidden_out[c] = __half_as_ushort(hout);
-                }
+            } else {
+                emit_column<H>(P, L, t, c, y, res, err, good, tag, chain, lane);
             }
         }
         csync(P, t, cph, limit, lane);  // red2 is reused by the next block
+    }
+    if (P.world > 1 && warp == 0) {
+        // Gather pass (tensor parallel): every block of this CTA was published
+        // above, so no rank waits on another while holding back its own. Each
+        // block's columns of every rank are read from the local exchange
+        // buffer once they carry the tag and summed in rank order (the
+        // allreduce, the same bits on every rank); the block then continues
+        // as on one GPU.
+        // Slot reuse: slot (tag-1)&1 of rank q still holds layer l-2 until q's
+        // reducers of l-2 have read it. A rank publishes layer l only after its
+        // CTAs computed layer l, which needs the whole input of layer l, hence
+        // every rank's layer l-1 partials; a rank publishes those only after
+        // its own CTAs loaded the input of layer l-1, which its reducers of
+        // layer l-2 had formed from the slot.
+        const uint32_t slot = (tag - 1u) & 1u;
+        const uint32_t err = ld_relaxed_gpu(P.ws + kWsErr);
+        for (uint32_t blk = blk0; blk < NBLK; blk += step) {
+            const uint32_t c = 32 * blk + lane;
+            const uint16_t res = (L.hidden_out && L.residual) ? __ldcg(L.residual + c) : uint16_t(0);
+            const unsigned long long* mine = P.xpeer[P.rank] + size_t(slot) * P.world * H + c;
+            float y = 0.f;
+            for (uint32_t r = 0; r < P.world; ++r) {
+                unsigned long long v = ld_volatile_u64(mine + size_t(r) * H);
+                uint32_t spins = 0, polls = 0;
+                while (!__all_sync(0xffffffffu, uint32_t(v >> 32) == tag)) {
+                    uint32_t late = 0;
+                    if (lane == 0 && (++spins & 15u) == 0 && (t->abort || grid_failed(P) || gtimer() > limit))
+                        late = 1;
+                    if (__shfl_sync(0xffffffffu, late, 0)) {
+                        if (lane == 0 && !t->abort && !grid_failed(P)) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, 11);
+                        break;
+                    }
+                    poll_backoff(polls++, 32);
+                    if (uint32_t(v >> 32) != tag) v = ld_volatile_u64(mine + size_t(r) * H);
+                }
+                y += __uint_as_float(uint32_t(v));
+            }
+            emit_column<H>(P, L, t, c, y, res, __shfl_sync(0xffffffffu, err, 0), good, tag, chain, lane);
+        }
     }
     // Reduced blocks: an unchained next layer (or the host's view of the
     // layer outputs) waits on this count. A chained next layer reads the
