@@ -83,6 +83,20 @@ def active_sets(step: int):
     return out
 
 
+def rank_balance(first: int, last: int, world: int) -> dict:
+    """Load imbalance of round-robin sharding over the timed tokens: per layer,
+    the busiest rank's active groups against the mean over ranks (the active
+    set is global, so one layer's time follows its busiest rank)."""
+    ratios, per_rank = [], []
+    for step in range(first, last):
+        for ids in active_sets(step):
+            counts = np.bincount(np.asarray(ids) % world, minlength=world)
+            per_rank.append(counts.mean())
+            ratios.append(counts.max() / max(counts.mean(), 1e-9))
+    return {"mean_groups_per_rank_layer": float(np.mean(per_rank)), "busiest_over_mean": float(np.mean(ratios)),
+            "worst_busiest_over_mean": float(np.max(ratios))}
+
+
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
     """SM clock and throttle reasons sampled during the timed region: NVML
@@ -490,6 +504,7 @@ def run_gpu(args, rank, world, local_rank):
             pass
         peak = float(peaks.get("hbm_gbs", 6650.0))
         mean_active = float(np.mean([sum(c) for c in st.active_local[args.warmup:]])) / LAYERS
+        balance = rank_balance(args.warmup, args.warmup + args.steps, world) if world > 1 else None
         # DRAM bytes (read + write) of one launch, from the ncu capture of
         # the same kernel on an 8-layer stack, scaled by the algorithmic
         # bytes the launch processes (traffic grows with the active groups).
@@ -511,6 +526,7 @@ def run_gpu(args, rank, world, local_rank):
             "config": {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
                        "group_size": G, "active_fraction": [FMIN, FMAX], "batch": 1,
                        "mean_active_groups_per_layer": mean_active,
+                       "rank_balance": balance,
                        "parallelism": f"tp{world} (groups round-robin; fp32 partials exchanged over NVLink peer memory "
                                       "inside the persistent launch)" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: ~841 MB of distinct weights per token",
