@@ -7,7 +7,9 @@ this module, as the checker or the timed CPU baseline. The product package
 Two libraries:
   * libls_oracle.so  -- ls_oracle.c, the C restatement of the reference math;
   * _ref/libls_predictor_ref.so -- the reference's own predictor/predictor_cpu.cpp
-    compiled unmodified from /root/reference by oracle/Makefile (`make ref`).
+    compiled unmodified from the reference tree (REFERENCE_ROOT) by
+    oracle/Makefile (`make ref`), which also builds the reference runtime
+    and the integration driver of tests/native.
 """
 from __future__ import annotations
 
