@@ -158,3 +158,71 @@ def test_attached_decode_matches_oracle(native_lib, cuda_device, tmp_path, mode)
     finally:
         att.close()
     assert isinstance(model.model.layers[0].mlp, _MLP) and not hasattr(model, "_leanstream_attachment")
+
+
+def test_layer_runtime_protocol_on_cpu():
+    """The layer step of LayerRuntime against fakes of the queue, IO backend
+    and kernel backend (weight_manager.cpp:135-205): update passes only
+    non-resident EMPTY groups within the IO budget; finalize writes cached
+    rows (kind 0, cache slot) and streamed rows (kind 1, slot = id) with dest
+    = core count + position, appends cached and already-READY rows
+    unpublished, then activates and consumes the non-resident final reads;
+    a landing publishes its row only after finalize and only once."""
+    from leanstream_b200 import _native as N
+    from leanstream_b200 import torch_attach as T
+
+    calls = []
+
+    class FakeQueue:
+        def reset(self, e): calls.append(("reset", e))
+        def write_descriptors(self, rows): calls.append(("rows", np.array(rows).tolist()))
+        def prepare(self, n): calls.append(("prepare", n))
+        def append_unpublished(self, i): calls.append(("append", i))
+        def activate(self): calls.append(("activate",))
+        def publish(self, i): calls.append(("publish", i))
+        def fail(self, e): calls.append(("fail", e))
+
+    class FakeIO:
+        def __init__(self):
+            self.cb = None
+        def begin(self, cb, epoch): self.cb = cb; return 0
+        def update(self, ids): calls.append(("update", list(ids))); return 0
+        def consume(self, ids): calls.append(("consume", list(ids))); return 0
+        def retire(self): return 0
+        def wait(self, ms): return 0
+
+    class FakeEngine:
+        io_states = np.zeros(9, np.uint32)
+
+    rt = T.LayerRuntime.__new__(T.LayerRuntime)
+    rt.n = 8
+    rt.policy = T.CachePolicy(resident=(0, 1, 2), core=(0,))
+    rt.cache_slot = np.array([0, 1, 2, -1, -1, -1, -1, -1])
+    rt.physical = np.arange(8, dtype=np.uint32)[::-1].copy()
+    rt.queue, rt.io, rt.engine = FakeQueue(), FakeIO(), FakeEngine()
+    rt.execs = None
+    rt.lock = T.threading.Lock()
+    rt.epoch, rt.active, rt.finalized = 0, False, False
+    rt.final_index, rt.published = {}, set()
+
+    rt.begin()
+    assert calls[0] == ("reset", 1) and rt.active
+    rt.engine.io_states[5] = N.IO_READY
+    rt.update([1, 3, 5, 6, 7], io_budget=2)  # 1 resident, 5 already READY
+    assert calls[-1] == ("update", [3, 6])
+    rt._landed(1, 6, 6, 0, 1)  # before finalize: ignored (picked up at finalize)
+    assert not any(c[0] == "publish" for c in calls)
+    rt.engine.io_states[6] = N.IO_READY
+    calls.clear()
+    rt.finalize([0, 2, 5, 6, 3])
+    rows = next(c[1] for c in calls if c[0] == "rows")
+    # [logical, physical, slot, dest, kind]; core group 0 is not in the queue
+    assert rows == [[2, 5, 2, 1, 0], [5, 2, 5, 2, 1], [6, 1, 6, 3, 1], [3, 4, 3, 4, 1]]
+    assert [c for c in calls if c[0] in ("prepare", "append", "activate", "consume")] == [
+        ("prepare", 4), ("append", 0), ("append", 1), ("append", 2), ("activate",), ("consume", [5, 6, 3])]
+    rt._landed(1, 3, 3, 0, 2)
+    rt._landed(1, 3, 3, 0, 3)  # a repeated completion publishes nothing more
+    rt._landed(0, 7, 7, 0, 4)  # a stale epoch is ignored
+    assert [c for c in calls if c[0] == "publish"] == [("publish", 3)]
+    with pytest.raises(ValueError):
+        rt.finalize([2, 5])  # the core group must be in the final set
