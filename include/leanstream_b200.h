@@ -19,7 +19,11 @@
  *     optional activation / counter buffers are DEVICE memory.
  *   - Descriptors, ready indices and ls_queue_control may be either device
  *     memory or mapped pinned host memory (cudaHostAllocMapped). The kernel
- *     reads them with system-scope acquire loads and never writes them.
+ *     reads them with system-scope acquire loads and never writes them; a
+ *     queue in host memory is read by one thread of the grid at a time,
+ *     which copies what was published into backend-owned device memory
+ *     for the other CTAs (reads over PCIe are slow and compete with the
+ *     copy engine).
  *   - Claim counters live in a backend-owned device workspace. Discrete GPUs
  *     do not provide host-native atomics, so QueueControl.claim_count and
  *     consumer_path are left untouched.
@@ -237,7 +241,9 @@ int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream);
 /* No counterpart in the reference. The launch of ls_b200_launch for callers
  * that must not allocate device memory: no backend object, no cudaMalloc,
  * no allocating library routine. The scratch is a fixed set of device
- * arrays in the library (32 MiB of partial rows), one set per device.
+ * arrays in the library, one set per device that loads it, held until exit:
+ * 32 MiB of partial rows, 128 KiB of layer hand-off words and 512 KiB for a
+ * device copy of a queue kept in host memory.
  * geometry: as for ls_b200_configure (max_layers is ignored). Returns
  * E2BIG when group_count * ceil(group_size / 16) * hidden exceeds 2^22 or
  * args->layer >= 256, EINVAL for the cases ls_b200_launch rejects. status:
