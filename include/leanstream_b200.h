@@ -352,6 +352,39 @@ int ls_b200_queue_publish(ls_b200_queue* queue, uint32_t index);
 int ls_b200_queue_fail(ls_b200_queue* queue, uint32_t error);
 
 /* ------------------------------------------------------------------ */
+/* Batched decode over the union of the tokens' active groups.          */
+/* ------------------------------------------------------------------ */
+
+/* (new; the reference decodes one token at a time) Up to 8 tokens share one
+ * pass over the union of their active groups: every weight byte is read once
+ * and the tokens are the N dimension of the tensor-core MMAs. mask
+ * (optional, [tokens][union_count] bytes): token b uses union group u only
+ * where mask is nonzero, so its output equals the one-token MLP over its own
+ * groups; NULL gives every token the whole union. Rounding as the one-token
+ * path (w = fp16(q*s), fp16 g, u, silu and h, fp32 partial sums, one fp16
+ * rounding of y), fixed summation order (deterministic). The descriptors are
+ * trusted (device memory; physical_group selects the scales, source_slot the
+ * group in cache (kind 0) or staging (kind 1)). scratch: device memory of at
+ * least ls_b200_batch_scratch_bytes(), 16-byte aligned. */
+typedef struct ls_b200_batch_args {
+    uint32_t hidden, group_size, union_count, tokens;  /* tokens 1..8 */
+    const void* x;            /* fp16 [tokens][H] */
+    void* output;             /* fp16 [tokens][H] */
+    float* output_f32;        /* optional fp32 [tokens][H] */
+    const void* residual;     /* optional fp16 [tokens][H]: hidden_out = fp16(residual + y) */
+    void* hidden_out;         /* optional fp16 [tokens][H] */
+    const uint8_t* cache;
+    const uint8_t* staging;   /* optional (NULL = cache) */
+    const void* scales;       /* fp16 [physical_group][G][3][H/128] */
+    const ls_exec_desc* union_descs;  /* device [union_count] */
+    const uint8_t* mask;      /* optional device [tokens][union_count] */
+    void* scratch;
+    uint64_t scratch_bytes;
+} ls_b200_batch_args;
+uint64_t ls_b200_batch_scratch_bytes(uint32_t hidden, uint32_t group_size, uint32_t union_count);
+int ls_b200_batch_mlp(const ls_b200_batch_args* args, void* stream);
+
+/* ------------------------------------------------------------------ */
 /* Streaming IO: IOBackend (include/leanstream/weight_manager.h:8-24)  */
 /* over pinned host memory -> HBM staging copies.                      */
 /* ------------------------------------------------------------------ */

@@ -117,6 +117,15 @@ class StreamStats(C.Structure):
 
 IO_EMPTY, IO_INFLIGHT, IO_READY, IO_ERROR = 0, 1, 2, 3
 
+
+class BatchArgs(C.Structure):
+    """ls_b200_batch_args: up to 8 tokens over the union of their groups."""
+    _fields_ = [("hidden", C.c_uint32), ("group_size", C.c_uint32), ("union_count", C.c_uint32),
+                ("tokens", C.c_uint32), ("x", C.c_void_p), ("output", C.c_void_p), ("output_f32", C.c_void_p),
+                ("residual", C.c_void_p), ("hidden_out", C.c_void_p), ("cache", C.c_void_p),
+                ("staging", C.c_void_p), ("scales", C.c_void_p), ("union_descs", C.c_void_p), ("mask", C.c_void_p),
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64)]
+
 assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 72
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32
 
@@ -159,6 +168,8 @@ SIGNATURES = {
     "ls_b200_tp_setup": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "ls_b200_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "ls_b200_spin": (C.c_int, [C.c_uint64, C.c_void_p]),
+    "ls_b200_batch_scratch_bytes": (C.c_uint64, [C.c_uint32, C.c_uint32, C.c_uint32]),
+    "ls_b200_batch_mlp": (C.c_int, [C.POINTER(BatchArgs), C.c_void_p]),
     "ls_b200_stream_create": (C.c_void_p, [C.POINTER(StreamConfig)]),
     "ls_b200_stream_view": (C.c_int, [C.c_void_p, C.POINTER(IOBackend)]),
     "ls_b200_stream_stats": (C.c_int, [C.c_void_p, C.POINTER(StreamStats)]),

@@ -17,7 +17,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libleanstream_b200.so"
-SOURCES = ("ls_kernel.cu", "ls_kernel_traced.cu", "ls_backend.cu", "ls_aux.cu", "ls_stream.cu")
+SOURCES = ("ls_kernel.cu", "ls_kernel_traced.cu", "ls_backend.cu", "ls_aux.cu", "ls_stream.cu", "ls_batch.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

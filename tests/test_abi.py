@@ -193,3 +193,22 @@ def test_geometry_validation_before_device_use(native_lib):
 
 def test_build_info(native_lib):
     assert b"sm_100a" in native_lib.ls_b200_build_info()
+
+
+def test_batch_argument_validation_without_gpu(native_lib):
+    """ls_b200_batch_mlp rejects bad arguments before any CUDA call."""
+    from leanstream_b200 import _native as N
+
+    lib = native_lib
+    need = lib.ls_b200_batch_scratch_bytes(1024, 64, 10)
+    assert need >= 8 * 640 * 2 + 4 * 8 * 1024 * 4
+    good = dict(hidden=1024, group_size=64, union_count=10, tokens=8, x=1 << 20, output=1 << 21, output_f32=None,
+                residual=None, hidden_out=None, cache=1 << 22, staging=None, scales=1 << 23, union_descs=1 << 24,
+                mask=None, scratch=1 << 25, scratch_bytes=need)
+    for key, bad in [("tokens", 9), ("tokens", 0), ("hidden", 1000), ("hidden", 16384), ("union_count", 0),
+                     ("x", None), ("cache", None), ("scratch", None), ("hidden_out", 1 << 26), ("x", (1 << 20) + 8)]:
+        a = N.BatchArgs(**{**good, key: bad})
+        assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL, key
+    a = N.BatchArgs(**{**good, "scratch_bytes": need - 1})
+    assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.ENOSPC
+    assert lib.ls_b200_batch_mlp(None, None) == errno.EINVAL

@@ -1,0 +1,89 @@
+"""Batched decode over the union of up to 8 tokens' active groups
+(ls_b200_batch_mlp): with the per-token mask each token's output equals the
+one-token oracle over its own groups; without it, the oracle over the whole
+union; within the output tolerance of the one-token path (2e-3 of max|y|).
+Partial batches, the fp32 output, the residual and determinism (two calls,
+identical bits) are checked too; H 1024 and 8192 (config 5's geometry)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def _run(lib, H, G, L, union_rows, x, mask, tokens, residual=None):
+    import torch
+    from leanstream_b200 import _native as N
+
+    dev = "cuda"
+    U = len(union_rows)
+    cache = torch.from_numpy(L.packed).to(dev)
+    scales = torch.from_numpy(L.scales.reshape(-1).view(np.int16)).to(dev)
+    desc = torch.from_numpy(np.ascontiguousarray(union_rows, dtype=np.uint32).reshape(-1).view(np.int32)).to(dev)
+    xt = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev)
+    y = torch.zeros(tokens, H, dtype=torch.int16, device=dev)
+    y32 = torch.zeros(tokens, H, dtype=torch.float32, device=dev)
+    mk = torch.from_numpy(np.ascontiguousarray(mask, dtype=np.uint8)).to(dev) if mask is not None else None
+    res = torch.from_numpy(np.ascontiguousarray(residual).view(np.int16)).to(dev) if residual is not None else None
+    hid = torch.zeros(tokens, H, dtype=torch.int16, device=dev) if residual is not None else None
+    nbytes = int(lib.ls_b200_batch_scratch_bytes(H, G, U))
+    scratch = torch.full((nbytes,), 0xFF, dtype=torch.uint8, device=dev)  # stale bytes: must not leak in
+    a = N.BatchArgs(H, G, U, tokens, xt.data_ptr(), y.data_ptr(), y32.data_ptr(),
+                    res.data_ptr() if res is not None else None, hid.data_ptr() if hid is not None else None,
+                    cache.data_ptr(), None, scales.data_ptr(), desc.data_ptr(),
+                    mk.data_ptr() if mk is not None else None, scratch.data_ptr(), nbytes)
+    assert lib.ls_b200_batch_mlp(C.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    out = (y.cpu().numpy().view(np.float16), y32.cpu().numpy())
+    return out + ((hid.cpu().numpy().view(np.float16),) if hid is not None else ())
+
+
+@pytest.mark.parametrize("H,n_groups", [(1024, 32), (8192, 20)])
+def test_batch_matches_one_token_oracle(native_lib, cuda_device, H, n_groups):
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    G, B = 64, 8
+    L = make_layer(17, H, n_groups, G)
+    rng = np.random.default_rng(3)
+    sets = [np.sort(rng.permutation(n_groups)[: rng.integers(3, n_groups // 2)]) for _ in range(B)]
+    union = np.unique(np.concatenate(sets))
+    rows = descriptors(union)
+    x = (rng.standard_normal((B, H)) * 0.5).astype(np.float16)
+    mask = np.array([[u in set(s.tolist()) for u in union] for s in sets], np.uint8)
+    y, y32 = _run(native_lib, H, G, L, rows, x, mask, B)
+    y_again, _ = _run(native_lib, H, G, L, rows, x, mask, B)
+    assert np.array_equal(y.view(np.uint16), y_again.view(np.uint16)), "deterministic"
+    for b in range(B):
+        ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
+        ref = ref.astype(np.float32)
+        assert np.abs(y[b].astype(np.float32) - ref).max() <= TOL * np.abs(ref).max(), b
+        assert np.array_equal(y[b], y32[b].astype(np.float16))
+    # no mask: every token over the whole union
+    yu, _ = _run(native_lib, H, G, L, rows, x, None, B)
+    for b in (0, B - 1):
+        ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, rows)
+        ref = ref.astype(np.float32)
+        assert np.abs(yu[b].astype(np.float32) - ref).max() <= TOL * np.abs(ref).max(), b
+
+
+def test_partial_batch_with_residual(native_lib, cuda_device):
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    H, G, n_groups, B = 1024, 40, 9, 3  # G not a multiple of 16: neurons past the union's end
+    L = make_layer(23, H, n_groups, G)
+    rng = np.random.default_rng(8)
+    union = np.array([0, 2, 3, 7, 8])
+    rows = descriptors(union)
+    x = (rng.standard_normal((B, H)) * 0.5).astype(np.float16)
+    resid = rng.standard_normal((B, H)).astype(np.float16)
+    y, y32, hid = _run(native_lib, H, G, L, rows, x, None, B, residual=resid)
+    for b in range(B):
+        ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, rows)
+        ref = ref.astype(np.float32)
+        assert np.abs(y[b].astype(np.float32) - ref).max() <= TOL * np.abs(ref).max()
+        assert np.array_equal(hid[b].view(np.uint16), O.residual(resid[b], y[b]).view(np.uint16))
