@@ -17,25 +17,31 @@
 // chosen to pair coordinates i and i + 4 of each 8-coordinate word. The
 // product with the scale is then the one fp16 rounding of q * s.
 //
-// Three kernels, each with a fixed summation order (deterministic):
+// Three kernels, each with a fixed summation order (deterministic). The two
+// weight kernels stream their rows through a 4-stage shared-memory ring
+// filled with cp.async (completion by cp.async.wait_group: no spin loop), so
+// three stages of loads are in flight while one is multiplied.
 //   gate/up  -- one CTA per 16 union neurons (two octets), 8 warps splitting
-//               K in 64-coordinate blocks, two blocks per iteration. A rows
-//               0-7 are the octet's gate rows, 8-15 its up rows; B columns
-//               are the tokens, shared by both octets. Lane t of a quad holds
-//               coordinates c = 64kb + 16t + 8w .. +7 (w = 0, 1); MMA m of a
-//               word takes k 2t, 2t+1 = coordinates c + 2m, c + 2m + 4 and
-//               k 2t+8, 2t+9 = c + 2m + 1, c + 2m + 5. h is stored token-major.
-//   down     -- one CTA per 128 output columns and eighth of the union's
-//               neurons. A rows are output columns, K the neurons, B = h
-//               (neurons x tokens). Lane group g holds columns c0 + 16g .. +15
-//               of each neuron; in tile T row g is column c0 + 16g + 2T and
-//               row g + 8 column c0 + 16g + 2T + 1. The next 16-neuron unit's
-//               loads are issued before the current unit's MMAs.
+//               each 1024-coordinate stage in 64-coordinate blocks, two
+//               blocks per warp. A rows 0-7 are the octet's gate rows, 8-15
+//               its up rows; B columns are the tokens (x read from L2), shared
+//               by both octets. Lane t of a quad holds coordinates
+//               c = 64kb + 16t + 8w .. +7 (w = 0, 1); MMA m of a word takes
+//               k 2t, 2t+1 = coordinates c + 2m, c + 2m + 4 and k 2t+8, 2t+9 =
+//               c + 2m + 1, c + 2m + 5. h is stored token-major.
+//   down     -- one CTA per 256 output columns (128 contiguous bytes of each
+//               down row) and thirteenth of the union's neurons; each stage
+//               holds four 16-neuron units with their scales and h. Warp
+//               (unit slot, half) computes 128 columns: A rows are output
+//               columns, K the neurons, B = h (neurons x tokens). Lane group g
+//               holds columns 16g .. +15 of the half; in tile T row g is
+//               column 16g + 2T and row g + 8 column 16g + 2T + 1.
 //   epilogue -- y = sum of the splits in split order, fp16 rounding, the
 //               optional residual.
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cerrno>
 
 #include "ls_internal.h"
@@ -45,9 +51,10 @@ namespace {
 
 constexpr int kBatchTokens = 8;
 constexpr int kBatchThreads = 256;  // 8 warps
-constexpr uint32_t kGateUpNeurons = 16;
-constexpr uint32_t kDownCols = 128;
-constexpr uint32_t kDownSplits = 8;
+constexpr int kOctets = 2;  // gate/up octets per CTA, sharing each x fragment
+constexpr uint32_t kGateUpNeurons = 8 * kOctets;
+constexpr uint32_t kDownCols = 256;
+constexpr uint32_t kDownSplits = 13;
 
 struct BatchParams {
     uint32_t H, G, U, B, NT, NTP;  // NT union neurons, NTP padded row length of hT
@@ -98,39 +105,94 @@ __device__ __forceinline__ Row neuron_row(const BatchParams& p, uint32_t n) {
     return r;
 }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Gate/up stage: 16 blocks of 64 coordinates = 512 B of each of the CTA's
+// 16 * kOctets rows (row 16o + 8gu + g: octet o, gate (gu 0) or up (gu 1),
+// neuron g), at a 544-B row stride so that a warp's 8-row fragment load takes
+// the minimum two shared-memory wavefronts.
+constexpr uint32_t kGuStageBlocks = 16;
+constexpr uint32_t kGuRowBytes = kGuStageBlocks * 32;
+constexpr uint32_t kGuRowStride = kGuRowBytes + 32;
+constexpr uint32_t kGuRows = 16 * kOctets;
+constexpr uint32_t kGuStageBytes = kGuRows * kGuRowStride;
+constexpr int kGuStages = 4;
+constexpr uint32_t kGuSmem = kGuStages * kGuStageBytes;
+static_assert(8 * 4 * kOctets * 32 * sizeof(float) <= kGuSmem, "reduction fits the ring");
+
 __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const BatchParams p) {
-    __shared__ float red[8][8][32];  // [warp][octet * 4 + d][lane]
+    extern __shared__ __align__(16) uint8_t gu_ring[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint32_t n[2];
-    bool valid[2];
-    Row r[2];
+    const uint32_t n_base = blockIdx.x * kGateUpNeurons;
+    const uint32_t half_bytes = p.H / 2, KB = p.H / 64;
+    // copy role: 16-B chunk `lane` of the gate and up rows of neuron n_base + 8o + warp
+    const uint8_t* csrc[kOctets];
 #pragma unroll
-    for (int o = 0; o < 2; ++o) {
-        n[o] = blockIdx.x * kGateUpNeurons + 8 * o + g;  // gate row g, up row g + 8 of octet o
-        valid[o] = n[o] < p.NT;
-        r[o] = valid[o] ? neuron_row(p, n[o]) : Row{nullptr, nullptr};
+    for (int o = 0; o < kOctets; ++o) {
+        const uint32_t n = n_base + 8 * o + warp;
+        csrc[o] = n < p.NT ? neuron_row(p, n).src : nullptr;
+    }
+    // compute role: gate row g, up row g + 8 of octet o = neuron n_base + 8o + g
+    bool valid[kOctets];
+    const __half* sc[kOctets];
+#pragma unroll
+    for (int o = 0; o < kOctets; ++o) {
+        const uint32_t n = n_base + 8 * o + g;
+        valid[o] = n < p.NT;
+        sc[o] = valid[o] ? neuron_row(p, n).sc : nullptr;
     }
     const bool tok = uint32_t(g) < p.B;  // this lane's B column (token g)
-    const uint32_t KB = p.H / 64;
     const __half* xrow = p.x + size_t(g) * p.H + 16 * t;
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    for (uint32_t kb0 = warp; kb0 < KB; kb0 += 16) {
-        uint2 wg[2][2], wu[2][2];
-        __half2 sg[2][2], su[2][2];
+    const uint32_t nst = (half_bytes + kGuRowBytes - 1) / kGuRowBytes;
+
+    auto issue = [&](uint32_t s) {
+        uint8_t* buf = gu_ring + (s % kGuStages) * kGuStageBytes;
+        const uint32_t off = s * kGuRowBytes + 16 * lane;
+        if (off >= half_bytes) return;
+#pragma unroll
+        for (int o = 0; o < kOctets; ++o) {
+            if (!csrc[o]) continue;
+            cp_async16(buf + (16 * o + warp) * kGuRowStride + 16 * lane, csrc[o] + off);
+            cp_async16(buf + (16 * o + 8 + warp) * kGuRowStride + 16 * lane, csrc[o] + half_bytes + off);
+        }
+    };
+
+    float acc[kOctets][4];
+#pragma unroll
+    for (int o = 0; o < kOctets; ++o) acc[o][0] = acc[o][1] = acc[o][2] = acc[o][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < kGuStages - 1; ++s) {
+        if (uint32_t(s) < nst) issue(s);
+        cp_async_commit();
+    }
+    for (uint32_t s = 0; s < nst; ++s) {
+        const uint32_t blocks = min(kGuStageBlocks, KB - s * kGuStageBlocks);
+        // this warp's blocks warp and warp + 8 of the stage: x and scales
+        // (L2-resident) are requested before waiting for the stage
+        __half2 sg[2][kOctets], su[2][kOctets];
         uint4 xv[2][2];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const uint32_t kb = kb0 + 8 * j;
-            const bool inb = kb < KB;
+            const uint32_t kbl = warp + 8 * j, kb = s * kGuStageBlocks + kbl;
+            const bool inb = kbl < blocks;
 #pragma unroll
-            for (int o = 0; o < 2; ++o) {
-                wg[j][o] = wu[j][o] = make_uint2(0u, 0u);
+            for (int o = 0; o < kOctets; ++o) {
                 sg[j][o] = su[j][o] = __float2half2_rn(0.f);
                 if (inb && valid[o]) {
-                    wg[j][o] = *reinterpret_cast<const uint2*>(r[o].src + kb * 32 + 8 * t);
-                    wu[j][o] = *reinterpret_cast<const uint2*>(r[o].src + p.H / 2 + kb * 32 + 8 * t);
-                    sg[j][o] = __half2half2(r[o].sc[kb / 2]);
-                    su[j][o] = __half2half2(r[o].sc[p.H / 128 + kb / 2]);
+                    sg[j][o] = __half2half2(sc[o][kb / 2]);
+                    su[j][o] = __half2half2(sc[o][p.H / 128 + kb / 2]);
                 }
             }
             xv[j][0] = xv[j][1] = make_uint4(0u, 0u, 0u, 0u);
@@ -140,9 +202,24 @@ __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const Batch
                 xv[j][1] = xp[1];
             }
         }
+        cp_async_wait<kGuStages - 2>();
+        __syncthreads();  // stage s visible; every warp is done with stage s - 1
+        if (s + kGuStages - 1 < nst) issue(s + kGuStages - 1);
+        cp_async_commit();
+        const uint8_t* buf = gu_ring + (s % kGuStages) * kGuStageBytes;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            if (kb0 + 8 * j >= KB) continue;  // warp-uniform
+            const uint32_t kbl = warp + 8 * j;
+            if (kbl >= blocks) continue;  // warp-uniform
+            uint2 wg[kOctets], wu[kOctets];
+#pragma unroll
+            for (int o = 0; o < kOctets; ++o) {
+                wg[o] = wu[o] = make_uint2(0u, 0u);
+                if (valid[o]) {
+                    wg[o] = *reinterpret_cast<const uint2*>(buf + (16 * o + g) * kGuRowStride + kbl * 32 + 8 * t);
+                    wu[o] = *reinterpret_cast<const uint2*>(buf + (16 * o + 8 + g) * kGuRowStride + kbl * 32 + 8 * t);
+                }
+            }
 #pragma unroll
             for (int w = 0; w < 2; ++w) {
                 const uint4 X = xv[j][w];  // x[c .. c+7] as (c, c+1) (c+2, c+3) (c+4, c+5) (c+6, c+7)
@@ -152,8 +229,8 @@ __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const Batch
                     const uint32_t b0 = __byte_perm(xa, xb, 0x5410);  // x[c + 2m], x[c + 2m + 4]
                     const uint32_t b1 = __byte_perm(xa, xb, 0x7632);  // x[c + 2m + 1], x[c + 2m + 5]
 #pragma unroll
-                    for (int o = 0; o < 2; ++o) {
-                        const uint32_t gw = w ? wg[j][o].y : wg[j][o].x, uw = w ? wu[j][o].y : wu[j][o].x;
+                    for (int o = 0; o < kOctets; ++o) {
+                        const uint32_t gw = w ? wg[o].y : wg[o].x, uw = w ? wu[o].y : wu[o].x;
                         mma_f16(acc[o], deq(gw, 2 * m, sg[j][o]), deq(uw, 2 * m, su[j][o]),
                                 deq(gw, 2 * m + 1, sg[j][o]), deq(uw, 2 * m + 1, su[j][o]), b0, b1);
                     }
@@ -161,13 +238,16 @@ __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const Batch
             }
         }
     }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: reuse it for the cross-warp sums
+    float (*red)[4 * kOctets][32] = reinterpret_cast<float (*)[4 * kOctets][32]>(gu_ring);  // [warp][4o + d][lane]
 #pragma unroll
-    for (int o = 0; o < 2; ++o)
+    for (int o = 0; o < kOctets; ++o)
 #pragma unroll
         for (int e = 0; e < 4; ++e) red[warp][4 * o + e][lane] = acc[o][e];
     __syncthreads();
-    if (warp >= 2) return;
-    const int o = warp;  // warp 0 finishes octet 0, warp 1 octet 1
+    if (warp >= kOctets) return;
+    const int o = warp;  // warp o finishes octet o
     float gs[2] = {0.f, 0.f}, us[2] = {0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
@@ -176,7 +256,7 @@ __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const Batch
         us[0] += red[w][4 * o + 2][lane];
         us[1] += red[w][4 * o + 3][lane];
     }
-    const uint32_t nrow = o ? n[1] : n[0];
+    const uint32_t nrow = n_base + 8 * o + g;
     if (nrow >= p.NT) return;
     const uint32_t u = nrow / p.G;
 #pragma unroll
@@ -193,36 +273,10 @@ __global__ void __launch_bounds__(kBatchThreads) batch_gateup_kernel(const Batch
 
 // one 16-neuron unit's down inputs of a lane: neurons 2t, 2t+1, 2t+8, 2t+9
 struct DownIn {
-    uint2 w[4];      // columns c0 + 16g .. +15
-    __half s[4];     // their down scale (one 128-column block)
+    uint2 w[4];       // 16 columns of the lane's column group
+    __half s[4];      // their down scale (one 128-column block)
     uint32_t b0, b1;  // h of token g: neurons (2t, 2t+1), (2t+8, 2t+9)
 };
-
-__device__ __forceinline__ DownIn down_load(const BatchParams& p, uint32_t n0, uint32_t c0, int g, int t, bool tok) {
-    DownIn v;
-    const uint32_t nn[4] = {n0 + 2 * t, n0 + 2 * t + 1, n0 + 2 * t + 8, n0 + 2 * t + 9};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        v.w[k] = make_uint2(0u, 0u);
-        v.s[k] = __float2half_rn(0.f);
-        if (nn[k] < p.NT) {
-            const Row r = neuron_row(p, nn[k]);
-            v.w[k] = *reinterpret_cast<const uint2*>(r.src + p.H + c0 / 2 + 8 * g);
-            v.s[k] = r.sc[2 * (p.H / 128) + c0 / 128];
-        }
-    }
-    v.b0 = v.b1 = 0u;
-    if (tok) {
-        // h of neurons past the union is never written: zero it here (a zero
-        // weight times a stale NaN pattern would still poison the sum)
-        const __half* hb = p.hT + size_t(g) * p.NTP + n0;
-        if (nn[0] < p.NT) v.b0 = *reinterpret_cast<const uint32_t*>(hb + 2 * t);
-        if (nn[2] < p.NT) v.b1 = *reinterpret_cast<const uint32_t*>(hb + 2 * t + 8);
-        if (nn[1] >= p.NT) v.b0 &= 0xffffu;
-        if (nn[3] >= p.NT) v.b1 &= 0xffffu;
-    }
-    return v;
-}
 
 __device__ __forceinline__ void down_mma(float (&acc)[8][4], const DownIn& v) {
     const __half2 s01 = __halves2half2(v.s[0], v.s[1]), s23 = __halves2half2(v.s[2], v.s[3]);
@@ -244,52 +298,125 @@ __device__ __forceinline__ void down_mma(float (&acc)[8][4], const DownIn& v) {
     }
 }
 
+// Down stage: kDnUnits 16-neuron units, one per warp pair. Per neuron the
+// CTA's 256 columns are 128 contiguous bytes of its down row (stride 144 B:
+// a warp's four-neuron fragment load takes the minimum two wavefronts), its
+// two down scales (one per 128-column half) and, per unit, h of the 8 tokens.
+constexpr uint32_t kDnUnits = 4;
+constexpr uint32_t kDnNeuronStride = 144;
+constexpr uint32_t kDnW = kDnUnits * 16 * kDnNeuronStride;
+constexpr uint32_t kDnS = kDnUnits * 16 * 2 * sizeof(__half);
+constexpr uint32_t kDnHT = kDnUnits * kBatchTokens * 16 * sizeof(__half);
+constexpr uint32_t kDnStageBytes = kDnW + kDnS + kDnHT;
+constexpr int kDnStages = 6;
+constexpr uint32_t kDnSmem = kDnStages * kDnStageBytes;
+static_assert(kDnW % 16 == 0 && kDnS % 16 == 0 && kDnStageBytes % 16 == 0, "16-B aligned stage parts");
+static_assert(kDnUnits * 2 * 32 * 32 * sizeof(float) <= kDnSmem, "reduction fits the ring");
+
+// one stage's unit `un` (slot nw) for the lane's 128-column half ch
+__device__ __forceinline__ void down_unit(float (&acc)[8][4], const BatchParams& p, const uint8_t* buf, uint32_t un,
+                                          int nw, int ch, int g, int t, bool tok) {
+    const uint32_t n0 = un * 16;
+    const uint32_t kk[4] = {2u * t, 2u * t + 1, 2u * t + 8, 2u * t + 9};
+    DownIn v;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        v.w[q] = make_uint2(0u, 0u);
+        v.s[q] = __float2half_rn(0.f);
+        if (n0 + kk[q] < p.NT) {  // never-copied slots stay zero here
+            const uint32_t slot = nw * 16 + kk[q];
+            v.w[q] = *reinterpret_cast<const uint2*>(buf + slot * kDnNeuronStride + 64 * ch + 8 * g);
+            v.s[q] = reinterpret_cast<const __half*>(buf + kDnW)[2 * slot + ch];
+        }
+    }
+    v.b0 = v.b1 = 0u;
+    if (tok) {
+        // h of neurons past the union is never written: zero it (a zero
+        // weight times a stale NaN pattern would still poison the sum)
+        const uint32_t* hb = reinterpret_cast<const uint32_t*>(buf + kDnW + kDnS + (nw * kBatchTokens + g) * 32);
+        if (n0 + kk[0] < p.NT) v.b0 = hb[t];      // neurons 2t, 2t+1
+        if (n0 + kk[2] < p.NT) v.b1 = hb[t + 4];  // neurons 2t+8, 2t+9
+        if (n0 + kk[1] >= p.NT) v.b0 &= 0xffffu;
+        if (n0 + kk[3] >= p.NT) v.b1 &= 0xffffu;
+    }
+    down_mma(acc, v);
+}
+
 __global__ void __launch_bounds__(kBatchThreads) batch_down_kernel(const BatchParams p) {
-    __shared__ float red[8][32][32];  // [warp][tile * 4 + d][lane]
+    extern __shared__ __align__(16) uint8_t dn_ring[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int nw = warp >> 1, ch = warp & 1;  // unit slot of the stage, 128-column half
     const uint32_t c0 = blockIdx.x * kDownCols, split = blockIdx.y;
     const uint32_t units = (p.NT + 15) / 16;
     const uint32_t u_begin = uint32_t(uint64_t(units) * split / kDownSplits);
     const uint32_t u_end = uint32_t(uint64_t(units) * (split + 1) / kDownSplits);
+    const uint32_t nst = (u_end - u_begin + kDnUnits - 1) / kDnUnits;
     const bool tok = uint32_t(g) < p.B;
+
+    auto issue = [&](uint32_t s) {
+        uint8_t* buf = dn_ring + (s % kDnStages) * kDnStageBytes;
+        const uint32_t u0 = u_begin + s * kDnUnits;
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {  // 2 x 256 chunks: unit, neuron, 16-B part
+            const uint32_t c = threadIdx.x + 256 * m, us = c >> 7, k = (c >> 3) & 15, j = c & 7;
+            const uint32_t un = u0 + us, n = un * 16 + k;
+            if (un >= u_end || n >= p.NT) continue;
+            const Row r = neuron_row(p, n);
+            cp_async16(buf + (us * 16 + k) * kDnNeuronStride + 16 * j, r.src + p.H + c0 / 2 + 16 * j);
+            if (j == 0) cp_async4(buf + kDnW + (us * 16 + k) * 4, r.sc + 2 * (p.H / 128) + c0 / 128);
+        }
+        if (threadIdx.x < kDnUnits * kBatchTokens * 2) {  // h: unit, token, 8-neuron half
+            const uint32_t us = threadIdx.x >> 4, b = (threadIdx.x >> 1) & 7, hf = threadIdx.x & 1;
+            const uint32_t un = u0 + us;
+            if (un < u_end && b < p.B)
+                cp_async16(buf + kDnW + kDnS + (us * kBatchTokens + b) * 32 + 16 * hf,
+                           p.hT + size_t(b) * p.NTP + un * 16 + 8 * hf);
+        }
+    };
+
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    uint32_t un = u_begin + warp;
-    if (un < u_end) {
-        DownIn cur = down_load(p, un * 16, c0, g, t, tok);
-        for (;;) {
-            const uint32_t next = un + 8;
-            if (next < u_end) {
-                const DownIn nxt = down_load(p, next * 16, c0, g, t, tok);
-                down_mma(acc, cur);
-                cur = nxt;
-                un = next;
-            } else {
-                down_mma(acc, cur);
-                break;
-            }
-        }
+#pragma unroll
+    for (int s = 0; s < kDnStages - 1; ++s) {
+        if (uint32_t(s) < nst) issue(s);
+        cp_async_commit();
     }
+    for (uint32_t s = 0; s < nst; ++s) {
+        cp_async_wait<kDnStages - 2>();
+        __syncthreads();  // stage s visible; every warp is done with stage s - 1
+        const uint32_t un = u_begin + s * kDnUnits + nw;
+        if (un < u_end) down_unit(acc, p, dn_ring + (s % kDnStages) * kDnStageBytes, un, nw, ch, g, t, tok);
+        // refill the buffer of stage s - 1 after the MMAs: its descriptor
+        // loads then do not delay this stage's compute
+        if (s + kDnStages - 1 < nst) issue(s + kDnStages - 1);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: reuse it for the cross-warp sums
+    float (*red)[2][32][32] = reinterpret_cast<float (*)[2][32][32]>(dn_ring);  // [nw][ch][4T + d][lane]
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][4 * i + e][lane] = acc[i][e];
+        for (int e = 0; e < 4; ++e) red[nw][ch][4 * i + e][lane] = acc[i][e];
     __syncthreads();
-    // warp T sums tile T over the 8 warps in warp order
-    const int T = warp;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w = 0; w < 8; ++w)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] += red[w][4 * T + e][lane];
+    // warp (pair, ch) sums tiles 2 pair, 2 pair + 1 of half ch over the unit slots in order
     float* out = p.partial + size_t(split) * p.B * p.H;
-    const uint32_t col = c0 + 16 * g + 2 * T;  // row g; row g+8 is col + 1
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const uint32_t b = 2 * t + j;
-        if (b >= p.B) continue;
-        *reinterpret_cast<float2*>(out + size_t(b) * p.H + col) = make_float2(v[j], v[2 + j]);
+    for (int i = 0; i < 2; ++i) {
+        const int T = 2 * nw + i;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (uint32_t w = 0; w < kDnUnits; ++w)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] += red[w][ch][4 * T + e][lane];
+        const uint32_t col = c0 + 128 * ch + 16 * g + 2 * T;  // row g; row g+8 is col + 1
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t b = 2 * t + j;
+            if (b >= p.B) continue;
+            *reinterpret_cast<float2*>(out + size_t(b) * p.H + col) = make_float2(v[j], v[2 + j]);
+        }
     }
 }
 
@@ -312,6 +439,24 @@ uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) {
 
 bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
+// dynamic shared memory above 48 KB is an opt-in per function and device
+cudaError_t set_ring_attributes() {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(batch_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGuSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(batch_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDnSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(batch_gateup_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 int(cudaSharedmemCarveoutMaxShared));
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
 }  // namespace
 }  // namespace lsb
 
@@ -332,7 +477,9 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
         (a->hidden_out && !a->residual))
         return EINVAL;
     if (a->scratch_bytes < batch_scratch(H, G, U)) return ENOSPC;
-    if (!al16(a->x) || !al16(a->cache) || (a->staging && !al16(a->staging)) || !al16(a->scratch)) return EINVAL;
+    if (!al16(a->x) || !al16(a->cache) || (a->staging && !al16(a->staging)) || !al16(a->scratch) ||
+        (reinterpret_cast<uintptr_t>(a->scales) & 3u))
+        return EINVAL;
     BatchParams p{};
     p.H = H;
     p.G = G;
@@ -354,8 +501,9 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     const uint64_t ht_bytes = uint64_t(p.NTP) * kBatchTokens * sizeof(__half);
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + (ht_bytes + 255) / 256 * 256);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, 0, s>>>(p);
-    batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, 0, s>>>(p);
+    if (const cudaError_t e = set_ring_attributes(); e != cudaSuccess) return int(e);
+    batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, kGuSmem, s>>>(p);
+    batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, kDnSmem, s>>>(p);
     const uint32_t total = B * H;
     batch_epilogue_kernel<<<(total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024, 256, 0, s>>>(p);
     const cudaError_t e = cudaGetLastError();
