@@ -206,7 +206,8 @@ def test_batch_argument_validation_without_gpu(native_lib):
                 residual=None, hidden_out=None, cache=1 << 22, staging=None, scales=1 << 23, union_descs=1 << 24,
                 mask=None, scratch=1 << 25, scratch_bytes=need)
     for key, bad in [("tokens", 9), ("tokens", 0), ("hidden", 1000), ("hidden", 16384), ("union_count", 0),
-                     ("x", None), ("cache", None), ("scratch", None), ("hidden_out", 1 << 26), ("x", (1 << 20) + 8)]:
+                     ("x", None), ("cache", None), ("scratch", None), ("hidden_out", 1 << 26), ("x", (1 << 20) + 8),
+                     ("scales", (1 << 23) + 2), ("staging", (1 << 27) + 8), ("scratch", (1 << 25) + 4)]:
         a = N.BatchArgs(**{**good, key: bad})
         assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL, key
     a = N.BatchArgs(**{**good, "scratch_bytes": need - 1})
