@@ -22,7 +22,13 @@ Configuration 5 (--config 5): an 80-layer stack at 8192/28672 (448 groups
 of 64, 20 % active: 90 groups per layer), batch 1 -- ~5.8 GB of weights per
 token.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 3|5]
+--batch 8 (one GPU): each step decodes 8 tokens of the same seeded stream
+through ls_b200_batch_mlp, over the union of their active groups per layer
+(~83 % of the groups at 20 % per token), each token masked to its own set.
+The layers are not chained (no fused RMSNorm on this path), so every layer
+takes the same 8 hidden states; the bytes and work per layer are a stack's.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 3|5] [--batch 1|8]
 """
 from __future__ import annotations
 
@@ -80,6 +86,23 @@ def active_sets(step: int):
         rng = np.random.default_rng([SEED, step, layer])
         k = int(round(rng.uniform(FMIN, FMAX) * NGROUPS))
         out.append(np.sort(rng.permutation(NGROUPS)[:k]).astype(np.int64))
+    return out
+
+
+BATCH = 8  # tokens per step of the batched (--batch 8) workload
+
+
+def batch_union(step: int):
+    """Batch step `step` decodes tokens 8*step .. 8*step + 7 of the same seeded
+    stream as the batch-1 workload. Per layer: the sorted union of their
+    active groups and the [token][union] mask of each token's own set."""
+    per_token = [active_sets(BATCH * step + b) for b in range(BATCH)]
+    out = []
+    for layer in range(LAYERS):
+        sets = [per_token[b][layer] for b in range(BATCH)]
+        union = np.unique(np.concatenate(sets))
+        mask = np.stack([np.isin(union, s) for s in sets]).astype(np.uint8)
+        out.append((union, mask))
     return out
 
 
@@ -560,6 +583,183 @@ def run_gpu(args, rank, world, local_rank):
     return result
 
 
+def run_batch(args, rank, world, local_rank):
+    """Batch-8 union decode (--batch 8): each step runs the stack's layers for
+    8 tokens through ls_b200_batch_mlp, over the union of the tokens' active
+    groups with each token masked to its own set. Every layer takes the same
+    8 hidden states: the batch path has no fused RMSNorm, and un-normalised
+    residual chaining of random-weight layers overflows fp16, so layers are
+    not chained; the work and bytes of each layer are those of a chained
+    stack. One GPU."""
+    import ctypes as C
+
+    import torch
+
+    from leanstream_b200.synthetic import descriptors
+
+    if world > 1:
+        raise SystemExit("--batch runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    steps_total = args.warmup + args.steps
+    t_start = time.time()
+
+    def progress(msg):
+        print(f"[bench batch {time.time() - t_start:7.2f}s] {msg}", file=sys.stderr, flush=True)
+
+    st = Stack(0, 1, 1)  # the batch-1 workload's weights (all groups resident); its plans go unused
+    N, dev = st.N, st.dev
+    lib = N.load()
+    # per step, one image of every layer's [descriptors U x 20 B | mask 8 x U B]
+    lstride = ((NGROUPS * 20 + BATCH * NGROUPS + 255) // 256) * 256
+    img_host = torch.zeros((steps_total, LAYERS * lstride), dtype=torch.uint8, pin_memory=True)
+    unions = np.zeros((steps_total, LAYERS), np.int64)
+    for s in range(steps_total):
+        a = img_host[s].numpy()
+        for layer, (union, mask) in enumerate(batch_union(s)):
+            rows = descriptors(union).reshape(-1).view(np.uint8)
+            off = layer * lstride
+            a[off:off + rows.size] = rows
+            a[off + NGROUPS * 20:off + NGROUPS * 20 + mask.size] = mask.reshape(-1)
+            unions[s, layer] = len(union)
+    img_dev = img_host.to(dev)
+    slot_dev = torch.zeros(LAYERS * lstride, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    x = torch.randn(BATCH, H, device=dev, generator=gen).half()
+    y = torch.zeros(BATCH, H, dtype=torch.float16, device=dev)
+    nbytes = int(lib.ls_b200_batch_scratch_bytes(H, G, NGROUPS))
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    progress("weights and batch plans resident")
+
+    def layer_args(s, layer, base):
+        off = base + layer * lstride
+        return N.BatchArgs(H, G, int(unions[s, layer]), BATCH, x.data_ptr(), y.data_ptr(), None, None, None,
+                           st.cache[layer].data_ptr(), None, st.scales[layer].data_ptr(), off,
+                           off + NGROUPS * 20, scratch.data_ptr(), nbytes)
+
+    stream = torch.cuda.Stream()
+
+    def enqueue_step(s, base, strm):
+        for layer in range(LAYERS):
+            rc = lib.ls_b200_batch_mlp(C.byref(layer_args(s, layer, base)), strm.cuda_stream)
+            if rc:
+                raise RuntimeError(f"ls_b200_batch_mlp returned {rc}")
+
+    # first calls outside capture (the call opts the kernels into their ring size)
+    with torch.cuda.stream(stream):
+        enqueue_step(0, img_dev[0].data_ptr(), stream)
+    torch.cuda.synchronize()
+    graphs, e2e_graphs = [], []
+    for s in range(steps_total):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enqueue_step(s, img_dev[s].data_ptr(), torch.cuda.current_stream())
+        graphs.append(g)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enqueue_step(s, slot_dev.data_ptr(), torch.cuda.current_stream())
+        e2e_graphs.append(g)
+    torch.cuda.synchronize()
+    progress(f"{2 * steps_total} step graphs captured")
+
+    # ---- value: device-resident inputs and plans
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            graphs[s].replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    clocks.mark()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for s in range(args.warmup, steps_total):
+            graphs[s].replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clock = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    progress(f"timed region: {ms / args.steps:.3f} ms per step")
+
+    # ---- e2e: the step's plans and hidden states from pinned host memory,
+    # outputs back to the host, every step
+    x_host = x.cpu().pin_memory()
+    y_host = torch.zeros(BATCH, H, dtype=torch.float16, pin_memory=True)
+    h2d = img_host[0].numel() + x_host.numel() * 2
+    d2h = y_host.numel() * 2
+
+    def e2e_step(s):
+        slot_dev.copy_(img_host[s], non_blocking=True)
+        x.copy_(x_host, non_blocking=True)
+        e2e_graphs[s].replay()
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            e2e_step(s)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for s in range(args.warmup, steps_total):
+            e2e_step(s)
+        f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    if not np.isfinite(y_host.numpy().astype(np.float32)).all():
+        raise RuntimeError("non-finite batch output")
+    progress("end-to-end timing done")
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    timed = unions[args.warmup:]
+    alg_bytes = float(timed.sum()) * ALG_BYTES_PER_GROUP
+    achieved = alg_bytes / (ms * 1e-3) / 1e9
+    result = {
+        "metric": METRIC,
+        "value": BATCH * args.steps / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "us_per_layer": ms / args.steps * 1e3 / LAYERS,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int4 weights x fp16 activations, fp32 accumulate",
+        "data": "synthetic (seeded INT4/fp16, BASELINE.json shapes)",
+        "config": {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
+                   "group_size": G, "active_fraction": [FMIN, FMAX], "batch": BATCH,
+                   "mean_union_groups_per_layer": float(timed.mean()),
+                   "layers_chained": False,
+                   "parallelism": "single GPU",
+                   "l2": f"inputs larger than L2: ~{timed.mean() * ALG_BYTES_PER_GROUP / 1e6:.0f} MB of distinct "
+                         "weights per layer",
+                   "timing": "CUDA graph per step, CUDA events on the launching stream"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None,
+                     "kernel": "batch_gateup_kernel + batch_down_kernel + batch_epilogue_kernel (one layer)",
+                     "algorithmic_bytes_per_group": ALG_BYTES_PER_GROUP,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback"},
+        "e2e": {"value": BATCH * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": 3 * LAYERS * args.steps,
+        "clocks": clock,
+    }
+    torch.cuda.synchronize()
+    for g in graphs + e2e_graphs:
+        g.reset()
+    progress("done")
+    return result
+
+
 # --------------------------------------------------------------------- CPU arm
 def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
     """The oracle port of the MLP (OpenMP over active neurons) on a bounded
@@ -639,12 +839,17 @@ def main():
     p.add_argument("--trace", action="store_true", help="print per-CTA phase stamps of one launch to stderr")
     p.add_argument("--config", type=int, choices=[3, 5], default=3,
                    help="BASELINE.json configuration: 3 (headline, H 4096, 36 layers) or 5 (H 8192, 80 layers)")
+    p.add_argument("--batch", type=int, choices=[1, 8], default=1,
+                   help="tokens per step: 1 (the default workload) or 8 (union decode, one GPU)")
     p.add_argument("--layers", type=int, default=0,
                    help="stack depth; smaller values only for profiling captures (the metric is quoted at the "
                         "configuration's depth)")
     args = p.parse_args()
-    global LAYERS
+    global LAYERS, METRIC, WORKLOAD
     set_config(args.config)
+    if args.batch == BATCH:
+        METRIC = METRIC.replace("batch-1 decode", f"batch-{BATCH} union decode")
+        WORKLOAD = WORKLOAD.replace("batch 1", f"batch {BATCH} over the union of the tokens' active groups")
     if args.layers:
         if not 1 <= args.layers <= LAYERS:
             p.error(f"--layers must be in [1, {LAYERS}]")
@@ -659,7 +864,7 @@ def main():
         if res is not None:
             print(json.dumps(res), flush=True)
         return
-    res = run_gpu(args, rank, world, local_rank)
+    res = run_batch(args, rank, world, local_rank) if args.batch == BATCH else run_gpu(args, rank, world, local_rank)
     if rank == 0 and res is not None:
         if world == 1 and not args.no_cpu_baseline:
             try:

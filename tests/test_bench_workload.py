@@ -54,3 +54,29 @@ def test_round_robin_sharding_and_balance():
         assert bal["busiest_over_mean"] >= 1.0 and bal["worst_busiest_over_mean"] >= bal["busiest_over_mean"]
         assert abs(bal["mean_groups_per_rank_layer"] * world - np.mean(
             [len(s) for st in range(3, 5) for s in b.active_sets(st)])) < 1e-9
+
+
+def test_config5_batch8_union_and_masks():
+    """--batch 8: step s decodes tokens 8s .. 8s+7; per layer the union is the
+    sorted set of their groups (about 1 - 0.8^8 = 83 % of 448 at 20 % each)
+    and mask row b marks exactly token 8s + b's own groups."""
+    from leanstream_b200.synthetic import descriptors
+
+    b = _bench(5)
+    per_token = [b.active_sets(8 * 2 + t) for t in range(8)]
+    layers = b.batch_union(2)
+    assert len(layers) == 80
+    fractions = []
+    for layer, (union, mask) in enumerate(layers):
+        expect = sorted(set().union(*(set(per_token[t][layer].tolist()) for t in range(8))))
+        assert union.tolist() == expect
+        assert mask.shape == (8, len(union)) and mask.dtype == np.uint8
+        for t in range(8):
+            assert union[mask[t] == 1].tolist() == per_token[t][layer].tolist()
+        fractions.append(len(union) / 448)
+        rows = descriptors(union)  # what the bench uploads: logical = physical = cache slot
+        assert rows.shape == (len(union), 5) and rows[:, 0].tolist() == expect
+        assert np.array_equal(rows[:, 2], rows[:, 0]) and np.array_equal(rows[:, 3], np.arange(len(union)))
+    assert 0.78 < np.mean(fractions) < 0.88
+    # the per-layer image the bench writes fits its fixed stride
+    assert 448 * 20 + 8 * 448 <= ((448 * 20 + 8 * 448 + 255) // 256) * 256
