@@ -473,6 +473,8 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     if (H < 256 || H > uint32_t(kMaxHidden) || H % 256 || !G || G > uint32_t(kMaxGroupSize) || !U || !B ||
         B > uint32_t(kBatchTokens))
         return EINVAL;
+    // union neurons index rows of h and the gate/up grid in 32 bits
+    if (uint64_t(G) * U > (uint64_t(1) << 30)) return EINVAL;
     if (!a->x || !a->output || !a->cache || !a->scales || !a->union_descs || !a->scratch ||
         (a->hidden_out && !a->residual))
         return EINVAL;

@@ -210,6 +210,9 @@ def test_batch_argument_validation_without_gpu(native_lib):
                      ("scales", (1 << 23) + 2), ("staging", (1 << 27) + 8), ("scratch", (1 << 25) + 4)]:
         a = N.BatchArgs(**{**good, key: bad})
         assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL, key
+    # G * union_count beyond 2^30 neurons is refused (32-bit neuron indices)
+    a = N.BatchArgs(**{**good, "union_count": (1 << 30) // 64 + 1, "scratch_bytes": 1 << 62})
+    assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL
     a = N.BatchArgs(**{**good, "scratch_bytes": need - 1})
     assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.ENOSPC
     assert lib.ls_b200_batch_mlp(None, None) == errno.EINVAL
