@@ -368,7 +368,8 @@ int ls_b200_queue_fail(ls_b200_queue* queue, uint32_t error);
  * least ls_b200_batch_scratch_bytes(), 16-byte aligned; x, cache and staging
  * 16-byte aligned, scales 4-byte aligned. Hidden a multiple of 256 up to
  * 8192. Bad arguments return EINVAL (ENOSPC for short scratch) before any
- * CUDA call; nothing is allocated. */
+ * CUDA call; nothing is allocated. The first call on a device sets the
+ * kernels' shared-memory attributes: make it before any stream capture. */
 typedef struct ls_b200_batch_args {
     uint32_t hidden, group_size, union_count, tokens;  /* tokens 1..8 */
     const void* x;            /* fp16 [tokens][H] */
