@@ -96,12 +96,12 @@ def batch_union(step: int):
     """Batch step `step` decodes tokens 8*step .. 8*step + 7 of the same seeded
     stream as the batch-1 workload. Per layer: the sorted union of their
     active groups and the [token][union] mask of each token's own set."""
+    from leanstream_b200.batch import union_plan
+
     per_token = [active_sets(BATCH * step + b) for b in range(BATCH)]
     out = []
     for layer in range(LAYERS):
-        sets = [per_token[b][layer] for b in range(BATCH)]
-        union = np.unique(np.concatenate(sets))
-        mask = np.stack([np.isin(union, s) for s in sets]).astype(np.uint8)
+        union, _, mask = union_plan([per_token[b][layer] for b in range(BATCH)])
         out.append((union, mask))
     return out
 
@@ -591,11 +591,9 @@ def run_batch(args, rank, world, local_rank):
     residual chaining of random-weight layers overflows fp16, so layers are
     not chained; the work and bytes of each layer are those of a chained
     stack. One GPU."""
-    import ctypes as C
-
     import torch
 
-    from leanstream_b200.synthetic import descriptors
+    from leanstream_b200.batch import BatchMLP, union_plan
 
     if world > 1:
         raise SystemExit("--batch runs on one GPU")
@@ -607,8 +605,7 @@ def run_batch(args, rank, world, local_rank):
         print(f"[bench batch {time.time() - t_start:7.2f}s] {msg}", file=sys.stderr, flush=True)
 
     st = Stack(0, 1, 1)  # the batch-1 workload's weights (all groups resident); its plans go unused
-    N, dev = st.N, st.dev
-    lib = N.load()
+    dev = st.dev
     # per step, one image of every layer's [descriptors U x 20 B | mask 8 x U B]
     lstride = ((NGROUPS * 20 + BATCH * NGROUPS + 255) // 256) * 256
     img_host = torch.zeros((steps_total, LAYERS * lstride), dtype=torch.uint8, pin_memory=True)
@@ -616,7 +613,7 @@ def run_batch(args, rank, world, local_rank):
     for s in range(steps_total):
         a = img_host[s].numpy()
         for layer, (union, mask) in enumerate(batch_union(s)):
-            rows = descriptors(union).reshape(-1).view(np.uint8)
+            rows = union_plan([union])[1].reshape(-1).view(np.uint8)  # all groups resident: slot = id
             off = layer * lstride
             a[off:off + rows.size] = rows
             a[off + NGROUPS * 20:off + NGROUPS * 20 + mask.size] = mask.reshape(-1)
@@ -627,23 +624,15 @@ def run_batch(args, rank, world, local_rank):
     gen.manual_seed(SEED)
     x = torch.randn(BATCH, H, device=dev, generator=gen).half()
     y = torch.zeros(BATCH, H, dtype=torch.float16, device=dev)
-    nbytes = int(lib.ls_b200_batch_scratch_bytes(H, G, NGROUPS))
-    scratch = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    mlp = BatchMLP(H, G, NGROUPS, device=dev)  # the public batch API; scratch sized for every group
     progress("weights and batch plans resident")
-
-    def layer_args(s, layer, base):
-        off = base + layer * lstride
-        return N.BatchArgs(H, G, int(unions[s, layer]), BATCH, x.data_ptr(), y.data_ptr(), None, None, None,
-                           st.cache[layer].data_ptr(), None, st.scales[layer].data_ptr(), off,
-                           off + NGROUPS * 20, scratch.data_ptr(), nbytes)
-
     stream = torch.cuda.Stream()
 
     def enqueue_step(s, base, strm):
         for layer in range(LAYERS):
-            rc = lib.ls_b200_batch_mlp(C.byref(layer_args(s, layer, base)), strm.cuda_stream)
-            if rc:
-                raise RuntimeError(f"ls_b200_batch_mlp returned {rc}")
+            off = base + layer * lstride
+            mlp.run(stream=strm, x=x, output=y, cache=st.cache[layer], scales=st.scales[layer], union_descs=off,
+                    union_count=int(unions[s, layer]), tokens=BATCH, mask=off + NGROUPS * 20)
 
     # first calls outside capture (the call opts the kernels into their ring size)
     with torch.cuda.stream(stream):

@@ -6,5 +6,7 @@ the reference's native-backend API, plus the seeded synthetic data format.
 """
 from ._native import load as load_library, LIBRARY  # noqa: F401
 from .backend import B200Backend, DeviceQueue, ExecutionQueue, quantize_io_load  # noqa: F401
+from .batch import BatchMLP, union_plan  # noqa: F401
 
-__all__ = ["B200Backend", "DeviceQueue", "ExecutionQueue", "quantize_io_load", "load_library", "LIBRARY"]
+__all__ = ["B200Backend", "BatchMLP", "DeviceQueue", "ExecutionQueue", "quantize_io_load", "union_plan",
+           "load_library", "LIBRARY"]
