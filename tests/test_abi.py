@@ -216,3 +216,16 @@ def test_batch_argument_validation_without_gpu(native_lib):
     a = N.BatchArgs(**{**good, "scratch_bytes": need - 1})
     assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.ENOSPC
     assert lib.ls_b200_batch_mlp(None, None) == errno.EINVAL
+
+
+def test_selection_path_has_no_timing_or_search():
+    """tests/check_selector_contract.py:1-13: the kernel choice is a table
+    lookup, never timed or searched at run time. The files of the selection
+    and enqueue path here carry none of the timing or tuning calls."""
+    files = [ROOT / "leanstream_b200" / "csrc" / "ls_backend.cu", ROOT / "leanstream_b200" / "csrc" / "ls_internal.h",
+             ROOT / "leanstream_b200" / "backend.py"]
+    forbidden = ("cudaevent", "autotune", "onlineprofiler", "runtimetuner", "autotuner", "benchmark", "cupti")
+    for f in files:
+        text = f.read_text().lower()
+        for word in forbidden:
+            assert word not in text, (f.name, word)
