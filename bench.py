@@ -120,6 +120,34 @@ def rank_balance(first: int, last: int, world: int) -> dict:
             "worst_busiest_over_mean": float(np.max(ratios))}
 
 
+def workload_config(world: int, args) -> dict:
+    """The `config` object of the JSON line: the workload only (shapes,
+    active sets of the timed steps, sharding), identical for the GPU arm and
+    the CPU reference arm of the same arguments. How each arm times it is
+    the line's `timing` key."""
+    first, last = args.warmup, args.warmup + args.steps
+    cfg = {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
+           "group_size": G, "active_fraction": [FMIN, FMAX],
+           "int4_values": "signed INT4 uniform in [-7, 7] (zero-mean like the reference quantizer, "
+                          "examples/ministral/pack/int4_format.py:16; BASELINE.json's [-8, 7] has mean -0.5, "
+                          "which overflows fp16 through the residual stack); fp16 scales U(0.005, 0.02)"}
+    if getattr(args, "batch", 1) == BATCH:
+        unions = [len(u) for s in range(first, last) for (u, _) in batch_union(s)]
+        cfg.update({"batch": BATCH, "mean_union_groups_per_layer": float(np.mean(unions)), "layers_chained": False,
+                    "parallelism": "single GPU",
+                    "l2": f"inputs larger than L2: ~{np.mean(unions) * ALG_BYTES_PER_GROUP / 1e6:.0f} MB of "
+                          "distinct weights per layer"})
+        return cfg
+    mean_active = float(np.mean([len(ids) for s in range(first, last) for ids in active_sets(s)]))
+    cfg.update({"batch": 1, "mean_active_groups_per_layer": mean_active,
+                "rank_balance": rank_balance(first, last, world) if world > 1 else None,
+                "parallelism": f"tp{world} (groups round-robin; fp32 partials exchanged over NVLink peer memory "
+                               "inside the persistent launch)" if world > 1 else "single GPU",
+                "l2": f"inputs larger than L2: ~{mean_active * LAYERS * ALG_BYTES_PER_GROUP / 1e6:.0f} MB of "
+                      "distinct weights per token"})
+    return cfg
+
+
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
     """SM clock and throttle reasons sampled during the timed region: NVML
@@ -527,7 +555,6 @@ def run_gpu(args, rank, world, local_rank):
             pass
         peak = float(peaks.get("hbm_gbs", 6650.0))
         mean_active = float(np.mean([sum(c) for c in st.active_local[args.warmup:]])) / LAYERS
-        balance = rank_balance(args.warmup, args.warmup + args.steps, world) if world > 1 else None
         # DRAM bytes (read + write) of one launch, from the ncu capture of
         # the same kernel on an 8-layer stack, scaled by the algorithmic
         # bytes the launch processes (traffic grows with the active groups).
@@ -546,14 +573,11 @@ def run_gpu(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "int4 weights x fp16 activations, fp32 accumulate",
             "data": "synthetic (seeded INT4/fp16, BASELINE.json shapes)",
-            "config": {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
-                       "group_size": G, "active_fraction": [FMIN, FMAX], "batch": 1,
-                       "mean_active_groups_per_layer": mean_active,
-                       "rank_balance": balance,
-                       "parallelism": f"tp{world} (groups round-robin; fp32 partials exchanged over NVLink peer memory "
-                                      "inside the persistent launch)" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2: ~841 MB of distinct weights per token",
-                       "timing": "CUDA graph per token, CUDA events on the launching stream, max over ranks"},
+            "config": workload_config(world, args),
+            "timing": "CUDA graph per token, CUDA events on the launching stream, max over ranks",
+            "arithmetic": "variant 1 (KernelSelector default): exact integer/fp32 sums with the fp16 scales "
+                          "applied per 128-block; the reference rounds each weight to fp16 first (variant 0, "
+                          "candidate 5); outputs within the 2e-3 x max|y| tolerance of the reference math",
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                          "frac": achieved_gbs / peak, "traffic": traffic,
                          "kernel": kernel_name, "kernel_us_mean": 1e3 * float(np.mean(kern_ms)),
@@ -724,14 +748,9 @@ def run_batch(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "int4 weights x fp16 activations, fp32 accumulate",
         "data": "synthetic (seeded INT4/fp16, BASELINE.json shapes)",
-        "config": {"workload": WORKLOAD, "hidden": H, "intermediate": I, "layers": LAYERS, "groups": NGROUPS,
-                   "group_size": G, "active_fraction": [FMIN, FMAX], "batch": BATCH,
-                   "mean_union_groups_per_layer": float(timed.mean()),
-                   "layers_chained": False,
-                   "parallelism": "single GPU",
-                   "l2": f"inputs larger than L2: ~{timed.mean() * ALG_BYTES_PER_GROUP / 1e6:.0f} MB of distinct "
-                         "weights per layer",
-                   "timing": "CUDA graph per step, CUDA events on the launching stream"},
+        "config": workload_config(1, args),
+        "timing": "CUDA graph per step, CUDA events on the launching stream",
+        "arithmetic": "w = fp16(q * s) as the reference (backends/triton/core.py:17), fp32 accumulation",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None,
                      "kernel": "batch_gateup_kernel + batch_down_kernel + batch_epilogue_kernel (one layer)",
@@ -750,69 +769,137 @@ def run_batch(args, rank, world, local_rank):
 
 
 # --------------------------------------------------------------------- CPU arm
-def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
-    """The oracle port of the MLP (OpenMP over active neurons) on a bounded
-    sample of the same workload: layers of token 0 until `budget_s` elapses."""
-    from oracle import oracle as O
-    from leanstream_b200.synthetic import make_layer
+def host_cores() -> int:
+    """Threads the CPU path may use: the process's CPU affinity set (as the
+    reference's ls_available_cores, predictor/predictor_cpu.cpp:128). Under
+    torchrun OMP_NUM_THREADS is 1, so the OpenMP default is not used."""
+    return len(os.sched_getaffinity(0))
 
+
+class CpuPath:
+    """The reference's CPU path for one layer of the workload, on the host
+    cores: group selection by the reference's own ls_predict
+    (predictor/predictor_cpu.cpp:144-204, compiled unmodified into
+    oracle/_ref) followed by the sparse INT4 MLP of the oracle port
+    (OpenMP over active neurons; examples/custom_pytorch/run.py:43-50
+    arithmetic). The reference has no native CPU MLP kernel, so the MLP leg
+    is the port. Weight values do not change the arithmetic cost: one
+    seeded layer stands for every layer."""
+
+    def __init__(self, threads: int):
+        from oracle import oracle as O
+        from leanstream_b200.synthetic import make_layer
+
+        self.O, self.threads = O, threads
+        self.layer = make_layer(1000, H, NGROUPS, G)
+        self.pred = None
+        self.pred_weights = None
+        try:
+            rng = np.random.default_rng(SEED)
+            # one representative fp32 gate/up row pair per group
+            self.pred_weights = rng.standard_normal((NGROUPS, 2, H)).astype(np.float32)
+            self.pred_x = self.layer.x.astype(np.float32)
+        except Exception:  # pragma: no cover
+            self.pred_weights = None
+
+    def _predict(self, k: int):
+        """Top-k group IDs by ls_predict. One context ranks the most groups a
+        layer can have active (ls_create is set-up, not per-layer work); a
+        layer with fewer takes the prefix of that (score desc, id asc)
+        ranking, which is its own top-k."""
+        if self.pred_weights is None:
+            return None
+        if self.pred is None:
+            kmax = max(int(round(FMAX * NGROUPS)), 4)
+            self.pred = self.O.Predictor(NGROUPS, H, kmax, threads=self.threads)
+        return self.pred.predict(self.pred_weights, self.pred_x)[:k]
+
+    def layer_seconds(self, ids) -> float:
+        """Wall time of one layer: ls_predict (k = the layer's active count)
+        then the sparse MLP over those groups."""
+        t0 = time.perf_counter()
+        sel = self._predict(len(ids))
+        d = np.zeros((len(ids), 5), np.uint32)
+        d[:, 0] = d[:, 1] = d[:, 2] = np.asarray(ids if sel is None else np.sort(sel))
+        d[:, 3] = np.arange(len(ids))
+        self.O.mlp_omp(H, G, self.layer.x, self.layer.packed, self.layer.scales, d, threads=self.threads)
+        return time.perf_counter() - t0
+
+    def predictor_available(self) -> bool:
+        try:
+            self._predict(4)
+            return True
+        except Exception:
+            self.pred_weights = None
+            return False
+
+
+def cpu_layers_per_step() -> int:
+    """Layers in one timed step of the CPU path: a whole token for
+    configuration 3 (about a second on 16 host cores); for configuration 5
+    (about ten seconds per token) an 8-layer sample, so that a driver run
+    of tens of steps ends within minutes."""
+    return LAYERS if CONFIG == 3 else min(8, LAYERS)
+
+
+def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
+    """cpu_baseline of the GPU arm: the CPU path on a bounded sample of the
+    same workload (the layers of token 0, in order, until `budget_s`)."""
+    nthreads = threads or host_cores()
+    path = CpuPath(nthreads)
+    pred = path.predictor_available()
     sets = active_sets(0)
     done, elapsed = 0, 0.0
-    nthreads = threads or O.max_threads()
-    L = make_layer(1000, H, NGROUPS, G)  # arithmetic cost does not depend on the values
     for layer in range(LAYERS):
-        ids = sets[layer]
-        d = np.zeros((len(ids), 5), np.uint32)
-        d[:, 0] = d[:, 1] = d[:, 2] = ids
-        d[:, 3] = np.arange(len(ids))
-        x = L.x
-        t0 = time.perf_counter()
-        O.mlp_omp(H, G, x, L.packed, L.scales, d, threads=nthreads)
-        elapsed += time.perf_counter() - t0
+        elapsed += path.layer_seconds(sets[layer])
         done += 1
         if elapsed >= budget_s:
             break
     per_layer = elapsed / done
+    what = "ls_predict + sparse MLP port" if pred else "sparse MLP port (reference predictor library absent)"
     return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": int(nthreads), "kind": "port",
-            "sample": f"{done} of {LAYERS} layers of token 0 (same shapes and active fractions), "
+            "sample": f"{done} of {LAYERS} layers of token 0 ({what}; same shapes and active sets), "
                       f"{elapsed:.1f} s of CPU work; tokens/s = 1/({LAYERS} x mean layer time)"}
 
 
 def run_reference(args, rank, world):
-    """The reference has no CPU MLP implementation of this path; its CPU code
-    is the predictor and runtime. The timed CPU path is the oracle port of
-    the reference's host math (OpenMP, all host threads)."""
+    """--impl reference: the reference's CPU path of this workload on the
+    host cores (CpuPath: its own ls_predict, then the MLP port, since the
+    reference has no native CPU MLP), on rank 0 only. Each timed step runs
+    cpu_layers_per_step() consecutive layers of the token stream, so
+    ms_per_step is the wall time of exactly what one step did; tokens/s is
+    1 / (layers x mean layer time)."""
     if rank != 0:
         return None
-    from oracle import oracle as O
-    from leanstream_b200.synthetic import make_layer
-
-    sets = active_sets(0)
-    layers = [make_layer(1000 + layer, H, NGROUPS, G) for layer in range(min(2, LAYERS))]
-    threads = O.max_threads()
+    threads = host_cores()
+    path = CpuPath(threads)
+    pred = path.predictor_available()
+    lps = cpu_layers_per_step()
 
     def one(step):
-        L = layers[step % len(layers)]
-        ids = sets[step % len(layers)]
-        d = np.zeros((len(ids), 5), np.uint32)
-        d[:, 0] = d[:, 1] = d[:, 2] = ids
-        d[:, 3] = np.arange(len(ids))
-        t0 = time.perf_counter()
-        O.mlp_omp(H, G, L.x, L.packed, L.scales, d, threads=threads)
-        return time.perf_counter() - t0
+        tok, first = divmod(step * lps, LAYERS)
+        sets = active_sets(tok)
+        return sum(path.layer_seconds(sets[(first + j) % LAYERS]) for j in range(lps))
 
     for s in range(args.warmup):
         one(s)
-    t = [one(s) for s in range(args.steps)]
-    per_layer = float(np.mean(t))
+    t = [one(args.warmup + s) for s in range(args.steps)]
+    per_step = float(np.mean(t))
+    per_layer = per_step / lps
     value = 1.0 / (per_layer * LAYERS)
-    sample = f"each step = 1 MLP layer of the stack ({args.steps} steps); tokens/s = 1/({LAYERS} x mean layer time)"
+    what = "ls_predict + sparse MLP port" if pred else "sparse MLP port (reference predictor library absent)"
+    sample = (f"each step = {lps} consecutive layers of the token stream ({what}), {threads} host threads; "
+              f"tokens/s = 1/({LAYERS} x mean layer time)")
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3 * LAYERS,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "us_per_layer": per_layer * 1e6,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4 weights x fp16 activations, fp32 accumulate", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "parallelism": "host CPU, OpenMP"},
+        "dtype": "int4 weights x fp16 activations, fp32 accumulate",
+        "data": "synthetic (seeded INT4/fp16, BASELINE.json shapes)",
+        "config": workload_config(world, args),
+        "timing": "host wall clock (time.perf_counter) around each step",
+        "arithmetic": "the reference's rounding boundaries (w, g, u, SiLU, h in fp16; fp32 sums)",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

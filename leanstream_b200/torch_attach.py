@@ -22,7 +22,6 @@ from __future__ import annotations
 
 import threading
 from dataclasses import dataclass
-from functools import wraps
 from pathlib import Path
 from typing import Callable, Optional
 
@@ -34,9 +33,20 @@ from .backend import B200Backend, ExecutionQueue
 from .stream import IOBackendView, StreamEngine
 
 
-# ------------------------------------------------------------------ contracts (contracts.py)
+# ------------------------------------------------------------------ contracts
+# Field names follow leanstream/integrations/torch/contracts.py so that
+# attach_leanstream callers pass the same objects; every check below is this
+# module's own (failures raise ValueError naming the offending field).
+def _require(ok, what: str) -> None:
+    if not ok:
+        raise ValueError(what)
+
+
 @dataclass(frozen=True)
 class ModelPoints:
+    """Where the decoder layers, their MLP, attention and pre-MLP norm live
+    (dotted attribute paths; integers index sequences). layers="auto"
+    searches the model for the decoder-layer list."""
     layers: str = "model.layers"
     mlp: str = "mlp"
     attention: str = "self_attn"
@@ -75,36 +85,43 @@ class WeightSpec:
         return self.group_size * 3 * self.width // 2
 
     def validate(self):
-        n, b = self.group_count, self.group_bytes
-        if n < 1 or self.width < 256 or self.width % 256 or not 1 <= self.group_size <= 256:
-            raise ValueError("width must be a multiple of 256 (<= 8192), group size 1..256")
-        if {x.logical_group for x in self.layout} != set(range(n)) or \
-                {x.physical_group for x in self.layout} != set(range(n)):
-            raise ValueError("Logical and physical IDs must each be permutations")
-        if any(x.bytes != b or x.file_offset < 0 for x in self.layout):
-            raise ValueError("Invalid extents")
-        ranges = sorted((x.file_offset, x.file_offset + b) for x in self.layout)
-        if any(a[1] > c[0] for a, c in zip(ranges, ranges[1:])):
-            raise ValueError("Overlapping weight extents")
-        if not Path(self.path).is_file() or Path(self.path).stat().st_size < ranges[-1][1]:
-            raise ValueError("Missing/truncated weight file")
-        if self.scales.device.type != "cpu" or self.scales.dtype != torch.float16 or \
-                self.scales.numel() != n * self.group_size * 3 * self.width // 128 or \
-                not torch.isfinite(self.scales).all():
-            raise ValueError("Expected finite CPU FP16 physical scale table")
+        n, gb, H, G = self.group_count, self.group_bytes, self.width, self.group_size
+        _require(n >= 1, "WeightSpec.layout: no groups")
+        _require(256 <= H <= 8192 and H % 256 == 0, f"WeightSpec.width {H}: a multiple of 256 up to 8192")
+        _require(1 <= G <= 256, f"WeightSpec.group_size {G}: 1..256")
+        logical = np.sort(np.fromiter((e.logical_group for e in self.layout), np.int64, n))
+        physical = np.sort(np.fromiter((e.physical_group for e in self.layout), np.int64, n))
+        _require(np.array_equal(logical, np.arange(n)), "WeightSpec.layout: logical_group must cover 0..n-1 once")
+        _require(np.array_equal(physical, np.arange(n)), "WeightSpec.layout: physical_group must cover 0..n-1 once")
+        starts = np.sort(np.fromiter((e.file_offset for e in self.layout), np.int64, n))
+        _require(all(e.bytes == gb for e in self.layout), f"WeightSpec.layout: every extent is {gb} bytes")
+        _require(starts[0] >= 0 and np.all(np.diff(starts) >= gb), "WeightSpec.layout: extents overlap")
+        path = Path(self.path)
+        _require(path.is_file(), f"WeightSpec.path {path}: not a file")
+        _require(path.stat().st_size >= starts[-1] + gb, f"WeightSpec.path {path}: shorter than the layout")
+        sc = self.scales
+        _require(isinstance(sc, torch.Tensor) and sc.device.type == "cpu" and sc.dtype == torch.float16,
+                 "WeightSpec.scales: a CPU float16 tensor")
+        _require(sc.numel() == n * G * 3 * (H // 128), "WeightSpec.scales: [physical_group, G, 3, H/128] elements")
+        _require(bool(torch.isfinite(sc).all()), "WeightSpec.scales: non-finite entries")
 
 
 @dataclass(frozen=True)
 class CachePolicy:
+    """Groups kept in HBM (resident, slot = position) and the core groups,
+    a resident subset computed in every step."""
     resident: tuple
     core: tuple
 
     def validate(self, n):
-        for ids in (self.resident, self.core):
-            if len(set(ids)) != len(ids) or any(type(i) != int or not 0 <= i < n for i in ids):
-                raise ValueError("Invalid resident/core IDs")
-        if not set(self.core) <= set(self.resident):
-            raise ValueError("Core must be a resident subset")
+        for name in ("resident", "core"):
+            ids = getattr(self, name)
+            _require(all(isinstance(i, int) and not isinstance(i, bool) for i in ids),
+                     f"CachePolicy.{name}: Python int group IDs")
+            _require(len(ids) == len(set(ids)), f"CachePolicy.{name}: repeated group IDs")
+            _require(all(0 <= i < n for i in ids), f"CachePolicy.{name}: group IDs outside 0..{n - 1}")
+        missing = sorted(set(self.core) - set(self.resident))
+        _require(not missing, f"CachePolicy.core: groups {missing} are not resident")
 
 
 @dataclass(frozen=True)
@@ -116,18 +133,24 @@ class PredictionStage:
 
 @dataclass(frozen=True)
 class PredictionSchedule:
+    """`final` chooses each step's groups; `early` (Progressive only) starts
+    the reads before the final choice."""
     final: PredictionStage
     early: Optional[PredictionStage] = None
 
     def validate(self, n, mode):
-        if mode not in ("basic", "progressive"):
-            raise ValueError("Mode must be basic or progressive")
-        if (mode == "progressive") != (self.early is not None):
-            raise ValueError("Progressive requires early; Basic excludes early")
-        for stage in (self.early, self.final):
-            if stage and (not callable(stage.predictor) or not 0 < stage.budget <= n or
-                          not 0 <= stage.io_budget <= n):
-                raise ValueError("Invalid prediction budget")
+        _require(mode in ("basic", "progressive"), f"mode {mode!r}: 'basic' or 'progressive'")
+        if mode == "progressive":
+            _require(self.early is not None, "PredictionSchedule.early: required in progressive mode")
+        else:
+            _require(self.early is None, "PredictionSchedule.early: only used in progressive mode")
+        for name in ("early", "final"):
+            st = getattr(self, name)
+            if st is None:
+                continue
+            _require(callable(st.predictor), f"PredictionSchedule.{name}.predictor: not callable")
+            _require(0 < st.budget <= n, f"PredictionSchedule.{name}.budget {st.budget}: 1..{n}")
+            _require(0 <= st.io_budget <= n, f"PredictionSchedule.{name}.io_budget {st.io_budget}: 0..{n}")
 
 
 @dataclass(frozen=True)
@@ -138,64 +161,108 @@ class ComputeSpec:
     check_execution: bool = False  # per-dest execution counters (correctness only)
 
 
-def ranked_ids(value, n, budget):
+def checked_selection(value, n, budget):
+    """A predictor's answer as a list of distinct group IDs in 0..n-1, at
+    most `budget` of them, in the predictor's (priority) order."""
     ids = list(value)
-    if len(ids) > budget or any(type(i) != int or not 0 <= i < n for i in ids) or len(set(ids)) != len(ids):
-        raise ValueError("Predictor must return unique, in-range Python integer logical IDs within budget")
+    _require(len(ids) <= budget, f"prediction: {len(ids)} groups exceed the budget {budget}")
+    _require(all(isinstance(i, int) and not isinstance(i, bool) for i in ids), "prediction: Python int group IDs")
+    _require(all(0 <= i < n for i in ids), f"prediction: group IDs outside 0..{n - 1}")
+    _require(len(set(ids)) == len(ids), "prediction: repeated group IDs")
     return ids
 
 
-# ------------------------------------------------------------------ inspection (inspection.py)
-def resolve(root, path):
-    value = root
-    for part in path.split("."):
-        value = value[int(part)] if part.isdecimal() else getattr(value, part)
-    return value
+# ------------------------------------------------------------------ model inspection
+def _walk(root, dotted: str):
+    """The object at a dotted path below `root` (decimal parts index)."""
+    obj = root
+    for part in filter(None, dotted.split(".")):
+        obj = obj[int(part)] if part.isdigit() else getattr(obj, part)
+    return obj
+
+
+def _has(root, dotted: str) -> bool:
+    try:
+        _walk(root, dotted)
+        return True
+    except (AttributeError, IndexError, KeyError, TypeError):
+        return False
+
+
+def _decoder_lists(model, points):
+    """(path, ModuleList) pairs of the model whose every element carries
+    the configured MLP point: the decoder-layer lists."""
+    found = []
+    for name, mod in model.named_modules():
+        if isinstance(mod, torch.nn.ModuleList) and len(mod) and all(_has(m, points.mlp) for m in mod):
+            found.append((name, mod))
+    return found
+
+
+class _Row(dict):
+    """One decoder layer of an inspection report (dict access kept for
+    callers of the reference's report)."""
 
 
 def inspect_model(model, points=None):
-    """Structural discovery of decoder layers with gated (gate/up/down) MLPs."""
+    """Finds the decoder layers and checks that each has a bias-free gated
+    MLP (gate/up: H -> I, down: I -> H) and a pre-MLP norm of width H.
+
+    Returns a dict: compatible (bool), points (the resolved ModelPoints),
+    layers (per layer: index, path, compatible, hidden, intermediate or
+    reason), missing (what stops attachment) and ambiguities (candidate
+    layer paths when the search is not unique)."""
     points = points or ModelPoints.auto()
-    paths = [points.layers] if points.layers != "auto" else ["model.layers", "model.model.layers", "layers"]
-    candidates = []
-    for path in paths:
+    report = {"compatible": False, "points": None, "layers": [], "missing": [], "ambiguities": []}
+    if points.layers == "auto":
+        found = _decoder_lists(model, points)
+        if len(found) != 1:
+            report["ambiguities"] = [name for name, _ in found]
+            report["missing"].append(f"{len(found)} module lists carry '{points.mlp}': set ModelPoints.layers")
+            return report
+        path, layers = found[0]
+    else:
+        path = points.layers
         try:
-            layers = resolve(model, path)
-            if len(layers) > 0:
-                candidates.append((path, layers))
-        except (AttributeError, TypeError, KeyError):
-            pass
-    report = dict(compatible=False, ambiguities=[], missing=[], layers=[], points=None)
-    if len(candidates) != 1:
-        report["ambiguities"] = [p for p, _ in candidates]
-        report["missing"] = ["Specify a unique decoder layer path"]
-        return report
-    path, layers = candidates[0]
-    chosen = ModelPoints(path, points.mlp, points.attention, points.pre_mlp_norm)
-    seen = set()
+            layers = _walk(model, path)
+            len(layers)
+        except (AttributeError, IndexError, KeyError, TypeError):
+            report["missing"].append(f"no decoder-layer sequence at '{path}'")
+            return report
+    points = ModelPoints(path, points.mlp, points.attention, points.pre_mlp_norm)
+    owners = {}
     for i, layer in enumerate(layers):
-        row = dict(index=i, path=f"{path}.{i}", compatible=False)
-        try:
-            mlp = resolve(layer, chosen.mlp)
-            norm = resolve(layer, chosen.pre_mlp_norm)
-            if id(layer) in seen or id(mlp) in seen:
-                raise ValueError("Shared/reentrant layers or MLPs unsupported")
-            seen.update([id(layer), id(mlp)])
-            g, u, d = mlp.gate_proj, mlp.up_proj, mlp.down_proj
-            h, j = g.in_features, g.out_features
-            if u.in_features != h or u.out_features != j or d.in_features != j or d.out_features != h:
-                raise ValueError("Inconsistent gated projections")
-            if any(getattr(p, "bias", None) is not None for p in (g, u, d)):
-                raise ValueError("Bias unsupported")
-            if norm.weight.numel() != h:
-                raise ValueError("Normalization geometry")
-            row.update(compatible=True, hidden=h, intermediate=j)
-        except (AttributeError, ValueError, TypeError) as e:
-            row["reason"] = str(e)
-            report["missing"].append(f"{path}.{i}: {e}")
+        row = _Row(index=i, path=f"{path}.{i}", compatible=False)
         report["layers"].append(row)
-    report["compatible"] = bool(report["layers"]) and all(r["compatible"] for r in report["layers"])
-    report["points"] = chosen
+        problem = None
+        try:
+            mlp, norm = _walk(layer, points.mlp), _walk(layer, points.pre_mlp_norm)
+            for obj in (layer, mlp):
+                if id(obj) in owners:
+                    problem = f"shares a module with layer {owners[id(obj)]}"
+                owners.setdefault(id(obj), i)
+            proj = [getattr(mlp, k, None) for k in ("gate_proj", "up_proj", "down_proj")]
+            if problem is None and any(not isinstance(p, torch.nn.Linear) for p in proj):
+                problem = "MLP without gate_proj/up_proj/down_proj linear layers"
+            if problem is None:
+                gate, up, down = proj
+                hid, inter = gate.in_features, gate.out_features
+                shapes = [(p.in_features, p.out_features) for p in proj]
+                if shapes != [(hid, inter), (hid, inter), (inter, hid)]:
+                    problem = f"projection shapes {shapes} are not a gated MLP"
+                elif any(p.bias is not None for p in proj):
+                    problem = "projections with bias"
+                elif getattr(norm, "weight", None) is None or norm.weight.numel() != hid:
+                    problem = f"pre-MLP norm is not of width {hid}"
+                else:
+                    row.update(compatible=True, hidden=hid, intermediate=inter)
+        except (AttributeError, IndexError, KeyError, TypeError) as exc:
+            problem = f"missing module ({exc})"
+        if problem:
+            row["reason"] = problem
+            report["missing"].append(f"{row['path']}: {problem}")
+    report["points"] = points
+    report["compatible"] = bool(report["layers"]) and not report["missing"]
     return report
 
 
@@ -361,176 +428,204 @@ class LayerRuntime:
         self.backend.close()
 
 
-# ------------------------------------------------------------------ module replacement (attachment.py)
+# ------------------------------------------------------------------ module replacement
+def _single_token(x) -> bool:
+    """Batch-1 decode input: [1, 1, H]."""
+    return x.dim() == 3 and x.shape[0] == 1 and x.shape[1] == 1
+
+
+def _hidden_states(args, kwargs):
+    """The decoder layer's hidden-state input: the `hidden_states` keyword,
+    else the first positional argument."""
+    x = kwargs.get("hidden_states", args[0] if args else None)
+    if not isinstance(x, torch.Tensor):
+        raise ValueError("decoder layer called without a hidden_states tensor (first argument or keyword)")
+    return x
+
+
+class _LayerStep:
+    """One open decode step of one layer, from the decoder's pre-hook to the
+    MLP's output. The order of its calls is the reference runtime's layer
+    step (begin -> early update -> [Progressive: enqueue] -> final
+    prediction -> finalize -> [basic: wait for the reads, enqueue] ->
+    output -> commit; runtime.h, weight_manager.cpp:124-205)."""
+
+    def __init__(self, mlp: "SparseMLP", hidden):
+        self.mlp, self.rt = mlp, mlp.runtime
+        self.closed = False
+        self.rt.begin()
+        early = mlp.owner.prediction.early
+        if early is not None:
+            try:
+                self.deliver(early.predictor("layer_input", mlp.index, hidden, early.budget), early)
+            except BaseException:
+                self.cancel()
+                raise
+
+    def deliver(self, answer, stage):
+        """Hands a prediction to the reads; None while a future is pending."""
+        if hasattr(answer, "done"):
+            if not answer.done():
+                return None
+            answer = answer.result()
+        ids = checked_selection(answer, self.rt.n, stage.budget)
+        self.rt.update(ids, stage.io_budget)
+        return ids
+
+    def run(self, x):
+        rt, mlp = self.rt, self.mlp
+        _require(x.is_cuda and x.dtype == torch.float16 and x.shape[-1] == rt.spec.width,
+                 f"layer {mlp.index} MLP input: CUDA float16 [1, 1, {rt.spec.width}]")
+        stream = torch.cuda.current_stream()
+        basic = mlp.owner.mode == "basic"
+        if not basic:  # the kernel is queued first and consumes groups as they are published
+            rt.enqueue(x, stream)
+            mlp.trace.append("pre_enqueue")
+        final = mlp.owner.prediction.final
+        ids = self.deliver(final.predictor("mlp_input", mlp.index, x, final.budget), final)
+        _require(ids is not None, f"layer {mlp.index}: the final prediction returned an unfinished future")
+        rt.finalize(ids)
+        mlp.trace.append("finalize")
+        if basic:
+            rc = rt.wait_io(5000)
+            if rc:
+                raise RuntimeError(f"layer {mlp.index}: reads did not complete (rc {rc})")
+            rt.enqueue(x, stream)
+            mlp.trace.append("basic_enqueue_after_io")
+        out = rt.output(x.shape)
+        rt.commit()
+        self.closed = True
+        return out
+
+    def cancel(self):
+        if not self.closed:
+            self.closed = True
+            self.rt.abort()
+
+
 class SparseMLP(torch.nn.Module):
+    """Replacement MLP of one decoder layer: single-token decode runs the
+    sparse B200 path over the predicted groups, any other input shape the
+    original module."""
+
     def __init__(self, original, owner, index, runtime: LayerRuntime):
         super().__init__()
         self.original, self.owner, self.index, self.runtime = original, owner, index, runtime
-        self.pending = False
-        self.future = None
+        self.step: Optional[_LayerStep] = None
         self.trace = []
 
-    @staticmethod
-    def decode(x):
-        return x.ndim == 3 and tuple(x.shape[:2]) == (1, 1)
+    @property
+    def pending(self) -> bool:
+        return self.step is not None and not self.step.closed
 
-    def predict(self, stage, x, source):
-        return stage.predictor(source, self.index, x, stage.budget)
-
-    def publish(self, value, stage):
-        if hasattr(value, "done"):
-            if not value.done():
-                return False
-            value = value.result()
-        ids = ranked_ids(value, self.runtime.n, stage.budget)
-        self.runtime.update(ids, stage.io_budget)
-        return ids
-
-    def begin(self, x):
+    def open(self, hidden):
+        """Decoder pre-hook: opens this layer's decode step."""
         if torch.is_grad_enabled():
-            raise RuntimeError("Use torch.inference_mode(); training/autograd unsupported")
-        if not self.decode(x):
-            if x.ndim != 3 or x.shape[0] != 1:
-                raise ValueError("Only batch1 [1,sequence,H] supported")
+            raise RuntimeError("the LeanStream attachment is inference-only: use torch.inference_mode()")
+        if not _single_token(hidden):
+            _require(hidden.dim() == 3 and hidden.shape[0] == 1,
+                     f"hidden_states {tuple(hidden.shape)}: only batch 1, [1, S, H]")
             return
-        if x.device.type != "cuda" or x.dtype != torch.float16:
-            raise ValueError("Decode requires CUDA FP16")
-        self.runtime.begin()
-        self.pending = True
+        _require(hidden.is_cuda and hidden.dtype == torch.float16, "decode hidden_states must be CUDA float16")
         self.trace = []
-        early = self.owner.prediction.early
-        if early:
-            try:
-                self.future = self.predict(early, x, "layer_input")
-                self.publish(self.future, early)
-            except BaseException:
-                self.abort()
-                raise
+        self.step = None
+        self.step = _LayerStep(self, hidden)
 
     def abort(self):
-        if self.pending:
-            self.runtime.abort()
-            self.pending = False
+        if self.step is not None:
+            step, self.step = self.step, None
+            step.cancel()
 
     def forward(self, x):
-        if not self.decode(x):
+        if not _single_token(x):
             return self.original(x)
         if not self.pending:
-            raise RuntimeError("MLP must run inside its configured decoder layer")
+            raise RuntimeError(f"layer {self.index}: the sparse MLP ran outside its decoder layer's step")
         try:
-            if x.dtype != torch.float16 or x.device.type != "cuda" or x.shape[-1] != self.runtime.spec.width:
-                raise ValueError("MLP input geometry/dtype")
-            final = self.owner.prediction.final
-            stream = torch.cuda.current_stream()
-            if self.owner.mode == "progressive":
-                # the launch precedes the final prediction: the kernel consumes
-                # the queue as descriptors are published
-                self.runtime.enqueue(x, stream)
-                self.trace.append("pre_enqueue")
-            ids = self.publish(self.predict(final, x, "mlp_input"), final)
-            if ids is False:
-                raise ValueError("Final prediction must already be CPU-ready")
-            self.runtime.finalize(ids)
-            self.trace.append("finalize")
-            if self.owner.mode == "basic":
-                rc = self.runtime.wait_io(5000)
-                if rc:
-                    raise RuntimeError(f"IO wait failed: {rc}")
-                self.runtime.enqueue(x, stream)
-                self.trace.append("basic_enqueue_after_io")
-            result = self.runtime.output(x.shape)
-            self.runtime.commit()
-            self.pending = False
-            return result
+            return self.step.run(x)
         except BaseException:
             self.abort()
             raise
+        finally:
+            if self.step is not None and self.step.closed:
+                self.step = None
+
+
+def _check_attachment(model, report, layers, weights, cache_policy, prediction, mode):
+    _require(getattr(model, "_leanstream_attachment", None) is None, "this model already has an attachment")
+    _require(not model.training, "attach to a model in eval() mode")
+    _require(report["compatible"], f"model not attachable: {report['missing'] or report['ambiguities']}")
+    _require(len(weights) == len(layers) and len(cache_policy) == len(layers),
+             f"{len(layers)} decoder layers need as many WeightSpecs and CachePolicies "
+             f"({len(weights)}, {len(cache_policy)} given)")
+    for row, w, p in zip(report["layers"], weights, cache_policy):
+        w.validate()
+        p.validate(w.group_count)
+        prediction.validate(w.group_count, mode)
+        _require(row["hidden"] == w.width and row["intermediate"] == w.group_count * w.group_size,
+                 f"{row['path']}: model H={row['hidden']}, I={row['intermediate']}; packed weights "
+                 f"H={w.width}, I={w.group_count * w.group_size}")
 
 
 class Attachment:
+    """Lifecycle handle of attach_leanstream: the replaced MLP modules and
+    the decoder hooks that open and close their decode steps."""
+
     def __init__(self, model, points, weights, compute, cache_policy, prediction, mode):
-        if getattr(model, "_leanstream_attachment", None) is not None:
-            raise ValueError("Model already attached")
-        if model.training:
-            raise ValueError("Call model.eval(); training is unsupported")
         report = inspect_model(model, points)
-        if not report["compatible"]:
-            raise ValueError(f"Manual inspection required: {report}")
-        points = report["points"]
-        layers = resolve(model, points.layers)
-        if not len(weights) == len(cache_policy) == len(layers):
-            raise ValueError("One weight/policy specification per layer required")
+        layers = _walk(model, report["points"].layers) if report["points"] else []
+        _check_attachment(model, report, layers, weights, cache_policy, prediction, mode)
         self.model, self.prediction, self.mode = model, prediction, mode
-        self.entries, self.hooks, self.guards, self.closed = [], [], [], False
-        for row, w, p in zip(report["layers"], weights, cache_policy):
-            w.validate()
-            p.validate(w.group_count)
-            prediction.validate(w.group_count, mode)
-            if row["hidden"] != w.width or row["intermediate"] != w.group_count * w.group_size:
-                raise ValueError("Packed weight/model dimensions differ")
+        self.points = report["points"]
+        self.entries, self.handles, self.closed = [], [], False
         try:
             for i, (layer, w, p) in enumerate(zip(layers, weights, cache_policy)):
-                original = resolve(layer, points.mlp)
-                replacement = SparseMLP(original, self, i, LayerRuntime(w, p, compute))
-                parent = resolve(layer, points.mlp.rsplit(".", 1)[0]) if "." in points.mlp else layer
-                name = points.mlp.split(".")[-1]
-                setattr(parent, name, replacement)
-                self.entries.append((parent, name, original, replacement))
-
-                def begin(module, args, kwargs, r=replacement):
-                    x = args[0] if args else kwargs.get("hidden_states")
-                    if not isinstance(x, torch.Tensor):
-                        raise ValueError("Decoder must expose hidden_states as first positional/keyword Tensor")
-                    r.begin(x)
-
-                original_forward = layer.forward
-
-                @wraps(original_forward)
-                def guarded(*args, _forward=original_forward, _r=replacement, **kwargs):
-                    try:
-                        return _forward(*args, **kwargs)
-                    finally:
-                        if _r.pending:
-                            _r.abort()
-
-                self.guards.append((layer, original_forward))
-                layer.forward = guarded
-                self.hooks.append(layer.register_forward_pre_hook(begin, with_kwargs=True))
+                self._install(i, layer, LayerRuntime(w, p, compute))
             model._leanstream_attachment = self
         except BaseException:
             self.close()
             raise
 
+    def _install(self, index, layer, runtime):
+        parent_path, _, name = self.points.mlp.rpartition(".")
+        parent = _walk(layer, parent_path) if parent_path else layer
+        original = getattr(parent, name)
+        mlp = SparseMLP(original, self, index, runtime)
+        setattr(parent, name, mlp)
+        self.entries.append((parent, name, original, mlp))
+        self.handles.append(layer.register_forward_pre_hook(
+            lambda _m, args, kwargs: mlp.open(_hidden_states(args, kwargs)), with_kwargs=True))
+        # always_call: runs when the decoder layer raises too, so a step that
+        # its MLP never reached (or left open) is cancelled
+        self.handles.append(layer.register_forward_hook(lambda *_: mlp.abort() if mlp.pending else None,
+                                                        always_call=True))
+
     def refine(self, layer, ids, io_budget):
-        r = self.entries[layer][3]
-        if not r.pending:
-            raise ValueError("No active layer to refine")
-        ids = ranked_ids(ids, r.runtime.n, r.runtime.n)
-        if not 0 <= io_budget <= r.runtime.n:
-            raise ValueError("Invalid I/O budget")
-        r.runtime.update(ids, io_budget)
+        """A mid-step prediction update for `layer` (reorders its pending reads)."""
+        mlp = self.entries[layer][3]
+        _require(mlp.pending, f"layer {layer} has no open decode step to refine")
+        n = mlp.runtime.n
+        _require(0 <= io_budget <= n, f"io_budget {io_budget}: 0..{n}")
+        mlp.runtime.update(checked_selection(ids, n, n), io_budget)
 
     def reset(self):
-        for *_, r in self.entries:
-            r.abort()
+        for entry in self.entries:
+            entry[3].abort()
 
     def close(self):
         if self.closed:
             return
-        for hook in self.hooks:
-            hook.remove()
-        self.hooks.clear()
-        for layer, original_forward in self.guards:
-            layer.forward = original_forward
-        self.guards.clear()
-        for parent, name, original, r in reversed(self.entries):
+        self.closed = True
+        for handle in self.handles:
+            handle.remove()
+        self.handles.clear()
+        while self.entries:
+            parent, name, original, mlp = self.entries.pop()
             try:
-                r.abort()
-                r.runtime.close()
+                mlp.abort()
+                mlp.runtime.close()
             finally:
                 setattr(parent, name, original)
-        self.entries.clear()
-        self.closed = True
         if getattr(self.model, "_leanstream_attachment", None) is self:
             del self.model._leanstream_attachment
 
@@ -544,5 +639,7 @@ class Attachment:
 
 
 def attach_leanstream(model, *, points, weights, compute, cache_policy, prediction, mode="progressive"):
-    """Returns a lifecycle handle; keep calling the original model.forward/generate."""
+    """Attaches the B200 sparse MLP to every decoder layer of `model` and
+    returns the handle (close() restores the model); keep calling the
+    model's own forward / generate."""
     return Attachment(model, points, weights, compute, cache_policy, prediction, mode)

@@ -24,7 +24,10 @@ HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "libls_oracle.so"
 REF_DIR = HERE / "_ref"
 PREDICTOR_LIB = REF_DIR / "libls_predictor_ref.so"
-REFERENCE_ROOT = Path("/root/reference")
+# The reference checkout: $LEANSTREAM_REFERENCE, else the directory
+# `reference` beside this repository's root. It is only read to build the
+# reference objects of _ref/ (absent on machines without the checkout).
+REFERENCE_ROOT = Path(os.environ.get("LEANSTREAM_REFERENCE") or (HERE.parents[1] / "reference")).resolve()
 
 _oracle = None
 _predictor = None
@@ -34,7 +37,7 @@ def build(reference: bool = True) -> None:
     """Compiles the oracle; the reference objects too when the reference is mounted."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     if reference and REFERENCE_ROOT.exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_ROOT}"], check=True)
 
 
 def _u16(a):

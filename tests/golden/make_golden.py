@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -25,7 +26,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REFERENCE = Path("/root/reference")
+# the reference checkout: $LEANSTREAM_REFERENCE, else `reference` beside the repository root
+REFERENCE = Path(os.environ.get("LEANSTREAM_REFERENCE") or (ROOT.parent / "reference")).resolve()
 sys.path.insert(0, str(ROOT))
 
 

@@ -105,7 +105,7 @@ def test_contracts_and_inspection_on_cpu(tmp_path):
     assert report["compatible"] and report["points"].layers == "model.layers"
     assert [r["hidden"] for r in report["layers"]] == [H, H] and report["layers"][0]["intermediate"] == NG * G
     with pytest.raises(ValueError):
-        T.ranked_ids([3, 3], NG, 4)
+        T.checked_selection([3, 3], NG, 4)
 
 
 @pytest.mark.gpu
