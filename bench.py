@@ -385,18 +385,26 @@ def trace_report(st, encoded, stream, rank=0):
         for i, n in names.items()), file=sys.stderr)
     lnames = ["decided", "issued", "pieces_done", "partials_ready", "reduced", "next_ready", "loaded"]
     print("layer  " + " ".join(f"{n:>14s}" for n in lnames) + "   (median over CTAs / max)", file=sys.stderr)
-    for l in range(min(LAYERS, 6)):
+    for l in range(min(LAYERS, 12)):
         cols = []
         for w in range(7):
             v = rel(lay[:, l, w])
             cols.append(f"{np.nanmedian(v):6.1f}/{np.nanmax(v):6.1f}" if np.isfinite(v).any() else f"{'-':>13s}")
         print(f"{l:5d}  " + " ".join(f"{c:>14s}" for c in cols), file=sys.stderr)
-    print("CTA0 pieces: idx issued closed ready done (us)", file=sys.stderr)
-    for i in range(min(pieces, 40)):
-        v = rel(pcs[0, i])
-        if not np.isfinite(v).any():
-            break
-        print(f"  {i:3d} " + " ".join(f"{x:7.1f}" for x in v), file=sys.stderr)
+    wst = t[grid * 8 + grid * LAYERS * 8 + 64 * 4: grid * 8 + grid * LAYERS * 8 + 64 * 4 + 12 * 16].reshape(12, 16)
+    print("CTA0 per-warp piece completion, pieces 8..19 (us after the piece's first warp; warps 0..15)",
+          file=sys.stderr)
+    for i in range(12):
+        v = rel(wst[i])
+        if np.isfinite(v).any():
+            print(f"  {8 + i:3d} " + " ".join(f"{x - np.nanmin(v):5.2f}" for x in v), file=sys.stderr)
+    for c in range(2):
+        print(f"CTA{c} pieces: idx issued closed ready done (us)", file=sys.stderr)
+        for i in range(min(pieces, 64)):
+            v = rel(pcs[c, i])
+            if not np.isfinite(v).any():
+                break
+            print(f"  {i:3d} " + " ".join(f"{x:7.2f}" for x in v), file=sys.stderr)
 
 
 def run_gpu(args, rank, world, local_rank):

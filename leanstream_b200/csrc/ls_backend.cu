@@ -330,6 +330,7 @@ int launch(Backend& b, const ls_b200_layer_args& a, cudaStream_t stream) {
     KernelParams p = base_params(b, 1, a.trace, stream);
     p.plans = nullptr;
     p.first = plan;
+    p.lean = lean_plans(&plan, 1, p.world) ? 1u : 0u;
     b.last_epoch[a.layer] = a.epoch;
     const int grid = grid_for(b, a.candidate, &p.variant);
     rc = launch_fused(p, grid, stream);
@@ -577,6 +578,7 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.trace = a.trace;
     p.plans = nullptr;
     p.first = plan;
+    p.lean = lean_plans(&plan, 1, 1) ? 1u : 0u;
     const int grid = grid_for(b, a.candidate, &p.variant);
     rc = launch_fused(p, grid, stream);
     return rc ? cuda_rc(cudaError_t(rc)) : 0;
@@ -669,6 +671,7 @@ int ls_b200_launch_plans(void* backend, const void* device_plans, uint32_t count
     lsb::KernelParams p = lsb::base_params(*b, count, trace, static_cast<cudaStream_t>(stream));
     p.plans = static_cast<const lsb::LayerPlan*>(device_plans);
     p.first = hp[0];
+    p.lean = lsb::lean_plans(hp, count, p.world) ? 1u : 0u;
     const int grid = lsb::grid_for(*b, candidate, &p.variant);
     const int rc = lsb::launch_fused(p, grid, static_cast<cudaStream_t>(stream));
     return rc ? lsb::cuda_rc(cudaError_t(rc)) : 0;

@@ -59,7 +59,7 @@ struct alignas(16) LayerPlan {
 // kWsPollLock: 1 while one thread of the grid reads a host-memory queue.
 constexpr uint32_t kWsExit = 0, kWsErr = 1, kWsDetail = 2, kWsTag = 3, kWsPollClock = 4, kWsPollLock = 5,
                    kWsHeader = 8;
-// path, slab claim, reduction-block claim, reduced column blocks, (unused),
+// path, slab claim, (unused), reduced column blocks, (unused),
 // and for a host-memory queue:
 // queue positions mirrored into device memory, queue state (1 activated,
 // 2 failed), total_count at activation
@@ -106,7 +106,19 @@ struct KernelParams {
     // [2 slots][world][H] tagged fp32 words, mapped on every rank (xpeer[r]).
     uint32_t world, rank;
     unsigned long long* xpeer[kMaxRanks];
+    // 1 when every layer of the launch is BatchCompat / Auto on a
+    // device-memory queue and world == 1 (lean_plans): the kernel instance
+    // without the progressive, host-queue and tensor-parallel paths runs.
+    uint32_t lean;
 };
+
+// Whether a launch's plans allow the lean kernel instance.
+inline bool lean_plans(const LayerPlan* plans, uint32_t count, uint32_t world) {
+    if (world != 1) return false;
+    for (uint32_t i = 0; i < count; ++i)
+        if (plans[i].mode == LS_MODE_PROGRESSIVE || (plans[i].flags & kPlanHostQueue)) return false;
+    return true;
+}
 
 // Host-side launchers implemented in ls_kernel.cu.
 int launch_fused(const KernelParams& p, int grid, cudaStream_t stream);

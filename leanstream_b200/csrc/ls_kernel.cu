@@ -120,6 +120,13 @@ struct Geo {
     static_assert(NS <= kStages, "ring stages");
 };
 
+// Stamps the traced build keeps in shared memory: the first 64 pieces of
+// CTAs 0..3 and the first 48 layers of every CTA.
+constexpr uint32_t kTracePieces = 64, kTraceLayers = 40;
+// per-warp completion stamps of pieces [kTraceWarpBase, +kTraceWarpPieces) of CTA 0
+constexpr uint32_t kTraceWarpBase = 8, kTraceWarpPieces = 12;
+static_assert(kTracePieces <= LS_B200_PIECE_TRACE_PIECES && kTraceLayers > 0, "trace stamps");
+
 struct alignas(16) SmemTail {
     unsigned long long full_bar[kStages];
     unsigned long long empty_bar[kStages];
@@ -138,7 +145,20 @@ struct alignas(16) SmemTail {
     volatile uint32_t abort;
     volatile uint32_t flag;                // CTA-uniform decision broadcast by thread 0
     uint32_t last;
+    // Layer plans of the consumers and the epilogue warp: layer l in slot
+    // l % 3. Warp 0 of the consumers copies layer l+2's plan (cp.async) when
+    // layer l ends, and the copy is waited for before the barrier that ends
+    // the staging of layer l+1, so the plan fields read on the layer hand-off
+    // come from shared memory instead of a global round trip.
+    LayerPlan cplan[3];
+#if LS_KERNEL_TRACE
+    uint32_t tpiece[kTracePieces][4];                     // piece stamps (CTAs 0..3), see trace_piece
+    uint32_t tlayer[kTraceLayers][LS_B200_LAYER_TRACE_WORDS];  // layer stamps, see trace_layer
+    uint32_t twarp[kTraceWarpPieces][kConsumerWarps];      // per-warp piece completion (CTA 0)
+#endif
 };
+constexpr uint32_t kPlanChunks = sizeof(LayerPlan) / 16;
+static_assert(sizeof(LayerPlan) % 16 == 0, "plan copied in 16-byte chunks");
 
 // Activation of the current layer, after the tail (Geo<H>::XBYTES):
 // variant 1: three planes of signed 8-bit digits, 16 bytes per two
@@ -287,6 +307,8 @@ __device__ __forceinline__ void cp_async(uint32_t dst, const void* src) {
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
     }
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -353,7 +375,7 @@ __device__ __forceinline__ float h2f(uint16_t v) { return __half2float(__ushort_
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 __device__ __forceinline__ uint32_t* ws_layer(const KernelParams& P, uint32_t l) {
-    // [0] path [1] slab claim [2] block claim [3] reduced blocks [4] unused
+    // [0] path [1] slab claim [2] unused [3] reduced blocks [4] unused
     // [5] mirror of ready_count [6] mirror of the queue state
     return P.ws + kWsHeader + kWsPerLayer * l;
 }
@@ -369,21 +391,55 @@ __device__ __forceinline__ void trace(const KernelParams& P, uint32_t word) {
 }
 // Per-piece stamps of CTAs 0..3 after the per-layer block:
 // [4][LS_B200_PIECE_TRACE_PIECES][4] = issued, closed (producer), ready, done (consumer warp 0).
-__device__ __forceinline__ void trace_piece(const KernelParams& P, uint32_t piece, uint32_t word) {
-    if (!LS_KERNEL_TRACE) return;
-    if (P.trace && blockIdx.x < 4 && piece < LS_B200_PIECE_TRACE_PIECES)
-        P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(gridDim.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
-                (size_t(blockIdx.x) * LS_B200_PIECE_TRACE_PIECES + piece) * 4 + word] = gtimer();
+// Piece and layer stamps are kept in shared memory as the low 32 bits of
+// %globaltimer (a global store right after a burst of partial-row stores
+// can wait in the store queue and would shift the stamp) and written out
+// at the end of the launch (flush_trace).
+__device__ __forceinline__ void trace_piece(const KernelParams& P, SmemTail* t, uint32_t piece, uint32_t word) {
+#if LS_KERNEL_TRACE
+    if (P.trace && blockIdx.x < 4 && piece < kTracePieces) t->tpiece[piece][word] = uint32_t(gtimer());
+#endif
 }
 // Per-layer stamps after the launch-level block: [grid][nlayers][LS_B200_LAYER_TRACE_WORDS].
-__device__ __forceinline__ void trace_layer(const KernelParams& P, uint32_t l, uint32_t word) {
-    if (!LS_KERNEL_TRACE) return;
-    if (P.trace)
-        P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS +
-                (size_t(blockIdx.x) * P.nlayers + l) * LS_B200_LAYER_TRACE_WORDS + word] = gtimer();
+__device__ __forceinline__ void trace_layer(const KernelParams& P, SmemTail* t, uint32_t l, uint32_t word) {
+#if LS_KERNEL_TRACE
+    if (P.trace && l < kTraceLayers) t->tlayer[l][word] = uint32_t(gtimer());
+#endif
 }
+// Completion of piece `piece` by consumer warp `warp` (CTA 0, lane 0).
+__device__ __forceinline__ void trace_warp(const KernelParams& P, SmemTail* t, uint32_t piece, int warp) {
+#if LS_KERNEL_TRACE
+    if (P.trace && blockIdx.x == 0 && piece - kTraceWarpBase < kTraceWarpPieces)
+        t->twarp[piece - kTraceWarpBase][warp] = uint32_t(gtimer());
+#endif
+}
+// Writes the shared-memory stamps of this CTA to P.trace as 64-bit
+// %globaltimer values (after the final barrier of the launch).
+__device__ void flush_trace(const KernelParams& P, SmemTail* t, uint64_t entry) {
+#if LS_KERNEL_TRACE
+    if (!P.trace) return;
+    const auto full = [entry](uint32_t v) -> uint64_t {
+        return v ? entry + uint64_t(int64_t(int32_t(v - uint32_t(entry)))) : 0ull;
+    };
+    const uint32_t nl = P.nlayers < kTraceLayers ? P.nlayers : kTraceLayers;
+    for (uint32_t i = threadIdx.x; i < nl * LS_B200_LAYER_TRACE_WORDS; i += blockDim.x)
+        P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(blockIdx.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
+                i] = full(t->tlayer[i / LS_B200_LAYER_TRACE_WORDS][i % LS_B200_LAYER_TRACE_WORDS]);
+    if (blockIdx.x == 0)  // per-warp stamps: CTA 0's piece records from kTracePieces on
+        for (uint32_t i = threadIdx.x; i < kTraceWarpPieces * kConsumerWarps; i += blockDim.x)
+            P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(gridDim.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
+                    size_t(kTracePieces) * 4 + i] = full(t->twarp[i / kConsumerWarps][i % kConsumerWarps]);
+    if (blockIdx.x < 4)
+        for (uint32_t i = threadIdx.x; i < kTracePieces * 4; i += blockDim.x)
+            P.trace[size_t(gridDim.x) * LS_B200_TRACE_WORDS + size_t(gridDim.x) * P.nlayers * LS_B200_LAYER_TRACE_WORDS +
+                    (size_t(blockIdx.x) * LS_B200_PIECE_TRACE_PIECES + i / 4) * 4 + i % 4] = full(t->tpiece[i / 4][i % 4]);
+#endif
+}
+
 // Records the first error of this launch and asks the CTA to stop.
-__device__ __forceinline__ void raise_error(const KernelParams& P, SmemTail* t, uint32_t code, uint32_t detail) {
+// Out of line: an error path, kept out of the instruction-cache footprint of
+// the loops that call it.
+__device__ __noinline__ void raise_error(const KernelParams& P, SmemTail* t, uint32_t code, uint32_t detail) {
     if (atomicCAS(P.ws + kWsErr, 0u, code) == 0u) P.ws[kWsDetail] = detail;
     t->abort = 1;
 }
@@ -392,15 +448,29 @@ __device__ __forceinline__ const LayerPlan& plan_at(const KernelParams& P, uint3
     return P.plans ? P.plans[l] : P.first;
 }
 
+// Consumers' copy of layer l's plan (slot l % 3; see SmemTail::cplan).
+__device__ __forceinline__ const LayerPlan& cplan_at(const SmemTail* t, uint32_t l) { return t->cplan[l % 3]; }
+// Warp 0 of the consumers: asynchronous copy of layer l's plan into its slot
+// (multi-layer launches; a one-layer launch has its plan copied in the
+// prologue).
+__device__ __forceinline__ void fetch_plan(const KernelParams& P, SmemTail* t, uint32_t l, int tid) {
+    if (P.plans && l < P.nlayers && tid < int(kPlanChunks)) {
+        cp_async<16>(smem_u32(&t->cplan[l % 3]) + 16u * uint32_t(tid),
+                     reinterpret_cast<const uint8_t*>(P.plans + l) + 16u * uint32_t(tid));
+        cp_async_commit();
+    }
+}
+
 // ------------------------------------------------------------ descriptors
 // Descriptor at canonical position d: core[d] for d < core_count, else the
 // queue descriptor published at ready position d - core_count
 // (streaming_mlp.cu:60, persistent.py:80). Descriptor row: d for core, else
 // core_count + descriptor index (custom_triton.md:54).
+template <bool LEAN>
 __device__ DescView load_desc(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t d) {
     const uint32_t* c;
     uint32_t row;
-    if (L.flags & kPlanHostQueue) {
+    if (!LEAN && (L.flags & kPlanHostQueue)) {
         // the device copy made under the polling lease (mirror_queue)
         const uint4* e = P.qmirror + (size_t(l) * P.N + d) * 2;
         const uint4 a = e[0];
@@ -483,7 +553,7 @@ __device__ __forceinline__ void producer_close(Producer& pr, const KernelParams&
     __syncwarp();
     if (pr.lane == 0) {
         mbar_arrive(bar);
-        trace_piece(P, pr.idx, 1);
+        trace_piece(P, pr.t, pr.idx, 1);
     }
 }
 
@@ -499,7 +569,7 @@ __device__ bool producer_marker(Producer& pr, const KernelParams& P, uint32_t ki
         pc.layer = layer;
         pc.count = rows;
         pc.flags = flags;
-        trace_piece(P, pr.idx, 0);
+        trace_piece(P, pr.t, pr.idx, 0);
         mbar_arrive_expect_tx(smem_u32(&pr.t->full_bar[s]), 0);
     }
     producer_close(pr, P, s);
@@ -561,7 +631,7 @@ __device__ __forceinline__ bool producer_piece(Producer& pr, const KernelParams&
         pc.count = cnt;
         pc.need = need;
         pc.flags = flags;
-        trace_piece(P, pr.idx, 0);
+        trace_piece(P, pr.t, pr.idx, 0);
         mbar_arrive_expect_tx(bar, cnt * bytes);
     }
     __syncwarp();
@@ -678,12 +748,13 @@ __device__ bool producer_slab(Producer& pr, const KernelParams& P, const LayerPl
 
 // Loads the descriptor window [base, base+32) into shared memory, one
 // descriptor per lane.
+template <bool LEAN>
 __device__ bool producer_window(Producer& pr, const KernelParams& P, const LayerPlan& L, uint32_t layer,
                                 uint32_t base, uint32_t D) {
     const uint32_t d = base + pr.lane;
     uint32_t bad = 0;
     if (d < D) {
-        const DescView v = load_desc(P, L, layer, d);
+        const DescView v = load_desc<LEAN>(P, L, layer, d);
         pr.t->dtab[pr.lane] = v;
         bad = v.ok ? 0u : 1u;
     }
@@ -873,8 +944,11 @@ __device__ void stamp(const LayerPlan& L, const DescView& d) {
     if (L.stamps) L.stamps[d.dest] = gtimer();
 }
 
-// Producer warp main loop over the layers of the launch.
-template <int H, bool F>
+// Producer warp main loop over the layers of the launch. LEAN: every layer
+// of the launch takes the fast path (BatchCompat / Auto plans on a
+// device-memory queue, one GPU), so the progressive claim loop and the
+// host-queue reads are not compiled in.
+template <int H, bool F, bool LEAN>
 __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     Producer pr;
     pr.idx = 0;
@@ -892,14 +966,14 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
         uint32_t total = 0;
         const uint32_t path = decide(P, L, l, t, deadline, pr.lane, &total);
         if (pr.lane == 0 && l == 0) trace(P, LS_B200_TRACE_DECIDED);
-        if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_DECIDED);
+        if (pr.lane == 0) trace_layer(P, t, l, LS_B200_LTRACE_DECIDED);
         if (path == kPathAbort) break;
         const uint32_t D = L.core_count + total;
         const uint32_t NS = D * spg;
         pr.wbase = pr.wlayer = 0xffffffffu;
         PendingDown pd;
         pd.valid = false;
-        if (path == kPathFast) {
+        if (LEAN || path == kPathFast) {
             // Static balanced split of the layer's slab positions.
             const uint32_t b = blockIdx.x, grid = gridDim.x;
             const uint32_t u1 = uint32_t(uint64_t(NS) * (b + 1) / grid);
@@ -908,13 +982,14 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
             const uint32_t dend = u1 ? (u1 - 1) / spg + 1 : 0;
             for (uint32_t u = uint32_t(uint64_t(NS) * b / grid); ok && u < u1; ++u) {
                 const uint32_t d = u / spg, slab = u % spg;
-                if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32) ok = producer_window(pr, P, L, l, d, dend);
+                if (pr.wlayer != l || d < pr.wbase || d >= pr.wbase + 32)
+                    ok = producer_window<LEAN>(pr, P, L, l, d, dend);
                 if (!ok) break;
                 const DescView dv = t->dtab[d - pr.wbase];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
                 ok = producer_slab<H, F>(pr, P, L, dv, l, slab, pd);
             }
-        } else {
+        } else if constexpr (!LEAN) {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(L.q.control);
             uint32_t* claim = ws_layer(P, l) + 1;
             const bool host_queue = (L.flags & kPlanHostQueue) != 0;
@@ -993,7 +1068,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
                     if (code) break;
                 }
                 const uint32_t d = pos / spg, slab = pos % spg;
-                ok = producer_window(pr, P, L, l, d, d + 1);  // one descriptor, lane 0
+                ok = producer_window<LEAN>(pr, P, L, l, d, d + 1);  // one descriptor, lane 0
                 if (!ok) break;
                 const DescView dv = t->dtab[0];
                 if (slab == 0 && pr.lane == 0) stamp(L, dv);
@@ -1002,7 +1077,7 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
             if (t->abort) ok = false;
         }
         if (ok) ok = producer_slab_down<H, F>(pr, P, L, pd, l);
-        if (pr.lane == 0) trace_layer(P, l, LS_B200_LTRACE_ISSUED);
+        if (pr.lane == 0) trace_layer(P, t, l, LS_B200_LTRACE_ISSUED);
         if (ok) ok = producer_marker<H>(pr, P, kPieceLayer, l, NS, t->abort ? 0u : kLayerGood);
     }
     producer_marker<H>(pr, P, kPieceFinal, 0, 0, 0);
@@ -1066,6 +1141,17 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
                         int tid, bool tagged, uint32_t tag) {
     constexpr int NU = H / 8, UPT = Geo<H>::UPT;  // units u = tid + j * 512, j < UPT
     const int warp = tid >> 5, lane = tid & 31;
+    // The norm weights do not depend on the input: their loads are in flight
+    // while the input is polled.
+    const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
+    const bool weighted = norm && L.norm_w;
+    uint4 nw[UPT];
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+        const int u = tid + j * kConsumerThreads;
+        nw[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (weighted && u < NU) nw[j] = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + u);
+    }
     uint4 raw[UPT];
     float ss = 0.f;
 #pragma unroll
@@ -1104,15 +1190,6 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
             ss = fmaf(v.x, v.x, ss);
             ss = fmaf(v.y, v.y, ss);
         }
-    }
-    const bool norm = (L.flags & LS_B200_NORM_INPUT) != 0;
-    const bool weighted = norm && L.norm_w;
-    uint4 nw[UPT];
-#pragma unroll
-    for (int j = 0; j < UPT; ++j) {
-        const int u = tid + j * kConsumerThreads;
-        nw[j] = make_uint4(0u, 0u, 0u, 0u);
-        if (weighted && u < NU) nw[j] = __ldg(reinterpret_cast<const uint4*>(L.norm_w) + u);
     }
     // One reduction round: sum of squares (RMSNorm) and, for variant 1, the
     // maxima of |x| and |w| that bound max|x'| for the fixed-point exponent.
@@ -1212,6 +1289,7 @@ __device__ void stage_x(const KernelParams& P, const LayerPlan& L, SmemTail* t, 
             reinterpret_cast<uint4*>(xarea<H>(t))[u] = f;
         }
     }
+    if (tid < int(kPlanChunks)) cp_async_wait_all();  // the next layer's plan (fetch_plan), visible after the barrier
     csync(P, t, cph, limit, lane);
 }
 
@@ -1695,9 +1773,15 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
             v0 = fmaf(k, v0, hsum8);
             v1 = fmaf(k, v1, hsum8);
         }
-        unsigned long long* o = out + 64 * tile + 8 * g + tq;
-        st_volatile_u64(o, tag | __float_as_uint(v0));
-        st_volatile_u64(o + 4, tag | __float_as_uint(v1));
+        // One exchange with the neighbour lane gives every lane two adjacent
+        // columns: even t keeps 8g+t and takes 8g+t+1, odd t takes 8g+t+3 and
+        // keeps 8g+t+4. A warp then writes its tile's 64 tagged words with
+        // one 16-byte store per lane, 512 contiguous bytes (full sectors).
+        const float send = (tq & 1) ? v0 : v1;
+        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+        const float lo = (tq & 1) ? recv : v0, hi = (tq & 1) ? v1 : recv;
+        st_volatile_v2u64(out + 64 * tile + 8 * g + ((tq & 1) ? tq + 3 : tq), tag | __float_as_uint(lo),
+                          tag | __float_as_uint(hi));
     }
 }
 
@@ -1745,21 +1829,17 @@ __device__ __forceinline__ void emit_column(const KernelParams& P, const LayerPl
 // sums in warp order (reduction.py:6-28, streaming_mlp.cu:80-84 sum rows in
 // row order). With `chain`, hidden_out is also published as tagged fp16 pairs
 // for the next layer of the launch.
-template <int H>
+template <int H, bool LEAN>
 __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l, uint32_t rows, bool good,
                           SmemTail* t, uint32_t& cph, uint64_t limit, int tid, bool chain) {
     constexpr uint32_t NBLK = H / 32;
     const int warp = tid >> 5, lane = tid & 31;
-    uint32_t blk0 = blockIdx.x, step = gridDim.x;
-    if (gridDim.x >= NBLK) {
-        // One column block per CTA, handed out in the order in which the CTAs
-        // reach the end of the layer: a CTA still busy with its last pieces
-        // does not hold up a block's reduction.
-        if (tid == 0) t->flag = atomicAdd(ws_layer(P, l) + 2, 1u);
-        csync(P, t, cph, limit, lane);
-        blk0 = t->flag;
-        step = NBLK;
-    }
+    // CTA b reduces column blocks b, b + grid, ... (one block each with a
+    // full grid). A fixed assignment costs no claim round trip at the end of
+    // every layer; a reducer that is still computing when the other rows are
+    // in reads them in one round trip, as an early reducer would detect its
+    // last rows.
+    const uint32_t blk0 = blockIdx.x, step = gridDim.x;
     if (blk0 >= NBLK) return;
     const uint32_t tag = scratch_tag(t, l);
     const uint32_t nch = (rows + 15) / 16;
@@ -1803,12 +1883,12 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         t->red2[warp][lane] = acc;
         csync(P, t, cph, limit, lane);
         if (warp == 0) {
-            if (blk == blk0 && lane == 0) trace_layer(P, l, LS_B200_LTRACE_PARTIALS_READY);
+            if (blk == blk0 && lane == 0) trace_layer(P, t, l, LS_B200_LTRACE_PARTIALS_READY);
             float y = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
             const uint32_t c = 32 * blk + lane;
-            if (P.world > 1) {
+            if (!LEAN && P.world > 1) {
                 // Tensor parallel: this rank's fp32 partial of the column goes
                 // to every rank's exchange buffer over NVLink (peer stores);
                 // the ranks' partials are summed in the gather pass below.
@@ -1822,7 +1902,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         }
         csync(P, t, cph, limit, lane);  // red2 is reused by the next block
     }
-    if (P.world > 1 && warp == 0) {
+    if (!LEAN && P.world > 1 && warp == 0) {
         // Gather pass (tensor parallel): every block of this CTA was published
         // above, so no rank waits on another while holding back its own. Each
         // block's columns of every rank are read from the local exchange
@@ -1869,7 +1949,7 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         __syncwarp();
         if (lane == 0) red_release_gpu(ws_layer(P, l) + 3, 1u);
     }
-    if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_REDUCED);
+    if (tid == 0) trace_layer(P, t, l, LS_B200_LTRACE_REDUCED);
 }
 
 // Sums of neuron i's gate and up warp partials ([warp][8] float2 in a
@@ -1913,6 +1993,7 @@ __device__ bool wait_phase(const KernelParams& P, SmemTail* t, uint32_t bar, uin
             if (lane == 0 && !t->abort) raise_error(P, t, LS_B200_DEV_TIMEOUT_SYNC, detail);
             return false;
         }
+        __nanosleep(32);  // the epilogue warp shares a scheduler with four consumer warps
     }
 }
 
@@ -1935,14 +2016,14 @@ __device__ bool wait_full(SmemTail* t, uint32_t idx, uint64_t deadline, int lane
     }
 }
 
-template <int H, bool F>
+template <int H, bool F, bool LEAN>
 __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* t, uint64_t deadline) {
     constexpr uint32_t NBLK = H / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint64_t limit = deadline + kSyncGraceNs;
     uint32_t cph = 0;  // consumer-barrier phase
     uint32_t l = 0;
-    const LayerPlan* L = &plan_at(P, 0);
+    const LayerPlan* L = &cplan_at(t, 0);  // slots 0 and 1 were filled in the prologue
     stage_x<H, F>(P, *L, t, cph, limit, tid, false, 0);
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % Geo<H>::NS;
@@ -1953,9 +2034,9 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             break;
         }
         const Piece pc = t->piece[s];
-        if (tid == 0) trace_piece(P, idx, 2);
+        if (tid == 0) trace_piece(P, t, idx, 2);
         if (idx == 0 && tid == 0) trace(P, LS_B200_TRACE_FIRST);
-        if (tid == 0 && pc.kind == kPieceLayer) trace_layer(P, l, LS_B200_LTRACE_PIECES_DONE);
+        if (tid == 0 && pc.kind == kPieceLayer) trace_layer(P, t, l, LS_B200_LTRACE_PIECES_DONE);
         if (pc.kind == kPieceFinal) {
             if (tid == 0) trace(P, LS_B200_TRACE_PIECES);
             break;
@@ -1971,12 +2052,13 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
                     }
                     const uint32_t s2 = (idx + 1) % Geo<H>::NS;
                     const Piece pc2 = t->piece[s2];
-                    if (tid == 0) trace_piece(P, idx + 1, 2);
+                    if (tid == 0) trace_piece(P, t, idx + 1, 2);
                     consume_gateup_pair<H>(P, *L, pc, pc2, st, stages + size_t(s2) * kStageBytes, t, s, warp, lane);
                     __syncwarp();
+                    if (lane == 0) trace_warp(P, t, idx + 1, warp);
                     if (tid == 0) {
-                        trace_piece(P, idx, 3);
-                        trace_piece(P, idx + 1, 3);
+                        trace_piece(P, t, idx, 3);
+                        trace_piece(P, t, idx + 1, 3);
                     }
                     if (lane == 0) {
                         mbar_arrive(smem_u32(&t->empty_bar[s]));
@@ -2013,7 +2095,8 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
             }
         }
         __syncwarp();
-        if (tid == 0) trace_piece(P, idx, 3);
+        if (tid == 0) trace_piece(P, t, idx, 3);
+        if (lane == 0) trace_warp(P, t, idx, warp);
         if (lane == 0) mbar_arrive(smem_u32(&t->empty_bar[s]));
         if (pc.kind != kPieceLayer) continue;
 
@@ -2021,21 +2104,22 @@ __device__ void run_consumers(const KernelParams& P, uint8_t* stages, SmemTail* 
         // Chained layers (the next input is this layer's hidden_out) hand the
         // activation over through tagged words; otherwise every CTA waits
         // until all column blocks are reduced and reads the next input.
-        const LayerPlan* next = l + 1 < P.nlayers ? &plan_at(P, l + 1) : nullptr;
+        fetch_plan(P, t, l + 2, tid);  // slot (l+2) % 3 held layer l-1, whose hand-off is over
+        const LayerPlan* next = l + 1 < P.nlayers ? &cplan_at(t, l + 1) : nullptr;
         const bool chain = next && L->hidden_out && L->residual &&
                            reinterpret_cast<const void*>(next->x) == reinterpret_cast<const void*>(L->hidden_out);
-        end_layer<H>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid, chain);
+        end_layer<H, LEAN>(P, *L, l, pc.count, (pc.flags & kLayerGood) != 0, t, cph, limit, tid, chain);
         if (!next) continue;  // the FINAL marker follows
         if (!chain) {
             if (tid == 0) wait_count(P, t, ws_layer(P, l) + 3, NBLK, limit, 6);
             csync(P, t, cph, limit, lane);
         }
-        if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_NEXT_READY);
+        if (tid == 0) trace_layer(P, t, l, LS_B200_LTRACE_NEXT_READY);
         const uint32_t tag = scratch_tag(t, l);
         ++l;
         L = next;
         stage_x<H, F>(P, *L, t, cph, limit, tid, chain, tag);
-        if (tid == 0) trace_layer(P, l, LS_B200_LTRACE_LOADED);
+        if (tid == 0) trace_layer(P, t, l, LS_B200_LTRACE_LOADED);
     }
 }
 
@@ -2053,13 +2137,15 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
     float2 carry = make_float2(0.f, 0.f);  // gate/up sums of a slab's first K part
     for (uint32_t idx = 0;; ++idx) {
         const uint32_t s = idx % Geo<H>::NS;
-        if (!wait_full<H>(t, idx, deadline, lane)) break;  // the consumers report it
+        // back off between polls: this warp shares a scheduler with four
+        // consumer warps, whose pieces finish at the pace of the slowest
+        if (!wait_full<H>(t, idx, deadline, lane, 64)) break;  // the consumers report it
         const Piece pc = t->piece[s];
         if (pc.kind == kPieceFinal) break;
         if (pc.kind == kPieceGateUp) {
             if (!wait_phase(P, t, smem_u32(&t->pbar[s]), (phases >> s) & 1u, limit, lane, 10)) break;
             phases ^= 1u << s;
-            const LayerPlan& L = plan_at(P, pc.layer);
+            const LayerPlan& L = cplan_at(t, pc.layer);
             const uint32_t buf = (pc.flags & kHsBuf) ? 1u : 0u;
             const bool paired = F && (pc.flags & kPaired);
             uint32_t s2 = s, cnt = pc.count, n0 = pc.n0, i = uint32_t(lane);
@@ -2106,13 +2192,13 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
     }
 }
 
-template <int H, bool F>
+template <int H, bool F, bool LEAN>
 __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_constant__ KernelParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
     SmemTail* t = reinterpret_cast<SmemTail*>(smem + size_t(Geo<H>::NS) * kStageBytes);
     const int tid = threadIdx.x;
-    const uint64_t deadline = gtimer() + P.timeout_ns;
+    const uint64_t entry = gtimer(), deadline = entry + P.timeout_ns;
     if (tid == 0) {
         trace(P, LS_B200_TRACE_ENTRY);
         for (int s = 0; s < Geo<H>::NS; ++s) {
@@ -2132,14 +2218,23 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
         t->last = 0;
         fence_mbar_init();
     }
+#if LS_KERNEL_TRACE
+    for (uint32_t i = tid; i < kTracePieces * 4; i += blockDim.x) (&t->tpiece[0][0])[i] = 0u;
+    for (uint32_t i = tid; i < kTraceLayers * LS_B200_LAYER_TRACE_WORDS; i += blockDim.x) (&t->tlayer[0][0])[i] = 0u;
+    for (uint32_t i = tid; i < kTraceWarpPieces * kConsumerWarps; i += blockDim.x) (&t->twarp[0][0])[i] = 0u;
+#endif
+    if (tid < int(2 * kPlanChunks) && uint32_t(tid) / kPlanChunks < P.nlayers) {
+        const uint32_t l = uint32_t(tid) / kPlanChunks, c = uint32_t(tid) % kPlanChunks;
+        reinterpret_cast<uint4*>(&t->cplan[l])[c] = reinterpret_cast<const uint4*>(&plan_at(P, l))[c];
+    }
     __syncthreads();
 
     if (tid >= kConsumerThreads + 32) {
         run_epilogue<H, F>(P, stages, t, deadline);
     } else if (tid >= kConsumerThreads) {
-        run_producer<H, F>(P, stages, t, deadline);
+        run_producer<H, F, LEAN>(P, stages, t, deadline);
     } else {
-        run_consumers<H, F>(P, stages, t, deadline);
+        run_consumers<H, F, LEAN>(P, stages, t, deadline);
     }
     __syncthreads();
     if (tid == 0) {
@@ -2177,20 +2272,28 @@ __global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const __grid_con
             st_relaxed_sys(P.status + LS_B200_STATUS_LAUNCHES, next_base);
         }
     }
+    flush_trace(P, t, entry);
     if (tid == 0) trace(P, LS_B200_TRACE_EXIT);
 }
 
 template <int H, bool F>
 static int launch_t(const KernelParams& p, int grid, cudaStream_t stream) {
-    fused_mlp_kernel<H, F><<<grid, kThreads, kernel_smem_bytes<H>(), stream>>>(p);
+    if (p.lean)
+        fused_mlp_kernel<H, F, true><<<grid, kThreads, kernel_smem_bytes<H>(), stream>>>(p);
+    else
+        fused_mlp_kernel<H, F, false><<<grid, kThreads, kernel_smem_bytes<H>(), stream>>>(p);
     return int(cudaGetLastError());
 }
 
 template <int H, bool F>
 static cudaError_t raise_smem() {
     static_assert(kernel_smem_bytes<H>() <= 232448, "dynamic shared memory of one CTA");
-    return cudaFuncSetAttribute(fused_mlp_kernel<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(kernel_smem_bytes<H>()));
+    cudaError_t e = cudaFuncSetAttribute(fused_mlp_kernel<H, F, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(kernel_smem_bytes<H>()));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fused_mlp_kernel<H, F, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kernel_smem_bytes<H>()));
+    return e;
 }
 
 int prepare() {
@@ -2204,7 +2307,8 @@ int prepare() {
 }
 
 // H in {256, 512, 1024, 2048, 4096, 8192}; variant 0 up to 4096 (the
-// backend selects variant 1 above).
+// backend selects variant 1 above). p.lean selects the instance without the
+// progressive, host-queue and tensor-parallel paths.
 int launch(const KernelParams& p, int grid, cudaStream_t stream) {
     const bool f = p.variant != 0;
     switch (p.H) {
