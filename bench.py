@@ -239,6 +239,201 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- GPU arm
+def shard_weights(layer: int, rank: int, nloc: int, dev):
+    """Packed INT4 groups and fp16 scales of rank `rank`'s `nloc` groups of
+    one layer, drawn on the device from a seed of (layer, rank), so any rank
+    can regenerate another rank's shard. Zero-mean signed nibbles, uniform in
+    [-7, 7] as the reference quantizer produces
+    (examples/ministral/pack/int4_format.py:16); a [-8, 7] draw has mean
+    -0.5, and through the residual stack that bias feeds back into gate/up
+    until fp16 overflows."""
+    import torch
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 * SEED + 17 * layer + rank)
+    nib = torch.randint(-7, 8, (2, nloc * GROUP_BYTES), dtype=torch.int16, device=dev, generator=gen)
+    packed = ((nib[0] & 15) | ((nib[1] & 15) << 4)).to(torch.uint8)
+    del nib
+    s = torch.empty(nloc * G * 3 * (H // 128), dtype=torch.float32, device=dev)
+    s.uniform_(0.005, 0.02, generator=gen)
+    return packed, s.half()
+
+
+PARITY_LAYERS = 3  # layers of one token checked against the oracle after the timed region
+
+
+def stack_parity(st, graph, token: int, world: int, rank: int):
+    """Oracle check of the first PARITY_LAYERS layers of token `token`, run
+    through its own graph after the timed region, on every rank:
+    * the ranks' hidden states are all-gathered and must be bit-identical
+      (the in-kernel exchange sums the same partials in the same order);
+    * on rank 0, each layer equals the oracle: RMSNorm of the layer's input,
+      every rank's sparse MLP over its own shard (regenerated from the
+      shard seeds), the fp32 partials summed, one fp16 rounding and the
+      residual (backends/triton/reduction.py:14-20)."""
+    import torch
+    import torch.distributed as dist
+
+    from leanstream_b200.tp import local_groups, rank_descriptors
+
+    graph.replay()
+    torch.cuda.synchronize()
+    xs = torch.stack([st.xs[l] for l in range(PARITY_LAYERS + 1)])
+    identical = True
+    if world > 1:
+        gathered = [torch.empty_like(xs) for _ in range(world)]
+        dist.all_gather(gathered, xs)
+        identical = all(torch.equal(gathered[0], g) for g in gathered[1:])
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+
+    x_host = xs.cpu().numpy()
+    sets = active_sets(token)
+    worst, bound_min, ok = 0.0, None, identical
+    for l in range(PARITY_LAYERS):
+        x_l = x_host[l]
+        xin = O.rmsnorm(x_l, None, EPS)
+        total = np.zeros(H, np.float32)
+        for r in range(world):
+            rows = rank_descriptors(sets[l], r, world)
+            if not len(rows):
+                continue
+            nloc = len(local_groups(NGROUPS, r, world))
+            packed, sc = (st.cache[l], st.scales[l]) if r == rank else shard_weights(l, r, nloc, st.dev)
+            _, y32, _ = O.mlp(H, G, xin, packed.cpu().numpy(), sc.cpu().numpy(), rows)
+            total += y32
+        ref = O.residual(x_l, total.astype(np.float16)).astype(np.float32)
+        got = x_host[l + 1].astype(np.float32)
+        err = float(np.abs(got - ref).max())
+        bound = 2e-3 * float(np.abs(ref).max()) + 1e-3
+        worst = max(worst, err)
+        bound_min = bound if bound_min is None else min(bound_min, bound)
+        ok = ok and bool(np.isfinite(got).all()) and err <= bound
+    return {"ok": ok, "token": token, "layers_checked": PARITY_LAYERS, "max_abs": worst, "bound": bound_min,
+            "ranks_identical": identical,
+            "rule": "per layer: max|x_{l+1} - oracle| <= 2e-3 max|oracle| + 1e-3, oracle = fp16(x_l + "
+                    "fp16(sum over ranks of fp32 partials)); ranks all-gathered bit-identical"}
+
+
+CONFIG2_GROUPS = 58  # BASELINE.json configuration 2: round(0.3 * 192) groups, all resident and READY
+
+
+def run_layer_path(st, args, stream, world):
+    """The reference's per-layer call path on this backend: every layer is
+    one ComputeBackend.enqueue (ls_b200_view) as LayerStep::enqueue_compute
+    issues it (src/runtime/runtime.cpp:36-43), one launch per layer.
+
+    * config 2: one H 4096 layer, 58 of 192 groups, all resident and READY
+      (BatchCompat plan in device memory), no norm or residual; the launches
+      cycle over the stack's 36 weight sets with a seeded 58-group set each
+      (36 x 23.5 MB, far above the 126 MB L2, so every launch streams its
+      weights from HBM). Reported as us per layer (GPU time of `reps` launches
+      captured in one CUDA graph, and the same launches issued from the host).
+    * config 3, one launch per layer: the timed tokens' 36 layers chained
+      through per-layer enqueues (RMSNorm input, residual hidden_out), one
+      CUDA graph per token, tokens/s.
+    Both use the bound buffers of ls_b200_set_buffers for the per-layer
+    weights, as the reference's TritonBackend binds its MLP buffers."""
+    import torch
+
+    from leanstream_b200 import _native as N
+    from leanstream_b200.tp import local_groups, rank_descriptors
+
+    be = st.backend
+    vb = be.view()
+    span = N.ExecSpan(None, 0)
+    img = torch.zeros((LAYERS, st.slot_words), dtype=torch.int32, pin_memory=True)
+    sets = []
+    for layer in range(LAYERS):
+        ids = np.sort(np.random.default_rng([SEED, 2, layer]).permutation(NGROUPS)[:CONFIG2_GROUPS])
+        sets.append(ids)
+        st._write_plan(img[layer], ids)
+    img_dev = img.to(st.dev)
+    views = [st.queue_view(img_dev[layer]) for layer in range(LAYERS)]
+    x, y = st.xs[0], st.y
+
+    def enqueue_c2(i, strm):
+        layer = i % LAYERS
+        be.set_buffers(cache=st.cache[layer], scales=st.scales[layer])
+        rc = vb.enqueue(vb.context, layer, x.data_ptr(), y.data_ptr(), strm, span, views[layer], 1,
+                        N.MODE_BATCH_COMPAT)
+        if rc:
+            raise RuntimeError(f"ComputeBackend.enqueue returned {rc}")
+
+    reps = 4 * LAYERS
+    with torch.cuda.stream(stream):
+        for i in range(LAYERS):
+            enqueue_c2(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(reps):
+            enqueue_c2(i, torch.cuda.current_stream().cuda_stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        g.replay()  # warm-up
+        ev[0].record(stream)
+        g.replay()
+        ev[1].record(stream)
+        ev[2].record(stream)
+        for i in range(reps):
+            enqueue_c2(i, stream.cuda_stream)
+        ev[3].record(stream)
+    torch.cuda.synchronize()
+    us_graph = ev[0].elapsed_time(ev[1]) * 1e3 / reps
+    us_host = ev[2].elapsed_time(ev[3]) * 1e3 / reps
+    g.reset()
+    local = [len(rank_descriptors(ids, st.rank, world)) for ids in sets]
+    layer_bytes = float(np.mean(local)) * ALG_BYTES_PER_GROUP
+    out = {"config2": {
+        "metric": "us per layer (config 2: one H4096/I12288 layer, 58 of 192 groups READY, BatchCompat) through "
+                  "ComputeBackend.enqueue of ls_b200_view, one launch per layer",
+        "value": us_graph, "unit": "us/layer", "higher_is_better": False,
+        "host_launched_us_per_layer": us_host,
+        "launches": reps, "target_us_at_70pct_of_8TBs": 4.20,
+        "roofline": {"bound": "hbm", "achieved": layer_bytes / (us_graph * 1e-6) / 1e9, "unit": "GB/s",
+                     "bytes_per_layer_per_rank": layer_bytes},
+        "l2": "launches cycle over 36 weight sets (~845 MB), each read from HBM"}}
+
+    # config 3 through one enqueue per layer
+    tok_graphs = []
+    for k in range(args.steps):
+        s = args.warmup + k
+        gk = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gk, stream=stream):
+            cs = torch.cuda.current_stream().cuda_stream
+            for layer in range(LAYERS):
+                be.set_buffers(cache=st.cache[layer], scales=st.scales[layer], flags=N.NORM_INPUT,
+                               residual=st.xs[layer], hidden_out=st.xs[layer + 1])
+                rc = vb.enqueue(vb.context, layer, st.xs[layer].data_ptr(), y.data_ptr(), cs, span,
+                                st.queue_view(st.plans_dev[s][layer]), 1, N.MODE_BATCH_COMPAT)
+                if rc:
+                    raise RuntimeError(f"ComputeBackend.enqueue returned {rc}")
+        tok_graphs.append(gk)
+    with torch.cuda.stream(stream):
+        tok_graphs[0].replay()
+        ev[0].record(stream)
+        for gk in tok_graphs:
+            gk.replay()
+        ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1])
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, us_graph], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, out["config2"]["value"] = float(t[0].item()), float(t[1].item())
+    for gk in tok_graphs:
+        gk.reset()
+    out["config3_per_layer_launches"] = {
+        "metric": "MLP-stack tokens/s, config 3 with one ComputeBackend.enqueue (one launch) per layer",
+        "value": args.steps / (ms * 1e-3), "unit": "tokens/s", "us_per_layer": ms * 1e3 / (args.steps * LAYERS),
+        "launches_per_token": LAYERS}
+    return out
+
+
 class Stack:
     """Device state of one rank: weights of its groups for every layer, plan
     images (ExecutionQueue ready descriptors) and activation buffers."""
@@ -259,18 +454,9 @@ class Stack:
         gen = torch.Generator(device=dev)
         self.cache, self.scales = [], []
         for layer in range(LAYERS):
-            gen.manual_seed(1000 * SEED + 17 * layer + rank)
-            # zero-mean signed nibbles, uniform in [-7, 7] as the reference
-            # quantizer produces (examples/ministral/pack/int4_format.py:16);
-            # a [-8, 7] draw has mean -0.5, and through 36 residual layers that
-            # bias feeds back into gate/up until fp16 overflows.
-            nib = torch.randint(-7, 8, (2, self.nloc * GROUP_BYTES), dtype=torch.int16, device=dev, generator=gen)
-            packed = ((nib[0] & 15) | ((nib[1] & 15) << 4)).to(torch.uint8)
-            del nib
+            packed, sc = shard_weights(layer, rank, self.nloc, dev)
             self.cache.append(packed)
-            s = torch.empty(self.nloc * G * 3 * (H // 128), dtype=torch.float32, device=dev)
-            s.uniform_(0.005, 0.02, generator=gen)
-            self.scales.append(s.half())
+            self.scales.append(sc)
         gen.manual_seed(SEED)
         self.x0 = torch.randn(H, device=dev, generator=gen).half()
         self.xs = [torch.zeros(H, dtype=torch.float16, device=dev) for _ in range(LAYERS + 1)]
@@ -412,14 +598,6 @@ def run_gpu(args, rank, world, local_rank):
     import torch.distributed as dist
 
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        # NCCL carries only host-side setup and the timing reduction; a rank
-        # that dies while bound to an NVLink multicast object can fault the
-        # other GPUs, so NVLS stays off.
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     steps_total = args.warmup + args.steps
     t_start = time.time()
 
@@ -485,6 +663,11 @@ def run_gpu(args, rank, world, local_rank):
         raise RuntimeError(f"device status {status}")
     ms_per_step = ms / args.steps
     progress(f"timed region: {ms_per_step:.3f} ms per token")
+    barrier()
+    with torch.cuda.stream(stream):
+        parity = stack_parity(st, graphs[args.warmup], args.warmup, world, rank)
+    barrier()
+    progress(f"parity of {PARITY_LAYERS} layers: {parity}")
 
     # ---- kernel-only durations: pre-queued, event-bracketed multi-layer
     # launches (N GPUs: each rank's launch over its own groups, including the
@@ -512,6 +695,13 @@ def run_gpu(args, rank, world, local_rank):
     if args.trace:
         barrier()
         trace_report(st, encoded[args.warmup], stream, rank)
+    layer_path = None
+    if CONFIG == 3 and not args.headline_only and not args.layers:
+        barrier()
+        layer_path = run_layer_path(st, args, stream, world)
+        barrier()
+        progress(f"per-layer enqueue path: {layer_path['config2']['value']:.2f} us per config-2 layer, "
+                 f"{layer_path['config3_per_layer_launches']['value']:.0f} tokens/s with one launch per layer")
 
     # ---- e2e: host plans + host x in, host y out, through the C ABI each step
     barrier()
@@ -597,7 +787,10 @@ def run_gpu(args, rank, world, local_rank):
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches_per_token * args.steps,
             "clocks": clock,
+            "parity": parity,
         }
+        if layer_path:
+            result.update(layer_path)
     # Release every graph before tearing down the process group: a graph that
     # still holds NCCL work keeps destroy_process_group waiting for good (the
     # capture loop's own variable referenced the last token graph).
@@ -610,7 +803,7 @@ def run_gpu(args, rank, world, local_rank):
     progress("graphs released")
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+    del st
     progress("done")
     return result
 
@@ -925,6 +1118,8 @@ def main():
                    help="BASELINE.json configuration: 3 (headline, H 4096, 36 layers) or 5 (H 8192, 80 layers)")
     p.add_argument("--batch", type=int, choices=[1, 8], default=1,
                    help="tokens per step: 1 (the default workload) or 8 (union decode, one GPU)")
+    p.add_argument("--headline-only", action="store_true",
+                   help="skip the extra measurements printed beside the headline (per-layer enqueue path, config 5)")
     p.add_argument("--layers", type=int, default=0,
                    help="stack depth; smaller values only for profiling captures (the metric is quoted at the "
                         "configuration's depth)")
@@ -948,15 +1143,68 @@ def main():
         if res is not None:
             print(json.dumps(res), flush=True)
         return
+    import torch
+
+    if world > 1:
+        from datetime import timedelta
+
+        import torch.distributed as dist
+
+        # NCCL carries only host-side setup, the parity gather and the timing
+        # reductions; a rank that dies while bound to an NVLink multicast
+        # object can fault the other GPUs, so NVLS stays off.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     res = run_batch(args, rank, world, local_rank) if args.batch == BATCH else run_gpu(args, rank, world, local_rank)
+    if rank == 0 and res is not None and world == 1 and not args.no_cpu_baseline:
+        try:
+            res["cpu_baseline"] = cpu_stack_rate()
+        except Exception as exc:  # the oracle library is test infrastructure; report why it is absent
+            res["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "port",
+                                   "sample": f"unavailable: {exc}"}
+    if CONFIG == 3 and args.batch == 1 and not args.headline_only and not args.layers:
+        res5 = run_config5(args, rank, world, local_rank)
+        if rank == 0 and res is not None:
+            res.update(res5)
     if rank == 0 and res is not None:
-        if world == 1 and not args.no_cpu_baseline:
-            try:
-                res["cpu_baseline"] = cpu_stack_rate()
-            except Exception as exc:  # the oracle library is test infrastructure; report why it is absent
-                res["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "port",
-                                       "sample": f"unavailable: {exc}"}
         print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _summary(r: dict) -> dict:
+    keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "us_per_layer", "roofline",
+            "e2e", "parity", "gpu_launches", "config", "clocks")
+    return {k: r[k] for k in keep if k in r}
+
+
+def run_config5(args, rank, world, local_rank) -> dict:
+    """BASELINE.json configuration 5 beside the headline, in the same run:
+    batch 1 at N GPUs (the tensor-parallel launch at N > 1) and, on one GPU,
+    batch 8 over the union of the tokens' active groups. Fewer steps than
+    the headline (each step is an 80-layer token of ~5.8 GB of weights)."""
+    import argparse as _ap
+
+    set_config(5)
+    a = _ap.Namespace(**vars(args))
+    a.steps, a.warmup, a.trace, a.batch = min(args.steps, 10), 3, False, 1
+    out = {}
+    r = run_gpu(a, rank, world, local_rank)
+    if rank == 0:
+        out["config5_batch1"] = _summary(r)
+    if world == 1:
+        global METRIC, WORKLOAD
+        metric, workload = METRIC, WORKLOAD
+        METRIC = METRIC.replace("batch-1 decode", f"batch-{BATCH} union decode")
+        WORKLOAD = WORKLOAD.replace("batch 1", f"batch {BATCH} over the union of the tokens' active groups")
+        a.batch = BATCH
+        out["config5_batch8"] = _summary(run_batch(a, rank, world, local_rank))
+        METRIC, WORKLOAD = metric, workload
+    return out
 
 
 if __name__ == "__main__":

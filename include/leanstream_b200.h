@@ -251,8 +251,12 @@ int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream);
  * launch's device status; NULL sends it to a word set in the library that
  * no call reads. The first call on a device (that device current) does the
  * set-up: symbol lookup, kernel attributes and zeroing on `stream`; make it
- * before any stream capture. Calls whose launches overlap in time on one
- * device race on the shared scratch: order them on one stream. */
+ * before any stream capture. Under CUDA's lazy module loading the arrays
+ * are committed on the device by that set-up, so a caller whose memory pool
+ * will claim the rest of HBM makes it first: args == NULL runs the set-up
+ * alone (geometry and status are then ignored) and launches nothing. Calls
+ * whose launches overlap in time on one device race on the shared scratch:
+ * order them on one stream. */
 int ls_b200_launch_static(const ls_b200_geometry* geometry, const ls_b200_layer_args* args, uint32_t* status,
                           void* stream);
 /* Multi-layer launch: `count` layers in ONE persistent launch, each layer

@@ -481,8 +481,12 @@ struct StaticScratch {
     uint32_t* status = nullptr;
     uint32_t* done = nullptr;
     uint4* qmirror = nullptr;
-    uint64_t layers_issued = 0;  // layers launched on this device (tag counter wraps)
-    bool clear_tags = false;
+    // Layers launched on this device by successful calls, and whether the
+    // tag counter wrapped (the next call clears the tagged scratch first).
+    // Atomic: calls may come from several host threads (their launches must
+    // still be ordered on the GPU).
+    std::atomic<uint64_t> layers_issued{0};
+    std::atomic<bool> clear_tags{false};
 };
 StaticScratch g_static[kStaticDevices];
 std::mutex g_static_setup;
@@ -562,13 +566,14 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.nlayers = 1;
     p.max_layers = kStaticLayers;
     p.world = 1;  // one GPU: no exchange
-    if (s.clear_tags) {  // the tag counter wrapped: clear the tagged scratch on the stream
+    if (s.clear_tags.exchange(false)) {  // the tag counter wrapped: clear the tagged scratch on the stream
         cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
         if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
-        if (e != cudaSuccess) return cuda_rc(e);
-        s.clear_tags = false;
+        if (e != cudaSuccess) {
+            s.clear_tags.store(true);
+            return cuda_rc(e);
+        }
     }
-    if (++s.layers_issued % kTagWrap == 0) s.clear_tags = true;
     p.partial = s.partial;
     p.xbuf = s.xbuf;
     p.qmirror = s.qmirror;
@@ -581,7 +586,20 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.lean = lean_plans(&plan, 1, 1) ? 1u : 0u;
     const int grid = grid_for(b, a.candidate, &p.variant);
     rc = launch_fused(p, grid, stream);
-    return rc ? cuda_rc(cudaError_t(rc)) : 0;
+    if (rc) return cuda_rc(cudaError_t(rc));
+    // the device tag counter advanced by one layer: count it, and clear the
+    // tagged scratch before the next call when the counter wrapped
+    if ((s.layers_issued.fetch_add(1) + 1) % kTagWrap == 0) s.clear_tags.store(true);
+    return 0;
+}
+
+// Set-up only (args == NULL): looks up the arrays on the current device and
+// zeroes them on `stream`, without launching anything.
+int setup_static(cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticDevices) return ENODEV;
+    StaticScratch& s = g_static[dev];
+    return s.ready.load(std::memory_order_acquire) ? 0 : static_setup(s, dev, stream);
 }
 
 }  // namespace
@@ -631,7 +649,8 @@ int ls_b200_launch(void* backend, const ls_b200_layer_args* args, void* stream) 
 
 int ls_b200_launch_static(const ls_b200_geometry* geometry, const ls_b200_layer_args* args, uint32_t* status,
                           void* stream) {
-    if (!geometry || !args) return EINVAL;
+    if (!args) return lsb::setup_static(static_cast<cudaStream_t>(stream));  // set-up only
+    if (!geometry) return EINVAL;
     return lsb::launch_static(*geometry, *args, status, static_cast<cudaStream_t>(stream));
 }
 
