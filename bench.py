@@ -1063,6 +1063,37 @@ def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
                       f"{elapsed:.1f} s of CPU work; tokens/s = 1/({LAYERS} x mean layer time)"}
 
 
+def reference_cuda_backend() -> dict:
+    """The reference's own CUDA backend (kernels/streaming_mlp.cu, compiled
+    unmodified into oracle/_ref/ref_streaming_timer by `make -C oracle
+    ref-cuda`) timed on this box's GPU at BASELINE.json configurations 1 and
+    2: seeded inputs, an all-ready BatchCompat plan (the reference's
+    static-stripe path), CUDA events over back-to-back layers; the best of
+    several persistent-consumer worker counts. A GPU reference point beside
+    the CPU arm, not this arm's value."""
+    exe = ROOT / "oracle" / "_ref" / "ref_streaming_timer"
+    if not exe.exists():
+        return {"unavailable": "oracle/_ref/ref_streaming_timer not built (make -C oracle ref-cuda)"}
+    out = {}
+    for name, cfg in (("config1", ["1024", "64", "64", "16", "50"]), ("config2", ["4096", "64", "192", "58", "20"])):
+        try:
+            proc = subprocess.run([str(exe), *cfg, "16", "32", "64", "148"], capture_output=True, text=True,
+                                  timeout=120)
+            rows = [json.loads(l) for l in proc.stdout.splitlines() if l.startswith("{")]
+        except (subprocess.SubprocessError, ValueError) as exc:
+            out[name] = {"unavailable": str(exc)}
+            continue
+        if proc.returncode or not rows:
+            out[name] = {"unavailable": f"exit {proc.returncode}: {proc.stderr.strip()[-200:]}"}
+            continue
+        best = min(rows, key=lambda r: r["us_per_layer"])
+        out[name] = {"us_per_layer": best["us_per_layer"], "workers": best["workers"], "gb_per_s": best["gb_per_s"],
+                     "sweep": {r["workers"]: r["us_per_layer"] for r in rows}}
+    out["source"] = ("kernels/streaming_mlp.cu:85-93 enqueue_streaming_mlp (core kernel -> consumer -> reduction), "
+                     "compiled unmodified for sm_100a; timing driver tests/native/ref_streaming_timer.cu")
+    return out
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU path of this workload on the
     host cores (CpuPath: its own ls_predict, then the MLP port, since the
@@ -1091,7 +1122,9 @@ def run_reference(args, rank, world):
     what = "ls_predict + sparse MLP port" if pred else "sparse MLP port (reference predictor library absent)"
     sample = (f"each step = {lps} consecutive layers of the token stream ({what}), {threads} host threads; "
               f"tokens/s = 1/({LAYERS} x mean layer time)")
+    ref_gpu = reference_cuda_backend()
     return {
+        "reference_cuda_backend": ref_gpu,
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
         "us_per_layer": per_layer * 1e6,

@@ -156,6 +156,14 @@ typedef struct ls_b200_layer_args {
                                * per CTA and layer, then [4][LS_B200_PIECE_TRACE_PIECES][4]
                                * per piece of CTAs 0..3 (LS_B200_*TRACE_*); the Stamp
                                * buffers of backends/triton/core.py:25, persistent.py:37 */
+    float* importance;        /* optional fp32 [N], dest-indexed: sum over the group's G neurons
+                               * of |h| (the importance output of
+                               * examples/ministral/native/leanstream_mapped.cu:43-47,
+                               * summed exactly and rounded to fp32 once); entries of
+                               * destinations the layer did not execute are 0 */
+    uint32_t* importance_flag; /* optional: receives the epoch (release, system scope) once
+                               * every importance entry of the layer is written
+                               * (leanstream_mapped.cu:36-39 publish) */
 } ls_b200_layer_args;
 
 /* Phase stamps written per CTA when ls_b200_layer_args.trace is set. */

@@ -79,7 +79,7 @@ class LayerArgs(C.Structure):
                 ("candidate", C.c_int32), ("layer", C.c_uint32), ("activations", C.c_void_p),
                 ("executions", C.c_void_p), ("first_compute", C.c_void_p), ("residual", C.c_void_p),
                 ("hidden_out", C.c_void_p), ("output_f32", C.c_void_p), ("norm_weight", C.c_void_p),
-                ("trace", C.c_void_p)]
+                ("trace", C.c_void_p), ("importance", C.c_void_p), ("importance_flag", C.c_void_p)]
 
 
 class Queue(C.Structure):

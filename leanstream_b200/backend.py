@@ -162,7 +162,8 @@ class B200Backend:
     def layer_args(*, input=None, output=None, cache=None, staging=None, scales=None, core=None, core_count=0,
                    epoch=0, queue: Optional[N.DeviceExecQueue] = None, mode=N.MODE_PROGRESSIVE, flags=0,
                    candidate=-1, layer=0, activations=None, executions=None, first_compute=None, residual=None,
-                   hidden_out=None, output_f32=None, norm_weight=None, trace=None) -> N.LayerArgs:
+                   hidden_out=None, output_f32=None, norm_weight=None, trace=None, importance=None,
+                   importance_flag=None) -> N.LayerArgs:
         a = N.LayerArgs()
         a.input, a.output = _ptr(input), _ptr(output)
         a.cache, a.staging, a.scales = _ptr(cache), _ptr(staging), _ptr(scales)
@@ -174,6 +175,7 @@ class B200Backend:
         a.residual, a.hidden_out, a.output_f32, a.norm_weight = (_ptr(residual), _ptr(hidden_out),
                                                                   _ptr(output_f32), _ptr(norm_weight))
         a.trace = _ptr(trace)
+        a.importance, a.importance_flag = _ptr(importance), _ptr(importance_flag)
         return a
 
     def set_buffers(self, **kw) -> None:

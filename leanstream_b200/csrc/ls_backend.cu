@@ -71,6 +71,7 @@ struct Backend {
     unsigned long long* partial = nullptr;  // tagged slab partial rows
     unsigned long long* xbuf = nullptr;     // tagged layer output handed to the next layer
     uint4* qmirror = nullptr;               // device copy of host-memory queues' descriptors
+    unsigned long long* impacc = nullptr;   // importance sums [2][N] (zero at rest)
     size_t partial_bytes = 0, xbuf_bytes = 0;
     uint32_t* ws = nullptr;
     uint64_t layers_issued = 0;  // layers of the launches issued through this backend
@@ -128,6 +129,8 @@ struct Backend {
         if (xbuf) cudaFree(xbuf);
         if (qmirror) cudaFree(qmirror);
         qmirror = nullptr;
+        if (impacc) cudaFree(impacc);
+        impacc = nullptr;
         if (ws) cudaFree(ws);
         if (status_host) cudaFreeHost(status_host);
         if (done_host) cudaFreeHost(done_host);
@@ -176,6 +179,9 @@ int configure(Backend& b, const ls_b200_geometry& g) {
     if (e == cudaSuccess) e = cudaMalloc(&b.qmirror, qmirror_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&b.ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.ws, 0, ws_bytes);
+    const size_t impacc_bytes = size_t(2) * N * sizeof(unsigned long long);
+    if (e == cudaSuccess) e = cudaMalloc(&b.impacc, impacc_bytes);
+    if (e == cudaSuccess) e = cudaMemset(b.impacc, 0, impacc_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.partial, 0, partial_bytes);
     if (e == cudaSuccess) e = cudaMemset(b.xbuf, 0, xbuf_bytes);
     b.partial_bytes = partial_bytes;
@@ -197,7 +203,7 @@ int configure(Backend& b, const ls_b200_geometry& g) {
         b.release();
         return ENOMEM;
     }
-    b.scratch_bytes = partial_bytes + xbuf_bytes + ws_bytes + qmirror_bytes;
+    b.scratch_bytes = partial_bytes + xbuf_bytes + ws_bytes + qmirror_bytes + impacc_bytes;
     b.configured = true;
     return 0;
 }
@@ -251,6 +257,8 @@ int encode(const Backend& b, const ls_b200_layer_args& a, LayerPlan* out) {
     p.hidden_out = static_cast<uint16_t*>(a.hidden_out);
     p.y32 = a.output_f32;
     p.norm_w = static_cast<const uint16_t*>(a.norm_weight);
+    p.importance = a.importance;
+    p.imp_flag = a.importance_flag;
     p.epoch = a.epoch;
     p.mode = a.mode;
     p.flags = (a.flags & ~kPlanHostQueue) | (host_memory(b, a.queue.control) ? kPlanHostQueue : 0u);
@@ -288,6 +296,7 @@ KernelParams base_params(Backend& b, uint32_t nlayers, uint64_t* trace, cudaStre
     p.partial = b.partial;
     p.xbuf = b.xbuf;
     p.qmirror = b.qmirror;
+    p.impacc = b.impacc;
     p.ws = b.ws;
     p.status = b.status_dev;
     p.done = b.done_dev;
@@ -469,6 +478,8 @@ static __device__ __align__(256) uint32_t g_static_done[kStaticLayers];
 // (H >= 256, one slab per group at least)
 constexpr size_t kStaticMirror = kStaticPartialWords / 256;
 static __device__ __align__(256) uint4 g_static_qmirror[kStaticMirror * 2];
+// importance sums [2][N] (N <= kStaticMirror)
+static __device__ __align__(256) unsigned long long g_static_impacc[kStaticMirror * 2];
 
 namespace {
 
@@ -481,6 +492,7 @@ struct StaticScratch {
     uint32_t* status = nullptr;
     uint32_t* done = nullptr;
     uint4* qmirror = nullptr;
+    unsigned long long* impacc = nullptr;
     // Layers launched on this device by successful calls, and whether the
     // tag counter wrapped (the next call clears the tagged scratch first).
     // Atomic: calls may come from several host threads (their launches must
@@ -517,13 +529,15 @@ int static_setup(StaticScratch& s, int dev, cudaStream_t stream) {
     if (rc) return cuda_rc(cudaError_t(rc));
     if ((rc = symbol_address(&s.partial, g_static_partial)) || (rc = symbol_address(&s.xbuf, g_static_xbuf)) ||
         (rc = symbol_address(&s.ws, g_static_ws)) || (rc = symbol_address(&s.status, g_static_status)) ||
-        (rc = symbol_address(&s.done, g_static_done)) || (rc = symbol_address(&s.qmirror, g_static_qmirror)))
+        (rc = symbol_address(&s.done, g_static_done)) || (rc = symbol_address(&s.qmirror, g_static_qmirror)) ||
+        (rc = symbol_address(&s.impacc, g_static_impacc)))
         return rc;
     cudaError_t e = cudaMemsetAsync(s.partial, 0, sizeof(g_static_partial), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s.xbuf, 0, sizeof(g_static_xbuf), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s.ws, 0, sizeof(g_static_ws), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s.status, 0, sizeof(g_static_status), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(s.done, 0, sizeof(g_static_done), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.impacc, 0, sizeof(g_static_impacc), stream);
     if (e != cudaSuccess) return cuda_rc(e);
     s.sms = sms;
     s.ready.store(true, std::memory_order_release);
@@ -577,6 +591,7 @@ int launch_static(const ls_b200_geometry& g, const ls_b200_layer_args& a, uint32
     p.partial = s.partial;
     p.xbuf = s.xbuf;
     p.qmirror = s.qmirror;
+    p.impacc = s.impacc;
     p.ws = s.ws;
     p.status = status ? status : s.status;
     p.done = s.done;

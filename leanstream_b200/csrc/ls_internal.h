@@ -49,6 +49,8 @@ struct alignas(16) LayerPlan {
     uint16_t* hidden_out;
     float* y32;
     const uint16_t* norm_w;
+    float* importance;        // optional fp32 [N] per-destination sum of |h|
+    uint32_t* imp_flag;       // optional: epoch released once `importance` is written
     uint32_t epoch, mode, flags, layer, core_count;
     uint32_t pad[3];
 };
@@ -100,6 +102,7 @@ struct KernelParams {
     uint32_t* done;       // mapped host per-layer completion epochs
     uint64_t* trace;      // optional phase stamps
     uint4* qmirror;       // [max_layers][N][2]: device copy of a host queue's core + published descriptors
+    unsigned long long* impacc;  // [2][N]: exact sums of |h| * 2^24 per destination, by layer parity (zero at rest)
     const LayerPlan* plans;  // device array for nlayers > 1, else nullptr
     LayerPlan first;         // layer 0 when plans == nullptr
     // Tensor parallel inside one launch (world > 1): rank r's exchange buffer

@@ -1941,6 +1941,23 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
             emit_column<H>(P, L, t, c, y, res, __shfl_sync(0xffffffffu, err, 0), good, tag, chain, lane);
         }
     }
+    // Importance output (CTA 0, which reduced column block 0 and so saw every
+    // partial row of the layer, hence every h and its importance addition):
+    // each destination's exact sum of |h| * 2^24, read and reset to zero in
+    // one exchange, rounded to fp32 once and scaled by 2^-24; then the epoch
+    // is released (leanstream_mapped.cu:36-39, 43-47). After the column
+    // block's outputs, off the next layer's input path.
+    if (L.importance && blockIdx.x == 0) {
+        __threadfence();
+        unsigned long long* acc = P.impacc + size_t(l & 1u) * P.N;
+        for (uint32_t d = uint32_t(tid); d < P.N; d += kConsumerThreads)
+            L.importance[d] = float(atomicExch(acc + d, 0ull)) * 5.9604644775390625e-8f;  // 2^-24
+        csync(P, t, cph, limit, lane);
+        if (tid == 0 && L.imp_flag) {
+            __threadfence_system();
+            st_release_sys(L.imp_flag, L.epoch);
+        }
+    }
     // Reduced blocks: an unchained next layer (or the host's view of the
     // layer outputs) waits on this count. A chained next layer reads the
     // tagged words instead, so the fence stays off its critical path.
@@ -1971,13 +1988,21 @@ __device__ __forceinline__ float2 sum_partials(const uint8_t* st, uint32_t i) {
 // h from the gate and up sums, each rounded to fp16, then
 // fp16(fp16(silu(g)) * u) (kernels/streaming_mlp.cu:34-37,
 // backends/triton/core.py:49-52), for neuron n of the slab.
+// With an importance output, |h| * 2^24 -- an integer below 2^40 for every
+// fp16 value -- is added to the destination's 64-bit sum of this layer's
+// parity, so the per-group sum of |h| is exact and does not depend on which
+// CTA formed which neuron (examples/ministral/native/leanstream_mapped.cu:43-47
+// sums the group's |h| in fp32).
 __device__ __forceinline__ void finish_h(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t buf,
-                                         uint32_t dest, uint32_t n, float2 gu) {
+                                         uint32_t dest, uint32_t n, float2 gu, uint32_t layer) {
     const float g16 = round16(gu.x), u16 = round16(gu.y);
     const float sl = round16(g16 / (1.f + expf(-g16)));
     const __half h = __float2half_rn(sl * u16);
     t->hs[buf][n & (kSlab - 1)] = h;
     if (L.act) L.act[size_t(dest) * P.G + n] = __half_as_ushort(h);
+    if (L.importance)
+        atomicAdd(P.impacc + size_t(layer & 1u) * P.N + dest,
+                  static_cast<unsigned long long>(fabsf(__half2float(h)) * 16777216.f));
 }
 
 // Bounded wait of a warp on an mbarrier phase; false on abort or deadline.
@@ -2181,8 +2206,12 @@ __device__ void run_epilogue(const KernelParams& P, uint8_t* stages, SmemTail* t
                 }
                 gu = make_float2(carry.x + gu.x, carry.y + gu.y);
             }
-            if (mine) finish_h(P, L, t, buf, pc.dest, n0 + i, gu);
+            if (mine) finish_h(P, L, t, buf, pc.dest, n0 + i, gu, pc.layer);
             __syncwarp();
+            // the importance additions are performed before the slab's DOWN
+            // piece (and so its partial row) can be computed: the reducer that
+            // converts them has seen every partial row of the layer
+            if (L.importance) __threadfence();
             __threadfence_block();
             if (lane == 0) t->octets_done = t->octets_done + (paired ? 2u : 1u);
             if (paired) ++idx;

@@ -37,7 +37,7 @@ def build(reference: bool = True) -> None:
     """Compiles the oracle; the reference objects too when the reference is mounted."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     if reference and REFERENCE_ROOT.exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_ROOT}"], check=True)
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", "ref-cuda", f"REF={REFERENCE_ROOT}"], check=True)
 
 
 def _u16(a):

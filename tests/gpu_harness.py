@@ -40,7 +40,7 @@ def make_backend(H, G, N_groups, timeout_us=2_000_000, table=None, **kw) -> B200
 
 def run_layer(backend: B200Backend, buf: LayerBuffers, core_rows, queue_rows, *, mode=N.MODE_PROGRESSIVE,
               candidate=-1, epoch=1, order=None, publish="all", flags=0, residual=None, hidden_out=None,
-              stream=None, core_dev=None):
+              stream=None, core_dev=None, importance=None, importance_flag=None):
     """One layer with `core_rows` (A) and `queue_rows` (B) descriptors.
 
     publish="all": the plan is sealed and fully published before launch.
@@ -62,7 +62,7 @@ def run_layer(backend: B200Backend, buf: LayerBuffers, core_rows, queue_rows, *,
                               core=core, core_count=len(core_rows), epoch=epoch, queue=q.view, mode=mode,
                               candidate=candidate, activations=buf.act, executions=buf.execs,
                               first_compute=buf.stamps, output_f32=buf.y32, flags=flags, residual=residual,
-                              hidden_out=hidden_out)
+                              hidden_out=hidden_out, importance=importance, importance_flag=importance_flag)
     backend.launch(args, stream)
     return q, core
 
