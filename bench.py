@@ -24,9 +24,9 @@ token.
 
 --batch 8 (one GPU): each step decodes 8 tokens of the same seeded stream
 through ls_b200_batch_mlp, over the union of their active groups per layer
-(~83 % of the groups at 20 % per token), each token masked to its own set.
-The layers are not chained (no fused RMSNorm on this path), so every layer
-takes the same 8 hidden states; the bytes and work per layer are a stack's.
+(~83 % of the groups at 20 % per token), each token masked to its own set;
+the layers are chained (RMSNorm of each token in the batch call, residual
+hidden_out the next layer's input).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 3|5] [--batch 1|8]
 """
@@ -133,7 +133,7 @@ def workload_config(world: int, args) -> dict:
                           "which overflows fp16 through the residual stack); fp16 scales U(0.005, 0.02)"}
     if getattr(args, "batch", 1) == BATCH:
         unions = [len(u) for s in range(first, last) for (u, _) in batch_union(s)]
-        cfg.update({"batch": BATCH, "mean_union_groups_per_layer": float(np.mean(unions)), "layers_chained": False,
+        cfg.update({"batch": BATCH, "mean_union_groups_per_layer": float(np.mean(unions)), "layers_chained": True,
                     "parallelism": "single GPU",
                     "l2": f"inputs larger than L2: ~{np.mean(unions) * ALG_BYTES_PER_GROUP / 1e6:.0f} MB of "
                           "distinct weights per layer"})
@@ -811,11 +811,9 @@ def run_gpu(args, rank, world, local_rank):
 def run_batch(args, rank, world, local_rank):
     """Batch-8 union decode (--batch 8): each step runs the stack's layers for
     8 tokens through ls_b200_batch_mlp, over the union of the tokens' active
-    groups with each token masked to its own set. Every layer takes the same
-    8 hidden states: the batch path has no fused RMSNorm, and un-normalised
-    residual chaining of random-weight layers overflows fp16, so layers are
-    not chained; the work and bytes of each layer are those of a chained
-    stack. One GPU."""
+    groups with each token masked to its own set. Layers are chained: each
+    call normalises its 8 hidden states (HF RMSNorm) and writes
+    hidden_out = fp16(x + y), the next layer's input. One GPU."""
     import torch
 
     from leanstream_b200.batch import BatchMLP, union_plan
@@ -849,6 +847,9 @@ def run_batch(args, rank, world, local_rank):
     gen.manual_seed(SEED)
     x = torch.randn(BATCH, H, device=dev, generator=gen).half()
     y = torch.zeros(BATCH, H, dtype=torch.float16, device=dev)
+    # chained stack: layer l reads xs[l], RMSNorm in the batch call, and
+    # writes xs[l+1] = fp16(xs[l] + y)
+    xs = [x] + [torch.zeros(BATCH, H, dtype=torch.float16, device=dev) for _ in range(LAYERS)]
     mlp = BatchMLP(H, G, NGROUPS, device=dev)  # the public batch API; scratch sized for every group
     progress("weights and batch plans resident")
     stream = torch.cuda.Stream()
@@ -856,8 +857,9 @@ def run_batch(args, rank, world, local_rank):
     def enqueue_step(s, base, strm):
         for layer in range(LAYERS):
             off = base + layer * lstride
-            mlp.run(stream=strm, x=x, output=y, cache=st.cache[layer], scales=st.scales[layer], union_descs=off,
-                    union_count=int(unions[s, layer]), tokens=BATCH, mask=off + NGROUPS * 20)
+            mlp.run(stream=strm, x=xs[layer], output=y, cache=st.cache[layer], scales=st.scales[layer],
+                    union_descs=off, union_count=int(unions[s, layer]), tokens=BATCH, mask=off + NGROUPS * 20,
+                    residual=xs[layer], hidden_out=xs[layer + 1], norm_input=True, rms_eps=EPS)
 
     # first calls outside capture (the call opts the kernels into their ring size)
     with torch.cuda.stream(stream):
@@ -908,7 +910,7 @@ def run_batch(args, rank, world, local_rank):
         slot_dev.copy_(img_host[s], non_blocking=True)
         x.copy_(x_host, non_blocking=True)
         e2e_graphs[s].replay()
-        y_host.copy_(y, non_blocking=True)
+        y_host.copy_(xs[LAYERS], non_blocking=True)
 
     with torch.cuda.stream(stream):
         for s in range(args.warmup):

@@ -396,6 +396,11 @@ typedef struct ls_b200_batch_args {
     const uint8_t* mask;      /* optional device [tokens][union_count] */
     void* scratch;
     uint64_t scratch_bytes;
+    uint32_t flags;           /* 0 or LS_B200_NORM_INPUT: HF RMSNorm of each token before the MLP
+                               * (predictor_shared_input.cu:16-33), so that with residual and
+                               * hidden_out the call is one layer of a decode stack */
+    float rms_eps;            /* epsilon of the RMSNorm */
+    const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
 } ls_b200_batch_args;
 uint64_t ls_b200_batch_scratch_bytes(uint32_t hidden, uint32_t group_size, uint32_t union_count);
 int ls_b200_batch_mlp(const ls_b200_batch_args* args, void* stream);

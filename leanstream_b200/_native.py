@@ -124,7 +124,8 @@ class BatchArgs(C.Structure):
                 ("tokens", C.c_uint32), ("x", C.c_void_p), ("output", C.c_void_p), ("output_f32", C.c_void_p),
                 ("residual", C.c_void_p), ("hidden_out", C.c_void_p), ("cache", C.c_void_p),
                 ("staging", C.c_void_p), ("scales", C.c_void_p), ("union_descs", C.c_void_p), ("mask", C.c_void_p),
-                ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64)]
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64), ("flags", C.c_uint32),
+                ("rms_eps", C.c_float), ("norm_weight", C.c_void_p)]
 
 assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 72
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32

@@ -77,12 +77,16 @@ class BatchMLP:
                 raise ValueError(f"scratch of {have} B, {self.scratch_bytes} B needed")
 
     def args(self, *, x, output, cache, scales, union_descs, union_count: int, tokens: int, mask=None,
-             residual=None, hidden_out=None, output_f32=None, staging=None) -> N.BatchArgs:
+             residual=None, hidden_out=None, output_f32=None, staging=None, norm_input=False, rms_eps=1e-5,
+             norm_weight=None) -> N.BatchArgs:
+        """norm_input: HF RMSNorm of each token before the MLP (with residual
+        and hidden_out, one layer of a decode stack)."""
         if union_count > self.max_union:
             raise ValueError(f"union of {union_count} groups, BatchMLP sized for {self.max_union}")
         return N.BatchArgs(self.hidden, self.group_size, union_count, tokens, _ptr(x), _ptr(output),
                            _ptr(output_f32), _ptr(residual), _ptr(hidden_out), _ptr(cache), _ptr(staging),
-                           _ptr(scales), _ptr(union_descs), _ptr(mask), self.scratch_ptr, self.scratch_bytes)
+                           _ptr(scales), _ptr(union_descs), _ptr(mask), self.scratch_ptr, self.scratch_bytes,
+                           N.NORM_INPUT if norm_input else 0, rms_eps, _ptr(norm_weight))
 
     def run(self, stream=None, **kw) -> None:
         """Enqueues one layer (three launches) on `stream` (a torch stream,

@@ -432,9 +432,46 @@ __global__ void batch_epilogue_kernel(const BatchParams p) {
     }
 }
 
+// Optional prologue (LS_B200_NORM_INPUT): the HF RMSNorm of every token,
+// one CTA per token, as the batch-1 kernel's stage_x applies it
+// (examples/ministral/native/predictor_shared_input.cu:16-33):
+// inv = rsqrt(sum(x^2) / H + eps), x' = fp16(w * fp16(x * inv)) (w = 1 when
+// no weight is given). The sum of squares runs in a fixed order (per thread
+// strided, then a shuffle tree, then the warps in order), so two calls give
+// identical bits. x' goes to the scratch row of the token, which the gate/up
+// kernel reads in place of x.
+__global__ void __launch_bounds__(256) batch_norm_kernel(const __half* x, const __half* w, float eps, uint32_t H,
+                                                         __half* xn) {
+    __shared__ float part[8];
+    const __half* row = x + size_t(blockIdx.x) * H;
+    __half* out = xn + size_t(blockIdx.x) * H;
+    float ss = 0.f;
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        const float v = __half2float(row[c]);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += part[i];
+    const float inv = rsqrtf(tot / float(H) + eps);
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        __half v = __float2half_rn(__half2float(row[c]) * inv);
+        if (w) v = __hmul(w[c], v);
+        out[c] = v;
+    }
+}
+
+// Scratch: h [8][NTP] fp16, then the down partials [kDownSplits][8][H] fp32,
+// then the normalised activations [8][H] fp16 (LS_B200_NORM_INPUT).
 uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) {
     const uint64_t nt = uint64_t(G) * U, ntp = (nt + 15) / 16 * 16 + 16;
-    return ntp * kBatchTokens * sizeof(__half) + uint64_t(kDownSplits) * kBatchTokens * H * sizeof(float) + 256;
+    const uint64_t ht = (ntp * kBatchTokens * sizeof(__half) + 255) / 256 * 256;
+    const uint64_t part = (uint64_t(kDownSplits) * kBatchTokens * H * sizeof(float) + 255) / 256 * 256;
+    return ht + part + uint64_t(kBatchTokens) * H * sizeof(__half) + 256;
 }
 
 bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
@@ -476,7 +513,8 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     // union neurons index rows of h and the gate/up grid in 32 bits
     if (uint64_t(G) * U > (uint64_t(1) << 30)) return EINVAL;
     if (!a->x || !a->output || !a->cache || !a->scales || !a->union_descs || !a->scratch ||
-        (a->hidden_out && !a->residual))
+        (a->hidden_out && !a->residual) || (a->flags & ~uint32_t(LS_B200_NORM_INPUT)) ||
+        (a->norm_weight && !(a->flags & LS_B200_NORM_INPUT)))
         return EINVAL;
     if (a->scratch_bytes < batch_scratch(H, G, U)) return ENOSPC;
     if (!al16(a->x) || !al16(a->cache) || (a->staging && !al16(a->staging)) || !al16(a->scratch) ||
@@ -500,10 +538,16 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     p.desc = a->union_descs;
     p.mask = a->mask;
     p.hT = static_cast<__half*>(a->scratch);
-    const uint64_t ht_bytes = uint64_t(p.NTP) * kBatchTokens * sizeof(__half);
-    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + (ht_bytes + 255) / 256 * 256);
+    const uint64_t ht_bytes = (uint64_t(p.NTP) * kBatchTokens * sizeof(__half) + 255) / 256 * 256;
+    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + ht_bytes);
+    const uint64_t part_bytes = (uint64_t(kDownSplits) * kBatchTokens * H * sizeof(float) + 255) / 256 * 256;
+    __half* xn = reinterpret_cast<__half*>(static_cast<uint8_t*>(a->scratch) + ht_bytes + part_bytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (const cudaError_t e = set_ring_attributes(); e != cudaSuccess) return int(e);
+    if (a->flags & LS_B200_NORM_INPUT) {
+        batch_norm_kernel<<<B, 256, 0, s>>>(p.x, static_cast<const __half*>(a->norm_weight), a->rms_eps, H, xn);
+        p.x = xn;
+    }
     batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, kGuSmem, s>>>(p);
     batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, kDnSmem, s>>>(p);
     const uint32_t total = B * H;

@@ -87,3 +87,46 @@ def test_partial_batch_with_residual(native_lib, cuda_device):
         ref = ref.astype(np.float32)
         assert np.abs(y[b].astype(np.float32) - ref).max() <= TOL * np.abs(ref).max()
         assert np.array_equal(hid[b].view(np.uint16), O.residual(resid[b], y[b]).view(np.uint16))
+
+
+@pytest.mark.parametrize("H", [1024, 8192])
+def test_batch_norm_chains_layers(native_lib, cuda_device, H):
+    """LS_B200_NORM_INPUT with residual and hidden_out: three chained batch
+    layers (x_{l+1} = hidden_out of layer l), each token masked to its own
+    groups, equal per token the one-token oracle chain
+    x_{l+1} = fp16(x_l + MLP(RMSNorm_HF(x_l))) within the output tolerance."""
+    import torch
+    from leanstream_b200.batch import BatchMLP, union_plan
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    G, n_groups, B, layers = 64, 24, 8, 3
+    Ls = [make_layer(60 + l, H, n_groups, G) for l in range(layers)]
+    rng = np.random.default_rng(9)
+    x0 = (rng.standard_normal((B, H)) * 3.0).astype(np.float16)  # un-normalised: the norm matters
+    mlp = BatchMLP(H, G, n_groups, device="cuda")
+    xs = [torch.from_numpy(x0.view(np.int16)).cuda().view(torch.float16)]
+    y = torch.zeros(B, H, dtype=torch.float16, device="cuda")
+    plans = []
+    for l in range(layers):
+        sets = [np.sort(rng.permutation(n_groups)[: rng.integers(3, 9)]) for _ in range(B)]
+        union, rows, mask = union_plan(sets)
+        plans.append((sets, union))
+        desc = torch.from_numpy(np.ascontiguousarray(rows.reshape(-1).view(np.int32))).cuda()
+        mk = torch.from_numpy(np.ascontiguousarray(mask)).cuda()
+        cache = torch.from_numpy(Ls[l].packed).cuda()
+        scales = torch.from_numpy(Ls[l].scales.reshape(-1).view(np.int16)).cuda().view(torch.float16)
+        xs.append(torch.zeros(B, H, dtype=torch.float16, device="cuda"))
+        mlp.run(x=xs[l], output=y, cache=cache, scales=scales, union_descs=desc, union_count=len(union),
+                tokens=B, mask=mk, residual=xs[l], hidden_out=xs[l + 1], norm_input=True, rms_eps=1e-5)
+        torch.cuda.synchronize()
+    got = [t.cpu().numpy() for t in xs]
+    for b in range(B):
+        for l in range(layers):
+            x_l = got[l][b]
+            assert np.isfinite(x_l.astype(np.float32)).all()
+            xin = O.rmsnorm(x_l, None, 1e-5)
+            y_ref, _, _ = O.mlp(H, G, xin, Ls[l].packed, Ls[l].scales, descriptors(plans[l][0][b]))
+            ref = O.residual(x_l, y_ref).astype(np.float32)
+            out = got[l + 1][b].astype(np.float32)
+            assert np.abs(out - ref).max() <= TOL * np.abs(ref).max() + 1e-3, (b, l, np.abs(out - ref).max())
