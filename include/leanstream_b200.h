@@ -451,6 +451,19 @@ typedef struct ls_b200_stream_config {
     float delay_mean_us;           /* emulated IO latency: each landed group becomes READY after an
                                     * extra delay ~ Exp(mean) (seeded); 0 = none */
     uint64_t delay_seed;
+    /* Optional SSD leg (src/io/stream_io.cpp:75-148): with file_path set, an
+     * admitted group is first read from the file (pread by a pool of reader
+     * threads) into its host slot host_base + host_offsets[g], then copied
+     * to HBM as above; NULL = host_base already holds every group. */
+    const char* file_path;
+    const uint64_t* file_offsets;  /* [group_count]: byte offset of group g in the file */
+    uint32_t read_workers;         /* reader threads, 1..16 (0 = 4) */
+    uint32_t o_direct;             /* 1: open with O_DIRECT (no page cache). Each read is then
+                                    * group_bytes rounded up to file_alignment, so every host slot
+                                    * must hold that many bytes; when the file system refuses
+                                    * O_DIRECT or an offset / slot is not aligned, buffered reads
+                                    * are used (ls_b200_stream_counters.direct tells which) */
+    uint32_t file_alignment;       /* O_DIRECT alignment in bytes, a power of two (0 = 4096) */
 } ls_b200_stream_config;
 
 typedef struct ls_b200_stream_counters {
@@ -460,7 +473,11 @@ typedef struct ls_b200_stream_counters {
     uint64_t first_issue_ns, last_land_ns;  /* CLOCK_MONOTONIC of the first copy issue / last landing */
     uint64_t copy_ns;       /* sum over copies of issue -> landing as the worker observed it */
     int32_t error;          /* first error (CUDA error code or errno), 0 if none */
-    uint32_t outstanding;   /* copies in flight now */
+    uint32_t outstanding;   /* reads and copies in flight now */
+    uint32_t direct;        /* file source: 1 when reads bypass the page cache (O_DIRECT) */
+    uint32_t reserved;
+    uint64_t read_bytes;    /* file source: bytes read from the file */
+    uint64_t read_ns;       /* file source: sum over reads of the pread time */
 } ls_b200_stream_counters;
 
 /* (new; the reference transport reads an O_DIRECT file into host memory the

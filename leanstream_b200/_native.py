@@ -106,13 +106,16 @@ class StreamConfig(C.Structure):
     _fields_ = [("host_base", C.c_void_p), ("host_offsets", C.c_void_p), ("staging", C.c_void_p),
                 ("staging_stride", C.c_uint64), ("group_bytes", C.c_uint64), ("io_states", C.c_void_p),
                 ("group_count", C.c_uint32), ("queue_depth", C.c_uint32), ("device", C.c_int32),
-                ("delay_mean_us", C.c_float), ("delay_seed", C.c_uint64)]
+                ("delay_mean_us", C.c_float), ("delay_seed", C.c_uint64), ("file_path", C.c_char_p),
+                ("file_offsets", C.c_void_p), ("read_workers", C.c_uint32), ("o_direct", C.c_uint32),
+                ("file_alignment", C.c_uint32)]
 
 
 class StreamStats(C.Structure):
     _fields_ = [("admissions", C.c_uint64), ("completions", C.c_uint64), ("bytes", C.c_uint64),
                 ("first_issue_ns", C.c_uint64), ("last_land_ns", C.c_uint64), ("copy_ns", C.c_uint64),
-                ("error", C.c_int32), ("outstanding", C.c_uint32)]
+                ("error", C.c_int32), ("outstanding", C.c_uint32), ("direct", C.c_uint32), ("reserved", C.c_uint32),
+                ("read_bytes", C.c_uint64), ("read_ns", C.c_uint64)]
 
 
 IO_EMPTY, IO_INFLIGHT, IO_READY, IO_ERROR = 0, 1, 2, 3
@@ -127,7 +130,7 @@ class BatchArgs(C.Structure):
                 ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64), ("flags", C.c_uint32),
                 ("rms_eps", C.c_float), ("norm_weight", C.c_void_p)]
 
-assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 72
+assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 104
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32
 
 # name -> (restype, argtypes); every entry point declared in include/leanstream_b200.h

@@ -125,6 +125,7 @@ struct Geo {
 constexpr uint32_t kTracePieces = 64, kTraceLayers = 40;
 // per-warp completion stamps of pieces [kTraceWarpBase, +kTraceWarpPieces) of CTA 0
 constexpr uint32_t kTraceWarpBase = 8, kTraceWarpPieces = 12;
+static_assert(kTraceWarpBase + kTraceWarpPieces <= 64, "per-warp stamps of the first pieces");
 static_assert(kTracePieces <= LS_B200_PIECE_TRACE_PIECES && kTraceLayers > 0, "trace stamps");
 
 struct alignas(16) SmemTail {

@@ -10,8 +10,16 @@
 // (release) and the completion callback runs on the worker thread; the
 // WeightManager then publishes the descriptor to the ExecutionQueue, from
 // which the running kernel claims it (system-scope acquire).
+//
+// With a file source (the SSD leg of src/io/stream_io.cpp:75-148), an
+// admitted group is first read from the file into its pinned host slot by a
+// pool of reader threads (pread, O_DIRECT when the file system and the
+// alignment allow it); the worker issues the group's copy once its read has
+// returned. Reads and copies together are bounded by queue_depth.
 #include <cuda_runtime.h>
+#include <fcntl.h>
 #include <time.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <cerrno>
@@ -50,6 +58,11 @@ struct Landed {
     int32_t id;
     uint64_t due;
 };
+struct ReadDone {
+    int32_t id;
+    uint32_t event;
+    int error;
+};
 
 struct Engine {
     ls_b200_stream_config cfg{};
@@ -71,6 +84,16 @@ struct Engine {
     size_t cursor = 0, fallback = 0;
     std::deque<Inflight> inflight;
     std::vector<Landed> landed;
+    // file source: reads waiting for a reader, reads in progress, returned reads
+    int fd = -1;
+    bool direct = false;
+    uint64_t read_size = 0;  // bytes per read (group_bytes, rounded up to the alignment with O_DIRECT)
+    std::vector<uint64_t> file_offsets;
+    std::vector<std::thread> readers;
+    std::condition_variable read_work;
+    std::deque<std::pair<int32_t, uint32_t>> to_read;
+    uint32_t reading = 0;
+    std::vector<ReadDone> read_done;
     uint64_t sequence = 0;
     std::mt19937_64 rng;
     ls_b200_stream_counters stats{};
@@ -125,6 +148,12 @@ struct Engine {
                 const uint64_t now = mono_ns();
                 if (!stats.first_issue_ns) stats.first_issue_ns = now;
                 ++stats.admissions;
+                if (fd >= 0) {  // the read first; the copy when it returns
+                    to_read.emplace_back(id, ev);
+                    read_work.notify_one();
+                    progressed = true;
+                    continue;
+                }
                 cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(cfg.staging) + uint64_t(id) * cfg.staging_stride,
                                                 static_cast<const uint8_t*>(cfg.host_base) + offsets[id],
                                                 cfg.group_bytes, cudaMemcpyHostToDevice, stream);
@@ -137,6 +166,26 @@ struct Engine {
                 inflight.push_back({id, ev, now});
                 progressed = true;
             }
+            // returned reads: copy the group to HBM
+            for (const ReadDone& r : read_done) {
+                progressed = true;
+                if (r.error) {
+                    free_events.push_back(r.event);
+                    fail(l, r.id, r.error);
+                    continue;
+                }
+                cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(cfg.staging) + uint64_t(r.id) * cfg.staging_stride,
+                                                static_cast<const uint8_t*>(cfg.host_base) + offsets[r.id],
+                                                cfg.group_bytes, cudaMemcpyHostToDevice, stream);
+                if (e == cudaSuccess) e = cudaEventRecord(events[r.event], stream);
+                if (e != cudaSuccess) {
+                    free_events.push_back(r.event);
+                    fail(l, r.id, int(e));
+                    continue;
+                }
+                inflight.push_back({r.id, r.event, mono_ns()});
+            }
+            read_done.clear();
             // landings, in issue order (one stream)
             while (!inflight.empty()) {
                 const cudaError_t q = cudaEventQuery(events[inflight.front().event]);
@@ -175,7 +224,7 @@ struct Engine {
                 l.lock();
                 progressed = true;
             }
-            stats.outstanding = uint32_t(inflight.size());
+            stats.outstanding = uint32_t(inflight.size() + to_read.size() + reading);
             if (progressed) {
                 changed.notify_all();
                 continue;
@@ -189,6 +238,42 @@ struct Engine {
                 changed.notify_all();
                 work.wait(l);
             }
+        }
+    }
+
+    // Reader thread: pread of an admitted group into its host slot (EINTR and
+    // short reads retried; a read that ends early is EIO).
+    void read_loop() {
+        std::unique_lock<std::mutex> l(m);
+        for (;;) {
+            read_work.wait(l, [&] { return stop || !to_read.empty(); });
+            if (to_read.empty()) return;  // stop
+            const auto [id, ev] = to_read.front();
+            to_read.pop_front();
+            ++reading;
+            l.unlock();
+            uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(cfg.host_base)) + offsets[id];
+            const uint64_t t0 = mono_ns();
+            uint64_t done = 0;
+            int error = 0;
+            while (done < read_size) {
+                const ssize_t got = pread(fd, dst + done, read_size - done, off_t(file_offsets[id] + done));
+                if (got < 0 && errno == EINTR) continue;
+                if (got < 0) {
+                    error = errno ? errno : EIO;
+                    break;
+                }
+                if (got == 0) break;
+                done += uint64_t(got);
+            }
+            if (!error && done < cfg.group_bytes) error = EIO;  // the file ends inside the group
+            const uint64_t t1 = mono_ns();
+            l.lock();
+            --reading;
+            stats.read_ns += t1 - t0;
+            stats.read_bytes += done;
+            read_done.push_back({id, ev, error});
+            work.notify_one();
         }
     }
 
@@ -239,7 +324,8 @@ struct Engine {
         if (!active) return EINVAL;
         closing = true;
         work.notify_one();
-        changed.wait(l, [&] { return inflight.empty() && landed.empty(); });
+        changed.wait(l, [&] { return inflight.empty() && landed.empty() && to_read.empty() && !reading &&
+                                     read_done.empty(); });
         active = false;
         return int(load_state(states() + cfg.group_count));
     }
@@ -319,6 +405,42 @@ void* ls_b200_stream_create(const ls_b200_stream_config* c) {
         if (ok) e->free_events.push_back(i);
     }
     cudaSetDevice(previous);
+    int open_error = 0;
+    if (ok && c->file_path) {
+        // SSD leg: O_DIRECT when asked for and every offset and host slot is
+        // aligned (each read is then rounded up to the alignment), else
+        // buffered reads of exactly group_bytes
+        const uint64_t align = c->file_alignment ? c->file_alignment : 4096;
+        bool aligned = c->file_offsets && (align & (align - 1)) == 0;
+        try {
+            if (c->file_offsets) e->file_offsets.assign(c->file_offsets, c->file_offsets + c->group_count);
+        } catch (...) {
+            ok = false;
+        }
+        for (uint32_t g = 0; ok && aligned && g < c->group_count; ++g)
+            aligned = e->file_offsets[g] % align == 0 &&
+                      (reinterpret_cast<uintptr_t>(c->host_base) + c->host_offsets[g]) % align == 0;
+        int fd = -1;
+        if (ok && c->file_offsets && c->o_direct && aligned) {
+            fd = open(c->file_path, O_RDONLY | O_DIRECT);
+            e->direct = fd >= 0;
+        }
+        if (ok && c->file_offsets && fd < 0) fd = open(c->file_path, O_RDONLY);
+        if (fd < 0) {
+            open_error = c->file_offsets ? errno : EINVAL;
+            ok = false;
+        }
+        e->fd = fd;
+        e->read_size = e->direct ? (c->group_bytes + align - 1) / align * align : c->group_bytes;
+        const uint32_t n = c->read_workers ? std::min<uint32_t>(c->read_workers, 16) : 4;
+        for (uint32_t i = 0; ok && i < n; ++i) {
+            try {
+                e->readers.emplace_back([e] { e->read_loop(); });
+            } catch (...) {
+                ok = false;
+            }
+        }
+    }
     if (ok) {
         try {
             e->worker = std::thread([e] { e->run(); });
@@ -327,11 +449,18 @@ void* ls_b200_stream_create(const ls_b200_stream_config* c) {
         }
     }
     if (!ok) {
+        {
+            std::lock_guard<std::mutex> g(e->m);
+            e->stop = true;
+            e->read_work.notify_all();
+        }
+        for (std::thread& t : e->readers) t.join();
+        if (e->fd >= 0) close(e->fd);
         for (cudaEvent_t ev : e->events)
             if (ev) cudaEventDestroy(ev);
         if (e->stream) cudaStreamDestroy(e->stream);
         delete e;
-        errno = ENOMEM;
+        errno = open_error ? open_error : ENOMEM;
         return nullptr;
     }
     return e;
@@ -355,7 +484,8 @@ int ls_b200_stream_stats(void* engine, ls_b200_stream_counters* out) {
     auto* e = static_cast<lsb::Engine*>(engine);
     std::lock_guard<std::mutex> g(e->m);
     *out = e->stats;
-    out->outstanding = uint32_t(e->inflight.size());
+    out->outstanding = uint32_t(e->inflight.size() + e->to_read.size() + e->reading);
+    out->direct = e->direct ? 1u : 0u;
     return 0;
 }
 
@@ -375,11 +505,17 @@ void ls_b200_stream_destroy(void* engine) {
         std::unique_lock<std::mutex> l(e->m);
         e->closing = true;
         e->work.notify_all();
-        e->changed.wait(l, [&] { return e->inflight.empty() && e->landed.empty(); });
+        e->changed.wait(l, [&] {
+            return e->inflight.empty() && e->landed.empty() && e->to_read.empty() && !e->reading &&
+                   e->read_done.empty();
+        });
         e->stop = true;
         e->work.notify_all();
+        e->read_work.notify_all();
     }
     e->worker.join();
+    for (std::thread& t : e->readers) t.join();
+    if (e->fd >= 0) close(e->fd);
     int previous = 0;
     cudaGetDevice(&previous);
     cudaSetDevice(e->cfg.device);

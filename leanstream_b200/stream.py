@@ -38,13 +38,22 @@ class StreamEngine:
     the staging area (stride `stride` >= `group_bytes`)."""
 
     def __init__(self, host_base: int, offsets: Sequence[int], staging: int, stride: int, group_bytes: int,
-                 queue_depth: int = 8, device: int = 0, delay_mean_us: float = 0.0, delay_seed: int = 0):
+                 queue_depth: int = 8, device: int = 0, delay_mean_us: float = 0.0, delay_seed: int = 0,
+                 file_path: Optional[str] = None, file_offsets: Optional[Sequence[int]] = None,
+                 read_workers: int = 4, o_direct: bool = True, file_alignment: int = 4096):
+        """With `file_path`, each admitted group is first read from the file
+        at `file_offsets[g]` into its host slot (the SSD leg), then copied."""
         self.lib = N.load()
         self.count = len(offsets)
         self.offsets = np.ascontiguousarray(np.asarray(offsets, dtype=np.uint64))
         self.io_states = np.zeros(self.count + 1, dtype=np.uint32)  # shared with the worker
+        self.file_offsets = (np.ascontiguousarray(np.asarray(file_offsets, dtype=np.uint64))
+                             if file_offsets is not None else None)
+        self._path = file_path.encode() if file_path else None
         cfg = N.StreamConfig(host_base, self.offsets.ctypes.data, staging, stride, group_bytes,
-                             self.io_states.ctypes.data, self.count, queue_depth, device, delay_mean_us, delay_seed)
+                             self.io_states.ctypes.data, self.count, queue_depth, device, delay_mean_us, delay_seed,
+                             self._path, self.file_offsets.ctypes.data if self.file_offsets is not None else None,
+                             read_workers, 1 if o_direct else 0, file_alignment)
         self.engine = self.lib.ls_b200_stream_create(C.byref(cfg))
         if not self.engine:
             raise RuntimeError(f"ls_b200_stream_create failed (errno {C.get_errno()})")

@@ -115,6 +115,73 @@ def test_engine_priority_order_reorder_and_bytes(native_lib, cuda_device):
     eng.close()
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("o_direct", [True, False])
+def test_engine_reads_groups_from_a_file(native_lib, cuda_device, tmp_path, o_direct):
+    """The SSD leg (src/io/stream_io.cpp:75-148): groups are read from a file
+    (pread by the reader pool, O_DIRECT when the file system allows it) into
+    their pinned host slots, then copied to HBM staging. The layout is
+    config 1's groups (101,376 B) at 4 KB-aligned file offsets, host slots
+    rounded up to the alignment; every committed group lands byte-exact, and
+    the counters report the bytes read and whether O_DIRECT was in effect."""
+    import torch
+
+    from leanstream_b200 import _native as N
+    from leanstream_b200.stream import IOBackendView, StreamEngine
+
+    n, gb, align = 24, 64 * 3 * 1024 // 2, 4096
+    slot = (gb + align - 1) // align * align
+    rng = np.random.default_rng(12)
+    data = rng.integers(0, 256, (n, gb), dtype=np.uint8)
+    file_offsets = [align + g * (slot + align) for g in range(n)]  # gaps between groups, as a packed layout may have
+    path = tmp_path / "groups.bin"
+    blob = np.zeros(file_offsets[-1] + slot, np.uint8)
+    for g in range(n):
+        blob[file_offsets[g]:file_offsets[g] + gb] = data[g]
+    blob.tofile(path)
+    host = torch.zeros(n * slot + align, dtype=torch.uint8).pin_memory()
+    base = (host.data_ptr() + align - 1) // align * align  # 4 KB-aligned host slots
+    staging = torch.zeros(n * gb, dtype=torch.uint8, device="cuda")
+    eng = StreamEngine(base, [g * slot for g in range(n)], staging.data_ptr(), gb, gb, queue_depth=8,
+                       file_path=str(path), file_offsets=file_offsets, read_workers=4, o_direct=o_direct)
+    io = IOBackendView(eng.view())
+    landed = []
+    assert io.begin(lambda e, g, s_, err, seq: landed.append((g, err)), 1) == 0
+    prio = [int(g) for g in rng.permutation(n)[:10]]
+    final = sorted(set(prio[:6]) | {int(rng.integers(n))})
+    assert io.update(prio) == 0
+    assert io.consume(final) == 0
+    assert io.wait(20000) == 0
+    assert io.retire() == 0
+    st = eng.stats()
+    issued = eng.issue_log()
+    assert st["error"] == 0 and st["completions"] == len(issued) and set(final) <= set(issued)
+    assert st["read_bytes"] >= len(issued) * gb and st["read_ns"] > 0
+    assert st["direct"] in (0, 1) and (o_direct or st["direct"] == 0)
+    got = staging.cpu().numpy().reshape(n, gb)
+    for g in issued:
+        assert np.array_equal(got[g], data[g]), g
+        assert int(eng.io_states[g]) == N.IO_READY
+    assert sorted(g for g, _ in landed) == sorted(issued) and all(err == 0 for _, err in landed)
+    eng.close()
+
+
+def test_engine_file_source_errors_on_host(native_lib, tmp_path):
+    """A file source that cannot be opened is refused at creation (errno of
+    open, here ENOENT), and one without file offsets is EINVAL -- before any
+    read is issued. Needs no GPU when none is visible: creation then fails
+    with ENODEV first, which is checked instead."""
+    from leanstream_b200 import _native as N
+
+    lib = native_lib
+    states = np.zeros(3, np.uint32)
+    offs = np.zeros(2, np.uint64)
+    cfg = N.StreamConfig(1 << 20, offs.ctypes.data, 1 << 30, 4096, 4096, states.ctypes.data, 2, 4, 0, 0.0, 0,
+                         str(tmp_path / "missing.bin").encode(), offs.ctypes.data, 2, 1, 4096)
+    assert not lib.ls_b200_stream_create(C.byref(cfg))
+    assert C.get_errno() in (errno.ENOENT, errno.ENODEV)
+
+
 def _config4_inputs(tmp_path, H=1024, G=64, N=64, seed=0):
     from leanstream_b200.synthetic import make_layer
 
