@@ -401,7 +401,17 @@ typedef struct ls_b200_batch_args {
                                * hidden_out the call is one layer of a decode stack */
     float rms_eps;            /* epsilon of the RMSNorm */
     const void* norm_weight;  /* optional fp16 [H] RMSNorm weight (NULL = ones) */
+    uint32_t* error;          /* optional device word: bit 0 set (atomic OR, never cleared) when a
+                               * bounded wait of the tensor-core kernels gave up; the call's
+                               * outputs are then invalid */
 } ls_b200_batch_args;
+/* Flags of ls_b200_batch_args.flags besides LS_B200_NORM_INPUT. */
+enum {
+    /* The two weight kernels on the legacy warp-level MMA (mma.sync m16n8k16)
+     * instead of the 5th-generation tensor cores (tcgen05.mma with the
+     * accumulator in tensor memory, the default) -- kept for comparison. */
+    LS_B200_BATCH_MMA_SYNC = 1u << 8
+};
 uint64_t ls_b200_batch_scratch_bytes(uint32_t hidden, uint32_t group_size, uint32_t union_count);
 int ls_b200_batch_mlp(const ls_b200_batch_args* args, void* stream);
 

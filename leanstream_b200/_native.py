@@ -13,6 +13,7 @@ LIBRARY = Path(__file__).resolve().parent / "libleanstream_b200.so"
 SOURCE_CACHE, SOURCE_STAGING = 0, 1
 MODE_BATCH_COMPAT, MODE_PROGRESSIVE, MODE_AUTO = 0, 1, 2
 NORM_INPUT, NO_OUTPUT = 1, 2
+BATCH_MMA_SYNC = 1 << 8  # ls_b200_batch_args.flags: legacy warp-level MMA instead of tcgen05
 STATUS_ERROR, STATUS_ERROR_EPOCH, STATUS_ERROR_DETAIL, STATUS_LAUNCHES, STATUS_WORDS = 0, 1, 2, 3, 4
 TP_HANDLE_BYTES = 64
 DEV_OK, DEV_QUEUE_ERROR, DEV_TIMEOUT_EPOCH, DEV_TIMEOUT_READY, DEV_TIMEOUT_SYNC, DEV_BAD_DESCRIPTOR, DEV_BAD_PLAN = range(7)
@@ -128,7 +129,7 @@ class BatchArgs(C.Structure):
                 ("residual", C.c_void_p), ("hidden_out", C.c_void_p), ("cache", C.c_void_p),
                 ("staging", C.c_void_p), ("scales", C.c_void_p), ("union_descs", C.c_void_p), ("mask", C.c_void_p),
                 ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64), ("flags", C.c_uint32),
-                ("rms_eps", C.c_float), ("norm_weight", C.c_void_p)]
+                ("rms_eps", C.c_float), ("norm_weight", C.c_void_p), ("error", C.c_void_p)]
 
 assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 104
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32

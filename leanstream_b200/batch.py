@@ -58,35 +58,51 @@ class BatchMLP:
     """One batched MLP layer call at a fixed geometry. Scratch is allocated
     once here (device memory for `max_union` groups) and reused by every
     call; calls on one BatchMLP must not overlap. `scratch` = (pointer,
-    bytes) supplies caller-owned device memory instead."""
+    bytes) supplies caller-owned device memory instead; `error` is then the
+    device address of a caller-owned, zeroed 32-bit error word (or None: the
+    kernels record none), so that nothing is allocated here."""
 
     def __init__(self, hidden: int, group_size: int, max_union: int, device=None,
-                 scratch: Optional[tuple] = None):
+                 scratch: Optional[tuple] = None, error: Optional[int] = None):
         self.lib = N.load()
         self.hidden, self.group_size, self.max_union = hidden, group_size, max_union
         self.scratch_bytes = int(self.lib.ls_b200_batch_scratch_bytes(hidden, group_size, max_union))
         self._scratch = None
-        if scratch is None:
+        if scratch is not None:
+            self.scratch_ptr, have = int(scratch[0]), int(scratch[1])
+            if have < self.scratch_bytes:
+                raise ValueError(f"scratch of {have} B, {self.scratch_bytes} B needed")
+            self._error = None
+            self.error_ptr = int(error or 0)
+        else:
             import torch
 
             self._scratch = torch.empty(self.scratch_bytes, dtype=torch.uint8, device=device or "cuda")
             self.scratch_ptr = self._scratch.data_ptr()
-        else:
-            self.scratch_ptr, have = int(scratch[0]), int(scratch[1])
-            if have < self.scratch_bytes:
-                raise ValueError(f"scratch of {have} B, {self.scratch_bytes} B needed")
+            # the tensor-core kernels' error word (ls_b200_batch_args.error), sticky
+            self._error = torch.zeros(1, dtype=torch.int32, device=device or "cuda")
+            self.error_ptr = self._error.data_ptr()
 
     def args(self, *, x, output, cache, scales, union_descs, union_count: int, tokens: int, mask=None,
              residual=None, hidden_out=None, output_f32=None, staging=None, norm_input=False, rms_eps=1e-5,
-             norm_weight=None) -> N.BatchArgs:
+             norm_weight=None, mma_sync=False) -> N.BatchArgs:
         """norm_input: HF RMSNorm of each token before the MLP (with residual
-        and hidden_out, one layer of a decode stack)."""
+        and hidden_out, one layer of a decode stack). mma_sync: the legacy
+        warp-level MMA kernels instead of tcgen05 (for comparison)."""
         if union_count > self.max_union:
             raise ValueError(f"union of {union_count} groups, BatchMLP sized for {self.max_union}")
         return N.BatchArgs(self.hidden, self.group_size, union_count, tokens, _ptr(x), _ptr(output),
                            _ptr(output_f32), _ptr(residual), _ptr(hidden_out), _ptr(cache), _ptr(staging),
                            _ptr(scales), _ptr(union_descs), _ptr(mask), self.scratch_ptr, self.scratch_bytes,
-                           N.NORM_INPUT if norm_input else 0, rms_eps, _ptr(norm_weight))
+                           (N.NORM_INPUT if norm_input else 0) | (N.BATCH_MMA_SYNC if mma_sync else 0), rms_eps,
+                           _ptr(norm_weight), self.error_ptr)
+
+    def error(self) -> int:
+        """Nonzero when a bounded wait of a tensor-core kernel gave up (the
+        outputs of that call are invalid); reads a device word."""
+        if self._error is None:
+            raise RuntimeError("the error word is caller-owned (BatchMLP(error=...)): read it there")
+        return int(self._error.item())
 
     def run(self, stream=None, **kw) -> None:
         """Enqueues one layer (three launches) on `stream` (a torch stream,

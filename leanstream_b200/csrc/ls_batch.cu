@@ -467,6 +467,335 @@ __global__ void __launch_bounds__(256) batch_norm_kernel(const __half* x, const 
 
 // Scratch: h [8][NTP] fp16, then the down partials [kDownSplits][8][H] fp32,
 // then the normalised activations [8][H] fp16 (LS_B200_NORM_INPUT).
+// ------------------------------------------------------------------ tcgen05
+// The union GEMMs on the 5th-generation tensor cores (tcgen05.mma, A and B
+// from shared memory, the fp32 accumulator in tensor memory). One CTA of
+// four warps per tile; the 128 threads convert the tile's int4 rows into
+// fp16 w = fp16(q * s) (deq, the same exact conversion as above) in the
+// canonical no-swizzle layout, one elected thread issues the MMAs
+// (M 128 x N 8 x K 16 each, the 8 tokens as N), and tcgen05.commit frees a
+// stage when its MMAs have read it. The accumulator comes back with
+// tcgen05.ld (warp w reads tensor-memory lanes 32w..32w+31).
+//
+// Layouts (bytes, 8-row x 16-byte core matrices, no swizzle):
+//   gate/up A, K-major:  row r, coordinate k of the stage at
+//     (r / 8) * 1024 + (k / 8) * 128 + (r % 8) * 16 + pos(k % 8) * 2
+//     (stride-dimension offset 1024, leading-dimension offset 128);
+//   gate/up B (x), K-major: token n at (k / 8) * 128 + n * 16 + pos(k % 8) * 2;
+//   down A, MN-major:  output column m, neuron k at
+//     (m / 8) * 1024 + (k / 8) * 128 + (k % 8) * 16 + pos(m % 8) * 2;
+//   down B (h), K-major: token n, neuron k at (k / 8) * 128 + n * 16 + (k % 8) * 2.
+// pos() is the order deq produces within 8 coordinates (0, 4, 1, 5, 2, 6, 3,
+// 7). Along K (gate/up) A and B share it, so the dot products are those of
+// the natural order; along M (down) it permutes the accumulator rows, which
+// the epilogue undoes (row 8g + p holds column 8g + (p >> 1) + 4 (p & 1)).
+//
+// Every wait is bounded (kTcTimeoutNs): on expiry the CTA sets bit 0 of the
+// caller's error word (ls_b200_batch_args.error), waits (bounded) for the
+// MMAs it issued, frees its tensor memory and returns.
+constexpr uint32_t kTcRows = 128;                      // MMA M
+constexpr uint32_t kTcK = 64;                          // coordinates (gate/up) or neurons (down) per stage
+constexpr uint32_t kTcStages = 4;
+constexpr uint32_t kTcA = kTcRows * kTcK * 2;          // 16 KB
+constexpr uint32_t kTcB = kBatchTokens * kTcK * 2;     // 1 KB
+constexpr uint32_t kTcStage = kTcA + kTcB;
+constexpr uint32_t kTcSmem = kTcStages * kTcStage + 128;  // + mbarriers and the tensor-memory address
+constexpr uint32_t kTcCols = 32;                       // tensor-memory columns allocated (8 used)
+constexpr uint64_t kTcTimeoutNs = 2000000000ull;
+static_assert(kTcStage % 128 == 0, "stage alignment");
+// kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0),
+// both K-major, N = 8 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4);
+// bit 15 makes A MN-major (the down projection).
+constexpr uint32_t kIdescK = (1u << 4) | (1u << 17) | (8u << 24);
+constexpr uint32_t kIdescMN = kIdescK | (1u << 15);
+
+__device__ __forceinline__ uint32_t sm_u32(const void* q) { return uint32_t(__cvta_generic_to_shared(q)); }
+__device__ __forceinline__ uint64_t tc_now() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Shared-memory matrix descriptor, no swizzle, version 1 (bit 46).
+__device__ __forceinline__ uint64_t tc_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+           (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
+}
+__device__ __forceinline__ void tc_mbar_init(uint32_t bar, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(n) : "memory");
+}
+__device__ __forceinline__ bool tc_mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the completion of phase `parity`; false at the deadline.
+__device__ bool tc_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
+    uint32_t spins = 0;
+    while (!tc_mbar_test(bar, parity)) {
+        if ((++spins & 255u) == 0 && tc_now() > deadline) return false;
+        __nanosleep(20);
+    }
+    return true;
+}
+__device__ __forceinline__ void tc_alloc(uint32_t slot) {  // warp-wide
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "n"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr) {  // warp-wide, the allocating warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(kTcCols) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Lanes 32w..32w+31, columns 0..7 of the accumulator (one token each).
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// The 8 fp16 of a 16-byte chunk of consecutive values x0..x7, reordered to
+// the deq order (x0, x4, x1, x5, x2, x6, x3, x7).
+__device__ __forceinline__ uint4 to_pos(uint4 w) {
+    return make_uint4(__byte_perm(w.x, w.z, 0x5410), __byte_perm(w.x, w.z, 0x7632), __byte_perm(w.y, w.w, 0x5410),
+                      __byte_perm(w.y, w.w, 0x7632));
+}
+// 8 weights of one packed word as fp16(q * s), in the deq order.
+__device__ __forceinline__ uint4 deq8(uint32_t w, __half2 s2) {
+    return make_uint4(deq(w, 0, s2), deq(w, 1, s2), deq(w, 2, s2), deq(w, 3, s2));
+}
+
+// Shared teardown: wait (bounded) for the MMAs this CTA issued, free the
+// tensor memory. `issued` commits were made; the last one was on stage
+// (issued - 1) % kTcStages with parity ((issued - 1) / kTcStages) & 1.
+__device__ void tc_finish(uint32_t* err, const uint64_t* mbar, uint32_t issued, uint32_t tmem, bool ok) {
+    if (threadIdx.x == 0 && issued) {
+        const uint32_t i = issued - 1;
+        if (!tc_wait(sm_u32(mbar + i % kTcStages), (i / kTcStages) & 1u, tc_now() + kTcTimeoutNs)) ok = false;
+    }
+    if (!ok && err) atomicOr(err, 1u);
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x < 32) tc_dealloc(tmem);
+}
+
+// gate/up: one CTA per 64 union neurons, 128 MMA rows (row 2j the gate row,
+// 2j + 1 the up row of neuron j), K = H in stages of 64 coordinates.
+__global__ void __launch_bounds__(128) batch_gateup_tc_kernel(const BatchParams p, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kTcStages * kTcStage);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + kTcStages);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 0) tc_alloc(sm_u32(tslot));
+    if (tid == 0) {
+        for (uint32_t i = 0; i < kTcStages; ++i) tc_mbar_init(sm_u32(mbar + i), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint64_t deadline = tc_now() + kTcTimeoutNs;
+    // this thread's A row: neuron j = tid / 2 of the tile, gate (even) or up (odd)
+    const uint32_t nrow = blockIdx.x * 64 + uint32_t(tid >> 1);
+    const bool valid = nrow < p.NT;
+    const uint8_t* src = nullptr;
+    const __half* sc = nullptr;
+    if (valid) {
+        const Row r = neuron_row(p, nrow);
+        src = r.src + (tid & 1) * (p.H / 2);
+        sc = r.sc + (tid & 1) * (p.H / 128);
+    }
+    const uint32_t nst = p.H / kTcK;
+    uint8_t* arow = sm + (tid / 8) * 1024 + (tid % 8) * 16;  // chunk c of this row at + c * 128
+    uint4 cur0 = make_uint4(0u, 0u, 0u, 0u), cur1 = cur0;
+    if (valid) {
+        cur0 = __ldg(reinterpret_cast<const uint4*>(src));
+        cur1 = __ldg(reinterpret_cast<const uint4*>(src) + 1);
+    }
+    bool ok = true;
+    uint32_t issued = 0;
+    for (uint32_t i = 0; i < nst; ++i) {
+        const uint32_t s = i % kTcStages;
+        uint8_t* stage = sm + s * kTcStage;
+        if (i >= kTcStages && !tc_wait(sm_u32(mbar + s), ((i / kTcStages) - 1) & 1u, deadline)) ok = false;
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+        }
+        // next stage's 32 bytes in flight while this one is converted
+        uint4 nx0 = make_uint4(0u, 0u, 0u, 0u), nx1 = nx0;
+        if (valid && i + 1 < nst) {
+            nx0 = __ldg(reinterpret_cast<const uint4*>(src + 32 * (i + 1)));
+            nx1 = __ldg(reinterpret_cast<const uint4*>(src + 32 * (i + 1)) + 1);
+        }
+        const __half2 s2 = __half2half2(valid ? sc[(kTcK * i) / 128] : __float2half_rn(0.f));
+        const uint32_t w[8] = {cur0.x, cur0.y, cur0.z, cur0.w, cur1.x, cur1.y, cur1.z, cur1.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stage + (arow - sm) + c * 128) = deq8(w[c], s2);
+        if (tid < 64) {  // x of the stage: token n = tid / 8, coordinates 8c .. 8c + 7
+            const uint32_t n = tid >> 3, c = tid & 7;
+            uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+            if (n < p.B) xv = __ldg(reinterpret_cast<const uint4*>(p.x + size_t(n) * p.H + kTcK * i + 8 * c));
+            *reinterpret_cast<uint4*>(stage + kTcA + c * 128 + n * 16) = to_pos(xv);
+        }
+        proxy_fence();  // generic-proxy stores -> visible to the tensor core (async proxy)
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a = sm_u32(stage), b = sm_u32(stage + kTcA);
+#pragma unroll
+            for (uint32_t kk = 0; kk < kTcK / 16; ++kk)
+                tc_mma(tmem, tc_desc(a + 256 * kk, 128, 1024), tc_desc(b + 256 * kk, 128, 1024), kIdescK,
+                       (i | kk) ? 1u : 0u);
+            tc_commit(sm_u32(mbar + s));
+        }
+        ++issued;
+        cur0 = nx0;
+        cur1 = nx1;
+    }
+    if (ok) {  // every MMA done: the accumulator rows
+        const uint32_t last = issued - 1;
+        if (!tc_wait(sm_u32(mbar + last % kTcStages), (last / kTcStages) & 1u, deadline)) ok = false;
+    }
+    if (__syncthreads_and(ok)) {
+        tc_fence_after();
+        float v[8];
+        tc_ld8(tmem + (uint32_t(32 * warp) << 16), v);
+        const uint32_t u = valid ? nrow / p.G : 0u;
+#pragma unroll
+        for (int b = 0; b < kBatchTokens; ++b) {
+            const float up = __shfl_xor_sync(0xffffffffu, v[b], 1);  // odd lane: the up row
+            if ((lane & 1) || !valid || uint32_t(b) >= p.B) continue;
+            const float g16 = __half2float(__float2half_rn(v[b])), u16 = __half2float(__float2half_rn(up));
+            const float sl = __half2float(__float2half_rn(g16 / (1.f + expf(-g16))));
+            __half h = __float2half_rn(sl * u16);
+            if (p.mask && !p.mask[size_t(b) * p.U + u]) h = __float2half_rn(0.f);
+            p.hT[size_t(b) * p.NTP + nrow] = h;
+        }
+    }
+    tc_finish(err, mbar, issued, tmem, ok);
+}
+
+// down: one CTA per 128 output columns and split of the union's neurons
+// (the splits of the mma.sync kernel, summed by the epilogue).
+__global__ void __launch_bounds__(128) batch_down_tc_kernel(const BatchParams p, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kTcStages * kTcStage);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + kTcStages);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 0) tc_alloc(sm_u32(tslot));
+    if (tid == 0) {
+        for (uint32_t i = 0; i < kTcStages; ++i) tc_mbar_init(sm_u32(mbar + i), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint64_t deadline = tc_now() + kTcTimeoutNs;
+    const uint32_t c0 = blockIdx.x * kTcRows, split = blockIdx.y;
+    // split boundaries on 64-neuron stage boundaries (16-byte aligned h rows)
+    const uint32_t k_begin = uint32_t(uint64_t(p.NT) * split / kDownSplits) / kTcK * kTcK;
+    const uint32_t k_end =
+        split + 1 == kDownSplits ? p.NT : uint32_t(uint64_t(p.NT) * (split + 1) / kDownSplits) / kTcK * kTcK;
+    const uint32_t nst = (k_end - k_begin + kTcK - 1) / kTcK;
+    // converter: neuron kl = tid % 64 of the stage, columns 64 * (tid / 64) .. +63
+    const uint32_t kl = uint32_t(tid) & 63u, half = uint32_t(tid) >> 6;
+    bool ok = true;
+    uint32_t issued = 0;
+    for (uint32_t i = 0; i < nst; ++i) {
+        const uint32_t s = i % kTcStages;
+        uint8_t* stage = sm + s * kTcStage;
+        if (i >= kTcStages && !tc_wait(sm_u32(mbar + s), ((i / kTcStages) - 1) & 1u, deadline)) ok = false;
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+        }
+        const uint32_t k = k_begin + kTcK * i + kl;
+        uint4 w0 = make_uint4(0u, 0u, 0u, 0u), w1 = w0;
+        __half2 s2 = __float2half2_rn(0.f);
+        if (k < k_end) {
+            const Row r = neuron_row(p, k);
+            const uint8_t* d = r.src + p.H + (c0 + 64 * half) / 2;  // 32 bytes: 64 columns
+            w0 = __ldg(reinterpret_cast<const uint4*>(d));
+            w1 = __ldg(reinterpret_cast<const uint4*>(d) + 1);
+            s2 = __half2half2(r.sc[2 * (p.H / 128) + c0 / 128]);
+        }
+        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // columns c0 + 64 half + 8q .. +7: M group 8 half + q
+            const uint32_t g = 8 * half + uint32_t(q);
+            *reinterpret_cast<uint4*>(stage + g * 1024 + (kl / 8) * 128 + (kl % 8) * 16) = deq8(w[q], s2);
+        }
+        if (tid < 64) {  // h of the stage: token n = tid / 8, neurons 8c .. 8c + 7
+            const uint32_t n = tid >> 3, c = tid & 7, k8 = k_begin + kTcK * i + 8 * c;
+            uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+            if (n < p.B && k8 < k_end) {
+                hv = *reinterpret_cast<const uint4*>(p.hT + size_t(n) * p.NTP + k8);
+                // neurons past the split's end (and past the union) contribute nothing
+                const uint32_t valid_n = k_end - k8;
+                if (valid_n < 8) {
+                    uint32_t* hw = reinterpret_cast<uint32_t*>(&hv);
+#pragma unroll
+                    for (uint32_t e = 0; e < 4; ++e) {
+                        if (2 * e >= valid_n) hw[e] = 0u;
+                        else if (2 * e + 1 >= valid_n) hw[e] &= 0xffffu;
+                    }
+                }
+            }
+            *reinterpret_cast<uint4*>(stage + kTcA + c * 128 + n * 16) = hv;
+        }
+        proxy_fence();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a = sm_u32(stage), b = sm_u32(stage + kTcA);
+#pragma unroll
+            for (uint32_t kk = 0; kk < kTcK / 16; ++kk)
+                tc_mma(tmem, tc_desc(a + 256 * kk, 128, 1024), tc_desc(b + 256 * kk, 128, 1024), kIdescMN,
+                       (i | kk) ? 1u : 0u);
+            tc_commit(sm_u32(mbar + s));
+        }
+        ++issued;
+    }
+    if (ok && issued) {
+        const uint32_t last = issued - 1;
+        if (!tc_wait(sm_u32(mbar + last % kTcStages), (last / kTcStages) & 1u, deadline)) ok = false;
+    }
+    if (__syncthreads_and(ok)) {
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (issued) {
+            tc_fence_after();
+            tc_ld8(tmem + (uint32_t(32 * warp) << 16), v);
+        }
+        const uint32_t m = uint32_t(32 * warp + lane), col = c0 + 8 * (m / 8) + ((m % 8) >> 1) + 4 * (m & 1);
+        float* out = p.partial + size_t(split) * p.B * p.H;
+        for (uint32_t b = 0; b < p.B; ++b) out[size_t(b) * p.H + col] = v[b];
+    }
+    tc_finish(err, mbar, issued, tmem, ok);
+}
+
 uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) {
     const uint64_t nt = uint64_t(G) * U, ntp = (nt + 15) / 16 * 16 + 16;
     const uint64_t ht = (ntp * kBatchTokens * sizeof(__half) + 255) / 256 * 256;
@@ -485,6 +814,10 @@ cudaError_t set_ring_attributes() {
     const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
     if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
     e = cudaFuncSetAttribute(batch_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGuSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(batch_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(batch_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(batch_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDnSmem));
     if (e == cudaSuccess)
@@ -513,7 +846,8 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     // union neurons index rows of h and the gate/up grid in 32 bits
     if (uint64_t(G) * U > (uint64_t(1) << 30)) return EINVAL;
     if (!a->x || !a->output || !a->cache || !a->scales || !a->union_descs || !a->scratch ||
-        (a->hidden_out && !a->residual) || (a->flags & ~uint32_t(LS_B200_NORM_INPUT)) ||
+        (a->hidden_out && !a->residual) ||
+        (a->flags & ~uint32_t(LS_B200_NORM_INPUT | LS_B200_BATCH_MMA_SYNC)) ||
         (a->norm_weight && !(a->flags & LS_B200_NORM_INPUT)))
         return EINVAL;
     if (a->scratch_bytes < batch_scratch(H, G, U)) return ENOSPC;
@@ -548,8 +882,13 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
         batch_norm_kernel<<<B, 256, 0, s>>>(p.x, static_cast<const __half*>(a->norm_weight), a->rms_eps, H, xn);
         p.x = xn;
     }
-    batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, kGuSmem, s>>>(p);
-    batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, kDnSmem, s>>>(p);
+    if (a->flags & LS_B200_BATCH_MMA_SYNC) {
+        batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, kGuSmem, s>>>(p);
+        batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, kDnSmem, s>>>(p);
+    } else {
+        batch_gateup_tc_kernel<<<(p.NT + 63) / 64, 128, kTcSmem, s>>>(p, a->error);
+        batch_down_tc_kernel<<<dim3(H / kTcRows, kDownSplits), 128, kTcSmem, s>>>(p, a->error);
+    }
     const uint32_t total = B * H;
     batch_epilogue_kernel<<<(total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024, 256, 0, s>>>(p);
     const cudaError_t e = cudaGetLastError();

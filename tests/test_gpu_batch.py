@@ -130,3 +130,45 @@ def test_batch_norm_chains_layers(native_lib, cuda_device, H):
             ref = O.residual(x_l, y_ref).astype(np.float32)
             out = got[l + 1][b].astype(np.float32)
             assert np.abs(out - ref).max() <= TOL * np.abs(ref).max() + 1e-3, (b, l, np.abs(out - ref).max())
+
+
+@pytest.mark.parametrize("H,n_groups", [(1024, 40), (8192, 24)])
+def test_tcgen05_matches_warp_mma(native_lib, cuda_device, H, n_groups):
+    """The default tensor-core kernels (tcgen05.mma, accumulator in tensor
+    memory) and the legacy warp-level MMA kernels run the same arithmetic
+    (w = fp16(q * s), fp32 sums) in different summation orders: their
+    outputs agree within the output tolerance, both equal the masked
+    one-token oracle, and the tcgen05 error word stays clear."""
+    import torch
+    from leanstream_b200.batch import BatchMLP, union_plan
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    G, B = 64, 8
+    L = make_layer(23, H, n_groups, G)
+    rng = np.random.default_rng(5)
+    sets = [np.sort(rng.permutation(n_groups)[: rng.integers(4, n_groups // 2)]) for _ in range(B)]
+    union, rows, mask = union_plan(sets)
+    x = (rng.standard_normal((B, H)) * 0.5).astype(np.float16)
+    mlp = BatchMLP(H, G, n_groups, device="cuda")
+    cache = torch.from_numpy(L.packed).cuda()
+    scales = torch.from_numpy(L.scales.reshape(-1).view(np.int16)).cuda().view(torch.float16)
+    desc = torch.from_numpy(np.ascontiguousarray(rows.reshape(-1).view(np.int32))).cuda()
+    mk = torch.from_numpy(np.ascontiguousarray(mask)).cuda()
+    xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    outs = {}
+    for legacy in (False, True):
+        y = torch.zeros(B, H, dtype=torch.float16, device="cuda")
+        y32 = torch.zeros(B, H, dtype=torch.float32, device="cuda")
+        mlp.run(x=xt, output=y, output_f32=y32, cache=cache, scales=scales, union_descs=desc,
+                union_count=len(union), tokens=B, mask=mk, mma_sync=legacy)
+        torch.cuda.synchronize()
+        outs[legacy] = (y.cpu().numpy().astype(np.float32), y32.cpu().numpy())
+    assert mlp.error() == 0
+    tc, mm = outs[False][1], outs[True][1]
+    assert np.isfinite(tc).all()
+    assert np.abs(tc - mm).max() <= TOL * np.abs(mm).max(), np.abs(tc - mm).max()
+    for b in range(B):
+        y_ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
+        ref = y_ref.astype(np.float32)
+        assert np.abs(outs[False][0][b] - ref).max() <= TOL * np.abs(ref).max(), b
