@@ -851,6 +851,7 @@ def run_batch(args, rank, world, local_rank):
     # writes xs[l+1] = fp16(xs[l] + y)
     xs = [x] + [torch.zeros(BATCH, H, dtype=torch.float16, device=dev) for _ in range(LAYERS)]
     mlp = BatchMLP(H, G, NGROUPS, device=dev)  # the public batch API; scratch sized for every group
+    mma_sync = args.batch_kernels == "mma_sync"
     progress("weights and batch plans resident")
     stream = torch.cuda.Stream()
 
@@ -859,7 +860,8 @@ def run_batch(args, rank, world, local_rank):
             off = base + layer * lstride
             mlp.run(stream=strm, x=xs[layer], output=y, cache=st.cache[layer], scales=st.scales[layer],
                     union_descs=off, union_count=int(unions[s, layer]), tokens=BATCH, mask=off + NGROUPS * 20,
-                    residual=xs[layer], hidden_out=xs[layer + 1], norm_input=True, rms_eps=EPS)
+                    residual=xs[layer], hidden_out=xs[layer + 1], norm_input=True, rms_eps=EPS,
+                    mma_sync=mma_sync)
 
     # first calls outside capture (the call opts the kernels into their ring size)
     with torch.cuda.stream(stream):
@@ -956,14 +958,21 @@ def run_batch(args, rank, world, local_rank):
         "arithmetic": "w = fp16(q * s) as the reference (backends/triton/core.py:17), fp32 accumulation",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None,
-                     "kernel": "batch_gateup_kernel + batch_down_kernel + batch_epilogue_kernel (one layer)",
+                     "kernel": ("batch_gateup_kernel + batch_down_kernel" if mma_sync else
+                                "batch_gateup_tc_kernel + batch_down_tc_kernel") +
+                               " + batch_norm_kernel + batch_epilogue_kernel (one layer)",
                      "algorithmic_bytes_per_group": ALG_BYTES_PER_GROUP,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback"},
         "e2e": {"value": BATCH * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": 3 * LAYERS * args.steps,
+        # per layer: RMSNorm + gate/up + down + epilogue (warp MMA), or x image
+        # (with the RMSNorm) + gate/up + h + down + epilogue (tcgen05)
+        "gpu_launches": (4 if mma_sync else 5) * LAYERS * args.steps,
+        "batch_kernels": args.batch_kernels,
         "clocks": clock,
     }
+    if mlp.error():
+        raise RuntimeError("a tensor-core batch kernel gave up a bounded wait")
     torch.cuda.synchronize()
     for g in graphs + e2e_graphs:
         g.reset()
@@ -1153,6 +1162,8 @@ def main():
                    help="BASELINE.json configuration: 3 (headline, H 4096, 36 layers) or 5 (H 8192, 80 layers)")
     p.add_argument("--batch", type=int, choices=[1, 8], default=1,
                    help="tokens per step: 1 (the default workload) or 8 (union decode, one GPU)")
+    p.add_argument("--batch-kernels", choices=["tcgen05", "mma_sync"], default="tcgen05",
+                   help="--batch 8 projections: tcgen05 MMAs (default) or the warp-level MMA kernels")
     p.add_argument("--headline-only", action="store_true",
                    help="skip the extra measurements printed beside the headline (per-layer enqueue path, config 5)")
     p.add_argument("--layers", type=int, default=0,

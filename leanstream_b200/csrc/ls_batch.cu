@@ -68,8 +68,13 @@ struct BatchParams {
     const __half* scales;
     const ls_exec_desc* desc;
     const uint8_t* mask;
-    __half* hT;      // [8][NTP] h, token-major
-    float* partial;  // [kDownSplits][B][H]
+    __half* hT;      // [8][NTP] h, token-major (warp-MMA path)
+    float* partial;  // [dn_splits][B][H]
+    // tensor-core path
+    const uint8_t* ximg;  // x image [H / 8][8 tokens][8] fp16, K-major core matrices
+    float* gpart;         // gate/up split sums [gu_splits][rows_total][8]
+    __half* hB;           // h image [NT64 / 8][8 tokens][8] fp16
+    uint32_t gu_splits, dn_splits, rows_total;
 };
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -424,7 +429,7 @@ __global__ void batch_epilogue_kernel(const BatchParams p) {
     const uint32_t total = p.B * p.H;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         float y = 0.f;
-        for (uint32_t s = 0; s < kDownSplits; ++s) y += p.partial[size_t(s) * total + i];
+        for (uint32_t s = 0; s < p.dn_splits; ++s) y += p.partial[size_t(s) * total + i];
         const __half y16 = __float2half_rn(y);
         if (p.y32) p.y32[i] = y;
         if (p.y) p.y[i] = y16;
@@ -465,49 +470,112 @@ __global__ void __launch_bounds__(256) batch_norm_kernel(const __half* x, const 
     }
 }
 
-// Scratch: h [8][NTP] fp16, then the down partials [kDownSplits][8][H] fp32,
-// then the normalised activations [8][H] fp16 (LS_B200_NORM_INPUT).
 // ------------------------------------------------------------------ tcgen05
-// The union GEMMs on the 5th-generation tensor cores (tcgen05.mma, A and B
-// from shared memory, the fp32 accumulator in tensor memory). One CTA of
-// four warps per tile; the 128 threads convert the tile's int4 rows into
-// fp16 w = fp16(q * s) (deq, the same exact conversion as above) in the
-// canonical no-swizzle layout, one elected thread issues the MMAs
-// (M 128 x N 8 x K 16 each, the 8 tokens as N), and tcgen05.commit frees a
-// stage when its MMAs have read it. The accumulator comes back with
-// tcgen05.ld (warp w reads tensor-memory lanes 32w..32w+31).
+// The union GEMMs on the 5th-generation tensor cores. Both kernels are
+// warp-specialised: a producer warp streams the raw int4 rows of the union
+// into a shared-memory ring with cp.async.bulk (completion on mbarriers),
+// eight converter warps turn them into w = fp16(q * s) (deq, the exact
+// conversion above), and one thread issues tcgen05.mma with the fp32
+// accumulator in tensor memory; tcgen05.commit releases every buffer an MMA
+// has read. Per 16-coordinate (gate/up) or 16-neuron (down) step the tensor
+// core does what 8 to 16 warp-level MMAs did, so the converter warps spend
+// their issue slots on the conversion alone, and the ring keeps several
+// stages of HBM reads in flight per SM.
 //
-// Layouts (bytes, 8-row x 16-byte core matrices, no swizzle):
-//   gate/up A, K-major:  row r, coordinate k of the stage at
-//     (r / 8) * 1024 + (k / 8) * 128 + (r % 8) * 16 + pos(k % 8) * 2
-//     (stride-dimension offset 1024, leading-dimension offset 128);
-//   gate/up B (x), K-major: token n at (k / 8) * 128 + n * 16 + pos(k % 8) * 2;
-//   down A, MN-major:  output column m, neuron k at
-//     (m / 8) * 1024 + (k / 8) * 128 + (k % 8) * 16 + pos(m % 8) * 2;
-//   down B (h), K-major: token n, neuron k at (k / 8) * 128 + n * 16 + (k % 8) * 2.
+// gate/up (batch_gateup_tc_kernel): CTA = tile of 64 union neurons (128 A
+// rows: row 2j the gate row, 2j + 1 the up row of neuron j) x one of S
+// splits of the hidden dimension. A lives in TENSOR memory: each converter
+// thread owns one row (tcgen05.st.32x32b, lane = row), so the fp16 weights
+// never pass through shared memory. B is the stage's slice of the x image
+// (batch_ximg_kernel: 8 tokens, K-major core matrices, one 4 KB bulk copy
+// per stage). The form with A in tensor memory takes N >= 16 at M = 128:
+// B rows 8..15 alias rows 0..7 (zero stride between the two 8-row groups)
+// and D columns 8..15 are never read. Each split stores its fp32 sums;
+// batch_h_tc_kernel adds the splits in split order and applies the SiLU
+// chain. The per-stage scales (two per row) are copied by the producer.
+//
+// down (batch_down_tc_kernel): CTA = 256 output columns (two M = 128 tiles,
+// two accumulators) x one split of the union's neurons. The MMA's A is the
+// down rows (M = output columns, K = neurons), which only shared memory can
+// hold in that orientation: the converters write M-major core matrices into
+// a double-buffered A area; B = h from the K-major image batch_h_tc_kernel
+// writes (one 1 KB bulk copy per 64 neurons).
+//
+// Core-matrix layouts (8 rows x 16 bytes, no swizzle):
+//   x image / h image, K-major: coordinate k of token n at
+//     (k / 8) * 128 + n * 16 + pos(k % 8) * 2 (x) or + (k % 8) * 2 (h);
+//   down A, M-major: output column m, neuron k of the stage at
+//     (m / 128) * 16384 + ((m % 128) / 8) * 1024 + (k / 8) * 128 + (k % 8) * 16
+//     + pos(m % 8) * 2.
 // pos() is the order deq produces within 8 coordinates (0, 4, 1, 5, 2, 6, 3,
-// 7). Along K (gate/up) A and B share it, so the dot products are those of
-// the natural order; along M (down) it permutes the accumulator rows, which
-// the epilogue undoes (row 8g + p holds column 8g + (p >> 1) + 4 (p & 1)).
+// 7). Along K (gate/up) the tensor-memory A and the x image share it, so the
+// dot products are those of the natural order; along M (down) it permutes
+// the accumulator rows, which the epilogue undoes (row 8g + p holds column
+// 8g + (p >> 1) + 4 (p & 1)).
 //
-// Every wait is bounded (kTcTimeoutNs): on expiry the CTA sets bit 0 of the
-// caller's error word (ls_b200_batch_args.error), waits (bounded) for the
-// MMAs it issued, frees its tensor memory and returns.
-constexpr uint32_t kTcRows = 128;                      // MMA M
-constexpr uint32_t kTcK = 64;                          // coordinates (gate/up) or neurons (down) per stage
-constexpr uint32_t kTcStages = 4;
-constexpr uint32_t kTcA = kTcRows * kTcK * 2;          // 16 KB
-constexpr uint32_t kTcB = kBatchTokens * kTcK * 2;     // 1 KB
-constexpr uint32_t kTcStage = kTcA + kTcB;
-constexpr uint32_t kTcSmem = kTcStages * kTcStage + 128;  // + mbarriers and the tensor-memory address
-constexpr uint32_t kTcCols = 32;                       // tensor-memory columns allocated (8 used)
+// Every wait is bounded (kTcTimeoutNs): on expiry the waiting role sets bit 0
+// of the caller's error word (ls_b200_batch_args.error) and leaves its loop;
+// the producer then waits (bounded) for the copies it issued, the MMA thread
+// for the MMAs it issued, and the tensor memory is freed before the CTA ends.
 constexpr uint64_t kTcTimeoutNs = 2000000000ull;
-static_assert(kTcStage % 128 == 0, "stage alignment");
 // kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0),
-// both K-major, N = 8 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4);
-// bit 15 makes A MN-major (the down projection).
-constexpr uint32_t kIdescK = (1u << 4) | (1u << 17) | (8u << 24);
-constexpr uint32_t kIdescMN = kIdescK | (1u << 15);
+// K-major unless bit 15 (A M-major) is set, N >> 3 in bits 17-22, M >> 4 in
+// bits 24-28.
+constexpr uint32_t kIdescGateUp = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);   // M 128 N 16
+constexpr uint32_t kIdescDown = (1u << 4) | (1u << 15) | ((8u >> 3) << 17) | ((128u >> 4) << 24);  // M 128 N 8
+
+// gate/up geometry. A ring stage is 256 coordinates of the tile's 128 rows
+// (128 B of each row); an A chunk is 128 of them (one scale block, 64
+// tensor-memory columns, 8 MMAs), converted by one of two warp groups in
+// turn. Each wait of the MMA thread drains the MMA pipeline (measured: a
+// few hundred cycles, and even a plain shared-memory load of the issuing
+// thread stalls behind its MMAs), so it waits once per chunk; with two CTAs
+// per SM the other CTA's MMAs keep the tensor core busy meanwhile, and the
+// sixteen converter warps of the SM hide each other's latency. (Measured
+// alternative, slower: one CTA per SM waiting once per 16 MMAs.)
+constexpr uint32_t kGtK = 256;                          // coordinates per ring stage
+constexpr uint32_t kGtChunk = 128;                      // coordinates per tensor-memory A buffer
+constexpr uint32_t kGtChunks = kGtK / kGtChunk;         // 2: converter group g takes chunk g of each stage
+constexpr uint32_t kGtRowPitch = kGtK / 2 + 16;         // int4 of a row + 16 (conflict-free reads)
+constexpr uint32_t kGtW = 128 * kGtRowPitch;            // 18432
+constexpr uint32_t kGtX = kGtK * kBatchTokens * 2;      // 4096: the stage's x image
+constexpr uint32_t kGtS = 128 * (kGtK / 128) * 2;       // 512: the rows' two fp16 scales
+constexpr uint32_t kGtStage = kGtW + kGtX + kGtS;       // 23040
+constexpr uint32_t kGtStages = 4;
+constexpr uint32_t kGtABufs = 3;                        // A buffers of kGtChunk / 2 columns, in rotation
+constexpr uint32_t kGtDCol = kGtABufs * kGtChunk / 2;   // two accumulators (consecutive units) of 16 columns
+constexpr uint32_t kGtTmemCols = 256;
+constexpr uint32_t kGtBars = 2 * kGtStages + 2 * kGtABufs + 4;  // full, empty, afull, aempty, dfull[2], dempty[2]
+constexpr uint32_t kGtSmem = kGtStages * kGtStage + 256;
+constexpr uint32_t kGtCtasPerSm = 2;
+constexpr uint32_t kGtThreads = 448;                    // producer, MMA, 8 converter, 4 epilogue warps
+static_assert(kGtStage % 128 == 0 && kGtW % 16 == 0 && (kGtW + kGtX) % 16 == 0, "stage alignment");
+static_assert(kGtBars * 8 + 4 <= 256 && kGtSmem * kGtCtasPerSm <= 227 * 1024, "barrier area, shared memory");
+static_assert(kGtDCol + 2 * 16 <= kGtTmemCols, "tensor-memory budget");
+
+// down geometry. A stage is 128 neurons: 16 MMAs (two M tiles x 8 K
+// steps) per wait of the MMA thread. The converters also copy the stage's h
+// slice next to A, so that one barrier (A ready) covers both operands.
+constexpr uint32_t kDtK = 128;                          // neurons per ring stage
+constexpr uint32_t kDtCols = 256;                       // output columns per CTA
+constexpr uint32_t kDtRowPitch = 144;                   // 128 B of int4 per neuron + 16
+constexpr uint32_t kDtW = kDtK * kDtRowPitch;           // 18432
+constexpr uint32_t kDtH = kDtK * kBatchTokens * 2;      // 2048: the stage's h image
+constexpr uint32_t kDtS = kDtK * 4;                     // two fp16 scales per neuron
+constexpr uint32_t kDtRaw = kDtW + kDtH + kDtS;         // 20992
+constexpr uint32_t kDtRawStages = 4;
+constexpr uint32_t kDtMTile = 128 * kDtK * 2;           // 32768: one M tile of A
+constexpr uint32_t kDtA = 2 * kDtMTile + kDtH;          // two M tiles + the h copy
+constexpr uint32_t kDtABufs = 2;
+constexpr uint32_t kDtBars = 2 * kDtRawStages + 2 * kDtABufs + 4;  // rfull, rempty, afull, aempty, dfull[2], dempty[2]
+constexpr uint32_t kDtDescCache = 256;                  // union groups cached by the producer
+constexpr uint32_t kDtSmem = kDtABufs * kDtA + kDtRawStages * kDtRaw + 256 + kDtDescCache * 8;
+constexpr uint32_t kDtThreads = 448;                    // producer, MMA, 8 converter, 4 epilogue warps
+constexpr uint32_t kDtTmemCols = 32;                    // [2 units][2 M tiles] x 8 columns
+constexpr uint32_t kMaxDownSplits = 16;
+static_assert(kDtRaw % 128 == 0 && kDtA % 1024 == 0 && kDtSmem <= 227 * 1024, "stage alignment, budget");
+static_assert(kDtBars * 8 + 4 <= 256, "barrier area");
+static_assert(kMaxDownSplits >= kDownSplits, "partials sized for both paths");
 
 __device__ __forceinline__ uint32_t sm_u32(const void* q) { return uint32_t(__cvta_generic_to_shared(q)); }
 __device__ __forceinline__ uint64_t tc_now() {
@@ -515,7 +583,9 @@ __device__ __forceinline__ uint64_t tc_now() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Shared-memory matrix descriptor, no swizzle, version 1 (bit 46).
+// Shared-memory matrix descriptor, no swizzle, version 1 (bit 46): start,
+// leading-dimension byte offset (between core matrices along K for K-major
+// operands), stride-dimension byte offset (between 8-row groups along M/N).
 __device__ __forceinline__ uint64_t tc_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
     return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
            (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
@@ -523,37 +593,58 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t addr, uint32_t lbo, uint32_
 __device__ __forceinline__ void tc_mbar_init(uint32_t bar, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(n) : "memory");
 }
-__device__ __forceinline__ bool tc_mbar_test(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool tc_mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
 }
 // Bounded wait for the completion of phase `parity`; false at the deadline.
-__device__ bool tc_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
-    uint32_t spins = 0;
-    while (!tc_mbar_test(bar, parity)) {
-        if ((++spins & 255u) == 0 && tc_now() > deadline) return false;
-        __nanosleep(20);
+__device__ __noinline__ bool tc_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
+    for (uint32_t spins = 1;; ++spins) {
+        if (tc_mbar_try(bar, parity)) return true;
+        if ((spins & 63u) == 0 && tc_now() > deadline) return false;
     }
-    return true;
 }
+__device__ __forceinline__ void tc_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// global -> shared bulk copy completing on `bar` (no multicast)
+__device__ __forceinline__ void tc_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+template <uint32_t kCols>
 __device__ __forceinline__ void tc_alloc(uint32_t slot) {  // warp-wide
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "n"(kTcCols)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "n"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
+template <uint32_t kCols>
 __device__ __forceinline__ void tc_dealloc(uint32_t taddr) {  // warp-wide, the allocating warp
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(kTcCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(kCols) : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+// D (tensor memory) += A (shared memory) x B (shared memory)
+__device__ __forceinline__ void tc_mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+// D (tensor memory) += A (tensor memory) x B (shared memory)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
         : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -563,7 +654,7 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// Lanes 32w..32w+31, columns 0..7 of the accumulator (one token each).
+// Lanes 32w..32w+31 (w = warp % 4), columns 0..7 of the accumulator at taddr.
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
     uint32_t r[8];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -572,6 +663,18 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // The 8 fp16 of a 16-byte chunk of consecutive values x0..x7, reordered to
 // the deq order (x0, x4, x1, x5, x2, x6, x3, x7).
@@ -583,130 +686,105 @@ __device__ __forceinline__ uint4 to_pos(uint4 w) {
 __device__ __forceinline__ uint4 deq8(uint32_t w, __half2 s2) {
     return make_uint4(deq(w, 0, s2), deq(w, 1, s2), deq(w, 2, s2), deq(w, 3, s2));
 }
-
-// Shared teardown: wait (bounded) for the MMAs this CTA issued, free the
-// tensor memory. `issued` commits were made; the last one was on stage
-// (issued - 1) % kTcStages with parity ((issued - 1) / kTcStages) & 1.
-__device__ void tc_finish(uint32_t* err, const uint64_t* mbar, uint32_t issued, uint32_t tmem, bool ok) {
-    if (threadIdx.x == 0 && issued) {
-        const uint32_t i = issued - 1;
-        if (!tc_wait(sm_u32(mbar + i % kTcStages), (i / kTcStages) & 1u, tc_now() + kTcTimeoutNs)) ok = false;
-    }
-    if (!ok && err) atomicOr(err, 1u);
-    tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x < 32) tc_dealloc(tmem);
+__device__ __forceinline__ void tc_fail(uint32_t* err) {
+    if (err) atomicOr(err, 1u);
+}
+// Every lane waits (each acquires the phase); the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
+    return __all_sync(0xffffffffu, tc_wait(bar, parity, deadline)) != 0;
+}
+// Arrives on `bar` once every cp.async this thread issued so far has landed
+// (counted among the barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Producer exit: wait (bounded) for the last ring stages it filled, so no
+// copy lands after the CTA has ended.
+__device__ void drain_ring(const uint64_t* full, uint32_t stages, uint32_t issued, uint64_t deadline) {
+    const uint32_t first = issued > stages ? issued - stages : 0u;
+    for (uint32_t s = first; s < issued; ++s)
+        if (!tc_wait(sm_u32(full + s % stages), (s / stages) & 1u, deadline)) return;
 }
 
-// gate/up: one CTA per 64 union neurons, 128 MMA rows (row 2j the gate row,
-// 2j + 1 the up row of neuron j), K = H in stages of 64 coordinates.
-__global__ void __launch_bounds__(128) batch_gateup_tc_kernel(const BatchParams p, uint32_t* err) {
-    extern __shared__ __align__(1024) uint8_t sm[];
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kTcStages * kTcStage);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + kTcStages);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (warp == 0) tc_alloc(sm_u32(tslot));
-    if (tid == 0) {
-        for (uint32_t i = 0; i < kTcStages; ++i) tc_mbar_init(sm_u32(mbar + i), 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tslot;
-    const uint64_t deadline = tc_now() + kTcTimeoutNs;
-    // this thread's A row: neuron j = tid / 2 of the tile, gate (even) or up (odd)
-    const uint32_t nrow = blockIdx.x * 64 + uint32_t(tid >> 1);
-    const bool valid = nrow < p.NT;
-    const uint8_t* src = nullptr;
-    const __half* sc = nullptr;
-    if (valid) {
-        const Row r = neuron_row(p, nrow);
-        src = r.src + (tid & 1) * (p.H / 2);
-        sc = r.sc + (tid & 1) * (p.H / 128);
-    }
-    const uint32_t nst = p.H / kTcK;
-    uint8_t* arow = sm + (tid / 8) * 1024 + (tid % 8) * 16;  // chunk c of this row at + c * 128
-    uint4 cur0 = make_uint4(0u, 0u, 0u, 0u), cur1 = cur0;
-    if (valid) {
-        cur0 = __ldg(reinterpret_cast<const uint4*>(src));
-        cur1 = __ldg(reinterpret_cast<const uint4*>(src) + 1);
-    }
-    bool ok = true;
-    uint32_t issued = 0;
-    for (uint32_t i = 0; i < nst; ++i) {
-        const uint32_t s = i % kTcStages;
-        uint8_t* stage = sm + s * kTcStage;
-        if (i >= kTcStages && !tc_wait(sm_u32(mbar + s), ((i / kTcStages) - 1) & 1u, deadline)) ok = false;
-        if (!__syncthreads_and(ok)) {
-            ok = false;
-            break;
-        }
-        // next stage's 32 bytes in flight while this one is converted
-        uint4 nx0 = make_uint4(0u, 0u, 0u, 0u), nx1 = nx0;
-        if (valid && i + 1 < nst) {
-            nx0 = __ldg(reinterpret_cast<const uint4*>(src + 32 * (i + 1)));
-            nx1 = __ldg(reinterpret_cast<const uint4*>(src + 32 * (i + 1)) + 1);
-        }
-        const __half2 s2 = __half2half2(valid ? sc[(kTcK * i) / 128] : __float2half_rn(0.f));
-        const uint32_t w[8] = {cur0.x, cur0.y, cur0.z, cur0.w, cur1.x, cur1.y, cur1.z, cur1.w};
+// x image of the gate/up kernel (and the HF RMSNorm of LS_B200_NORM_INPUT,
+// the arithmetic of batch_norm_kernel: inv = rsqrt(sum(x^2) / H + eps),
+// x' = fp16(w * fp16(x * inv))): CTA b writes token b's coordinates in
+// K-major core matrices, zeros for b >= B. Each thread holds up to four
+// 8-coordinate blocks (H <= 8192) in registers; the sum of squares runs in a
+// fixed order (per thread, a shuffle tree, then the warps in order).
+__global__ void __launch_bounds__(256) batch_ximg_kernel(const __half* x, const __half* w, float eps, uint32_t H,
+                                                         uint32_t B, uint32_t norm, uint8_t* img) {
+    __shared__ float part[8];
+    const uint32_t b = blockIdx.x, nkg = H / 8;
+    const __half* row = x + size_t(b) * H;
+    uint4 v[4];
+    float ss = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(stage + (arow - sm) + c * 128) = deq8(w[c], s2);
-        if (tid < 64) {  // x of the stage: token n = tid / 8, coordinates 8c .. 8c + 7
-            const uint32_t n = tid >> 3, c = tid & 7;
-            uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-            if (n < p.B) xv = __ldg(reinterpret_cast<const uint4*>(p.x + size_t(n) * p.H + kTcK * i + 8 * c));
-            *reinterpret_cast<uint4*>(stage + kTcA + c * 128 + n * 16) = to_pos(xv);
-        }
-        proxy_fence();  // generic-proxy stores -> visible to the tensor core (async proxy)
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t kg = threadIdx.x + 256 * j;
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (b < B && kg < nkg) v[j] = *reinterpret_cast<const uint4*>(row + 8 * kg);
+        const __half* e = reinterpret_cast<const __half*>(&v[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(__half2float(e[i]), __half2float(e[i]), ss);
+    }
+    float inv = 1.f;
+    if (norm) {
+#pragma unroll
+        for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
         __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t a = sm_u32(stage), b = sm_u32(stage + kTcA);
+        float tot = 0.f;
 #pragma unroll
-            for (uint32_t kk = 0; kk < kTcK / 16; ++kk)
-                tc_mma(tmem, tc_desc(a + 256 * kk, 128, 1024), tc_desc(b + 256 * kk, 128, 1024), kIdescK,
-                       (i | kk) ? 1u : 0u);
-            tc_commit(sm_u32(mbar + s));
-        }
-        ++issued;
-        cur0 = nx0;
-        cur1 = nx1;
+        for (int i = 0; i < 8; ++i) tot += part[i];
+        inv = rsqrtf(tot / float(H) + eps);
     }
-    if (ok) {  // every MMA done: the accumulator rows
-        const uint32_t last = issued - 1;
-        if (!tc_wait(sm_u32(mbar + last % kTcStages), (last / kTcStages) & 1u, deadline)) ok = false;
-    }
-    if (__syncthreads_and(ok)) {
-        tc_fence_after();
-        float v[8];
-        tc_ld8(tmem + (uint32_t(32 * warp) << 16), v);
-        const uint32_t u = valid ? nrow / p.G : 0u;
 #pragma unroll
-        for (int b = 0; b < kBatchTokens; ++b) {
-            const float up = __shfl_xor_sync(0xffffffffu, v[b], 1);  // odd lane: the up row
-            if ((lane & 1) || !valid || uint32_t(b) >= p.B) continue;
-            const float g16 = __half2float(__float2half_rn(v[b])), u16 = __half2float(__float2half_rn(up));
-            const float sl = __half2float(__float2half_rn(g16 / (1.f + expf(-g16))));
-            __half h = __float2half_rn(sl * u16);
-            if (p.mask && !p.mask[size_t(b) * p.U + u]) h = __float2half_rn(0.f);
-            p.hT[size_t(b) * p.NTP + nrow] = h;
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t kg = threadIdx.x + 256 * j;
+        if (kg >= nkg) continue;
+        if (norm && b < B) {
+            __half* e = reinterpret_cast<__half*>(&v[j]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                __half t = __float2half_rn(__half2float(e[i]) * inv);
+                if (w) t = __hmul(w[8 * kg + i], t);
+                e[i] = t;
+            }
         }
+        *reinterpret_cast<uint4*>(img + size_t(kg) * 128 + b * 16) = to_pos(v[j]);
     }
-    tc_finish(err, mbar, issued, tmem, ok);
 }
 
-// down: one CTA per 128 output columns and split of the union's neurons
-// (the splits of the mma.sync kernel, summed by the epilogue).
-__global__ void __launch_bounds__(128) batch_down_tc_kernel(const BatchParams p, uint32_t* err) {
+// Persistent: CTA c takes work units c, c + grid, ... (unit = tile x split,
+// tile-major); the ring, the tensor-memory A buffers and two accumulators
+// run on across units, so a CTA's set-up is paid once.
+__global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kernel(const BatchParams p,
+                                                                                  uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm[];
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kTcStages * kTcStage);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + kTcStages);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (warp == 0) tc_alloc(sm_u32(tslot));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kGtSmem - 256);
+    uint64_t* full = bars;                    // [kGtStages] producer -> converters
+    uint64_t* empty = bars + kGtStages;       // [kGtStages] MMA -> producer
+    uint64_t* afull = bars + 2 * kGtStages;   // [kGtABufs] converters -> MMA
+    uint64_t* aempty = afull + kGtABufs;      // [kGtABufs] MMA -> converters
+    uint64_t* dfull = aempty + kGtABufs;      // [2] MMA -> epilogue
+    uint64_t* dempty = dfull + 2;             // [2] epilogue -> MMA
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kGtBars);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 1) tc_alloc<kGtTmemCols>(sm_u32(tslot));
     if (tid == 0) {
-        for (uint32_t i = 0; i < kTcStages; ++i) tc_mbar_init(sm_u32(mbar + i), 1);
+        for (uint32_t i = 0; i < kGtStages; ++i) {
+            tc_mbar_init(sm_u32(full + i), 32);  // the producer's 32 lanes (+ the x copy's bytes)
+            tc_mbar_init(sm_u32(empty + i), 1);  // tcgen05.commit after the stage's last MMA
+        }
+        for (uint32_t i = 0; i < kGtABufs; ++i) {
+            tc_mbar_init(sm_u32(afull + i), 4);   // one converter warp per tensor-memory lane quarter
+            tc_mbar_init(sm_u32(aempty + i), 1);  // tcgen05.commit
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            tc_mbar_init(sm_u32(dfull + i), 1);
+            tc_mbar_init(sm_u32(dempty + i), 4);  // the four epilogue warps
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
@@ -714,93 +792,475 @@ __global__ void __launch_bounds__(128) batch_down_tc_kernel(const BatchParams p,
     tc_fence_after();
     const uint32_t tmem = *tslot;
     const uint64_t deadline = tc_now() + kTcTimeoutNs;
-    const uint32_t c0 = blockIdx.x * kTcRows, split = blockIdx.y;
-    // split boundaries on 64-neuron stage boundaries (16-byte aligned h rows)
-    const uint32_t k_begin = uint32_t(uint64_t(p.NT) * split / kDownSplits) / kTcK * kTcK;
-    const uint32_t k_end =
-        split + 1 == kDownSplits ? p.NT : uint32_t(uint64_t(p.NT) * (split + 1) / kDownSplits) / kTcK * kTcK;
-    const uint32_t nst = (k_end - k_begin + kTcK - 1) / kTcK;
-    // converter: neuron kl = tid % 64 of the stage, columns 64 * (tid / 64) .. +63
-    const uint32_t kl = uint32_t(tid) & 63u, half = uint32_t(tid) >> 6;
+    const uint32_t S = p.gu_splits, units = ((p.NT + 63) / 64) * S, stages_all = p.H / kGtK;
+    auto unit_stages = [&](uint32_t split, uint32_t& st0, uint32_t& st1) {
+        st0 = stages_all * split / S;
+        st1 = stages_all * (split + 1) / S;
+    };
     bool ok = true;
-    uint32_t issued = 0;
-    for (uint32_t i = 0; i < nst; ++i) {
-        const uint32_t s = i % kTcStages;
-        uint8_t* stage = sm + s * kTcStage;
-        if (i >= kTcStages && !tc_wait(sm_u32(mbar + s), ((i / kTcStages) - 1) & 1u, deadline)) ok = false;
-        if (!__syncthreads_and(ok)) {
-            ok = false;
-            break;
-        }
-        const uint32_t k = k_begin + kTcK * i + kl;
-        uint4 w0 = make_uint4(0u, 0u, 0u, 0u), w1 = w0;
-        __half2 s2 = __float2half2_rn(0.f);
-        if (k < k_end) {
-            const Row r = neuron_row(p, k);
-            const uint8_t* d = r.src + p.H + (c0 + 64 * half) / 2;  // 32 bytes: 64 columns
-            w0 = __ldg(reinterpret_cast<const uint4*>(d));
-            w1 = __ldg(reinterpret_cast<const uint4*>(d) + 1);
-            s2 = __half2half2(r.sc[2 * (p.H / 128) + c0 / 128]);
-        }
-        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+
+    if (warp == 0) {
+        // producer: 16-byte cp.async, one instruction = 4 rows x 128 B (lanes
+        // 8i .. 8i + 7 take row i of the four); lane l holds the source of
+        // rows l, l + 32, l + 64, l + 96, passed by shuffle
+        uint32_t gs = 0;  // stages issued by this CTA
+        const uint32_t part = lane & 7u, rsub = lane >> 3;
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const uint32_t tile = u / S;
+            uint32_t st0, st1;
+            unit_stages(u % S, st0, st1);
+            const uint32_t rows_valid = min(128u, 2u * (p.NT - 64u * tile));
+            const uint8_t* src[4];
+            const __half* scp[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {  // columns c0 + 64 half + 8q .. +7: M group 8 half + q
-            const uint32_t g = 8 * half + uint32_t(q);
-            *reinterpret_cast<uint4*>(stage + g * 1024 + (kl / 8) * 128 + (kl % 8) * 16) = deq8(w[q], s2);
-        }
-        if (tid < 64) {  // h of the stage: token n = tid / 8, neurons 8c .. 8c + 7
-            const uint32_t n = tid >> 3, c = tid & 7, k8 = k_begin + kTcK * i + 8 * c;
-            uint4 hv = make_uint4(0u, 0u, 0u, 0u);
-            if (n < p.B && k8 < k_end) {
-                hv = *reinterpret_cast<const uint4*>(p.hT + size_t(n) * p.NTP + k8);
-                // neurons past the split's end (and past the union) contribute nothing
-                const uint32_t valid_n = k_end - k8;
-                if (valid_n < 8) {
-                    uint32_t* hw = reinterpret_cast<uint32_t*>(&hv);
-#pragma unroll
-                    for (uint32_t e = 0; e < 4; ++e) {
-                        if (2 * e >= valid_n) hw[e] = 0u;
-                        else if (2 * e + 1 >= valid_n) hw[e] &= 0xffffu;
-                    }
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t row = lane + 32u * j;
+                src[j] = nullptr;
+                scp[j] = nullptr;
+                if (row < rows_valid) {
+                    const Row r = neuron_row(p, 64u * tile + row / 2);
+                    src[j] = r.src + (row & 1u) * (p.H / 2);
+                    scp[j] = r.sc + (row & 1u) * (p.H / 128);
                 }
             }
-            *reinterpret_cast<uint4*>(stage + kTcA + c * 128 + n * 16) = hv;
-        }
-        proxy_fence();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t a = sm_u32(stage), b = sm_u32(stage + kTcA);
+            for (uint32_t s = st0; s < st1; ++s, ++gs) {
+                const uint32_t slot = gs % kGtStages;
+                if (gs >= kGtStages && !warp_wait(sm_u32(empty + slot), ((gs / kGtStages) - 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t bar = sm_u32(full + slot);
+                uint8_t* st = sm + slot * kGtStage;
+                const uint32_t k0 = s * kGtK;  // first coordinate of the stage
+                if (lane == 0) {
+                    tc_expect_tx(bar, kGtX);
+                    tc_bulk(sm_u32(st + kGtW), p.ximg + size_t(k0) * 16, kGtX, bar);
+                }
 #pragma unroll
-            for (uint32_t kk = 0; kk < kTcK / 16; ++kk)
-                tc_mma(tmem, tc_desc(a + 256 * kk, 128, 1024), tc_desc(b + 256 * kk, 128, 1024), kIdescMN,
-                       (i | kk) ? 1u : 0u);
-            tc_commit(sm_u32(mbar + s));
+                for (uint32_t i = 0; i < 32; ++i) {
+                    const uint32_t row = 4 * i + rsub;  // rows of one instruction share row / 32
+                    const uint8_t* rs = reinterpret_cast<const uint8_t*>(
+                        __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src[i / 8]), row & 31u));
+                    if (row < rows_valid) cp_async16(st + row * kGtRowPitch + 16 * part, rs + k0 / 2 + 16 * part);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)  // scales of the stage's two 128-blocks
+                    if (scp[j]) cp_async4(st + kGtW + kGtX + 4 * (lane + 32u * j), scp[j] + k0 / 128);
+                cp_async_arrive(bar);  // arrives once this lane's copies have landed
+            }
         }
-        ++issued;
-    }
-    if (ok && issued) {
-        const uint32_t last = issued - 1;
-        if (!tc_wait(sm_u32(mbar + last % kTcStages), (last / kTcStages) & 1u, deadline)) ok = false;
-    }
-    if (__syncthreads_and(ok)) {
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (issued) {
+        if (!ok) tc_fail(err);
+        if (lane == 0) drain_ring(full, kGtStages, gs, deadline);
+        __syncwarp();
+    } else if (warp == 1) {
+        // MMA issuer: one wait (two at a stage's first chunk) and 8 MMAs per chunk
+        if (lane == 0) {
+            uint32_t gq = 0, ui = 0;
+            for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
+                uint32_t st0, st1;
+                unit_stages(u % S, st0, st1);
+                const uint32_t nch = (st1 - st0) * kGtChunks;
+                const uint32_t d = ui & 1u, dcol = tmem + kGtDCol + 16 * d;
+                if (ui >= 2 && !tc_wait(sm_u32(dempty + d), ((ui / 2) - 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (uint32_t q = 0; q < nch; ++q, ++gq) {
+                    const uint32_t gsi = gq / kGtChunks, c = gq % kGtChunks, slot = gsi % kGtStages, a = gq % kGtABufs;
+                    if (c == 0 && !tc_wait(sm_u32(full + slot), (gsi / kGtStages) & 1u, deadline)) ok = false;
+                    if (ok && !tc_wait(sm_u32(afull + a), (gq / kGtABufs) & 1u, deadline)) ok = false;
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t xb = sm_u32(sm + slot * kGtStage + kGtW) + c * kGtChunk * 16;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kGtChunk / 16; ++kk)
+                        tc_mma_ts(dcol, tmem + a * (kGtChunk / 2) + kk * 8, tc_desc(xb + 256 * kk, 128, 0),
+                                  kIdescGateUp, (q | kk) ? 1u : 0u);
+                    tc_commit(sm_u32(aempty + a));
+                    if (c == kGtChunks - 1) tc_commit(sm_u32(empty + slot));
+                }
+                tc_commit(sm_u32(dfull + d));  // arrives when every MMA so far has completed
+            }
+            // every MMA of this CTA complete before the tensor memory is freed
+            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, deadline)) ok = false;
+            if (!ok) tc_fail(err);
+        }
+        __syncwarp();
+    } else if (warp < 10) {
+        // converters: warp group g = (warp - 2) / 4 takes chunk g of each
+        // stage (coordinates 128 g .. 128 g + 127, one scale block), lane
+        // quarter = warp % 4 the rows
+        const uint32_t g = (warp - 2) / 4, quarter = warp & 3, row = 32 * quarter + lane;
+        const uint32_t lanebits = (32 * quarter) << 16;
+        uint32_t gq = 0;
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const uint32_t tile = u / S;
+            uint32_t st0, st1;
+            unit_stages(u % S, st0, st1);
+            const uint32_t nch = (st1 - st0) * kGtChunks;
+            const bool valid = row < min(128u, 2u * (p.NT - 64u * tile));
+            for (uint32_t q = g; q < nch; q += kGtChunks) {
+                const uint32_t Q = gq + q, gsi = Q / kGtChunks, c = Q % kGtChunks, slot = gsi % kGtStages,
+                               a = Q % kGtABufs;
+                if (!warp_wait(sm_u32(full + slot), (gsi / kGtStages) & 1u, deadline) ||
+                    (Q >= kGtABufs && !warp_wait(sm_u32(aempty + a), ((Q / kGtABufs) - 1) & 1u, deadline))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* st = sm + slot * kGtStage;
+                const __half2 s2 = valid ? __half2half2(reinterpret_cast<const __half*>(st + kGtW + kGtX)[2 * row + c])
+                                         : __float2half2_rn(0.f);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {  // two halves of 32 columns
+                    uint32_t v[32];
+                    uint4 w0 = make_uint4(0u, 0u, 0u, 0u), w1 = w0;
+                    if (valid) {
+                        w0 = *reinterpret_cast<const uint4*>(st + row * kGtRowPitch + 64 * c + 32 * h);
+                        w1 = *reinterpret_cast<const uint4*>(st + row * kGtRowPitch + 64 * c + 32 * h + 16);
+                    }
+                    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint4 dq = deq8(w[i], s2);
+                        v[4 * i] = dq.x;
+                        v[4 * i + 1] = dq.y;
+                        v[4 * i + 2] = dq.z;
+                        v[4 * i + 3] = dq.w;
+                    }
+                    tc_st32(tmem + lanebits + a * (kGtChunk / 2) + 32 * h, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc_arrive(sm_u32(afull + a));
+            }
+            gq += nch;
+        }
+        if (!ok) tc_fail(err);
+    } else {
+        // epilogue: the unit's gate/up sums of the 32 rows of this lane quarter
+        const uint32_t quarter = warp & 3, row = 32 * quarter + lane, lanebits = (32 * quarter) << 16;
+        uint32_t ui = 0;
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
+            const uint32_t tile = u / S, split = u % S, d = ui & 1u;
+            if (!warp_wait(sm_u32(dfull + d), (ui / 2) & 1u, deadline)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            tc_ld8(tmem + (uint32_t(32 * warp) << 16), v);
+            float r[8];
+            tc_ld8(tmem + lanebits + kGtDCol + 16 * d, r);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc_arrive(sm_u32(dempty + d));
+            if (row < min(128u, 2u * (p.NT - 64u * tile))) {
+                float4* out =
+                    reinterpret_cast<float4*>(p.gpart + (size_t(split) * p.rows_total + 128u * tile + row) * kBatchTokens);
+                out[0] = make_float4(r[0], r[1], r[2], r[3]);
+                out[1] = make_float4(r[4], r[5], r[6], r[7]);
+            }
         }
-        const uint32_t m = uint32_t(32 * warp + lane), col = c0 + 8 * (m / 8) + ((m % 8) >> 1) + 4 * (m & 1);
-        float* out = p.partial + size_t(split) * p.B * p.H;
-        for (uint32_t b = 0; b < p.B; ++b) out[size_t(b) * p.H + col] = v[b];
+        if (!ok) tc_fail(err);
     }
-    tc_finish(err, mbar, issued, tmem, ok);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tc_dealloc<kGtTmemCols>(tmem);
+    }
 }
 
-uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) {
-    const uint64_t nt = uint64_t(G) * U, ntp = (nt + 15) / 16 * 16 + 16;
-    const uint64_t ht = (ntp * kBatchTokens * sizeof(__half) + 255) / 256 * 256;
-    const uint64_t part = (uint64_t(kDownSplits) * kBatchTokens * H * sizeof(float) + 255) / 256 * 256;
-    return ht + part + uint64_t(kBatchTokens) * H * sizeof(__half) + 256;
+// h of every (union neuron, token): g and u = the splits' sums added in split
+// order, then the reference's rounding chain (fp16 g and u, s = fp16(silu(g)),
+// h = fp16(s * u)), the token mask, and the K-major h image of the down
+// kernel: neuron n of token b at (n / 8) * 64 + b * 8 + n % 8 (zero past the
+// union, rounded up to a whole down stage of 128 neurons, and for tokens >= B).
+__global__ void batch_h_tc_kernel(const BatchParams p) {
+    const uint32_t ntk = (p.NT + kDtK - 1) / kDtK * kDtK, total = ntk * kBatchTokens;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t b = (i / 8) % kBatchTokens, n = (i / 64) * 8 + i % 8;
+        __half h = __float2half_rn(0.f);
+        if (n < p.NT && b < p.B) {
+            float gs = 0.f, us = 0.f;
+            for (uint32_t s = 0; s < p.gu_splits; ++s) {
+                const float* r = p.gpart + (size_t(s) * p.rows_total + 2u * n) * kBatchTokens + b;
+                gs += r[0];
+                us += r[kBatchTokens];
+            }
+            const float g16 = __half2float(__float2half_rn(gs)), u16 = __half2float(__float2half_rn(us));
+            const float sl = __half2float(__float2half_rn(g16 / (1.f + expf(-g16))));
+            h = __float2half_rn(sl * u16);
+            if (p.mask && !p.mask[size_t(b) * p.U + n / p.G]) h = __float2half_rn(0.f);
+        }
+        p.hB[i] = h;
+    }
+}
+
+// Persistent: CTA c takes work units c, c + grid, ... (unit = split x
+// column block, split-major, so that the CTAs working at one time read
+// neighbouring pieces of the same down rows). The producer keeps the
+// physical group, source slot and kind of up to kDtDescCache union groups in
+// shared memory (refilled when a stage's groups fall outside), so no stage
+// waits on a global load before its copies are issued.
+__global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const BatchParams p, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    uint8_t* abuf = sm;                         // [kDtABufs][kDtA]
+    uint8_t* raw = sm + kDtABufs * kDtA;        // [kDtRawStages][kDtRaw]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kDtRawStages * kDtRaw);
+    uint64_t* rfull = bars;
+    uint64_t* rempty = bars + kDtRawStages;
+    uint64_t* afull = bars + 2 * kDtRawStages;
+    uint64_t* aempty = afull + kDtABufs;
+    uint64_t* dfull = aempty + kDtABufs;   // [2]
+    uint64_t* dempty = dfull + 2;          // [2]
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kDtBars);
+    uint2* dcache = reinterpret_cast<uint2*>(raw + kDtRawStages * kDtRaw + 256);  // [kDtDescCache]
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 1) tc_alloc<kDtTmemCols>(sm_u32(tslot));
+    if (tid == 0) {
+        for (uint32_t i = 0; i < kDtRawStages; ++i) {
+            tc_mbar_init(sm_u32(rfull + i), 32);
+            tc_mbar_init(sm_u32(rempty + i), 1);
+        }
+        for (uint32_t i = 0; i < kDtABufs; ++i) {
+            tc_mbar_init(sm_u32(afull + i), 8);  // the eight converter warps
+            tc_mbar_init(sm_u32(aempty + i), 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            tc_mbar_init(sm_u32(dfull + i), 1);
+            tc_mbar_init(sm_u32(dempty + i), 4);  // the four epilogue warps
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint64_t deadline = tc_now() + kTcTimeoutNs;
+    const uint32_t CB = p.H / kDtCols, units = CB * p.dn_splits;
+    // a split's stages: 64-neuron blocks [sb, se) of the union (whole h-image blocks)
+    const uint32_t stages_all = (p.NT + kDtK - 1) / kDtK;
+    auto split_range = [&](uint32_t split, uint32_t& sb, uint32_t& se) {
+        sb = stages_all * split / p.dn_splits;
+        se = stages_all * (split + 1) / p.dn_splits;
+    };
+    bool ok = true;
+
+    if (warp == 0) {
+        // producer: lane l fills neurons l and l + 32 of each stage
+        uint32_t gs = 0, cache_lo = 0xFFFFFFFFu;
+        const size_t rec = size_t(p.G) * (3 * p.H / 2);
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const uint32_t split = u / CB, c0 = (u % CB) * kDtCols;
+            uint32_t sb, se;
+            split_range(split, sb, se);
+            for (uint32_t s = sb; s < se; ++s, ++gs) {
+                const uint32_t slot = gs % kDtRawStages;
+                if (gs >= kDtRawStages &&
+                    !warp_wait(sm_u32(rempty + slot), ((gs / kDtRawStages) - 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t k0 = s * kDtK, n_valid = min(kDtK, p.NT - k0);
+                const uint32_t u_first = k0 / p.G, u_last = (k0 + n_valid - 1) / p.G;
+                if (cache_lo == 0xFFFFFFFFu || u_first < cache_lo || u_last >= cache_lo + kDtDescCache) {
+                    __syncwarp();
+                    cache_lo = u_first;
+                    for (uint32_t i = lane; i < kDtDescCache && cache_lo + i < p.U; i += 32) {
+                        const ls_exec_desc d = p.desc[cache_lo + i];
+                        dcache[i] = make_uint2(d.source_slot | (d.source_kind == LS_SOURCE_STAGING ? 0x80000000u : 0u),
+                                               d.physical_group);
+                    }
+                    __syncwarp();
+                }
+                const uint32_t bar = sm_u32(rfull + slot);
+                uint8_t* st = raw + slot * kDtRaw;
+                if (lane == 0) {
+                    tc_expect_tx(bar, kDtH);
+                    tc_bulk(sm_u32(st + kDtW), p.hB + size_t(k0) * kBatchTokens, kDtH, bar);
+                }
+                // lane l resolves neurons l, l + 32, l + 64, l + 96 (source, scale copy)
+                const uint8_t* src[kDtK / 32];
+#pragma unroll
+                for (uint32_t j = 0; j < kDtK / 32; ++j) {
+                    const uint32_t kl = lane + 32u * j;
+                    src[j] = nullptr;
+                    if (kl >= n_valid) continue;
+                    const uint32_t n = k0 + kl, nl = n % p.G;
+                    const uint2 e = dcache[n / p.G - cache_lo];
+                    const uint8_t* base = (e.x & 0x80000000u) ? p.staging : p.cache;
+                    src[j] = base + size_t(e.x & 0x7FFFFFFFu) * rec + size_t(nl) * (3 * p.H / 2) + p.H + c0 / 2;
+                    const __half* sc = p.scales + (size_t(e.y) * p.G + nl) * 3 * (p.H / 128);
+                    cp_async4(st + kDtW + kDtH + 4 * kl, sc + 2 * (p.H / 128) + c0 / 128);
+                }
+                // 16-byte cp.async, one instruction = 4 neurons x 128 B
+#pragma unroll
+                for (uint32_t i = 0; i < kDtK / 4; ++i) {
+                    const uint32_t kl = 4 * i + (lane >> 3), part = lane & 7u;  // i / 8 = kl / 32: uniform
+                    const uint8_t* rs = reinterpret_cast<const uint8_t*>(
+                        __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src[i / 8]), kl & 31u));
+                    if (kl < n_valid) cp_async16(st + kl * kDtRowPitch + 16 * part, rs + 16 * part);
+                }
+                cp_async_arrive(bar);
+            }
+        }
+        if (!ok) tc_fail(err);
+        if (lane == 0) drain_ring(rfull, kDtRawStages, gs, deadline);
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t gs = 0, ui = 0;
+            for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
+                uint32_t sb, se;
+                split_range(u / CB, sb, se);
+                const uint32_t d = ui & 1u, dcol = tmem + 16 * d;
+                if (ui >= 2 && !tc_wait(sm_u32(dempty + d), ((ui / 2) - 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (uint32_t s = sb; s < se; ++s, ++gs) {
+                    const uint32_t slot = gs % kDtRawStages, a = gs % kDtABufs;
+                    // A ready: the converters have read the raw stage, written A and copied h
+                    if (!tc_wait(sm_u32(afull + a), (gs / kDtABufs) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ab = sm_u32(abuf + a * kDtA), hb = ab + 2 * kDtMTile;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kDtK / 16; ++kk)
+#pragma unroll
+                        for (uint32_t mt = 0; mt < 2; ++mt)
+                            tc_mma_ss(dcol + 8 * mt, tc_desc(ab + mt * kDtMTile + 256 * kk, 128, 2048),
+                                      tc_desc(hb + 256 * kk, 128, 1024), kIdescDown, (s != sb || kk) ? 1u : 0u);
+                    tc_commit(sm_u32(rempty + slot));
+                    tc_commit(sm_u32(aempty + a));
+                }
+                tc_commit(sm_u32(dfull + d));
+            }
+            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, deadline)) ok = false;
+            if (!ok) tc_fail(err);
+        }
+        __syncwarp();
+    } else if (warp < 10) {
+        // converters: thread (neuron kl, 128-column half mt) of each stage
+        const uint32_t t = tid - 64, kl = t & (kDtK - 1), mt = t / kDtK;
+        uint32_t gs = 0;
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            uint32_t sb, se;
+            split_range(u / CB, sb, se);
+            for (uint32_t s = sb; s < se; ++s, ++gs) {
+                const uint32_t slot = gs % kDtRawStages, a = gs % kDtABufs;
+                if (!warp_wait(sm_u32(rfull + slot), (gs / kDtRawStages) & 1u, deadline) ||
+                    (gs >= kDtABufs && !warp_wait(sm_u32(aempty + a), ((gs / kDtABufs) - 1) & 1u, deadline))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* st = raw + slot * kDtRaw;
+                uint8_t* A = abuf + a * kDtA;
+                const bool live = s * kDtK + kl < p.NT;  // neurons past the union: zero weights
+                const __half2 s2 = live ? __half2half2(reinterpret_cast<const __half*>(st + kDtW + kDtH)[2 * kl + mt])
+                                        : __float2half2_rn(0.f);
+                uint8_t* Ak = A + mt * kDtMTile + (kl / 8) * 128 + (kl % 8) * 16;
+#pragma unroll
+                for (uint32_t h = 0; h < 4; ++h) {  // 32 columns at a time
+                    uint4 w0 = make_uint4(0u, 0u, 0u, 0u);
+                    if (live) w0 = *reinterpret_cast<const uint4*>(st + kl * kDtRowPitch + 64 * mt + 16 * h);
+                    const uint32_t w[4] = {w0.x, w0.y, w0.z, w0.w};
+#pragma unroll
+                    for (uint32_t q = 0; q < 4; ++q)  // columns 32h + 8q .. +7: core-matrix group 4h + q
+                        *reinterpret_cast<uint4*>(Ak + (4 * h + q) * 2048) = deq8(w[q], s2);
+                }
+                if (t < kDtH / 16)  // the stage's h image next to A
+                    reinterpret_cast<uint4*>(A + 2 * kDtMTile)[t] = reinterpret_cast<const uint4*>(st + kDtW)[t];
+                proxy_fence();  // generic-proxy stores -> visible to the tensor core
+                __syncwarp();
+                if (lane == 0) tc_arrive(sm_u32(afull + a));
+            }
+        }
+        if (!ok) tc_fail(err);
+    } else {
+        // epilogue: rows 32 quarter .. +31 of both M tiles of the unit
+        const uint32_t quarter = warp & 3, m = 32 * quarter + lane;
+        const uint32_t colm = 8 * (m / 8) + ((m % 8) >> 1) + 4 * (m & 1);
+        uint32_t ui = 0;
+        for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
+            const uint32_t split = u / CB, c0 = (u % CB) * kDtCols, d = ui & 1u;
+            uint32_t sb, se;
+            split_range(split, sb, se);
+            if (!warp_wait(sm_u32(dfull + d), (ui / 2) & 1u, deadline)) {
+                ok = false;
+                break;
+            }
+            float v[2][8];
+            if (se > sb) {
+                tc_fence_after();
+                tc_ld8(tmem + ((32 * quarter) << 16) + 16 * d, v[0]);
+                tc_ld8(tmem + ((32 * quarter) << 16) + 16 * d + 8, v[1]);
+            } else {  // an empty split contributes zeros
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[0][i] = v[1][i] = 0.f;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc_arrive(sm_u32(dempty + d));
+            float* out = p.partial + size_t(split) * p.B * p.H;
+            for (uint32_t b = 0; b < p.B; ++b) {
+                out[size_t(b) * p.H + c0 + colm] = v[0][b];
+                out[size_t(b) * p.H + c0 + 128 + colm] = v[1][b];
+            }
+        }
+        if (!ok) tc_fail(err);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tc_dealloc<kDtTmemCols>(tmem);
+    }
+}
+
+// Scratch (256-byte aligned parts): h [8][NTP] fp16 (warp-MMA path), the
+// down partials [splits][8][H] fp32, the normalised activations [8][H] fp16
+// (warp-MMA path, LS_B200_NORM_INPUT), the x image [H / 8][8][8] fp16, the
+// gate/up split sums [splits][rows][8] fp32 and the h image [NT64 / 8][8][8]
+// fp16 (tensor-core path).
+struct ScratchLayout {
+    uint64_t ht, part, xn, ximg, gpart, hb, total;
+};
+constexpr uint64_t up256(uint64_t v) { return (v + 255) / 256 * 256; }
+uint32_t max_gu_splits(uint32_t H) { return H >= 2048 ? H / 1024 : 1u; }  // splits of >= 1024 coordinates
+ScratchLayout scratch_layout(uint32_t H, uint32_t G, uint32_t U) {
+    const uint64_t nt = uint64_t(G) * U, ntp = (nt + 15) / 16 * 16 + 16, nt64 = (nt + 63) / 64 * 64;
+    ScratchLayout l{};
+    l.ht = 0;
+    l.part = l.ht + up256(ntp * kBatchTokens * sizeof(__half));
+    l.xn = l.part + up256(uint64_t(kMaxDownSplits) * kBatchTokens * H * sizeof(float));
+    l.ximg = l.xn + up256(uint64_t(kBatchTokens) * H * sizeof(__half));
+    l.gpart = l.ximg + up256(uint64_t(H) * kBatchTokens * sizeof(__half));
+    l.hb = l.gpart + up256(uint64_t(max_gu_splits(H)) * 2 * nt64 * kBatchTokens * sizeof(float));
+    l.total = l.hb + up256((nt + kDtK - 1) / kDtK * kDtK * kBatchTokens * sizeof(__half)) + 256;
+    return l;
+}
+uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) { return scratch_layout(H, G, U).total; }
+
+// Number of splits that balances `units_per_split * splits` work units over
+// `slots` persistent CTAs best (mean units per CTA / the most any CTA
+// takes); a larger count must gain more than 5 % (each split adds one
+// partial result per unit to write and to sum).
+uint32_t pick_splits(uint32_t units_per_split, uint32_t max_splits, uint32_t slots) {
+    uint32_t best = 1;
+    double best_eff = 0.0;
+    for (uint32_t s = 1; s <= max_splits; ++s) {
+        const double x = double(units_per_split) * s / slots;
+        const double eff = x / double(uint64_t(x) + (x > double(uint64_t(x)) ? 1 : 0));
+        if (eff > best_eff + 0.05) {
+            best = s;
+            best_eff = eff;
+        }
+    }
+    return best;
 }
 
 bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
@@ -815,9 +1275,9 @@ cudaError_t set_ring_attributes() {
     if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
     e = cudaFuncSetAttribute(batch_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGuSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(batch_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
+        e = cudaFuncSetAttribute(batch_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGtSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(batch_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
+        e = cudaFuncSetAttribute(batch_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDtSmem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(batch_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDnSmem));
     if (e == cudaSuccess)
@@ -871,23 +1331,44 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     p.scales = static_cast<const __half*>(a->scales);
     p.desc = a->union_descs;
     p.mask = a->mask;
-    p.hT = static_cast<__half*>(a->scratch);
-    const uint64_t ht_bytes = (uint64_t(p.NTP) * kBatchTokens * sizeof(__half) + 255) / 256 * 256;
-    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + ht_bytes);
-    const uint64_t part_bytes = (uint64_t(kDownSplits) * kBatchTokens * H * sizeof(float) + 255) / 256 * 256;
-    __half* xn = reinterpret_cast<__half*>(static_cast<uint8_t*>(a->scratch) + ht_bytes + part_bytes);
+    uint8_t* scratch = static_cast<uint8_t*>(a->scratch);
+    const ScratchLayout lay = scratch_layout(H, G, U);
+    p.hT = reinterpret_cast<__half*>(scratch + lay.ht);
+    p.partial = reinterpret_cast<float*>(scratch + lay.part);
+    __half* xn = reinterpret_cast<__half*>(scratch + lay.xn);
+    p.ximg = scratch + lay.ximg;
+    p.gpart = reinterpret_cast<float*>(scratch + lay.gpart);
+    p.hB = reinterpret_cast<__half*>(scratch + lay.hb);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (const cudaError_t e = set_ring_attributes(); e != cudaSuccess) return int(e);
-    if (a->flags & LS_B200_NORM_INPUT) {
-        batch_norm_kernel<<<B, 256, 0, s>>>(p.x, static_cast<const __half*>(a->norm_weight), a->rms_eps, H, xn);
-        p.x = xn;
-    }
+    const __half* norm_w = static_cast<const __half*>(a->norm_weight);
+    const bool norm = (a->flags & LS_B200_NORM_INPUT) != 0;
     if (a->flags & LS_B200_BATCH_MMA_SYNC) {
+        p.dn_splits = kDownSplits;
+        if (norm) {
+            batch_norm_kernel<<<B, 256, 0, s>>>(p.x, norm_w, a->rms_eps, H, xn);
+            p.x = xn;
+        }
         batch_gateup_kernel<<<(p.NT + kGateUpNeurons - 1) / kGateUpNeurons, kBatchThreads, kGuSmem, s>>>(p);
         batch_down_kernel<<<dim3(H / kDownCols, kDownSplits), kBatchThreads, kDnSmem, s>>>(p);
     } else {
-        batch_gateup_tc_kernel<<<(p.NT + 63) / 64, 128, kTcSmem, s>>>(p, a->error);
-        batch_down_tc_kernel<<<dim3(H / kTcRows, kDownSplits), 128, kTcSmem, s>>>(p, a->error);
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                      cudaSuccess || sms <= 0)
+            sms = 148;
+        const uint32_t tiles = (p.NT + 63) / 64, dn_stages = (p.NT + kDtK - 1) / kDtK;
+        p.rows_total = tiles * 128;
+        const uint32_t gu_slots = kGtCtasPerSm * uint32_t(sms);
+        p.gu_splits = pick_splits(tiles, max_gu_splits(H), gu_slots);
+        p.dn_splits = pick_splits(H / kDtCols, dn_stages < kMaxDownSplits ? dn_stages : kMaxDownSplits, uint32_t(sms));
+        batch_ximg_kernel<<<kBatchTokens, 256, 0, s>>>(p.x, norm_w, a->rms_eps, H, B, norm ? 1u : 0u,
+                                                       scratch + lay.ximg);
+        const uint32_t gu_units = tiles * p.gu_splits, dn_units = (H / kDtCols) * p.dn_splits;
+        batch_gateup_tc_kernel<<<gu_units < gu_slots ? gu_units : gu_slots, kGtThreads, kGtSmem, s>>>(p, a->error);
+        const uint32_t hn = dn_stages * kDtK * kBatchTokens;
+        batch_h_tc_kernel<<<(hn + 255) / 256 < 1024 ? (hn + 255) / 256 : 1024, 256, 0, s>>>(p);
+        batch_down_tc_kernel<<<dn_units < uint32_t(sms) ? dn_units : uint32_t(sms), kDtThreads, kDtSmem, s>>>(
+            p, a->error);
     }
     const uint32_t total = B * H;
     batch_epilogue_kernel<<<(total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024, 256, 0, s>>>(p);
