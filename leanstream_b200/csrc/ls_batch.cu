@@ -569,8 +569,9 @@ constexpr uint32_t kDtA = 2 * kDtMTile + kDtH;          // two M tiles + the h c
 constexpr uint32_t kDtABufs = 2;
 constexpr uint32_t kDtBars = 2 * kDtRawStages + 2 * kDtABufs + 4;  // rfull, rempty, afull, aempty, dfull[2], dempty[2]
 constexpr uint32_t kDtDescCache = 256;                  // union groups cached by the producer
-constexpr uint32_t kDtSmem = kDtABufs * kDtA + kDtRawStages * kDtRaw + 256 + kDtDescCache * 8;
-constexpr uint32_t kDtThreads = 448;                    // producer, MMA, 8 converter, 4 epilogue warps
+constexpr uint32_t kDtProducers = 2;                    // producer warps, 64 neurons of each stage apiece
+constexpr uint32_t kDtSmem = kDtABufs * kDtA + kDtRawStages * kDtRaw + 256 + kDtProducers * kDtDescCache * 8;
+constexpr uint32_t kDtThreads = 480;                    // producer, MMA, 8 converter, 4 epilogue, producer warps
 constexpr uint32_t kDtTmemCols = 32;                    // [2 units][2 M tiles] x 8 columns
 constexpr uint32_t kMaxDownSplits = 16;
 static_assert(kDtRaw % 128 == 0 && kDtA % 1024 == 0 && kDtSmem <= 227 * 1024, "stage alignment, budget");
@@ -998,7 +999,9 @@ __global__ void batch_h_tc_kernel(const BatchParams p) {
 
 // Persistent: CTA c takes work units c, c + grid, ... (unit = split x
 // column block, split-major, so that the CTAs working at one time read
-// neighbouring pieces of the same down rows). The producer keeps the
+// neighbouring pieces of the same down rows). Two producer warps (0 and 14)
+// fill neurons 0..63 and 64..127 of each stage (one warp was measured to
+// take longer per stage than the conversion and the MMAs); each keeps the
 // physical group, source slot and kind of up to kDtDescCache union groups in
 // shared memory (refilled when a stage's groups fall outside), so no stage
 // waits on a global load before its copies are issued.
@@ -1019,7 +1022,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
     if (warp == 1) tc_alloc<kDtTmemCols>(sm_u32(tslot));
     if (tid == 0) {
         for (uint32_t i = 0; i < kDtRawStages; ++i) {
-            tc_mbar_init(sm_u32(rfull + i), 32);
+            tc_mbar_init(sm_u32(rfull + i), 32 * kDtProducers);
             tc_mbar_init(sm_u32(rempty + i), 1);
         }
         for (uint32_t i = 0; i < kDtABufs; ++i) {
@@ -1046,10 +1049,16 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
     };
     bool ok = true;
 
-    if (warp == 0) {
-        // producer: lane l fills neurons l and l + 32 of each stage
+    if (warp == 0 || warp == 14) {
+        // producer pw: neurons 64 pw .. 64 pw + 63 of each stage; lane l
+        // resolves neurons 64 pw + l and 64 pw + l + 32
+        const uint32_t pw = warp == 0 ? 0u : 1u;
+        uint2* dc = dcache + pw * kDtDescCache;
         uint32_t gs = 0, cache_lo = 0xFFFFFFFFu;
         const size_t rec = size_t(p.G) * (3 * p.H / 2);
+        const bool pow2 = (p.G & (p.G - 1)) == 0;
+        const uint32_t gshift = uint32_t(__ffs(int(p.G)) - 1);
+        auto group_of = [&](uint32_t n) { return pow2 ? n >> gshift : n / p.G; };
         for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
             const uint32_t split = u / CB, c0 = (u % CB) * kDtCols;
             uint32_t sb, se;
@@ -1062,32 +1071,34 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
                     break;
                 }
                 const uint32_t k0 = s * kDtK, n_valid = min(kDtK, p.NT - k0);
-                const uint32_t u_first = k0 / p.G, u_last = (k0 + n_valid - 1) / p.G;
-                if (cache_lo == 0xFFFFFFFFu || u_first < cache_lo || u_last >= cache_lo + kDtDescCache) {
-                    __syncwarp();
-                    cache_lo = u_first;
-                    for (uint32_t i = lane; i < kDtDescCache && cache_lo + i < p.U; i += 32) {
-                        const ls_exec_desc d = p.desc[cache_lo + i];
-                        dcache[i] = make_uint2(d.source_slot | (d.source_kind == LS_SOURCE_STAGING ? 0x80000000u : 0u),
+                const uint32_t my0 = 64 * pw, my_valid = n_valid > my0 ? min(64u, n_valid - my0) : 0u;
+                if (my_valid) {
+                    const uint32_t u_first = group_of(k0 + my0), u_last = group_of(k0 + my0 + my_valid - 1);
+                    if (cache_lo == 0xFFFFFFFFu || u_first < cache_lo || u_last >= cache_lo + kDtDescCache) {
+                        __syncwarp();
+                        cache_lo = u_first;
+                        for (uint32_t i = lane; i < kDtDescCache && cache_lo + i < p.U; i += 32) {
+                            const ls_exec_desc d = p.desc[cache_lo + i];
+                            dc[i] = make_uint2(d.source_slot | (d.source_kind == LS_SOURCE_STAGING ? 0x80000000u : 0u),
                                                d.physical_group);
+                        }
+                        __syncwarp();
                     }
-                    __syncwarp();
                 }
                 const uint32_t bar = sm_u32(rfull + slot);
                 uint8_t* st = raw + slot * kDtRaw;
-                if (lane == 0) {
+                if (pw == 0 && lane == 0) {
                     tc_expect_tx(bar, kDtH);
                     tc_bulk(sm_u32(st + kDtW), p.hB + size_t(k0) * kBatchTokens, kDtH, bar);
                 }
-                // lane l resolves neurons l, l + 32, l + 64, l + 96 (source, scale copy)
-                const uint8_t* src[kDtK / 32];
+                const uint8_t* src[2];
 #pragma unroll
-                for (uint32_t j = 0; j < kDtK / 32; ++j) {
-                    const uint32_t kl = lane + 32u * j;
+                for (uint32_t j = 0; j < 2; ++j) {
+                    const uint32_t kl = my0 + lane + 32u * j;
                     src[j] = nullptr;
                     if (kl >= n_valid) continue;
-                    const uint32_t n = k0 + kl, nl = n % p.G;
-                    const uint2 e = dcache[n / p.G - cache_lo];
+                    const uint32_t n = k0 + kl, g = group_of(n), nl = n - g * p.G;
+                    const uint2 e = dc[g - cache_lo];
                     const uint8_t* base = (e.x & 0x80000000u) ? p.staging : p.cache;
                     src[j] = base + size_t(e.x & 0x7FFFFFFFu) * rec + size_t(nl) * (3 * p.H / 2) + p.H + c0 / 2;
                     const __half* sc = p.scales + (size_t(e.y) * p.G + nl) * 3 * (p.H / 128);
@@ -1095,11 +1106,11 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
                 }
                 // 16-byte cp.async, one instruction = 4 neurons x 128 B
 #pragma unroll
-                for (uint32_t i = 0; i < kDtK / 4; ++i) {
-                    const uint32_t kl = 4 * i + (lane >> 3), part = lane & 7u;  // i / 8 = kl / 32: uniform
+                for (uint32_t i = 0; i < 16; ++i) {
+                    const uint32_t kr = 4 * i + (lane >> 3), part = lane & 7u;  // i / 8 = kr / 32: uniform
                     const uint8_t* rs = reinterpret_cast<const uint8_t*>(
-                        __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src[i / 8]), kl & 31u));
-                    if (kl < n_valid) cp_async16(st + kl * kDtRowPitch + 16 * part, rs + 16 * part);
+                        __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src[i / 8]), kr & 31u));
+                    if (my0 + kr < n_valid) cp_async16(st + (my0 + kr) * kDtRowPitch + 16 * part, rs + 16 * part);
                 }
                 cp_async_arrive(bar);
             }
@@ -1181,7 +1192,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
         }
         if (!ok) tc_fail(err);
     } else {
-        // epilogue: rows 32 quarter .. +31 of both M tiles of the unit
+        // epilogue (warps 10..13): rows 32 quarter .. +31 of both M tiles of the unit
         const uint32_t quarter = warp & 3, m = 32 * quarter + lane;
         const uint32_t colm = 8 * (m / 8) + ((m % 8) >> 1) + 4 * (m & 1);
         uint32_t ui = 0;
