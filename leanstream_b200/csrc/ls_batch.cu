@@ -527,9 +527,10 @@ constexpr uint32_t kIdescDown = (1u << 4) | (1u << 15) | ((8u >> 3) << 17) | ((1
 // gate/up geometry. A ring stage is 256 coordinates of the tile's 128 rows
 // (128 B of each row); an A chunk is 128 of them (one scale block, 64
 // tensor-memory columns, 8 MMAs), converted by one of two warp groups in
-// turn. Each wait of the MMA thread drains the MMA pipeline (measured: a
-// few hundred cycles, and even a plain shared-memory load of the issuing
-// thread stalls behind its MMAs), so it waits once per chunk; with two CTAs
+// turn, which also copies the chunk's x slice next to the A buffer. Each
+// wait of the MMA thread drains the MMA pipeline (measured: a few hundred
+// cycles, and even a plain shared-memory load of the issuing thread stalls
+// behind its MMAs), so it waits once per chunk (A ready); with two CTAs
 // per SM the other CTA's MMAs keep the tensor core busy meanwhile, and the
 // sixteen converter warps of the SM hide each other's latency. (Measured
 // alternative, slower: one CTA per SM waiting once per 16 MMAs.)
@@ -545,8 +546,10 @@ constexpr uint32_t kGtStages = 4;
 constexpr uint32_t kGtABufs = 3;                        // A buffers of kGtChunk / 2 columns, in rotation
 constexpr uint32_t kGtDCol = kGtABufs * kGtChunk / 2;   // two accumulators (consecutive units) of 16 columns
 constexpr uint32_t kGtTmemCols = 256;
+constexpr uint32_t kGtXC = kGtChunk * kBatchTokens * 2;  // 2048: a chunk's x slice, copied next to its A buffer
+constexpr uint32_t kGtXCopy = kGtStages * kGtStage;     // the x copies [kGtABufs][kGtXC]
 constexpr uint32_t kGtBars = 2 * kGtStages + 2 * kGtABufs + 4;  // full, empty, afull, aempty, dfull[2], dempty[2]
-constexpr uint32_t kGtSmem = kGtStages * kGtStage + 256;
+constexpr uint32_t kGtSmem = kGtXCopy + kGtABufs * kGtXC + 256;
 constexpr uint32_t kGtCtasPerSm = 2;
 constexpr uint32_t kGtThreads = 448;                    // producer, MMA, 8 converter, 4 epilogue warps
 static_assert(kGtStage % 128 == 0 && kGtW % 16 == 0 && (kGtW + kGtX) % 16 == 0, "stage alignment");
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
     extern __shared__ __align__(1024) uint8_t sm[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kGtSmem - 256);
     uint64_t* full = bars;                    // [kGtStages] producer -> converters
-    uint64_t* empty = bars + kGtStages;       // [kGtStages] MMA -> producer
+    uint64_t* empty = bars + kGtStages;       // [kGtStages] converters -> producer
     uint64_t* afull = bars + 2 * kGtStages;   // [kGtABufs] converters -> MMA
     uint64_t* aempty = afull + kGtABufs;      // [kGtABufs] MMA -> converters
     uint64_t* dfull = aempty + kGtABufs;      // [2] MMA -> epilogue
@@ -776,7 +779,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
     if (tid == 0) {
         for (uint32_t i = 0; i < kGtStages; ++i) {
             tc_mbar_init(sm_u32(full + i), 32);  // the producer's 32 lanes (+ the x copy's bytes)
-            tc_mbar_init(sm_u32(empty + i), 1);  // tcgen05.commit after the stage's last MMA
+            tc_mbar_init(sm_u32(empty + i), 8);  // the eight converter warps, once they have read the stage
         }
         for (uint32_t i = 0; i < kGtABufs; ++i) {
             tc_mbar_init(sm_u32(afull + i), 4);   // one converter warp per tensor-memory lane quarter
@@ -854,7 +857,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
         if (lane == 0) drain_ring(full, kGtStages, gs, deadline);
         __syncwarp();
     } else if (warp == 1) {
-        // MMA issuer: one wait (two at a stage's first chunk) and 8 MMAs per chunk
+        // MMA issuer: one wait and 8 MMAs per chunk
         if (lane == 0) {
             uint32_t gq = 0, ui = 0;
             for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++ui) {
@@ -868,18 +871,18 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
                 }
                 tc_fence_after();
                 for (uint32_t q = 0; q < nch; ++q, ++gq) {
-                    const uint32_t gsi = gq / kGtChunks, c = gq % kGtChunks, slot = gsi % kGtStages, a = gq % kGtABufs;
-                    if (c == 0 && !tc_wait(sm_u32(full + slot), (gsi / kGtStages) & 1u, deadline)) ok = false;
-                    if (ok && !tc_wait(sm_u32(afull + a), (gq / kGtABufs) & 1u, deadline)) ok = false;
-                    if (!ok) break;
+                    const uint32_t a = gq % kGtABufs;
+                    if (!tc_wait(sm_u32(afull + a), (gq / kGtABufs) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    const uint32_t xb = sm_u32(sm + slot * kGtStage + kGtW) + c * kGtChunk * 16;
+                    const uint32_t xb = sm_u32(sm + kGtXCopy + a * kGtXC);
 #pragma unroll
                     for (uint32_t kk = 0; kk < kGtChunk / 16; ++kk)
                         tc_mma_ts(dcol, tmem + a * (kGtChunk / 2) + kk * 8, tc_desc(xb + 256 * kk, 128, 0),
                                   kIdescGateUp, (q | kk) ? 1u : 0u);
                     tc_commit(sm_u32(aempty + a));
-                    if (c == kGtChunks - 1) tc_commit(sm_u32(empty + slot));
                 }
                 tc_commit(sm_u32(dfull + d));  // arrives when every MMA so far has completed
             }
@@ -912,14 +915,20 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
                 const uint8_t* st = sm + slot * kGtStage;
                 const __half2 s2 = valid ? __half2half2(reinterpret_cast<const __half*>(st + kGtW + kGtX)[2 * row + c])
                                          : __float2half2_rn(0.f);
+                uint4 w4[4];
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i)
+                    w4[i] = valid ? *reinterpret_cast<const uint4*>(st + row * kGtRowPitch + 64 * c + 16 * i)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+                // the chunk's x slice next to the A buffer (thread `row` copies 16 B)
+                reinterpret_cast<uint4*>(sm + kGtXCopy + a * kGtXC)[row] =
+                    reinterpret_cast<const uint4*>(st + kGtW + c * kGtXC)[row];
+                __syncwarp();
+                if (lane == 0) tc_arrive(sm_u32(empty + slot));  // this warp is done with the raw stage
 #pragma unroll
                 for (uint32_t h = 0; h < 2; ++h) {  // two halves of 32 columns
                     uint32_t v[32];
-                    uint4 w0 = make_uint4(0u, 0u, 0u, 0u), w1 = w0;
-                    if (valid) {
-                        w0 = *reinterpret_cast<const uint4*>(st + row * kGtRowPitch + 64 * c + 32 * h);
-                        w1 = *reinterpret_cast<const uint4*>(st + row * kGtRowPitch + 64 * c + 32 * h + 16);
-                    }
+                    const uint4 w0 = w4[2 * h], w1 = w4[2 * h + 1];
                     const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -931,6 +940,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
                     }
                     tc_st32(tmem + lanebits + a * (kGtChunk / 2) + 32 * h, v);
                 }
+                proxy_fence();  // the x copy (generic proxy) -> visible to the tensor core
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc_arrive(sm_u32(afull + a));
