@@ -686,9 +686,21 @@ __device__ __forceinline__ uint4 to_pos(uint4 w) {
     return make_uint4(__byte_perm(w.x, w.z, 0x5410), __byte_perm(w.x, w.z, 0x7632), __byte_perm(w.y, w.w, 0x5410),
                       __byte_perm(w.y, w.w, 0x7632));
 }
-// 8 weights of one packed word as fp16(q * s), in the deq order.
+// 8 weights of one packed word as fp16(q * s), in the deq order: the same
+// values as deq(w, 0..3, s) with one shift instead of three. Pairs (0, 4)
+// and (2, 6) are the low nibbles of w and w >> 8 as in deq; pairs (1, 5) and
+// (3, 7) stay in place in mantissa bits 4..7 (mask 0x00F000F0), where the
+// biased nibble reads 1024 + 16 (q + 8), and v / 16 - 72 = q exactly (one
+// fma of exact operands); the product with s is the one rounding.
 __device__ __forceinline__ uint4 deq8(uint32_t w, __half2 s2) {
-    return make_uint4(deq(w, 0, s2), deq(w, 1, s2), deq(w, 2, s2), deq(w, 3, s2));
+    const uint32_t w8 = w >> 8;
+    const __half2 bias = __float2half2_rn(1032.f), sixteenth = __float2half2_rn(0.0625f),
+                  m72 = __float2half2_rn(-72.f);
+    const __half2 q0 = __hsub2(u2h((w & 0x000F000Fu) ^ 0x64086408u), bias);
+    const __half2 q1 = __hfma2(u2h((w & 0x00F000F0u) ^ 0x64806480u), sixteenth, m72);
+    const __half2 q2 = __hsub2(u2h((w8 & 0x000F000Fu) ^ 0x64086408u), bias);
+    const __half2 q3 = __hfma2(u2h((w8 & 0x00F000F0u) ^ 0x64806480u), sixteenth, m72);
+    return make_uint4(h2u(__hmul2(q0, s2)), h2u(__hmul2(q1, s2)), h2u(__hmul2(q2, s2)), h2u(__hmul2(q3, s2)));
 }
 __device__ __forceinline__ void tc_fail(uint32_t* err) {
     if (err) atomicOr(err, 1u);
