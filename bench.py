@@ -51,11 +51,13 @@ FMIN, FMAX = 0.2, 0.4
 GROUP_BYTES = G * 3 * H // 2                  # packed INT4 bytes per group
 SCALE_BYTES = G * 3 * (H // 128) * 2          # fp16 scale bytes per group
 ALG_BYTES_PER_GROUP = GROUP_BYTES + SCALE_BYTES  # 405,504 B (algorithmic bytes)
-# dram__bytes_read.sum + dram__bytes_write.sum of one fused_mlp_kernel launch
-# (8-layer stack, token 3: 183.12 MB + 6.43 MB) divided by that launch's
-# algorithmic bytes (449 groups x 405,504 B = 182.07 MB): weights are read
-# once, the excess is tagged scratch evicted from L2.
-TRAFFIC_PER_ALG_BYTE = 1.0411
+# DRAM bytes (read + write) per algorithmic byte of the fused kernel, from
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) over the 13 launches of
+# `bench.py --layers 8 --steps 2 --warmup 3 --headline-only --no-cpu-baseline`
+# (8-layer stacks: 189.3 MB read + 2.0 MB written per launch against 196.5 MB
+# algorithmic): weights are read once, slightly less at 8 layers because
+# consecutive tokens' active sets overlap in L2.
+TRAFFIC_PER_ALG_BYTE = 0.974
 SEED = 3
 EPS = 1e-5
 WORKLOAD = "config3: 36-layer MLP stack, H4096/I12288, 192x64 groups, 20-40% active/layer, batch 1"
@@ -71,7 +73,10 @@ def set_config(config: int) -> None:
     if config == 5:
         H, I, NGROUPS, LAYERS = 8192, 28672, 448, 80
         FMIN = FMAX = 0.2  # k = round(0.2 * 448) = 90 groups per layer
-        TRAFFIC_PER_ALG_BYTE = None  # no ncu capture of this geometry
+        # the same capture on `--config 5 --layers 4` (296.4 MB read + 29.7 MB
+        # written per launch against 292.0 MB algorithmic; the writes are
+        # partial rows evicted from L2)
+        TRAFFIC_PER_ALG_BYTE = 1.117
         WORKLOAD = "config5: 80-layer MLP stack, H8192/I28672, 448x64 groups, 20% active/layer, batch 1"
         METRIC = "MLP-stack tokens/s (batch-1 decode, 80 layers, H8192/I28672, 20% active INT4 groups)"
     GROUP_BYTES = G * 3 * H // 2
