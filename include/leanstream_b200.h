@@ -404,6 +404,9 @@ typedef struct ls_b200_batch_args {
     uint32_t* error;          /* optional device word: bit 0 set (atomic OR, never cleared) when a
                                * bounded wait of the tensor-core kernels gave up; the call's
                                * outputs are then invalid */
+    uint64_t timeout_ns;      /* bound of every wait of the tensor-core kernels (0 = 2 s, at most
+                               * 60 s); after it, the kernels still wait up to 1 s more for their
+                               * own copies and MMAs in flight before they end */
 } ls_b200_batch_args;
 /* Flags of ls_b200_batch_args.flags besides LS_B200_NORM_INPUT. */
 enum {

@@ -129,7 +129,8 @@ class BatchArgs(C.Structure):
                 ("residual", C.c_void_p), ("hidden_out", C.c_void_p), ("cache", C.c_void_p),
                 ("staging", C.c_void_p), ("scales", C.c_void_p), ("union_descs", C.c_void_p), ("mask", C.c_void_p),
                 ("scratch", C.c_void_p), ("scratch_bytes", C.c_uint64), ("flags", C.c_uint32),
-                ("rms_eps", C.c_float), ("norm_weight", C.c_void_p), ("error", C.c_void_p)]
+                ("rms_eps", C.c_float), ("norm_weight", C.c_void_p), ("error", C.c_void_p),
+                ("timeout_ns", C.c_uint64)]
 
 assert C.sizeof(IOCompletion) == 24 and C.sizeof(IOBackend) == 64 and C.sizeof(StreamConfig) == 104
 assert C.sizeof(ExecDesc) == 20 and C.sizeof(QueueControl) == 128 and C.sizeof(DeviceExecQueue) == 32

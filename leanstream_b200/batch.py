@@ -85,17 +85,24 @@ class BatchMLP:
 
     def args(self, *, x, output, cache, scales, union_descs, union_count: int, tokens: int, mask=None,
              residual=None, hidden_out=None, output_f32=None, staging=None, norm_input=False, rms_eps=1e-5,
-             norm_weight=None, mma_sync=False) -> N.BatchArgs:
+             norm_weight=None, mma_sync=False, timeout_ns=0) -> N.BatchArgs:
         """norm_input: HF RMSNorm of each token before the MLP (with residual
         and hidden_out, one layer of a decode stack). mma_sync: the legacy
-        warp-level MMA kernels instead of tcgen05 (for comparison)."""
+        warp-level MMA kernels instead of tcgen05 (for comparison).
+        timeout_ns: bound of the tcgen05 kernels' waits (0 = 2 s)."""
         if union_count > self.max_union:
             raise ValueError(f"union of {union_count} groups, BatchMLP sized for {self.max_union}")
         return N.BatchArgs(self.hidden, self.group_size, union_count, tokens, _ptr(x), _ptr(output),
                            _ptr(output_f32), _ptr(residual), _ptr(hidden_out), _ptr(cache), _ptr(staging),
                            _ptr(scales), _ptr(union_descs), _ptr(mask), self.scratch_ptr, self.scratch_bytes,
                            (N.NORM_INPUT if norm_input else 0) | (N.BATCH_MMA_SYNC if mma_sync else 0), rms_eps,
-                           _ptr(norm_weight), self.error_ptr)
+                           _ptr(norm_weight), self.error_ptr, int(timeout_ns))
+
+    def clear_error(self) -> None:
+        """Zeroes the owned error word (stream-ordered on torch's current stream)."""
+        if self._error is None:
+            raise RuntimeError("the error word is caller-owned (BatchMLP(error=...)): clear it there")
+        self._error.zero_()
 
     def error(self) -> int:
         """Nonzero when a bounded wait of a tensor-core kernel gave up (the

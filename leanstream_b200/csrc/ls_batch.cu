@@ -75,6 +75,7 @@ struct BatchParams {
     float* gpart;         // gate/up split sums [gu_splits][rows_total][8]
     __half* hB;           // h image [NT64 / 8][8 tokens][8] fp16
     uint32_t gu_splits, dn_splits, rows_total;
+    uint64_t timeout_ns;  // bound of the tensor-core kernels' waits
 };
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -513,11 +514,14 @@ __global__ void __launch_bounds__(256) batch_norm_kernel(const __half* x, const 
 // the accumulator rows, which the epilogue undoes (row 8g + p holds column
 // 8g + (p >> 1) + 4 (p & 1)).
 //
-// Every wait is bounded (kTcTimeoutNs): on expiry the waiting role sets bit 0
-// of the caller's error word (ls_b200_batch_args.error) and leaves its loop;
-// the producer then waits (bounded) for the copies it issued, the MMA thread
-// for the MMAs it issued, and the tensor memory is freed before the CTA ends.
-constexpr uint64_t kTcTimeoutNs = 2000000000ull;
+// Every wait is bounded (ls_b200_batch_args.timeout_ns, 2 s by default): on
+// expiry the waiting role sets bit 0 of the caller's error word
+// (ls_b200_batch_args.error) and leaves its loop; the producer then waits for
+// the copies it issued and the MMA thread for the MMAs it issued (bounded by
+// a further kTcGraceNs), and the tensor memory is freed before the CTA ends.
+constexpr uint64_t kTcTimeoutNs = 2000000000ull;        // default bound of every wait
+constexpr uint64_t kTcMaxTimeoutNs = 60000000000ull;
+constexpr uint64_t kTcGraceNs = 1000000000ull;          // drains of own copies / MMAs after a timeout
 // kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A and B fp16 (0),
 // K-major unless bit 15 (A M-major) is set, N >> 3 in bits 17-22, M >> 4 in
 // bits 24-28.
@@ -608,9 +612,9 @@ __device__ __forceinline__ bool tc_mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait for the completion of phase `parity`; false at the deadline.
 __device__ __noinline__ bool tc_wait(uint32_t bar, uint32_t parity, uint64_t deadline) {
-    for (uint32_t spins = 1;; ++spins) {
+    for (;;) {
         if (tc_mbar_try(bar, parity)) return true;
-        if ((spins & 63u) == 0 && tc_now() > deadline) return false;
+        if (tc_now() > deadline) return false;  // %globaltimer: a few cycles beside the try
     }
 }
 __device__ __forceinline__ void tc_arrive(uint32_t bar) {
@@ -807,7 +811,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint64_t deadline = tc_now() + kTcTimeoutNs;
+    const uint64_t deadline = tc_now() + p.timeout_ns, grace = deadline + kTcGraceNs;
     const uint32_t S = p.gu_splits, units = ((p.NT + 63) / 64) * S, stages_all = p.H / kGtK;
     auto unit_stages = [&](uint32_t split, uint32_t& st0, uint32_t& st1) {
         st0 = stages_all * split / S;
@@ -866,7 +870,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
             }
         }
         if (!ok) tc_fail(err);
-        if (lane == 0) drain_ring(full, kGtStages, gs, deadline);
+        if (lane == 0) drain_ring(full, kGtStages, gs, grace);
         __syncwarp();
     } else if (warp == 1) {
         // MMA issuer: one wait and 8 MMAs per chunk
@@ -899,7 +903,7 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
                 tc_commit(sm_u32(dfull + d));  // arrives when every MMA so far has completed
             }
             // every MMA of this CTA complete before the tensor memory is freed
-            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, deadline)) ok = false;
+            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, grace)) ok = false;
             if (!ok) tc_fail(err);
         }
         __syncwarp();
@@ -1061,7 +1065,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint64_t deadline = tc_now() + kTcTimeoutNs;
+    const uint64_t deadline = tc_now() + p.timeout_ns, grace = deadline + kTcGraceNs;
     const uint32_t CB = p.H / kDtCols, units = CB * p.dn_splits;
     // a split's stages: 64-neuron blocks [sb, se) of the union (whole h-image blocks)
     const uint32_t stages_all = (p.NT + kDtK - 1) / kDtK;
@@ -1138,7 +1142,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
             }
         }
         if (!ok) tc_fail(err);
-        if (lane == 0) drain_ring(rfull, kDtRawStages, gs, deadline);
+        if (lane == 0) drain_ring(rfull, kDtRawStages, gs, grace);
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
@@ -1172,7 +1176,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
                 }
                 tc_commit(sm_u32(dfull + d));
             }
-            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, deadline)) ok = false;
+            if (ui && !tc_wait(sm_u32(dfull + ((ui - 1) & 1u)), ((ui - 1) / 2) & 1u, grace)) ok = false;
             if (!ok) tc_fail(err);
         }
         __syncwarp();
@@ -1344,6 +1348,7 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
         (a->norm_weight && !(a->flags & LS_B200_NORM_INPUT)))
         return EINVAL;
     if (a->scratch_bytes < batch_scratch(H, G, U)) return ENOSPC;
+    if (a->timeout_ns > kTcMaxTimeoutNs) return EINVAL;
     if (!al16(a->x) || !al16(a->cache) || (a->staging && !al16(a->staging)) || !al16(a->scratch) ||
         (reinterpret_cast<uintptr_t>(a->scales) & 3u))
         return EINVAL;
@@ -1366,6 +1371,7 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     p.mask = a->mask;
     uint8_t* scratch = static_cast<uint8_t*>(a->scratch);
     const ScratchLayout lay = scratch_layout(H, G, U);
+    p.timeout_ns = a->timeout_ns ? a->timeout_ns : kTcTimeoutNs;
     p.hT = reinterpret_cast<__half*>(scratch + lay.ht);
     p.partial = reinterpret_cast<float*>(scratch + lay.part);
     __half* xn = reinterpret_cast<__half*>(scratch + lay.xn);

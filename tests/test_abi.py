@@ -215,6 +215,9 @@ def test_batch_argument_validation_without_gpu(native_lib):
     assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL
     a = N.BatchArgs(**{**good, "scratch_bytes": need - 1})
     assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.ENOSPC
+    # a wait bound above 60 s is refused
+    a = N.BatchArgs(**{**good, "timeout_ns": 60_000_000_001})
+    assert lib.ls_b200_batch_mlp(C.byref(a), None) == errno.EINVAL
     assert lib.ls_b200_batch_mlp(None, None) == errno.EINVAL
 
 

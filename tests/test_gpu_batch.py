@@ -172,3 +172,43 @@ def test_tcgen05_matches_warp_mma(native_lib, cuda_device, H, n_groups):
         y_ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
         ref = y_ref.astype(np.float32)
         assert np.abs(outs[False][0][b] - ref).max() <= TOL * np.abs(ref).max(), b
+
+
+def test_tcgen05_bounded_waits_report_and_recover(native_lib, cuda_device):
+    """Failure detection without a fault: with a wait bound shorter than the
+    work (timeout_ns = 1) the tensor-core kernels' bounded waits give up, the
+    call sets bit 0 of the error word and ends (each kernel waits, within a
+    further second, for its own copies and MMAs in flight, and frees its
+    tensor memory); the next call on the same stream and scratch, with the
+    default bound, reports no error and matches the oracle."""
+    import torch
+    from leanstream_b200.batch import BatchMLP, union_plan
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    H, G, n_groups, B = 1024, 64, 32, 4
+    L = make_layer(31, H, n_groups, G)
+    rng = np.random.default_rng(9)
+    sets = [np.sort(rng.permutation(n_groups)[: rng.integers(6, 14)]) for _ in range(B)]
+    union, rows, mask = union_plan(sets)
+    x = (rng.standard_normal((B, H)) * 0.5).astype(np.float16)
+    mlp = BatchMLP(H, G, n_groups, device="cuda")
+    kw = dict(x=torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16),
+              cache=torch.from_numpy(L.packed).cuda(),
+              scales=torch.from_numpy(L.scales.reshape(-1).view(np.int16)).cuda().view(torch.float16),
+              union_descs=torch.from_numpy(np.ascontiguousarray(rows.reshape(-1).view(np.int32))).cuda(),
+              union_count=len(union), tokens=B, mask=torch.from_numpy(np.ascontiguousarray(mask)).cuda())
+    y = torch.zeros(B, H, dtype=torch.float16, device="cuda")
+    mlp.run(output=y, timeout_ns=1, **kw)
+    torch.cuda.synchronize()
+    assert mlp.error() & 1
+    mlp.clear_error()
+    y.zero_()
+    mlp.run(output=y, **kw)
+    torch.cuda.synchronize()
+    assert mlp.error() == 0
+    got = y.cpu().numpy().astype(np.float32)
+    for b in range(B):
+        y_ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
+        ref = y_ref.astype(np.float32)
+        assert np.abs(got[b] - ref).max() <= TOL * np.abs(ref).max(), b
