@@ -212,3 +212,56 @@ def test_tcgen05_bounded_waits_report_and_recover(native_lib, cuda_device):
         y_ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
         ref = y_ref.astype(np.float32)
         assert np.abs(got[b] - ref).max() <= TOL * np.abs(ref).max(), b
+
+
+def test_tcgen05_edge_geometry_staging(native_lib, cuda_device):
+    """The tensor-core kernels' edge paths: a group size that is neither a
+    power of two nor a multiple of the 64-neuron tile (G 48: partial gate/up
+    tiles, partial 128-neuron down stages, the producer's division path),
+    some groups read from the staging buffer (kind 1), cache slots permuted,
+    5 tokens at H 2048. Each token matches the oracle over its own set, and
+    the warp-MMA kernels agree."""
+    import torch
+    from leanstream_b200.batch import BatchMLP, union_plan
+    from leanstream_b200.synthetic import descriptors, make_layer
+    from oracle import oracle as O
+
+    H, G, n_groups, B = 2048, 48, 22, 5
+    L = make_layer(77, H, n_groups, G)
+    rng = np.random.default_rng(13)
+    sets = [np.sort(rng.permutation(n_groups)[: rng.integers(5, 12)]) for _ in range(B)]
+    # logical group g sits in cache slot perm[g]
+    perm = rng.permutation(n_groups)
+    gbytes = G * 3 * H // 2
+    packed = L.packed.reshape(n_groups, gbytes)
+    cache_np = np.zeros_like(packed)
+    cache_np[perm] = packed
+    union_all = np.unique(np.concatenate(sets))
+    staged = {int(g): i for i, g in enumerate(union_all[::3])}  # every third union group from staging
+    staging_np = np.zeros((len(staged), gbytes), np.uint8)
+    for g, slot in staged.items():
+        staging_np[slot] = packed[g]
+    union, rows, mask = union_plan(sets, cache_slots=perm, physical=np.arange(n_groups), staging=staged)
+    x = (rng.standard_normal((B, H)) * 0.5).astype(np.float16)
+    mlp = BatchMLP(H, G, n_groups, device="cuda")
+    kw = dict(x=torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16),
+              cache=torch.from_numpy(cache_np.reshape(-1)).cuda(),
+              staging=torch.from_numpy(staging_np.reshape(-1)).cuda(),
+              scales=torch.from_numpy(L.scales.reshape(-1).view(np.int16)).cuda().view(torch.float16),
+              union_descs=torch.from_numpy(np.ascontiguousarray(rows.reshape(-1).view(np.int32))).cuda(),
+              union_count=len(union), tokens=B, mask=torch.from_numpy(np.ascontiguousarray(mask)).cuda())
+    outs = {}
+    for legacy in (False, True):
+        y32 = torch.zeros(B, H, dtype=torch.float32, device="cuda")
+        y = torch.zeros(B, H, dtype=torch.float16, device="cuda")
+        mlp.run(output=y, output_f32=y32, mma_sync=legacy, **kw)
+        torch.cuda.synchronize()
+        outs[legacy] = (y.cpu().numpy().astype(np.float32), y32.cpu().numpy())
+    assert mlp.error() == 0
+    tc, mm = outs[False][1], outs[True][1]
+    assert np.isfinite(tc).all()
+    assert np.abs(tc - mm).max() <= TOL * np.abs(mm).max(), np.abs(tc - mm).max()
+    for b in range(B):
+        y_ref, _, _ = O.mlp(H, G, x[b], L.packed, L.scales, descriptors(sets[b]))
+        ref = y_ref.astype(np.float32)
+        assert np.abs(outs[False][0][b] - ref).max() <= TOL * np.abs(ref).max(), b
