@@ -17,10 +17,17 @@
 // chosen to pair coordinates i and i + 4 of each 8-coordinate word. The
 // product with the scale is then the one fp16 rounding of q * s.
 //
-// Three kernels, each with a fixed summation order (deterministic). The two
-// weight kernels stream their rows through a 4-stage shared-memory ring
-// filled with cp.async (completion by cp.async.wait_group: no spin loop), so
-// three stages of loads are in flight while one is multiplied.
+// Two implementations of the same arithmetic. The default runs the union
+// GEMMs on the 5th-generation tensor cores (tcgen05.mma, accumulators in
+// tensor memory; the "tcgen05" section below, five launches per call). The
+// warp-level MMA kernels described next stay behind LS_B200_BATCH_MMA_SYNC
+// for comparison.
+//
+// Warp-level MMA kernels: three, each with a fixed summation order
+// (deterministic). The two weight kernels stream their rows through a
+// 4-stage shared-memory ring filled with cp.async (completion by
+// cp.async.wait_group: no spin loop), so three stages of loads are in flight
+// while one is multiplied.
 //   gate/up  -- one CTA per 16 union neurons (two octets), 8 warps splitting
 //               each 1024-coordinate stage in 64-coordinate blocks, two
 //               blocks per warp. A rows 0-7 are the octet's gate rows, 8-15
