@@ -963,7 +963,12 @@ __device__ void run_producer(const KernelParams& P, uint8_t* stages, SmemTail* t
     const uint32_t spg = slabs_per_group(P.G);
     bool ok = true;
     for (uint32_t l = 0; ok && l < P.nlayers; ++l) {
-        const LayerPlan& L = plan_at(P, l);
+        // Layers 0 and 1 from the prologue's shared-memory copies (a global
+        // read of the plan is a round trip on the launch's critical path; the
+        // consumers overwrite those slots only after finishing layers 1 and
+        // 2, which the producer has passed). Later layers from global memory:
+        // the producer runs ahead of the consumers' plan fetches.
+        const LayerPlan& L = l < 2 ? cplan_at(t, l) : plan_at(P, l);
         uint32_t total = 0;
         const uint32_t path = decide(P, L, l, t, deadline, pr.lane, &total);
         if (pr.lane == 0 && l == 0) trace(P, LS_B200_TRACE_DECIDED);
