@@ -1797,7 +1797,7 @@ __device__ void consume_down(const KernelParams& P, const Piece& pc, const uint8
 // layer's input is on the critical path, and it is published even after an
 // error so that no reader waits for it), then the outputs are written unless
 // an error had been reported when the reduction started (best effort: the
-// error word is the verdict).
+// error word decides).
 template <int H>
 __device__ __forceinline__ void emit_column(const KernelParams& P, const LayerPlan& L, SmemTail* t, uint32_t c,
                                             float y, uint16_t res, uint32_t err, bool good, uint32_t tag, bool chain,
