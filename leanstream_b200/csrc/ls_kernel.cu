@@ -1849,15 +1849,28 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
     if (blk0 >= NBLK) return;
     const uint32_t tag = scratch_tag(t, l);
     const uint32_t nch = (rows + 15) / 16;
-    for (uint32_t blk = blk0; blk < NBLK; blk += step) {
+    // Blocks are reduced in rounds: with two or more blocks left (hidden
+    // sizes above 32 x grid, e.g. H 8192), warps 0..7 take one block and
+    // warps 8..15 the next, so both blocks' row polls overlap and share the
+    // round's two barriers; a single block takes all 16 warps. A block's sum
+    // order is fixed by the round (chunks c = gw, gw + WG, ... per warp, then
+    // the warps of its group in order), so every launch with the same grid
+    // gives the same bits.
+    // Pairing is compiled only where a full grid leaves CTAs with two
+    // blocks (H / 32 > 148); smaller sizes keep the one-block loop as is.
+    constexpr bool kPair = NBLK > 148;
+    for (uint32_t blk_r = blk0; blk_r < NBLK;) {
+        const uint32_t nb = kPair && blk_r + step < NBLK ? 2u : 1u;
+        const uint32_t WG = kConsumerWarps / nb, grp = uint32_t(warp) / WG, gw = uint32_t(warp) % WG;
+        const uint32_t blk = blk_r + grp * step;
         // the residual and the error word are read now, off the critical
         // path of the last rows
         uint16_t res = 0;
         uint32_t err = 0;
-        if (warp == 0 && L.hidden_out && L.residual) res = __ldcg(L.residual + 32 * blk + lane);
-        if (warp == 0 && lane == 0) err = ld_relaxed_gpu(P.ws + kWsErr);
+        if (gw == 0 && L.hidden_out && L.residual) res = __ldcg(L.residual + 32 * blk + lane);
+        if (gw == 0 && lane == 0) err = ld_relaxed_gpu(P.ws + kWsErr);
         float acc = 0.f;
-        for (uint32_t c = warp; c < nch; c += kConsumerWarps) {
+        for (uint32_t c = gw; c < nch; c += WG) {
             const unsigned long long* p = P.partial + size_t(16 * c) * H + 32 * blk + lane;
             const uint32_t nr = rows - 16 * c < 16u ? rows - 16 * c : 16u;
             unsigned long long w[16];
@@ -1888,11 +1901,10 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
         }
         t->red2[warp][lane] = acc;
         csync(P, t, cph, limit, lane);
-        if (warp == 0) {
+        if (gw == 0) {
             if (blk == blk0 && lane == 0) trace_layer(P, t, l, LS_B200_LTRACE_PARTIALS_READY);
             float y = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) y += t->red2[w][lane];
+            for (uint32_t w = 0; w < WG; ++w) y += t->red2[grp * WG + w][lane];
             const uint32_t c = 32 * blk + lane;
             if (!LEAN && P.world > 1) {
                 // Tensor parallel: this rank's fp32 partial of the column goes
@@ -1906,7 +1918,8 @@ __device__ void end_layer(const KernelParams& P, const LayerPlan& L, uint32_t l,
                 emit_column<H>(P, L, t, c, y, res, err, good, tag, chain, lane);
             }
         }
-        csync(P, t, cph, limit, lane);  // red2 is reused by the next block
+        csync(P, t, cph, limit, lane);  // red2 is reused by the next round
+        blk_r += nb * step;
     }
     if (!LEAN && P.world > 1 && warp == 0) {
         // Gather pass (tensor parallel): every block of this CTA was published
