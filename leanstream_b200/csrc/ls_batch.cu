@@ -567,28 +567,37 @@ static_assert(kGtStage % 128 == 0 && kGtW % 16 == 0 && (kGtW + kGtX) % 16 == 0, 
 static_assert(kGtBars * 8 + 4 <= 256 && kGtSmem * kGtCtasPerSm <= 227 * 1024, "barrier area, shared memory");
 static_assert(kGtDCol + 2 * 16 <= kGtTmemCols, "tensor-memory budget");
 
-// down geometry. A stage is 128 neurons: 16 MMAs (two M tiles x 8 K
-// steps) per wait of the MMA thread. The converters also copy the stage's h
-// slice next to A, so that one barrier (A ready) covers both operands.
-constexpr uint32_t kDtK = 128;                          // neurons per ring stage
+// down geometry. Two CTAs per SM, each with stages of 64 neurons: 8 MMAs
+// (two M tiles x 4 K steps) per wait of a CTA's MMA thread. A wait drains
+// the issuing thread's MMAs (a stage timeline of one CTA per SM with
+// 128-neuron stages: ~1,565 cycles of MMAs, then ~430 of drain, per
+// ~2,000-cycle stage); with two CTAs the other CTA's MMAs keep the tensor
+// core busy meanwhile. The converters also copy the stage's h slice next to
+// A, so that one barrier (A ready) covers both operands.
+constexpr uint32_t kDtK = 64;                           // neurons per ring stage
 constexpr uint32_t kDtCols = 256;                       // output columns per CTA
 constexpr uint32_t kDtRowPitch = 144;                   // 128 B of int4 per neuron + 16
-constexpr uint32_t kDtW = kDtK * kDtRowPitch;           // 18432
-constexpr uint32_t kDtH = kDtK * kBatchTokens * 2;      // 2048: the stage's h image
+constexpr uint32_t kDtW = kDtK * kDtRowPitch;           // 9216
+constexpr uint32_t kDtH = kDtK * kBatchTokens * 2;      // 1024: the stage's h image
 constexpr uint32_t kDtS = kDtK * 4;                     // two fp16 scales per neuron
-constexpr uint32_t kDtRaw = kDtW + kDtH + kDtS;         // 20992
+constexpr uint32_t kDtRaw = kDtW + kDtH + kDtS;         // 10496
 constexpr uint32_t kDtRawStages = 4;
-constexpr uint32_t kDtMTile = 128 * kDtK * 2;           // 32768: one M tile of A
+constexpr uint32_t kDtMTile = 128 * kDtK * 2;           // 16384: one M tile of A
+constexpr uint32_t kDtMGroup = kDtK * 16;               // 1024: between 8-column groups of an M tile
 constexpr uint32_t kDtA = 2 * kDtMTile + kDtH;          // two M tiles + the h copy
 constexpr uint32_t kDtABufs = 2;
 constexpr uint32_t kDtBars = 2 * kDtRawStages + 2 * kDtABufs + 4;  // rfull, rempty, afull, aempty, dfull[2], dempty[2]
 constexpr uint32_t kDtDescCache = 256;                  // union groups cached by the producer
-constexpr uint32_t kDtProducers = 2;                    // producer warps, 64 neurons of each stage apiece
+constexpr uint32_t kDtProducers = 1;                    // producer warps, 64 neurons of each stage apiece
+constexpr uint32_t kDtConverters = 4;                   // converter warps: thread = (neuron, 128-column half)
 constexpr uint32_t kDtSmem = kDtABufs * kDtA + kDtRawStages * kDtRaw + 256 + kDtProducers * kDtDescCache * 8;
-constexpr uint32_t kDtThreads = 480;                    // producer, MMA, 8 converter, 4 epilogue, producer warps
+constexpr uint32_t kDtThreads = 32 * (2 + kDtConverters + 4);  // producer, MMA, converter, 4 epilogue warps
+constexpr uint32_t kDtCtasPerSm = 2;
 constexpr uint32_t kDtTmemCols = 32;                    // [2 units][2 M tiles] x 8 columns
-constexpr uint32_t kMaxDownSplits = 16;
-static_assert(kDtRaw % 128 == 0 && kDtA % 1024 == 0 && kDtSmem <= 227 * 1024, "stage alignment, budget");
+constexpr uint32_t kMaxDownSplits = 32;
+static_assert(kDtRaw % 128 == 0 && kDtA % 1024 == 0 && kDtCtasPerSm * (kDtSmem + 1024) <= 228 * 1024,
+              "stage alignment, budget");
+static_assert(32 * kDtConverters == 2 * kDtK && kDtK == 64 * kDtProducers, "one converter thread per neuron and half");
 static_assert(kDtBars * 8 + 4 <= 256, "barrier area");
 static_assert(kMaxDownSplits >= kDownSplits, "partials sized for both paths");
 
@@ -1032,13 +1041,11 @@ __global__ void batch_h_tc_kernel(const BatchParams p) {
 
 // Persistent: CTA c takes work units c, c + grid, ... (unit = split x
 // column block, split-major, so that the CTAs working at one time read
-// neighbouring pieces of the same down rows). Two producer warps (0 and 14)
-// fill neurons 0..63 and 64..127 of each stage (one warp was measured to
-// take longer per stage than the conversion and the MMAs); each keeps the
+// neighbouring pieces of the same down rows). The producer warp keeps the
 // physical group, source slot and kind of up to kDtDescCache union groups in
 // shared memory (refilled when a stage's groups fall outside), so no stage
 // waits on a global load before its copies are issued.
-__global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const BatchParams p, uint32_t* err) {
+__global__ void __launch_bounds__(kDtThreads, kDtCtasPerSm) batch_down_tc_kernel(const BatchParams p, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm[];
     uint8_t* abuf = sm;                         // [kDtABufs][kDtA]
     uint8_t* raw = sm + kDtABufs * kDtA;        // [kDtRawStages][kDtRaw]
@@ -1059,7 +1066,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
             tc_mbar_init(sm_u32(rempty + i), 1);
         }
         for (uint32_t i = 0; i < kDtABufs; ++i) {
-            tc_mbar_init(sm_u32(afull + i), 8);  // the eight converter warps
+            tc_mbar_init(sm_u32(afull + i), kDtConverters);  // the converter warps
             tc_mbar_init(sm_u32(aempty + i), 1);
         }
         for (uint32_t i = 0; i < 2; ++i) {
@@ -1082,10 +1089,10 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
     };
     bool ok = true;
 
-    if (warp == 0 || warp == 14) {
+    if (warp < kDtProducers) {
         // producer pw: neurons 64 pw .. 64 pw + 63 of each stage; lane l
         // resolves neurons 64 pw + l and 64 pw + l + 32
-        const uint32_t pw = warp == 0 ? 0u : 1u;
+        const uint32_t pw = warp;
         uint2* dc = dcache + pw * kDtDescCache;
         uint32_t gs = 0, cache_lo = 0xFFFFFFFFu;
         const size_t rec = size_t(p.G) * (3 * p.H / 2);
@@ -1176,7 +1183,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
                     for (uint32_t kk = 0; kk < kDtK / 16; ++kk)
 #pragma unroll
                         for (uint32_t mt = 0; mt < 2; ++mt)
-                            tc_mma_ss(dcol + 8 * mt, tc_desc(ab + mt * kDtMTile + 256 * kk, 128, 2048),
+                            tc_mma_ss(dcol + 8 * mt, tc_desc(ab + mt * kDtMTile + 256 * kk, 128, kDtMGroup),
                                       tc_desc(hb + 256 * kk, 128, 1024), kIdescDown, (s != sb || kk) ? 1u : 0u);
                     tc_commit(sm_u32(rempty + slot));
                     tc_commit(sm_u32(aempty + a));
@@ -1187,7 +1194,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
             if (!ok) tc_fail(err);
         }
         __syncwarp();
-    } else if (warp < 10) {
+    } else if (warp < 2 + kDtConverters) {
         // converters: thread (neuron kl, 128-column half mt) of each stage
         const uint32_t t = tid - 64, kl = t & (kDtK - 1), mt = t / kDtK;
         uint32_t gs = 0;
@@ -1214,7 +1221,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
                     const uint32_t w[4] = {w0.x, w0.y, w0.z, w0.w};
 #pragma unroll
                     for (uint32_t q = 0; q < 4; ++q)  // columns 32h + 8q .. +7: core-matrix group 4h + q
-                        *reinterpret_cast<uint4*>(Ak + (4 * h + q) * 2048) = deq8(w[q], s2);
+                        *reinterpret_cast<uint4*>(Ak + (4 * h + q) * kDtMGroup) = deq8(w[q], s2);
                 }
                 if (t < kDtH / 16)  // the stage's h image next to A
                     reinterpret_cast<uint4*>(A + 2 * kDtMTile)[t] = reinterpret_cast<const uint4*>(st + kDtW)[t];
@@ -1225,7 +1232,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) batch_down_tc_kernel(const Batc
         }
         if (!ok) tc_fail(err);
     } else {
-        // epilogue (warps 10..13): rows 32 quarter .. +31 of both M tiles of the unit
+        // epilogue (the last four warps): rows 32 quarter .. +31 of both M tiles of the unit
         const uint32_t quarter = warp & 3, m = 32 * quarter + lane;
         const uint32_t colm = 8 * (m / 8) + ((m % 8) >> 1) + 4 * (m & 1);
         uint32_t ui = 0;
@@ -1322,6 +1329,9 @@ cudaError_t set_ring_attributes() {
         e = cudaFuncSetAttribute(batch_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGtSmem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(batch_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDtSmem));
+    if (e == cudaSuccess)  // two CTAs per SM
+        e = cudaFuncSetAttribute(batch_down_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 int(cudaSharedmemCarveoutMaxShared));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(batch_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDnSmem));
     if (e == cudaSuccess)
@@ -1406,15 +1416,15 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
         p.rows_total = tiles * 128;
         const uint32_t gu_slots = kGtCtasPerSm * uint32_t(sms);
         p.gu_splits = pick_splits(tiles, max_gu_splits(H), gu_slots);
-        p.dn_splits = pick_splits(H / kDtCols, dn_stages < kMaxDownSplits ? dn_stages : kMaxDownSplits, uint32_t(sms));
+        const uint32_t dn_slots = kDtCtasPerSm * uint32_t(sms);
+        p.dn_splits = pick_splits(H / kDtCols, dn_stages < kMaxDownSplits ? dn_stages : kMaxDownSplits, dn_slots);
         batch_ximg_kernel<<<kBatchTokens, 256, 0, s>>>(p.x, norm_w, a->rms_eps, H, B, norm ? 1u : 0u,
                                                        scratch + lay.ximg);
         const uint32_t gu_units = tiles * p.gu_splits, dn_units = (H / kDtCols) * p.dn_splits;
         batch_gateup_tc_kernel<<<gu_units < gu_slots ? gu_units : gu_slots, kGtThreads, kGtSmem, s>>>(p, a->error);
         const uint32_t hn = dn_stages * kDtK * kBatchTokens;
         batch_h_tc_kernel<<<(hn + 255) / 256 < 1024 ? (hn + 255) / 256 : 1024, 256, 0, s>>>(p);
-        batch_down_tc_kernel<<<dn_units < uint32_t(sms) ? dn_units : uint32_t(sms), kDtThreads, kDtSmem, s>>>(
-            p, a->error);
+        batch_down_tc_kernel<<<dn_units < dn_slots ? dn_units : dn_slots, kDtThreads, kDtSmem, s>>>(p, a->error);
     }
     const uint32_t total = B * H;
     batch_epilogue_kernel<<<(total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024, 256, 0, s>>>(p);
