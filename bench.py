@@ -965,16 +965,16 @@ def run_batch(args, rank, world, local_rank):
         "arithmetic": "w = fp16(q * s) as the reference (backends/triton/core.py:17), fp32 accumulation",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None,
-                     "kernel": ("batch_gateup_kernel + batch_down_kernel" if mma_sync else
-                                "batch_gateup_tc_kernel + batch_down_tc_kernel") +
-                               " + batch_norm_kernel + batch_epilogue_kernel (one layer)",
+                     "kernel": ("batch_norm_kernel + batch_gateup_kernel + batch_down_kernel" if mma_sync else
+                                "batch_ximg_kernel + batch_gateup_tc_kernel + batch_down_tc_kernel") +
+                               " + batch_epilogue_kernel (one layer)",
                      "algorithmic_bytes_per_group": ALG_BYTES_PER_GROUP,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback"},
         "e2e": {"value": BATCH * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         # per layer: RMSNorm + gate/up + down + epilogue (warp MMA), or x image
-        # (with the RMSNorm) + gate/up + h + down + epilogue (tcgen05)
-        "gpu_launches": (4 if mma_sync else 5) * LAYERS * args.steps,
+        # (with the RMSNorm) + gate/up (with h) + down + epilogue (tcgen05)
+        "gpu_launches": 4 * LAYERS * args.steps,
         "batch_kernels": args.batch_kernels,
         "clocks": clock,
     }

@@ -19,7 +19,7 @@
 //
 // Two implementations of the same arithmetic. The default runs the union
 // GEMMs on the 5th-generation tensor cores (tcgen05.mma, accumulators in
-// tensor memory; the "tcgen05" section below, five launches per call). The
+// tensor memory; the "tcgen05" section below, four launches per call). The
 // warp-level MMA kernels described next stay behind LS_B200_BATCH_MMA_SYNC
 // for comparison.
 //
@@ -80,6 +80,7 @@ struct BatchParams {
     // tensor-core path
     const uint8_t* ximg;  // x image [H / 8][8 tokens][8] fp16, K-major core matrices
     float* gpart;         // gate/up split sums [gu_splits][rows_total][8]
+    uint32_t* gcnt;       // [tiles][4] stored splits per gate/up tile and lane quarter
     __half* hB;           // h image [NT64 / 8][8 tokens][8] fp16
     uint32_t gu_splits, dn_splits, rows_total;
     uint64_t timeout_ns;  // bound of the tensor-core kernels' waits
@@ -498,15 +499,17 @@ __global__ void __launch_bounds__(256) batch_norm_kernel(const __half* x, const 
 // (batch_ximg_kernel: 8 tokens, K-major core matrices, one 4 KB bulk copy
 // per stage). The form with A in tensor memory takes N >= 16 at M = 128:
 // B rows 8..15 alias rows 0..7 (zero stride between the two 8-row groups)
-// and D columns 8..15 are never read. Each split stores its fp32 sums;
-// batch_h_tc_kernel adds the splits in split order and applies the SiLU
-// chain. The per-stage scales (two per row) are copied by the producer.
+// and D columns 8..15 are never read. Each split stores its fp32 sums; the
+// epilogue warp that stores the last split of a tile's lane quarter (a
+// counter per tile and quarter) adds that quarter's splits in split order,
+// applies the SiLU chain and writes the h image. The per-stage scales (two
+// per row) are copied by the producer.
 //
 // down (batch_down_tc_kernel): CTA = 256 output columns (two M = 128 tiles,
 // two accumulators) x one split of the union's neurons. The MMA's A is the
 // down rows (M = output columns, K = neurons), which only shared memory can
 // hold in that orientation: the converters write M-major core matrices into
-// a double-buffered A area; B = h from the K-major image batch_h_tc_kernel
+// a double-buffered A area; B = h from the K-major image the gate/up kernel
 // writes (one 1 KB bulk copy per 64 neurons).
 //
 // Core-matrix layouts (8 rows x 16 bytes, no swizzle):
@@ -598,6 +601,7 @@ constexpr uint32_t kMaxDownSplits = 32;
 static_assert(kDtRaw % 128 == 0 && kDtA % 1024 == 0 && kDtCtasPerSm * (kDtSmem + 1024) <= 228 * 1024,
               "stage alignment, budget");
 static_assert(32 * kDtConverters == 2 * kDtK && kDtK == 64 * kDtProducers, "one converter thread per neuron and half");
+static_assert(kDtK == 64, "the gate/up tiles (64 neurons) write the h image of whole down stages");
 static_assert(kDtBars * 8 + 4 <= 256, "barrier area");
 static_assert(kMaxDownSplits >= kDownSplits, "partials sized for both paths");
 
@@ -742,15 +746,30 @@ __device__ void drain_ring(const uint64_t* full, uint32_t stages, uint32_t issue
         if (!tc_wait(sm_u32(full + s % stages), (s / stages) & 1u, deadline)) return;
 }
 
+// h of union neuron n for token b from its split sums: the reference's
+// rounding chain (fp16 g and u, s = fp16(silu(g)), h = fp16(s * u)), zero
+// where the token's mask excludes the neuron's group.
+__device__ __forceinline__ __half h_value(const BatchParams& p, float gs, float us, uint32_t n, uint32_t b) {
+    const float g16 = __half2float(__float2half_rn(gs)), u16 = __half2float(__float2half_rn(us));
+    const float sl = __half2float(__float2half_rn(g16 / (1.f + expf(-g16))));
+    __half h = __float2half_rn(sl * u16);
+    if (p.mask && !p.mask[size_t(b) * p.U + n / p.G]) h = __float2half_rn(0.f);
+    return h;
+}
+
 // x image of the gate/up kernel (and the HF RMSNorm of LS_B200_NORM_INPUT,
 // the arithmetic of batch_norm_kernel: inv = rsqrt(sum(x^2) / H + eps),
 // x' = fp16(w * fp16(x * inv))): CTA b writes token b's coordinates in
 // K-major core matrices, zeros for b >= B. Each thread holds up to four
 // 8-coordinate blocks (H <= 8192) in registers; the sum of squares runs in a
-// fixed order (per thread, a shuffle tree, then the warps in order).
+// fixed order (per thread, a shuffle tree, then the warps in order). It also
+// zeroes the gate/up kernel's split counters.
 __global__ void __launch_bounds__(256) batch_ximg_kernel(const __half* x, const __half* w, float eps, uint32_t H,
-                                                         uint32_t B, uint32_t norm, uint8_t* img) {
+                                                         uint32_t B, uint32_t norm, uint8_t* img, uint32_t* cnt,
+                                                         uint32_t ncnt) {
     __shared__ float part[8];
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x)
+        cnt[i] = 0u;  // the gate/up kernel's split counters
     const uint32_t b = blockIdx.x, nkg = H / 8;
     const __half* row = x + size_t(b) * H;
     uint4 v[4];
@@ -1002,6 +1021,37 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
                 out[0] = make_float4(r[0], r[1], r[2], r[3]);
                 out[1] = make_float4(r[4], r[5], r[6], r[7]);
             }
+            // This quarter's rows are the gate and up rows of neurons
+            // 16 quarter .. +15 of the tile. The warp that stores the last of
+            // the tile's S splits of them (stores, fence, then the count; the
+            // counters start at zero) sums the splits in split order and
+            // writes those neurons' h image: neuron n of token b at
+            // (n / 8) * 64 + b * 8 + n % 8, zero past the union and for
+            // tokens >= B. Lane: neuron jn = lane / 2, tokens 4 (lane & 1) .. +3.
+            __threadfence();
+            __syncwarp();
+            uint32_t arrived = 0;
+            if (lane == 0) arrived = atomicAdd(p.gcnt + 4u * tile + quarter, 1u);
+            if (__shfl_sync(0xffffffffu, arrived, 0) == S - 1) {
+                __threadfence();
+                const uint32_t n = 64u * tile + 16u * quarter + (lane >> 1), b0 = 4u * (lane & 1u);
+                float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+                if (n < p.NT)
+                    for (uint32_t sp = 0; sp < S; ++sp) {
+                        const float* q = p.gpart + (size_t(sp) * p.rows_total + 2u * n) * kBatchTokens + b0;
+                        const float4 a = __ldcg(reinterpret_cast<const float4*>(q));
+                        const float4 c = __ldcg(reinterpret_cast<const float4*>(q + kBatchTokens));
+                        g.x += a.x, g.y += a.y, g.z += a.z, g.w += a.w;
+                        up.x += c.x, up.y += c.y, up.z += c.z, up.w += c.w;
+                    }
+                const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {up.x, up.y, up.z, up.w};
+                __half* hb = p.hB + size_t(n / 8) * 64 + n % 8;
+#pragma unroll
+                for (uint32_t j = 0; j < 4; ++j) {
+                    const uint32_t b = b0 + j;
+                    hb[b * 8] = n < p.NT && b < p.B ? h_value(p, gv[j], uv[j], n, b) : __float2half_rn(0.f);
+                }
+            }
         }
         if (!ok) tc_fail(err);
     }
@@ -1010,32 +1060,6 @@ __global__ void __launch_bounds__(kGtThreads, kGtCtasPerSm) batch_gateup_tc_kern
     if (warp == 1) {
         tc_fence_after();
         tc_dealloc<kGtTmemCols>(tmem);
-    }
-}
-
-// h of every (union neuron, token): g and u = the splits' sums added in split
-// order, then the reference's rounding chain (fp16 g and u, s = fp16(silu(g)),
-// h = fp16(s * u)), the token mask, and the K-major h image of the down
-// kernel: neuron n of token b at (n / 8) * 64 + b * 8 + n % 8 (zero past the
-// union, rounded up to a whole down stage of 128 neurons, and for tokens >= B).
-__global__ void batch_h_tc_kernel(const BatchParams p) {
-    const uint32_t ntk = (p.NT + kDtK - 1) / kDtK * kDtK, total = ntk * kBatchTokens;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const uint32_t b = (i / 8) % kBatchTokens, n = (i / 64) * 8 + i % 8;
-        __half h = __float2half_rn(0.f);
-        if (n < p.NT && b < p.B) {
-            float gs = 0.f, us = 0.f;
-            for (uint32_t s = 0; s < p.gu_splits; ++s) {
-                const float* r = p.gpart + (size_t(s) * p.rows_total + 2u * n) * kBatchTokens + b;
-                gs += r[0];
-                us += r[kBatchTokens];
-            }
-            const float g16 = __half2float(__float2half_rn(gs)), u16 = __half2float(__float2half_rn(us));
-            const float sl = __half2float(__float2half_rn(g16 / (1.f + expf(-g16))));
-            h = __float2half_rn(sl * u16);
-            if (p.mask && !p.mask[size_t(b) * p.U + n / p.G]) h = __float2half_rn(0.f);
-        }
-        p.hB[i] = h;
     }
 }
 
@@ -1278,7 +1302,7 @@ __global__ void __launch_bounds__(kDtThreads, kDtCtasPerSm) batch_down_tc_kernel
 // gate/up split sums [splits][rows][8] fp32 and the h image [NT64 / 8][8][8]
 // fp16 (tensor-core path).
 struct ScratchLayout {
-    uint64_t ht, part, xn, ximg, gpart, hb, total;
+    uint64_t ht, part, xn, ximg, gpart, hb, gcnt, total;
 };
 constexpr uint64_t up256(uint64_t v) { return (v + 255) / 256 * 256; }
 uint32_t max_gu_splits(uint32_t H) { return H >= 2048 ? H / 1024 : 1u; }  // splits of >= 1024 coordinates
@@ -1291,7 +1315,8 @@ ScratchLayout scratch_layout(uint32_t H, uint32_t G, uint32_t U) {
     l.ximg = l.xn + up256(uint64_t(kBatchTokens) * H * sizeof(__half));
     l.gpart = l.ximg + up256(uint64_t(H) * kBatchTokens * sizeof(__half));
     l.hb = l.gpart + up256(uint64_t(max_gu_splits(H)) * 2 * nt64 * kBatchTokens * sizeof(float));
-    l.total = l.hb + up256((nt + kDtK - 1) / kDtK * kDtK * kBatchTokens * sizeof(__half)) + 256;
+    l.gcnt = l.hb + up256((nt + kDtK - 1) / kDtK * kDtK * kBatchTokens * sizeof(__half));
+    l.total = l.gcnt + up256((nt + 63) / 64 * 4 * sizeof(uint32_t)) + 256;
     return l;
 }
 uint64_t batch_scratch(uint32_t H, uint32_t G, uint32_t U) { return scratch_layout(H, G, U).total; }
@@ -1395,6 +1420,7 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
     p.ximg = scratch + lay.ximg;
     p.gpart = reinterpret_cast<float*>(scratch + lay.gpart);
     p.hB = reinterpret_cast<__half*>(scratch + lay.hb);
+    p.gcnt = reinterpret_cast<uint32_t*>(scratch + lay.gcnt);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (const cudaError_t e = set_ring_attributes(); e != cudaSuccess) return int(e);
     const __half* norm_w = static_cast<const __half*>(a->norm_weight);
@@ -1419,11 +1445,9 @@ int ls_b200_batch_mlp(const ls_b200_batch_args* a, void* stream) {
         const uint32_t dn_slots = kDtCtasPerSm * uint32_t(sms);
         p.dn_splits = pick_splits(H / kDtCols, dn_stages < kMaxDownSplits ? dn_stages : kMaxDownSplits, dn_slots);
         batch_ximg_kernel<<<kBatchTokens, 256, 0, s>>>(p.x, norm_w, a->rms_eps, H, B, norm ? 1u : 0u,
-                                                       scratch + lay.ximg);
+                                                       scratch + lay.ximg, p.gcnt, 4 * tiles);
         const uint32_t gu_units = tiles * p.gu_splits, dn_units = (H / kDtCols) * p.dn_splits;
         batch_gateup_tc_kernel<<<gu_units < gu_slots ? gu_units : gu_slots, kGtThreads, kGtSmem, s>>>(p, a->error);
-        const uint32_t hn = dn_stages * kDtK * kBatchTokens;
-        batch_h_tc_kernel<<<(hn + 255) / 256 < 1024 ? (hn + 255) / 256 : 1024, 256, 0, s>>>(p);
         batch_down_tc_kernel<<<dn_units < dn_slots ? dn_units : dn_slots, kDtThreads, kDtSmem, s>>>(p, a->error);
     }
     const uint32_t total = B * H;
