@@ -1063,21 +1063,24 @@ def cpu_layers_per_step() -> int:
 
 def cpu_stack_rate(budget_s: float = 12.0, threads: int = 0):
     """cpu_baseline of the GPU arm: the CPU path on a bounded sample of the
-    same workload (the layers of token 0, in order, until `budget_s`)."""
+    same workload (the layers of tokens 0, 1, ... in order, until `budget_s`
+    of CPU work or 64 tokens)."""
     nthreads = threads or host_cores()
     path = CpuPath(nthreads)
     pred = path.predictor_available()
-    sets = active_sets(0)
-    done, elapsed = 0, 0.0
-    for layer in range(LAYERS):
-        elapsed += path.layer_seconds(sets[layer])
-        done += 1
-        if elapsed >= budget_s:
-            break
+    done, elapsed, tokens = 0, 0.0, 0
+    while elapsed < budget_s and tokens < 64:
+        sets = active_sets(tokens)
+        for layer in range(LAYERS):
+            elapsed += path.layer_seconds(sets[layer])
+            done += 1
+            if elapsed >= budget_s:
+                break
+        tokens += 1
     per_layer = elapsed / done
     what = "ls_predict + sparse MLP port" if pred else "sparse MLP port (reference predictor library absent)"
     return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": int(nthreads), "kind": "port",
-            "sample": f"{done} of {LAYERS} layers of token 0 ({what}; same shapes and active sets), "
+            "sample": f"{done} layers of tokens 0-{tokens - 1} ({what}; same shapes and active sets), "
                       f"{elapsed:.1f} s of CPU work; tokens/s = 1/({LAYERS} x mean layer time)"}
 
 
